@@ -1,0 +1,211 @@
+/*
+ * include/sam3cu.h - C ABI of the B200 (sm_100a) backend for sam3.c's image
+ * encoder hot path.  Plain pointers and sizes only; no CUDA or torch types
+ * (streams are passed as `void *` holding a cudaStream_t, NULL = the
+ * library's default stream).
+ *
+ * Reference interfaces each entry point replaces (paths inside sam3.c):
+ *   sam3cu_linear / sam3cu_linear_q8
+ *       gh_linear = TRANSPOSE(W) -> MATMUL -> ADD(bias)
+ *       (src/model/graph_helpers.c:297-322) evaluated by cpu_kernel_matmul
+ *       (src/backend/cpu/kernels/cpu_matmul.c:196-257), _bf16
+ *       (cpu_matmul_bf16.c:183-251), _f16 (cpu_matmul_f16.c) and the F32 x
+ *       Q8_0 kernel (cpu_matmul_q8.c:168-235), plus the activation node of
+ *       gh_mlp (graph_helpers.c:1258-1278, tanh-GELU cpu_gelu.c:23-36) and
+ *       the residual ADD of the ViT block (image_encoder.c:868,896).
+ *   sam3cu_layernorm
+ *       SAM3_OP_LAYERNORM, cpu_kernel_layernorm (cpu_layernorm.c:210-254).
+ *   sam3cu_sdpa
+ *       SAM3_OP_SDPA, cpu_kernel_sdpa (cpu_sdpa.c:216-288), with the
+ *       surrounding SLICE/PERMUTE of gh_multihead_attention_rope
+ *       (graph_helpers.c:721-882) folded into strides.
+ *   sam3cu_q8_quantize
+ *       sam3_q8_quantize (src/core/quant.c:67-131), bit-identical output.
+ *   sam3cu_vit_*
+ *       sam3_vit_init / sam3_vit_load / sam3_vit_build
+ *       (src/model/image_encoder.h:112-173, image_encoder.c:513-963): the
+ *       whole encoder forward lowered to fused kernels on one GPU.
+ *   sam3_cuda_backend_ops (include/sam3cu_backend.h)
+ *       the backend vtable struct sam3_backend_ops (src/backend/backend.h:29-56).
+ *
+ * Every function returns 0 on success or a negative SAM3CU_E* code; the
+ * codes -1..-7 are the reference's enum sam3_error values.
+ */
+#ifndef SAM3CU_H
+#define SAM3CU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SAM3CU_API __attribute__((visibility("default")))
+#else
+#define SAM3CU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types: the reference's enum sam3_dtype codes (sam3_types.h:47-54). */
+enum sam3cu_dtype {
+	SAM3CU_F32  = 0,
+	SAM3CU_F16  = 1,
+	SAM3CU_BF16 = 2,
+	SAM3CU_Q8_0 = 5,
+};
+
+enum sam3cu_status {
+	SAM3CU_OK        = 0,
+	SAM3CU_EINVAL    = -1,   /* = SAM3_EINVAL */
+	SAM3CU_ENOMEM    = -2,   /* = SAM3_ENOMEM */
+	SAM3CU_EBACKEND  = -4,   /* = SAM3_EBACKEND */
+	SAM3CU_EDTYPE    = -6,   /* = SAM3_EDTYPE */
+	SAM3CU_ESHAPE    = -101, /* shape/alignment the kernels do not take */
+	SAM3CU_ETMA      = -102, /* TMA descriptor creation failed */
+	SAM3CU_ELAUNCH   = -103, /* kernel launch failed */
+	SAM3CU_ECUDA     = -104, /* CUDA runtime error */
+	SAM3CU_EDEVICE   = -105, /* a device-side bounded wait gave up */
+	SAM3CU_EDTYPE2   = -106, /* unsupported dtype combination */
+	SAM3CU_ENOMEM2   = -107, /* device allocation failed */
+};
+
+/* Activation fused into a linear's epilogue. */
+enum sam3cu_act {
+	SAM3CU_ACT_NONE = 0,
+	SAM3CU_ACT_GELU_TANH = 1, /* 0.5x(1+tanh(0.7978845608(x+0.044715x^3))) */
+};
+
+/* Select and initialise a CUDA device for the calling thread. */
+SAM3CU_API int sam3cu_init(int device);
+
+/* Human-readable text for a status code. */
+SAM3CU_API const char *sam3cu_strerror(int status);
+
+/* Synchronise the device and return (and clear) the first nonzero
+ * device-side error word recorded by any kernel; 0 if none. */
+SAM3CU_API unsigned int sam3cu_last_device_error(void);
+
+/* Number of kernel launches this library issued since the last reset. */
+SAM3CU_API uint64_t sam3cu_launch_count(int reset);
+
+/*
+ * y[M,N] = act(x[M,K] . w[N,K]^T + bias[N]) + residual[M,N]
+ *
+ * x, w: device, same 16-bit type (x_dtype = SAM3CU_BF16 or SAM3CU_F16),
+ * row-major, K % 8 == 0.  bias/residual: device F32 or NULL; residual may
+ * equal y when y is F32.  y_dtype: SAM3CU_F32, _BF16 or _F16.  act: enum
+ * sam3cu_act.  FP32 accumulation on the tensor cores.
+ */
+SAM3CU_API int sam3cu_linear(const void *x, int x_dtype, const void *w, const float *bias,
+		  const float *residual, void *y, int y_dtype, int M, int K,
+		  int N, int act, void *stream);
+
+/*
+ * Same as sam3cu_linear with a Q8_0 weight, already repacked on the device
+ * by sam3cu_q8_repack: q [N,K] int8 and scales [K/32, N] F32.  K % 64 == 0.
+ * x is BF16 or F16 (the weight is dequantised to that type on chip).
+ */
+SAM3CU_API int sam3cu_linear_q8(const void *x, int x_dtype, const int8_t *q,
+		     const float *scales, const float *bias,
+		     const float *residual, void *y, int y_dtype, int M, int K,
+		     int N, int act, void *stream);
+
+/*
+ * Repack reference Q8_0 blocks ({float scale; int8 q[32]}, 36 bytes,
+ * quant.h:30-33) of a flattened [N,K] weight (K % 32 == 0, so each block is
+ * 32 consecutive K of one row) into q [N,K] int8 + scales [K/32, N] F32.
+ * All pointers device.
+ */
+SAM3CU_API int sam3cu_q8_repack(const void *blocks, int N, int K, int8_t *q,
+		     float *scales, void *stream);
+
+/* Quantise n F32 values (device) to Q8_0 blocks (device), bit-identical to
+ * sam3_q8_quantize (quant.c:67-131). */
+SAM3CU_API int sam3cu_q8_quantize(const float *src, void *blocks, int64_t n,
+		       void *stream);
+
+/* Row LayerNorm, eps 1e-5, two-pass statistics in F32 (cpu_layernorm.c).
+ * x/y: device, dtypes F32/BF16/F16; gamma/beta: device F32 or NULL. */
+SAM3CU_API int sam3cu_layernorm(const void *x, int x_dtype, const float *gamma,
+		     const float *beta, void *y, int y_dtype, int rows,
+		     int cols, void *stream);
+
+/*
+ * Multi-head attention O = softmax(Q K^T / sqrt(head_dim)) V over groups of
+ * `seq` consecutive rows.  Q, K, V, O device, dtype BF16 or F16; head h of
+ * row r lives at column h*head_dim of a row of ld_qkv (Q, K, V) / ld_o (O)
+ * elements.  head_dim must be 64.
+ */
+SAM3CU_API int sam3cu_sdpa(const void *q, const void *k, const void *v, int64_t ld_qkv,
+		void *o, int64_t ld_o, int dtype, int n_groups, int seq,
+		int heads, int head_dim, void *stream);
+
+/* ---------------------------------------------------------------- ViT */
+
+struct sam3cu_vit_config {
+	int img_size;    /* 1008 */
+	int patch_size;  /* 14 */
+	int embed_dim;   /* 1024 */
+	int depth;       /* 32; blocks 7, 15, 23, 31 are global */
+	int n_heads;     /* 16 (head_dim must be 64) */
+	int window_size; /* 24 */
+	int mlp_dim;     /* 4736 */
+};
+
+/* One block's weights, HOST F32 in the reference layouts
+ * (image_encoder.h:76-86): W [out,in] row-major, QKV fused [3e, e]. */
+struct sam3cu_vit_block_weights {
+	const float *ln1_w, *ln1_b, *qkv_w, *qkv_b, *proj_w, *proj_b;
+	const float *ln2_w, *ln2_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+};
+
+struct sam3cu_vit_weights {
+	const float *patch_w;  /* [e, ps, ps, 3] OHWI */
+	const float *patch_b;  /* [e] */
+	const float *pos_raw;  /* [1, 24*24+1, e], CLS row first */
+	const float *ln_pre_w, *ln_pre_b;
+	struct sam3cu_vit_block_weights blocks[32];
+};
+
+typedef struct sam3cu_vit sam3cu_vit;
+
+/*
+ * Create an encoder on the current device and upload its weights.
+ * weight_dtype: SAM3CU_BF16 or SAM3CU_F16 (weights rounded RNE, activations
+ * in the same type, residual stream F32) or SAM3CU_Q8_0 (linear weights
+ * quantised exactly as sam3_q8_quantize, activations BF16).  max_batch
+ * bounds the images per sam3cu_vit_encode call (activation memory is
+ * allocated once for it).  Returns NULL on failure (see *status).
+ */
+SAM3CU_API sam3cu_vit *sam3cu_vit_create(const struct sam3cu_vit_config *cfg,
+			      const struct sam3cu_vit_weights *w,
+			      int weight_dtype, int max_batch, int *status);
+
+SAM3CU_API void sam3cu_vit_destroy(sam3cu_vit *vit);
+
+/*
+ * Encode n_images planar CHW F32 images (normalised, [n, 3, img, img]) into
+ * features [n, np, e] F32 in raster patch order (the layout sam3_vit_build
+ * returns).  images/out: device pointers when on_device != 0, else host
+ * pointers (copied in/out on the encoder's stream).  Blocks until done.
+ */
+SAM3CU_API int sam3cu_vit_encode(sam3cu_vit *vit, const float *images, int n_images,
+		      float *out, int on_device);
+
+/* Device-resident variant for callers that time or pipeline: enqueue on the
+ * encoder's stream only (images/out device), return without waiting. */
+SAM3CU_API int sam3cu_vit_encode_async(sam3cu_vit *vit, const float *images,
+			    int n_images, float *out);
+
+/* cudaStream_t of the encoder, as void *. */
+SAM3CU_API void *sam3cu_vit_stream(sam3cu_vit *vit);
+
+/* Kernel launches one encode of n_images enqueues. */
+SAM3CU_API int sam3cu_vit_launches_per_encode(sam3cu_vit *vit, int n_images);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SAM3CU_H */

@@ -1,0 +1,549 @@
+/*
+ * oracle/oracle.c - CPU restatement of sam3.c's image-encoder hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker for the CUDA
+ * backend: only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline
+ * leg load it.  The product library (libsam3cu.so) never links or calls it.
+ *
+ * Every function restates one reference routine in plain C with FP32
+ * arithmetic, citing the reference file:line it follows (paths are relative
+ * to the sam3.c project root).  The restatement is pinned against the
+ * reference itself (oracle/_ref/libsam3_ref.so, built from the reference
+ * sources by oracle/Makefile) and against the known-answer values of the
+ * reference's own tests (tests/test_oracle_pin.py).
+ *
+ * Deliberate differences from the reference CPU backend, each a fix the
+ * north star asks for:
+ *   - F16 GEMM accumulates in FP32 (the reference's x86 kernel re-rounds the
+ *     accumulator to fp16 after every k, cpu_matmul_f16.c:87-93).
+ *   - Q8_0 linears compute x . dequant(W)^T (the reference's gh_linear path
+ *     transposes a Q8 tensor with element size 0, tensor.c:40, and so reads
+ *     unrelated bytes).
+ *
+ * Threading: OpenMP over rows; results do not depend on the thread count
+ * (each output element is produced by exactly one thread in a fixed order).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <float.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define Q8_BLOCK 32
+
+/* Q8_0 block as stored by the reference: {float scale; int8 data[32]},
+ * 36 bytes (src/core/quant.h:30-33). */
+struct orc_q8_block {
+	float  scale;
+	int8_t data[Q8_BLOCK];
+};
+
+int orc_num_threads(int n)
+{
+#ifdef _OPENMP
+	if (n > 0)
+		omp_set_num_threads(n);
+	return omp_get_max_threads();
+#else
+	(void)n;
+	return 1;
+#endif
+}
+
+/* ---- number formats (src/core/half.h:51-210) -------------------------- */
+
+/* f32 -> bf16 bits, round to nearest even; NaN kept quiet (half.h:181-210). */
+uint16_t orc_f32_to_bf16(float f)
+{
+	uint32_t u;
+	memcpy(&u, &f, 4);
+	if ((u & 0x7fffffffu) > 0x7f800000u)
+		return (uint16_t)((u >> 16) | 0x40);
+	u += 0x7fffu + ((u >> 16) & 1u);
+	return (uint16_t)(u >> 16);
+}
+
+float orc_bf16_to_f32(uint16_t b)
+{
+	uint32_t u = (uint32_t)b << 16;
+	float f;
+	memcpy(&f, &u, 4);
+	return f;
+}
+
+/* f32 -> IEEE fp16 bits, round to nearest even, with subnormals
+ * (half.h:98-160).  Written from the IEEE-754 binary16 definition. */
+uint16_t orc_f32_to_fp16(float f)
+{
+	uint32_t u;
+	memcpy(&u, &f, 4);
+	uint32_t sign = (u >> 16) & 0x8000u;
+	uint32_t absu = u & 0x7fffffffu;
+	if (absu > 0x7f800000u)
+		return (uint16_t)(sign | 0x7e00u);
+	if (absu >= 0x477ff000u) /* rounds to >= 65520 -> inf */
+		return (uint16_t)(sign | 0x7c00u);
+	if (absu < 0x38800000u) { /* below 2^-14: subnormal or zero */
+		float af;
+		memcpy(&af, &absu, 4);
+		/* scale so that one fp16 subnormal ulp (2^-24) becomes 1.0 */
+		float s = af * 16777216.0f;
+		uint32_t q = (uint32_t)lrintf(s); /* RNE under default mode */
+		return (uint16_t)(sign | q);
+	}
+	uint32_t mant = absu & 0x7fffffu;
+	int32_t exp = (int32_t)(absu >> 23) - 127 + 15;
+	uint32_t h = ((uint32_t)exp << 10) | (mant >> 13);
+	uint32_t rem = mant & 0x1fffu;
+	if (rem > 0x1000u || (rem == 0x1000u && (h & 1u)))
+		h += 1;
+	return (uint16_t)(sign | h);
+}
+
+float orc_fp16_to_f32(uint16_t h)
+{
+	uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
+	uint32_t exp = (h >> 10) & 0x1fu;
+	uint32_t mant = h & 0x3ffu;
+	float f;
+	if (exp == 0) {
+		f = (float)mant * (1.0f / 16777216.0f);
+		uint32_t u;
+		memcpy(&u, &f, 4);
+		u |= sign;
+		memcpy(&f, &u, 4);
+		return f;
+	}
+	uint32_t u;
+	if (exp == 31)
+		u = sign | 0x7f800000u | (mant << 13);
+	else
+		u = sign | ((exp - 15 + 127) << 23) | (mant << 13);
+	memcpy(&f, &u, 4);
+	return f;
+}
+
+void orc_round_bf16(const float *src, float *dst, int64_t n)
+{
+	for (int64_t i = 0; i < n; i++)
+		dst[i] = orc_bf16_to_f32(orc_f32_to_bf16(src[i]));
+}
+
+void orc_round_fp16(const float *src, float *dst, int64_t n)
+{
+	for (int64_t i = 0; i < n; i++)
+		dst[i] = orc_fp16_to_f32(orc_f32_to_fp16(src[i]));
+}
+
+/* ---- Q8_0 (src/core/quant.c:67-151) ----------------------------------- */
+
+/* Blocks of 32 over the flattened tensor; scale = absmax/127; q =
+ * roundf(x * (1/scale)) clamped to +-127; zero tail; scale 0 -> zero block
+ * (quant.c:67-131). */
+void orc_q8_quantize(const float *src, struct orc_q8_block *dst, int64_t n)
+{
+	int64_t nb = (n + Q8_BLOCK - 1) / Q8_BLOCK;
+	for (int64_t b = 0; b < nb; b++) {
+		int64_t off = b * Q8_BLOCK;
+		int cnt = (int)((n - off) < Q8_BLOCK ? (n - off) : Q8_BLOCK);
+		float amax = 0.0f;
+		for (int i = 0; i < cnt; i++) {
+			float a = fabsf(src[off + i]);
+			if (a > amax)
+				amax = a;
+		}
+		float scale = amax / 127.0f;
+		dst[b].scale = scale;
+		memset(dst[b].data, 0, Q8_BLOCK);
+		if (scale == 0.0f)
+			continue;
+		float inv = 1.0f / scale;
+		for (int i = 0; i < cnt; i++) {
+			int q = (int)roundf(src[off + i] * inv);
+			if (q > 127) q = 127;
+			if (q < -127) q = -127;
+			dst[b].data[i] = (int8_t)q;
+		}
+	}
+}
+
+/* value = data[i] * scale (quant.c:134-151). */
+void orc_q8_dequantize(const struct orc_q8_block *src, float *dst, int64_t n)
+{
+	for (int64_t i = 0; i < n; i++) {
+		const struct orc_q8_block *blk = &src[i / Q8_BLOCK];
+		dst[i] = (float)blk->data[i % Q8_BLOCK] * blk->scale;
+	}
+}
+
+/* ---- GELU (src/backend/cpu/kernels/cpu_gelu.c:23-36) ------------------ */
+
+static inline float gelu_tanh(float x)
+{
+	float inner = 0.7978845608f * (x + 0.044715f * x * x * x);
+	return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+void orc_gelu(const float *x, float *y, int64_t n)
+{
+	for (int64_t i = 0; i < n; i++)
+		y[i] = gelu_tanh(x[i]);
+}
+
+/* ---- Linear: gh_linear = TRANSPOSE(W) -> MATMUL -> ADD(bias) ----------
+ * (src/model/graph_helpers.c:297-322; MATMUL cpu_matmul.c:196-257,
+ *  bias ADD cpu_elementwise.c broadcast over the last dim).
+ *
+ * y[M,N] = x[M,K] . W[N,K]^T (+ b[N]) (then GELU if act==1) (+ res[M,N]).
+ * FP32 accumulation in k order, as the reference kernels accumulate.
+ * act: 0 none, 1 tanh-GELU (gh_mlp's activation node, graph_helpers.c).
+ */
+void orc_linear(const float *x, const float *w, const float *b,
+		const float *res, float *y, int M, int K, int N, int act)
+{
+#pragma omp parallel for schedule(static)
+	for (int i = 0; i < M; i++) {
+		const float *xr = x + (int64_t)i * K;
+		for (int j = 0; j < N; j++) {
+			const float *wr = w + (int64_t)j * K;
+			float acc = 0.0f;
+			for (int k = 0; k < K; k++)
+				acc += xr[k] * wr[k];
+			if (b)
+				acc += b[j];
+			if (act == 1)
+				acc = gelu_tanh(acc);
+			if (res)
+				acc += res[(int64_t)i * N + j];
+			y[(int64_t)i * N + j] = acc;
+		}
+	}
+}
+
+/* Q8_0 weight [N,K] quantised along the flattened tensor, i.e. 32
+ * consecutive K of one output row per block when K % 32 == 0 (the
+ * converter's rule, tools/cli_convert.c).  y = x . dequant(W)^T (+b). */
+void orc_linear_q8(const float *x, const struct orc_q8_block *wq,
+		   const float *b, const float *res, float *y,
+		   int M, int K, int N, int act)
+{
+	float *w = (float *)malloc(sizeof(float) * (size_t)N * K);
+	orc_q8_dequantize(wq, w, (int64_t)N * K);
+	orc_linear(x, w, b, res, y, M, K, N, act);
+	free(w);
+}
+
+/* ---- LayerNorm (src/backend/cpu/kernels/cpu_layernorm.c:31-64) --------
+ * mean, then sum of squared deviations, inv_std = 1/sqrtf(var/cols+1e-5),
+ * then (x-mean)*inv_std*gamma+beta; gamma/beta optional. */
+void orc_layernorm(const float *x, const float *g, const float *b, float *y,
+		   int rows, int cols)
+{
+#pragma omp parallel for schedule(static)
+	for (int r = 0; r < rows; r++) {
+		const float *in = x + (int64_t)r * cols;
+		float *out = y + (int64_t)r * cols;
+		float sum = 0.0f;
+		for (int j = 0; j < cols; j++)
+			sum += in[j];
+		float mean = sum / (float)cols;
+		float vs = 0.0f;
+		for (int j = 0; j < cols; j++) {
+			float d = in[j] - mean;
+			vs += d * d;
+		}
+		float inv_std = 1.0f / sqrtf(vs / (float)cols + 1e-5f);
+		for (int j = 0; j < cols; j++) {
+			float v = (in[j] - mean) * inv_std;
+			if (g)
+				v *= g[j];
+			if (b)
+				v += b[j];
+			out[j] = v;
+		}
+	}
+}
+
+/* ---- RoPE ---------------------------------------------------------------
+ * Table (src/model/image_encoder.c:55-115): 16 frequencies
+ * 1/theta^(4i/hd); entry i<hd/4 uses the column (x) position * scale,
+ * entry hd/4+i the row (y) position * scale; table [n_pos, hd/2]. */
+void orc_rope_table(int n_pos, int grid_w, int head_dim, float scale,
+		    float theta, float *cos_out, float *sin_out)
+{
+	int half = head_dim / 2, quarter = head_dim / 4;
+	float freqs[64];
+	for (int i = 0; i < quarter; i++)
+		freqs[i] = 1.0f / powf(theta, (float)(i * 4) / (float)head_dim);
+	int grid_h = n_pos / grid_w;
+	for (int py = 0; py < grid_h; py++) {
+		for (int px = 0; px < grid_w; px++) {
+			int pos = py * grid_w + px;
+			float sy = (float)py * scale, sx = (float)px * scale;
+			for (int i = 0; i < quarter; i++) {
+				cos_out[pos * half + i] = cosf(sx * freqs[i]);
+				sin_out[pos * half + i] = sinf(sx * freqs[i]);
+				cos_out[pos * half + quarter + i] = cosf(sy * freqs[i]);
+				sin_out[pos * half + quarter + i] = sinf(sy * freqs[i]);
+			}
+		}
+	}
+}
+
+/* Interleaved-pair rotation on [batch, seq, heads, hd] with a [seq, hd/2]
+ * table (src/backend/cpu/kernels/cpu_rope.c:35-110).  x and y may alias. */
+void orc_rope(const float *x, const float *cs, const float *sn, float *y,
+	      int batch, int seq, int heads, int hd)
+{
+	int half = hd / 2;
+#pragma omp parallel for schedule(static)
+	for (int bs = 0; bs < batch * seq; bs++) {
+		int s = bs % seq;
+		for (int h = 0; h < heads; h++) {
+			int64_t off = ((int64_t)bs * heads + h) * hd;
+			for (int d = 0; d < half; d++) {
+				float x0 = x[off + 2 * d], x1 = x[off + 2 * d + 1];
+				float c = cs[s * half + d], si = sn[s * half + d];
+				y[off + 2 * d] = x0 * c - x1 * si;
+				y[off + 2 * d + 1] = x0 * si + x1 * c;
+			}
+		}
+	}
+}
+
+/* ---- SDPA (src/backend/cpu/kernels/cpu_sdpa.c:49-159) -----------------
+ * Per query row, online softmax over keys in order; scale 1/sqrt(hd);
+ * q/k/v/o contiguous [BH, S, hd].  No mask on the encoder path. */
+void orc_sdpa(const float *q, const float *k, const float *v, float *o,
+	      int BH, int S, int hd)
+{
+	float scale = 1.0f / sqrtf((float)hd);
+#pragma omp parallel for schedule(dynamic, 16)
+	for (int64_t idx = 0; idx < (int64_t)BH * S; idx++) {
+		int64_t bh = idx / S;
+		const float *qr = q + idx * hd;
+		const float *K = k + bh * (int64_t)S * hd;
+		const float *V = v + bh * (int64_t)S * hd;
+		float *out = o + idx * hd;
+		float mx = -FLT_MAX, sum = 0.0f;
+		for (int d = 0; d < hd; d++)
+			out[d] = 0.0f;
+		for (int j = 0; j < S; j++) {
+			float sc = 0.0f;
+			for (int d = 0; d < hd; d++)
+				sc += qr[d] * K[(int64_t)j * hd + d];
+			sc *= scale;
+			if (sc > mx) {
+				float corr = expf(mx - sc);
+				sum *= corr;
+				for (int d = 0; d < hd; d++)
+					out[d] *= corr;
+				mx = sc;
+			}
+			float w = expf(sc - mx);
+			for (int d = 0; d < hd; d++)
+				out[d] += w * V[(int64_t)j * hd + d];
+			sum += w;
+		}
+		if (sum > 0.0f) {
+			float inv = 1.0f / sum;
+			for (int d = 0; d < hd; d++)
+				out[d] *= inv;
+		}
+	}
+}
+
+/* ---- ViT encoder (src/model/image_encoder.c:513-963) -------------------- */
+
+/* Configuration of sam3_vit (image_encoder.h:34-46); global blocks are the
+ * fixed indices {7,15,23,31} (image_encoder.c:35). */
+struct orc_vit_cfg {
+	int img_size, patch_size, embed_dim, depth, n_heads, window_size,
+	    mlp_dim;
+};
+
+/* Weights of one block, F32 [out,in] row-major; QKV fused [3e, e]
+ * (image_encoder.c:223-259, 346-452). */
+struct orc_vit_block {
+	const float *ln1_w, *ln1_b, *qkv_w, *qkv_b, *proj_w, *proj_b;
+	const float *ln2_w, *ln2_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+};
+
+struct orc_vit_weights {
+	const float *patch_w;  /* [e, ps, ps, 3] OHWI (image_encoder.c:266-278) */
+	const float *patch_b;  /* [e] */
+	const float *pos_raw;  /* [1, 24*24+1, e], CLS first (:294-306) */
+	const float *ln_pre_w, *ln_pre_b;
+	struct orc_vit_block blocks[32];
+};
+
+static int is_global_block(int i)
+{
+	return i == 7 || i == 15 || i == 23 || i == 31;
+}
+
+/* Window partition as a row permutation (graph_helpers.c:444-475):
+ * token (py,px) -> window (py/ws)*nw + px/ws, slot (py%ws)*ws + px%ws. */
+static void window_partition(const float *x, float *y, int gs, int ws, int e)
+{
+	int nw = gs / ws;
+	for (int py = 0; py < gs; py++)
+		for (int px = 0; px < gs; px++) {
+			int win = (py / ws) * nw + px / ws;
+			int slot = (py % ws) * ws + px % ws;
+			memcpy(y + ((int64_t)win * ws * ws + slot) * e,
+			       x + ((int64_t)py * gs + px) * e,
+			       sizeof(float) * e);
+		}
+}
+
+static void window_unpartition(const float *y, float *x, int gs, int ws,
+			       int e)
+{
+	int nw = gs / ws;
+	for (int py = 0; py < gs; py++)
+		for (int px = 0; px < gs; px++) {
+			int win = (py / ws) * nw + px / ws;
+			int slot = (py % ws) * ws + px % ws;
+			memcpy(x + ((int64_t)py * gs + px) * e,
+			       y + ((int64_t)win * ws * ws + slot) * e,
+			       sizeof(float) * e);
+		}
+}
+
+/* gh_multihead_attention_rope (graph_helpers.c:721-882) on x[B*S, e]:
+ * QKV linear, split Q|K|V columns, RoPE on Q and K with the [S, hd/2]
+ * table, per-head SDPA, merge heads, out projection. */
+static void mha_rope(const float *x, float *out, int B, int S, int e,
+		     int heads, const struct orc_vit_block *w,
+		     const float *cs, const float *sn)
+{
+	int hd = e / heads;
+	int64_t bs = (int64_t)B * S;
+	float *qkv = (float *)malloc(sizeof(float) * bs * 3 * e);
+	float *q = (float *)malloc(sizeof(float) * bs * e);
+	float *k = (float *)malloc(sizeof(float) * bs * e);
+	float *v = (float *)malloc(sizeof(float) * bs * e);
+	float *o = (float *)malloc(sizeof(float) * bs * e);
+	orc_linear(x, w->qkv_w, w->qkv_b, NULL, qkv, (int)bs, e, 3 * e, 0);
+	/* Slice (SLICE axis 1) then permute [B,S,H,hd] -> [B,H,S,hd]. */
+	float *tq = (float *)malloc(sizeof(float) * bs * e);
+	float *tk = (float *)malloc(sizeof(float) * bs * e);
+	for (int64_t r = 0; r < bs; r++) {
+		memcpy(tq + r * e, qkv + r * 3 * e, sizeof(float) * e);
+		memcpy(tk + r * e, qkv + r * 3 * e + e, sizeof(float) * e);
+	}
+	orc_rope(tq, cs, sn, tq, B, S, heads, hd);
+	orc_rope(tk, cs, sn, tk, B, S, heads, hd);
+	for (int b = 0; b < B; b++)
+		for (int s = 0; s < S; s++)
+			for (int h = 0; h < heads; h++) {
+				int64_t src = ((int64_t)b * S + s) * e + h * hd;
+				int64_t dst = (((int64_t)b * heads + h) * S + s) * hd;
+				memcpy(q + dst, tq + src, sizeof(float) * hd);
+				memcpy(k + dst, tk + src, sizeof(float) * hd);
+				memcpy(v + dst, qkv + ((int64_t)b * S + s) * 3 * e
+					   + 2 * e + h * hd, sizeof(float) * hd);
+			}
+	orc_sdpa(q, k, v, o, B * heads, S, hd);
+	/* permute back [B,H,S,hd] -> [B,S,H,hd] -> [B*S, e] */
+	for (int b = 0; b < B; b++)
+		for (int s = 0; s < S; s++)
+			for (int h = 0; h < heads; h++)
+				memcpy(tq + ((int64_t)b * S + s) * e + h * hd,
+				       o + (((int64_t)b * heads + h) * S + s) * hd,
+				       sizeof(float) * hd);
+	orc_linear(tq, w->proj_w, w->proj_b, NULL, out, (int)bs, e, e, 0);
+	free(qkv); free(q); free(k); free(v); free(o); free(tq); free(tk);
+}
+
+/* One pre-norm block in place on x[np, e] (image_encoder.c:755-900). */
+void orc_vit_block_forward(const struct orc_vit_cfg *c,
+			   const struct orc_vit_block *w, int is_global,
+			   float *x, const float *glo_cos, const float *glo_sin,
+			   const float *win_cos, const float *win_sin)
+{
+	int gs = c->img_size / c->patch_size, e = c->embed_dim;
+	int np = gs * gs, ws = c->window_size;
+	float *xn = (float *)malloc(sizeof(float) * (size_t)np * e);
+	float *att = (float *)malloc(sizeof(float) * (size_t)np * e);
+	float *h = (float *)malloc(sizeof(float) * (size_t)np * c->mlp_dim);
+	orc_layernorm(x, w->ln1_w, w->ln1_b, xn, np, e);
+	if (is_global) {
+		mha_rope(xn, att, 1, np, e, c->n_heads, w, glo_cos, glo_sin);
+	} else {
+		float *xw = (float *)malloc(sizeof(float) * (size_t)np * e);
+		float *aw = (float *)malloc(sizeof(float) * (size_t)np * e);
+		int nw = gs / ws;
+		window_partition(xn, xw, gs, ws, e);
+		mha_rope(xw, aw, nw * nw, ws * ws, e, c->n_heads, w, win_cos,
+			 win_sin);
+		window_unpartition(aw, att, gs, ws, e);
+		free(xw); free(aw);
+	}
+	for (int64_t i = 0; i < (int64_t)np * e; i++)
+		x[i] += att[i];
+	orc_layernorm(x, w->ln2_w, w->ln2_b, xn, np, e);
+	orc_linear(xn, w->fc1_w, w->fc1_b, NULL, h, np, e, c->mlp_dim, 1);
+	orc_linear(h, w->fc2_w, w->fc2_b, x, x, np, c->mlp_dim, e, 0);
+	free(xn); free(att); free(h);
+}
+
+/* Patch embed (conv ps x ps stride ps, NHWC input, OHWI weight) + bias +
+ * tiled pos-embed (24x24 pretrain grid tiled, CLS stripped,
+ * image_encoder.c:167-218) + ln_pre (image_encoder.c:554-662).
+ * image: planar CHW [3, img, img] F32 (already normalised). */
+void orc_vit_embed(const struct orc_vit_cfg *c,
+		   const struct orc_vit_weights *w, const float *image,
+		   float *x)
+{
+	int ps = c->patch_size, img = c->img_size, gs = img / ps;
+	int e = c->embed_dim, np = gs * gs;
+#pragma omp parallel for schedule(static)
+	for (int p = 0; p < np; p++) {
+		int py = p / gs, px = p % gs;
+		float *xr = x + (int64_t)p * e;
+		for (int o = 0; o < e; o++) {
+			float acc = 0.0f;
+			const float *wo = w->patch_w + (int64_t)o * ps * ps * 3;
+			for (int ky = 0; ky < ps; ky++)
+				for (int kx = 0; kx < ps; kx++)
+					for (int ch = 0; ch < 3; ch++)
+						acc += image[((int64_t)ch * img + py * ps + ky) * img
+							     + px * ps + kx]
+						       * wo[(ky * ps + kx) * 3 + ch];
+			xr[o] = acc + w->patch_b[o];
+		}
+		int sy = py % 24, sx = px % 24;
+		const float *pr = w->pos_raw + (int64_t)(1 + sy * 24 + sx) * e;
+		for (int o = 0; o < e; o++)
+			xr[o] += pr[o];
+	}
+	orc_layernorm(x, w->ln_pre_w, w->ln_pre_b, x, np, e);
+}
+
+/* Full sam3_vit_build forward: embed, then every block; the output has no
+ * final norm (image_encoder.c:950-962).  x: [np, e] F32 out. */
+void orc_vit_forward(const struct orc_vit_cfg *c,
+		     const struct orc_vit_weights *w, const float *image,
+		     float *x)
+{
+	int gs = c->img_size / c->patch_size, ws = c->window_size;
+	int hd = c->embed_dim / c->n_heads;
+	int np = gs * gs;
+	float *gc = (float *)malloc(sizeof(float) * np * hd / 2);
+	float *gsn = (float *)malloc(sizeof(float) * np * hd / 2);
+	float *wc = (float *)malloc(sizeof(float) * ws * ws * hd / 2);
+	float *wsn = (float *)malloc(sizeof(float) * ws * ws * hd / 2);
+	orc_rope_table(np, gs, hd, (float)ws / (float)gs, 10000.0f, gc, gsn);
+	orc_rope_table(ws * ws, ws, hd, 1.0f, 10000.0f, wc, wsn);
+	orc_vit_embed(c, w, image, x);
+	for (int i = 0; i < c->depth; i++)
+		orc_vit_block_forward(c, &w->blocks[i], is_global_block(i), x,
+				      gc, gsn, wc, wsn);
+	free(gc); free(gsn); free(wc); free(wsn);
+}

@@ -1,0 +1,290 @@
+"""ctypes front end to the parity checkers.  TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module.  The product (sam3.c_b200/, libsam3cu.so) never does.
+
+Two libraries sit behind it, both built by oracle/Makefile:
+  * ``lib/libsam3_oracle.so`` -- the C restatement in oracle/oracle.c.
+  * ``_ref/libsam3_ref.so``   -- the unmodified sam3.c CPU backend compiled
+    from the reference sources, plus oracle/ref_harness.c.  Present wherever
+    it was built (it travels with the repository snapshot as a built file).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "lib", "libsam3_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libsam3_ref.so")
+
+F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+VP = C.c_void_p
+
+_orc = None
+_ref = None
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(VP)
+
+
+def orc():
+    global _orc
+    if _orc is None:
+        if not os.path.exists(ORACLE_SO):
+            raise RuntimeError(f"{ORACLE_SO} missing: run `make -C oracle`")
+        _orc = C.CDLL(ORACLE_SO)
+        _orc.orc_f32_to_bf16.restype = C.c_uint16
+        _orc.orc_f32_to_bf16.argtypes = [C.c_float]
+        _orc.orc_f32_to_fp16.restype = C.c_uint16
+        _orc.orc_f32_to_fp16.argtypes = [C.c_float]
+        _orc.orc_rope_table.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float,
+                                        C.c_float, VP, VP]
+        _orc.orc_num_threads.argtypes = [C.c_int]
+    return _orc
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        if not ref_available():
+            raise RuntimeError(f"{REF_SO} missing: run `make -C oracle` "
+                               "where the sam3.c sources are present")
+        _ref = C.CDLL(REF_SO)
+        _ref.ref_quiet()
+    return _ref
+
+
+def set_threads(n: int = 0) -> int:
+    """Thread count for the restatement (OpenMP); 0 keeps the default."""
+    return orc().orc_num_threads(n)
+
+
+def ref_set_threads(n: int = 0) -> int:
+    return ref().ref_set_threads(n)
+
+
+# ---------------------------------------------------------------- formats
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    orc().orc_round_bf16(_p(x), _p(out), C.c_int64(x.size))
+    return out
+
+
+def round_fp16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    orc().orc_round_fp16(_p(x), _p(out), C.c_int64(x.size))
+    return out
+
+
+Q8_DTYPE = np.dtype([("scale", "<f4"), ("data", "i1", (32,))])
+
+
+def q8_quantize(x: np.ndarray) -> np.ndarray:
+    """Q8_0 blocks (36 bytes each) over the flattened tensor."""
+    x = np.ascontiguousarray(x, np.float32)
+    nb = (x.size + 31) // 32
+    out = np.zeros(nb, Q8_DTYPE)
+    orc().orc_q8_quantize(_p(x), _p(out), C.c_int64(x.size))
+    return out
+
+
+def q8_dequantize(q: np.ndarray, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    orc().orc_q8_dequantize(_p(q), _p(out), C.c_int64(n))
+    return out
+
+
+# ---------------------------------------------------------------- ops
+def linear(x, w, b=None, res=None, act=0):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    y = np.empty((M, N), np.float32)
+    if b is not None:
+        b = np.ascontiguousarray(b, np.float32)
+    if res is not None:
+        res = np.ascontiguousarray(res, np.float32)
+    orc().orc_linear(_p(x), _p(w), _p(b), _p(res), _p(y), M, K, N, act)
+    return y
+
+
+def layernorm(x, g=None, b=None):
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.reshape(-1, x.shape[-1]).shape
+    y = np.empty_like(x)
+    orc().orc_layernorm(_p(x), _p(g), _p(b), _p(y), rows, cols)
+    return y
+
+
+def gelu(x):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    orc().orc_gelu(_p(x), _p(y), C.c_int64(x.size))
+    return y
+
+
+def rope_table(n_pos, grid_w, head_dim, scale, theta=10000.0):
+    cs = np.empty((n_pos, head_dim // 2), np.float32)
+    sn = np.empty_like(cs)
+    orc().orc_rope_table(n_pos, grid_w, head_dim, scale, theta, _p(cs), _p(sn))
+    return cs, sn
+
+
+def rope(x, cs, sn):
+    """x: [batch, seq, heads, hd]."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    B, S, H, D = x.shape
+    orc().orc_rope(_p(x), _p(cs), _p(sn), _p(y), B, S, H, D)
+    return y
+
+
+def sdpa(q, k, v):
+    """q/k/v: [BH, S, hd] (any leading dims flattened)."""
+    q = np.ascontiguousarray(q, np.float32)
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    S, D = q.shape[-2:]
+    BH = q.size // (S * D)
+    o = np.empty_like(q)
+    orc().orc_sdpa(_p(q), _p(k), _p(v), _p(o), BH, S, D)
+    return o
+
+
+# ---------------------------------------------------------------- ViT
+class _Blk(C.Structure):
+    _fields_ = [(n, VP) for n in ("ln1_w", "ln1_b", "qkv_w", "qkv_b", "proj_w",
+                                  "proj_b", "ln2_w", "ln2_b", "fc1_w", "fc1_b",
+                                  "fc2_w", "fc2_b")]
+
+
+class _VitW(C.Structure):
+    _fields_ = [(n, VP) for n in ("patch_w", "patch_b", "pos_raw", "ln_pre_w",
+                                  "ln_pre_b")] + [("blocks", _Blk * 32)]
+
+
+class _Cfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("img_size", "patch_size", "embed_dim",
+                                       "depth", "n_heads", "window_size",
+                                       "mlp_dim")]
+
+
+BLOCK_KEYS = ("ln1_w", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ln2_w",
+              "ln2_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b")
+
+
+def _vit_struct(w):
+    s = _VitW()
+    keep = []
+    for n in ("patch_w", "patch_b", "pos_raw", "ln_pre_w", "ln_pre_b"):
+        a = np.ascontiguousarray(w[n], np.float32)
+        keep.append(a)
+        setattr(s, n, a.ctypes.data)
+    for i, blk in enumerate(w["blocks"]):
+        for n in BLOCK_KEYS:
+            a = np.ascontiguousarray(blk[n], np.float32)
+            keep.append(a)
+            setattr(s.blocks[i], n, a.ctypes.data)
+    return s, keep
+
+
+def vit_forward(cfg: dict, w: dict, image: np.ndarray) -> np.ndarray:
+    """Restated sam3_vit_build forward; image CHW F32 normalised."""
+    gs = cfg["img_size"] // cfg["patch_size"]
+    out = np.empty((gs * gs, cfg["embed_dim"]), np.float32)
+    s, keep = _vit_struct(w)
+    c = _Cfg(*(cfg[k] for k in ("img_size", "patch_size", "embed_dim", "depth",
+                                "n_heads", "window_size", "mlp_dim")))
+    image = np.ascontiguousarray(image, np.float32)
+    orc().orc_vit_forward(C.byref(c), C.byref(s), _p(image), _p(out))
+    del keep
+    return out
+
+
+# ---------------------------------------------------------------- reference
+def ref_matmul(a, b, dt="f32"):
+    """C = A[M,K] . B[K,N] with the reference kernel; dt f32|f16|bf16.
+
+    For f16/bf16 pass uint16 bit patterns; returns the same dtype."""
+    M, K = a.shape
+    N = b.shape[1]
+    code = {"f32": 0, "f16": 1, "bf16": 2}[dt]
+    out = np.empty((M, N), np.float32 if code == 0 else np.uint16)
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    rc = ref().ref_matmul(code, _p(a), _p(b), _p(out), M, K, N)
+    assert rc == 0, rc
+    return out
+
+
+def ref_matmul_q8(a, bq, K, N):
+    a = np.ascontiguousarray(a, np.float32)
+    M = a.shape[0]
+    out = np.empty((M, N), np.float32)
+    rc = ref().ref_matmul_q8(_p(a), _p(bq), _p(out), M, K, N)
+    assert rc == 0, rc
+    return out
+
+
+def ref_q8_quantize(x):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros((x.size + 31) // 32, Q8_DTYPE)
+    ref().ref_q8_quantize(_p(x), _p(out), x.size)
+    return out
+
+
+def ref_gelu(x):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    assert ref().ref_gelu(_p(x), _p(y), x.size) == 0
+    return y
+
+
+def ref_layernorm(x, g=None, b=None):
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.reshape(-1, x.shape[-1]).shape
+    y = np.empty_like(x)
+    assert ref().ref_layernorm(_p(x), _p(g), _p(b), _p(y), rows, cols) == 0
+    return y
+
+
+def ref_rope(x, cs, sn):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    B, S, H, D = x.shape
+    assert ref().ref_rope(_p(x), _p(cs), _p(sn), _p(y), B, S, H, D) == 0
+    return y
+
+
+def ref_sdpa(q, k, v):
+    """q/k/v [B, H, S, hd]."""
+    q, k, v = (np.ascontiguousarray(t, np.float32) for t in (q, k, v))
+    B, H, S, D = q.shape
+    o = np.empty_like(q)
+    assert ref().ref_sdpa(_p(q), _p(k), _p(v), _p(o), B, H, S, D) == 0
+    return o
+
+
+def ref_vit_encode(cfg: dict, w: dict, image: np.ndarray) -> np.ndarray:
+    gs = cfg["img_size"] // cfg["patch_size"]
+    out = np.empty((gs * gs, cfg["embed_dim"]), np.float32)
+    s, keep = _vit_struct(w)
+    image = np.ascontiguousarray(image, np.float32)
+    rc = ref().ref_vit_encode(*(C.c_int(cfg[k]) for k in (
+        "img_size", "patch_size", "embed_dim", "depth", "n_heads",
+        "window_size", "mlp_dim")), C.byref(s), _p(image), _p(out))
+    del keep
+    if rc != 0:
+        raise RuntimeError(f"ref_vit_encode failed rc={rc}")
+    return out

@@ -1,0 +1,119 @@
+// capi.cu - extern "C" single-op entry points of include/sam3cu.h.
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "../../include/sam3cu.h"
+#include "gemm_sm100.cuh"
+#include "misc.cuh"
+#include "sam3cu_internal.h"
+
+using namespace s3;
+
+namespace {
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int linear_common(const void* x, int x_dtype, const void* w, const int8_t* q, const float* sc, const float* bias,
+                  const float* residual, void* y, int y_dtype, int M, int K, int N, int act, void* stream) {
+  if (!x || !y || (!w && !q) || M < 0 || K <= 0 || N <= 0) return SAM3CU_EINVAL;
+  if (x_dtype != SAM3CU_BF16 && x_dtype != SAM3CU_F16) return SAM3CU_EDTYPE;
+  if (y_dtype != SAM3CU_F32 && y_dtype != SAM3CU_BF16 && y_dtype != SAM3CU_F16) return SAM3CU_EDTYPE;
+  if (act != SAM3CU_ACT_NONE && act != SAM3CU_ACT_GELU_TANH) return SAM3CU_EINVAL;
+  if (residual == y && y_dtype != SAM3CU_F32) return SAM3CU_EINVAL;
+  EpiParams ep;
+  memset(&ep, 0, sizeof(ep));
+  ep.out = y;
+  ep.out_type = y_dtype;
+  ep.ldo = N;
+  ep.bias = bias;
+  ep.act = act;
+  ep.residual = residual;
+  ep.ldr = N;
+  GemmShape shp{M, N, K};
+  return launch_gemm(x, K, w, K, q, sc, x_dtype, shp, ep, as_stream(stream), 0);
+}
+
+}  // namespace
+
+extern "C" {
+
+int sam3cu_init(int device) {
+  if (cudaSetDevice(device) != cudaSuccess) return SAM3CU_EBACKEND;
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (major != 10 || minor != 0) return SAM3CU_EBACKEND;  // built for sm_100a only
+  return cudaFree(nullptr) == cudaSuccess ? SAM3CU_OK : SAM3CU_EBACKEND;
+}
+
+const char* sam3cu_strerror(int s) {
+  switch (s) {
+    case SAM3CU_OK: return "ok";
+    case SAM3CU_EINVAL: return "invalid argument";
+    case SAM3CU_ENOMEM: return "out of memory";
+    case SAM3CU_EBACKEND: return "backend / device unavailable";
+    case SAM3CU_EDTYPE: return "unsupported dtype";
+    case SAM3CU_ESHAPE: return "unsupported shape or alignment";
+    case SAM3CU_ETMA: return "TMA descriptor creation failed";
+    case SAM3CU_ELAUNCH: return "kernel launch failed";
+    case SAM3CU_ECUDA: return "CUDA runtime error";
+    case SAM3CU_EDEVICE: return "device-side wait timed out";
+    case SAM3CU_EDTYPE2: return "unsupported dtype combination";
+    case SAM3CU_ENOMEM2: return "device allocation failed";
+    default: return "unknown status";
+  }
+}
+
+unsigned int sam3cu_last_device_error(void) {
+  cudaDeviceSynchronize();
+  unsigned int a = dev_error_gemm(), b = dev_error_attn(), c = dev_error_misc();
+  return a ? a : (b ? b : c);
+}
+
+uint64_t sam3cu_launch_count(int reset) {
+  uint64_t v = count_launches(0);
+  if (reset) count_launches(-static_cast<int64_t>(v));
+  return v;
+}
+
+int sam3cu_linear(const void* x, int x_dtype, const void* w, const float* bias, const float* residual, void* y,
+                  int y_dtype, int M, int K, int N, int act, void* stream) {
+  return linear_common(x, x_dtype, w, nullptr, nullptr, bias, residual, y, y_dtype, M, K, N, act, stream);
+}
+
+int sam3cu_linear_q8(const void* x, int x_dtype, const int8_t* q, const float* scales, const float* bias,
+                     const float* residual, void* y, int y_dtype, int M, int K, int N, int act, void* stream) {
+  if (!q || !scales) return SAM3CU_EINVAL;
+  return linear_common(x, x_dtype, nullptr, q, scales, bias, residual, y, y_dtype, M, K, N, act, stream);
+}
+
+int sam3cu_q8_repack(const void* blocks, int N, int K, int8_t* q, float* scales, void* stream) {
+  if (!blocks || !q || !scales || N <= 0 || K <= 0) return SAM3CU_EINVAL;
+  return launch_q8_repack(blocks, q, scales, N, K, as_stream(stream));
+}
+
+int sam3cu_q8_quantize(const float* src, void* blocks, int64_t n, void* stream) {
+  if (!src || !blocks || n <= 0) return SAM3CU_EINVAL;
+  return launch_q8_quantize(src, blocks, n, as_stream(stream));
+}
+
+int sam3cu_layernorm(const void* x, int x_dtype, const float* gamma, const float* beta, void* y, int y_dtype,
+                     int rows, int cols, void* stream) {
+  if (!x || !y || rows < 0 || cols <= 0) return SAM3CU_EINVAL;
+  if (x != y || x_dtype == y_dtype) {
+    // in-place is safe: each warp holds its whole row before writing
+  } else {
+    return SAM3CU_EINVAL;
+  }
+  return launch_layernorm(x, x_dtype, y, y_dtype, gamma, beta, rows, cols, nullptr, 0, as_stream(stream));
+}
+
+int sam3cu_sdpa(const void* q, const void* k, const void* v, int64_t ld_qkv, void* o, int64_t ld_o, int dtype,
+                int n_groups, int seq, int heads, int head_dim, void* stream) {
+  if (!q || !k || !v || !o) return SAM3CU_EINVAL;
+  if (dtype != SAM3CU_BF16 && dtype != SAM3CU_F16) return SAM3CU_EDTYPE;
+  return launch_attention(q, k, v, ld_qkv, o, ld_o, dtype, n_groups, seq, heads, head_dim, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,421 @@
+// gemm_sm100.cu - tcgen05 GEMM kernel bodies and launchers (see gemm_sm100.cuh).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstring>
+
+#include "gemm_sm100.cuh"
+#include "sam3cu_internal.h"
+#include "tma_host.cuh"
+
+namespace s3 {
+
+S3_DEV_ERROR_ACCESSOR(dev_error_gemm)
+
+namespace {
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // 0.5*x*(1+tanh(sqrt(2/pi)*(x+0.044715x^3))), cpu_gelu.c:23-36
+  float inner = 0.7978845608f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Apply the fused epilogue to 32 consecutive columns [col0, col0+32) of one
+// output row and store them.
+__device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, float (&v)[32], int row,
+                                               int col0, int N) {
+  const bool full = col0 + 32 <= N;
+  if (ep.bias) {
+    if (full) {
+      const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 b = __ldg(b4 + j);
+        v[4 * j] += b.x;
+        v[4 * j + 1] += b.y;
+        v[4 * j + 2] += b.z;
+        v[4 * j + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] += __ldg(ep.bias + col0 + j);
+    }
+  }
+  if (ep.act == 1) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+  }
+  if (col0 < ep.rope_cols) {
+    int p = row % ep.rope_period;
+    if (ep.rope_pos) p = __ldg(ep.rope_pos + p);
+    const int d0 = (col0 & 63) >> 1;  // first pair index within the head
+    const float* cs = ep.rope_cos + p * 32 + d0;
+    const float* sn = ep.rope_sin + p * 32 + d0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float c = __ldg(cs + i), s = __ldg(sn + i);
+      float x0 = v[2 * i], x1 = v[2 * i + 1];
+      v[2 * i] = x0 * c - x1 * s;
+      v[2 * i + 1] = x0 * s + x1 * c;
+    }
+  }
+  if (ep.residual) {
+    int rr = ep.res_row_period > 0 ? row % ep.res_row_period : row;
+    const float* r = ep.residual + static_cast<int64_t>(rr) * ep.ldr + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 x = *reinterpret_cast<const float4*>(r + 4 * j);
+        v[4 * j] += x.x;
+        v[4 * j + 1] += x.y;
+        v[4 * j + 2] += x.z;
+        v[4 * j + 3] += x.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] += r[j];
+    }
+  }
+  int orow = row;
+  if (ep.out_row_map) {
+    int per = ep.out_row_period;
+    orow = (row / per) * per + __ldg(ep.out_row_map + row % per);
+  }
+  const int64_t off = static_cast<int64_t>(orow) * ep.ldo + col0;
+  if (ep.out_type == kOutF32) {
+    float* o = static_cast<float*>(ep.out) + off;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        reinterpret_cast<float4*>(o)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) o[j] = v[j];
+    }
+  } else {
+    const bool bf = ep.out_type == kOutBF16;
+    uint16_t* o = static_cast<uint16_t*>(ep.out) + off;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 w;
+        w.x = bf ? pack_bf16(v[8 * j], v[8 * j + 1]) : pack_f16(v[8 * j], v[8 * j + 1]);
+        w.y = bf ? pack_bf16(v[8 * j + 2], v[8 * j + 3]) : pack_f16(v[8 * j + 2], v[8 * j + 3]);
+        w.z = bf ? pack_bf16(v[8 * j + 4], v[8 * j + 5]) : pack_f16(v[8 * j + 4], v[8 * j + 5]);
+        w.w = bf ? pack_bf16(v[8 * j + 6], v[8 * j + 7]) : pack_f16(v[8 * j + 6], v[8 * j + 7]);
+        reinterpret_cast<uint4*>(o)[j] = w;
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) {
+          uint16_t h;
+          if (bf) {
+            __nv_bfloat16 t = __float2bfloat16_rn(v[j]);
+            h = *reinterpret_cast<uint16_t*>(&t);
+          } else {
+            __half t = __float2half_rn(v[j]);
+            h = *reinterpret_cast<uint16_t*>(&t);
+          }
+          o[j] = h;
+        }
+    }
+  }
+}
+
+// Dequantise one k-tile of Q8 W (int8 [kBN rows x 64] + scales [2][kBN]) to
+// 16-bit values in the 128-byte-swizzled K-major layout the MMA reads.
+// 128 threads; thread t handles 16-byte chunk (t & 7) of rows (t>>3)+16i.
+template <bool kBf16>
+__device__ __forceinline__ void q8_dequant_tile(const int8_t* q, const float* sc, uint8_t* dst,
+                                                int t) {
+  const int c = t & 7;
+#pragma unroll 4
+  for (int i = 0; i < kBN / 16; ++i) {
+    const int n = (t >> 3) + 16 * i;
+    const uint2 raw = *reinterpret_cast<const uint2*>(q + n * kBK + c * 8);
+    const float s = sc[(c >> 2) * kBN + n];
+    const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+    uint4 w;
+    if (kBf16) {
+      w.x = pack_bf16(b[0] * s, b[1] * s);
+      w.y = pack_bf16(b[2] * s, b[3] * s);
+      w.z = pack_bf16(b[4] * s, b[5] * s);
+      w.w = pack_bf16(b[6] * s, b[7] * s);
+    } else {
+      w.x = pack_f16(b[0] * s, b[1] * s);
+      w.y = pack_f16(b[2] * s, b[3] * s);
+      w.z = pack_f16(b[4] * s, b[5] * s);
+      w.w = pack_f16(b[6] * s, b[7] * s);
+    }
+    *reinterpret_cast<uint4*>(dst + n * 128 + ((c ^ (n & 7)) << 4)) = w;
+  }
+}
+
+template <int kBMode>
+__global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                const __grid_constant__ CUtensorMap tmap_s, GemmShape shp, EpiParams ep, uint32_t idesc,
+                int b_is_bf16) {
+  using Cfg = GemmCfg<kBMode>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* conv_bar = empty_bar + S;   // Q8: dequantised tile ready
+  uint64_t* accf_bar = conv_bar + S;    // [2] accumulator committed
+  uint64_t* acce_bar = accf_bar + 2;    // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (shp.M + kBM - 1) / kBM;
+  const int n_tiles = (shp.N + kBN - 1) / kBN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_iters = (shp.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+      mbar_init(&conv_bar[s], 128);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf_bar[a], 1);
+      mbar_init(&acce_bar[a], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto stage_a = [&](int s) { return smem + s * Cfg::kStageBytes; };
+  auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + kATileBytes; };
+  auto stage_q = [&](int s) { return smem + s * Cfg::kStageBytes + kATileBytes + kBTileBytes; };
+  auto stage_sc = [&](int s) {
+    return smem + s * Cfg::kStageBytes + kATileBytes + kBTileBytes + kQ8TileBytes;
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_a);
+      tma_prefetch_desc(&tmap_b);
+      if (kBMode == kBQ8) tma_prefetch_desc(&tmap_s);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % m_tiles) * kBM;
+        const int n0 = (tile / m_tiles) * kBN;
+        for (int kt = 0; kt < k_iters; ++kt, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
+          if (kBMode == kBQ8) {
+            mbar_arrive_expect_tx(&full_bar[s], kATileBytes + kQ8TileBytes + kQ8ScaleBytes);
+            tma_load_2d(stage_a(s), &tmap_a, &full_bar[s], kt * kBK, m0);
+            tma_load_2d(stage_q(s), &tmap_b, &full_bar[s], kt * kBK, n0);
+            tma_load_2d(stage_sc(s), &tmap_s, &full_bar[s], n0, kt * (kBK / 32));
+          } else {
+            mbar_arrive_expect_tx(&full_bar[s], kATileBytes + kBTileBytes);
+            tma_load_2d(stage_a(s), &tmap_a, &full_bar[s], kt * kBK, m0);
+            tma_load_2d(stage_b(s), &tmap_b, &full_bar[s], kt * kBK, n0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&acce_bar[acc], aph ^ 1, kErrAccFree, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kBN;
+        for (int kt = 0; kt < k_iters; ++kt, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          uint64_t* ready = kBMode == kBQ8 ? &conv_bar[s] : &full_bar[s];
+          if (!mbar_wait(ready, ph, kErrTmaWait, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = make_sdesc_sw128(smem_u32(stage_a(s)));
+          const uint64_t bdesc = make_sdesc_sw128(smem_u32(stage_b(s)));
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            // advance 16 elements = 32 bytes = 2 (16-byte units) along K
+            umma_ss<0>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[s]);  // frees the smem stage when these MMAs finish
+        }
+        if (ok) umma_commit(&accf_bar[acc]);
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1)
+    const int quarter = warp & 3;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int m0 = (tile % m_tiles) * kBM;
+      const int n0 = (tile / m_tiles) * kBN;
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      // one lane waits, the warp follows its verdict (tcgen05.ld is .aligned)
+      int got = 0;
+      if (lane == 0) got = mbar_wait(&accf_bar[acc], aph, kErrAccFull, abort_flag) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
+      tc_fence_after();
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        const int col0 = n0 + c * 32;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (row < shp.M && col0 < shp.N) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          epilogue_chunk(ep, v, row, col0, shp.N);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[acc]);
+    }
+  } else if (kBMode == kBQ8) {
+    // ---------------- Q8 converters (warps 6..9, 128 threads)
+    const int t = threadIdx.x - 192;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int kt = 0; kt < k_iters; ++kt, ++it) {
+        const int s = it % S;
+        const uint32_t ph = (it / S) & 1;
+        if (!mbar_wait(&full_bar[s], ph, kErrTmaWait, abort_flag)) { ok = false; break; }
+        const int8_t* q = reinterpret_cast<const int8_t*>(stage_q(s));
+        const float* sc = reinterpret_cast<const float*>(stage_sc(s));
+        if (b_is_bf16)
+          q8_dequant_tile<true>(q, sc, stage_b(s), t);
+        else
+          q8_dequant_tile<false>(q, sc, stage_b(s), t);
+        fence_proxy_async_smem();  // make generic-proxy writes visible to tcgen05
+        mbar_arrive(&conv_bar[s]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+int g_num_sms = 0;
+std::atomic<uint64_t> g_launches{0};
+
+}  // namespace
+
+uint64_t count_launches(int64_t delta) {
+  return g_launches.fetch_add(static_cast<uint64_t>(delta)) + static_cast<uint64_t>(delta);
+}
+
+int num_sms() {
+  if (!g_num_sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return g_num_sms;
+}
+
+// Launch Y = epi(A . W^T).  ab_dtype: kBF16 or kF16 (A and 16-bit W share it).
+// W: 16-bit [N, ldw] or (q8 != null) int8 [N, K] + scales [K/32, N].
+int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8, const float* q8_scales,
+                int ab_dtype, GemmShape shp, const EpiParams& ep, cudaStream_t stream, int max_ctas) {
+  if (ab_dtype != kBF16 && ab_dtype != kF16) return kErrDtype;
+  const bool bf = ab_dtype == kBF16;
+  if (shp.M <= 0 || shp.N <= 0 || shp.K <= 0) return 0;
+  if (shp.K % 8 != 0 || lda % 8 != 0) return kErrShape;
+  if (ep.rope_cols > 0 && (ep.rope_period <= 0 || !ep.rope_cos || !ep.rope_sin)) return kErrShape;
+  if (ep.out_row_map && ep.out_row_period <= 0) return kErrShape;
+  // vector epilogue stores/loads: 16-byte aligned rows
+  if (ep.ldo % (ep.out_type == kOutF32 ? 4 : 8) != 0) return kErrShape;
+  if (ep.residual && ep.ldr % 4 != 0) return kErrShape;
+  if ((reinterpret_cast<uintptr_t>(ep.out) | reinterpret_cast<uintptr_t>(ep.residual) |
+       reinterpret_cast<uintptr_t>(ep.bias)) & 15u)
+    return kErrShape;
+  const CUtensorMapDataType dt =
+      bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb, ts;
+  memset(&ts, 0, sizeof(ts));
+  if (!make_tmap_2d(&ta, A, dt, 2, shp.M, shp.K, lda, kBM, kBK, CU_TENSOR_MAP_SWIZZLE_128B))
+    return kErrTma;
+  const int m_tiles = (shp.M + kBM - 1) / kBM, n_tiles = (shp.N + kBN - 1) / kBN;
+  int grid = m_tiles * n_tiles;
+  int cap = max_ctas > 0 ? max_ctas : num_sms();
+  if (grid > cap) grid = cap;
+  const uint32_t idesc = make_idesc(bf ? 1u : 0u, kBM, kBN);
+  count_launches(1);
+  if (q8) {
+    if (shp.K % 64 != 0) return kErrShape;
+    if (!make_tmap_2d(&tb, q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, shp.N, shp.K, shp.K, kBN, kBK,
+                      CU_TENSOR_MAP_SWIZZLE_NONE))
+      return kErrTma;
+    if (!make_tmap_2d(&ts, q8_scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, shp.K / 32, shp.N, shp.N,
+                      kBK / 32, kBN, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return kErrTma;
+    constexpr int smem = GemmCfg<kBQ8>::kSmemBytes;
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(gemm_kernel<kBQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      attr = true;
+    }
+    gemm_kernel<kBQ8><<<grid, GemmCfg<kBQ8>::kThreads, smem, stream>>>(ta, tb, ts, shp, ep, idesc,
+                                                                         bf ? 1 : 0);
+  } else {
+    if (ldw % 8 != 0) return kErrShape;
+    if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, kBN, kBK, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kErrTma;
+    constexpr int smem = GemmCfg<kBTma16>::kSmemBytes;
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(gemm_kernel<kBTma16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      attr = true;
+    }
+    gemm_kernel<kBTma16><<<grid, GemmCfg<kBTma16>::kThreads, smem, stream>>>(ta, tb, ts, shp, ep,
+                                                                              idesc, bf ? 1 : 0);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
+}
+
+}  // namespace s3

@@ -1,0 +1,84 @@
+// gemm_sm100.cuh - persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   Y[M,N] = epilogue( A[M,K] . W[N,K]^T )
+//
+// This is the whole of sam3.c's `gh_linear` (TRANSPOSE(W) -> MATMUL ->
+// ADD(bias), src/model/graph_helpers.c:297-322) plus what the encoder does
+// right after it (tanh-GELU, residual ADD, RoPE on Q/K, window un-partition),
+// in one kernel.  W is consumed as stored, [N,K] K-major, so the reference's
+// per-call weight transpose disappears.
+//
+// CTA layout (192 threads, 1 CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A and W tiles -> kStages-deep smem ring
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma into TMEM;
+//               owns TMEM allocation (2 accumulators x BN fp32 columns)
+//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> fused ops -> HBM
+// The two TMEM accumulators let the epilogue of tile i overlap the main loop
+// of tile i+1.
+//
+// B operand sources (template kBMode):
+//   kBTma16  W is bf16/fp16 [N,K]: loaded by TMA with the 128-byte swizzle.
+//   kBQ8     W is Q8_0 repacked as int8 [N,K] + fp32 scales [N,K/32]
+//            (same blocks as the reference's sam3_q8_block, quant.h:30-33):
+//            TMA brings the int8 tile and scales, four converter warps
+//            dequantise (q * scale -> bf16) straight into the swizzled
+//            operand layout in shared memory.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "sm100_ptx.cuh"
+
+namespace s3 {
+
+enum OutType : int { kOutF32 = 0, kOutF16 = 1, kOutBF16 = 2 };  // = sam3_dtype codes
+enum BMode : int { kBTma16 = 0, kBQ8 = 1 };
+
+// Fused epilogue description.  All pointers are device pointers.
+struct EpiParams {
+  void* out;             // [M, ldo] (row index possibly remapped)
+  int out_type;          // OutType
+  int ldo;
+  const float* bias;     // [N] or null
+  int act;               // 0 none, 1 tanh-GELU (cpu_gelu.c:23-36)
+  const float* residual; // [M, ldr] fp32 added last, may alias out
+  int ldr;
+  int res_row_period;    // >0: residual row = row % period (pos-embed tiling)
+  // RoPE on output columns [0, rope_cols): interleaved pairs within 64-wide
+  // heads rotated by cos/sin[pos, 32] (cpu_rope.c:35-110).
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_cols;
+  int rope_period;       // position index p = row % rope_period
+  const int* rope_pos;   // optional: position = rope_pos[p]
+  // Output row remap: stored row = (row / period) * period + map[row % period]
+  const int* out_row_map;
+  int out_row_period;
+};
+
+struct GemmShape {
+  int M, N, K;
+};
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;          // 64 x 16-bit = 128 B rows (SWIZZLE_128B)
+constexpr int kStages16 = 4;      // smem ring depth, 16-bit W
+constexpr int kStagesQ8 = 3;      // smem ring depth, Q8 W (bigger stages)
+constexpr int kUmmaK = 16;
+constexpr int kATileBytes = kBM * kBK * 2;   // 16 KiB
+constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KiB
+constexpr int kQ8TileBytes = kBN * kBK;      // 16 KiB int8
+constexpr int kQ8ScaleBytes = kBN * (kBK / 32) * 4;  // 2 KiB, scales stored [K/32, N]
+constexpr int kTmemCols = 2 * kBN;           // 512: double-buffered accumulator
+
+template <int kBMode>
+struct GemmCfg {
+  static constexpr int kThreads = kBMode == kBQ8 ? 320 : 192;  // + 4 converter warps
+  static constexpr int kStages = kBMode == kBQ8 ? kStagesQ8 : kStages16;
+  static constexpr int kStageBytes =
+      kATileBytes + kBTileBytes + (kBMode == kBQ8 ? kQ8TileBytes + kQ8ScaleBytes : 0);
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+}  // namespace s3

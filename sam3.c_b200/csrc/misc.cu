@@ -1,0 +1,349 @@
+// misc.cu - HBM-bound kernels around the GEMMs: LayerNorm, patch im2col,
+// row permutes, Q8 repack, dtype casts.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "misc.cuh"
+#include "sam3cu_internal.h"
+#include "sm100_ptx.cuh"
+
+namespace s3 {
+
+S3_DEV_ERROR_ACCESSOR(dev_error_misc)
+
+namespace {
+
+template <int T>
+struct IO;
+template <>
+struct IO<kF32> {
+  static __device__ __forceinline__ float4 ld4(const void* p, int64_t i) {
+    return *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+  }
+  static __device__ __forceinline__ void st4(void* p, int64_t i, float4 v) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = v;
+  }
+};
+template <>
+struct IO<kBF16> {
+  static __device__ __forceinline__ float4 ld4(const void* p, int64_t i) {
+    uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p) + i);
+    __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&r.x);
+    __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&r.y);
+    float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+    return make_float4(fa.x, fa.y, fb.x, fb.y);
+  }
+  static __device__ __forceinline__ void st4(void* p, int64_t i, float4 v) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 r;
+    r.x = *reinterpret_cast<uint32_t*>(&a);
+    r.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p) + i) = r;
+  }
+};
+template <>
+struct IO<kF16> {
+  static __device__ __forceinline__ float4 ld4(const void* p, int64_t i) {
+    uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __half*>(p) + i);
+    __half2 a = *reinterpret_cast<__half2*>(&r.x);
+    __half2 b = *reinterpret_cast<__half2*>(&r.y);
+    float2 fa = __half22float2(a), fb = __half22float2(b);
+    return make_float4(fa.x, fa.y, fb.x, fb.y);
+  }
+  static __device__ __forceinline__ void st4(void* p, int64_t i, float4 v) {
+    __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    uint2 r;
+    r.x = *reinterpret_cast<uint32_t*>(&a);
+    r.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(static_cast<__half*>(p) + i) = r;
+  }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// One warp per row; the row lives in registers (NV float4 per lane, cols ==
+// 128*NV).  Two-pass statistics exactly as cpu_layernorm.c:31-64: mean, then
+// sum of squared deviations, inv_std = 1/sqrtf(var/cols + 1e-5).
+template <int TI, int TO, int NV>
+__global__ void __launch_bounds__(256) layernorm_rows(const void* __restrict__ x, void* __restrict__ y,
+                                                      const float* __restrict__ g,
+                                                      const float* __restrict__ b, int rows, int cols,
+                                                      const int* __restrict__ out_row_map,
+                                                      int out_row_period) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int64_t base = static_cast<int64_t>(warp) * cols;
+  float4 v[NV];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] = IO<TI>::ld4(x, base + (i * 32 + lane) * 4);
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  const float mean = warp_sum(s) / static_cast<float>(cols);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    q += (a * a + bb * bb) + (c * c + d * d);
+  }
+  const float inv_std = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(cols) + 1e-5f);
+  int orow = warp;
+  if (out_row_map) orow = (warp / out_row_period) * out_row_period + out_row_map[warp % out_row_period];
+  const int64_t obase = static_cast<int64_t>(orow) * cols;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    float4 r;
+    r.x = (v[i].x - mean) * inv_std;
+    r.y = (v[i].y - mean) * inv_std;
+    r.z = (v[i].z - mean) * inv_std;
+    r.w = (v[i].w - mean) * inv_std;
+    if (g) {
+      float4 gg = __ldg(reinterpret_cast<const float4*>(g + c));
+      r.x *= gg.x; r.y *= gg.y; r.z *= gg.z; r.w *= gg.w;
+    }
+    if (b) {
+      float4 bb = __ldg(reinterpret_cast<const float4*>(b + c));
+      r.x += bb.x; r.y += bb.y; r.z += bb.z; r.w += bb.w;
+    }
+    IO<TO>::st4(y, obase + c, r);
+  }
+}
+
+// Generic fallback (any cols, scalar, three passes over the row).
+template <int TI, int TO>
+__global__ void layernorm_rows_generic(const void* __restrict__ x, void* __restrict__ y,
+                                       const float* __restrict__ g, const float* __restrict__ b,
+                                       int rows, int cols) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  auto ld = [&](int64_t i) -> float {
+    if (TI == kF32) return static_cast<const float*>(x)[i];
+    if (TI == kBF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(x)[i]);
+    return __half2float(static_cast<const __half*>(x)[i]);
+  };
+  const int64_t base = static_cast<int64_t>(warp) * cols;
+  float s = 0.f;
+  for (int c = lane; c < cols; c += 32) s += ld(base + c);
+  const float mean = warp_sum(s) / static_cast<float>(cols);
+  float q = 0.f;
+  for (int c = lane; c < cols; c += 32) {
+    float d = ld(base + c) - mean;
+    q += d * d;
+  }
+  const float inv_std = 1.0f / sqrtf(warp_sum(q) / static_cast<float>(cols) + 1e-5f);
+  for (int c = lane; c < cols; c += 32) {
+    float r = (ld(base + c) - mean) * inv_std;
+    if (g) r *= g[c];
+    if (b) r += b[c];
+    if (TO == kF32) static_cast<float*>(y)[base + c] = r;
+    else if (TO == kBF16) static_cast<__nv_bfloat16*>(y)[base + c] = __float2bfloat16_rn(r);
+    else static_cast<__half*>(y)[base + c] = __float2half_rn(r);
+  }
+}
+
+template <int TI, int TO>
+int ln_dispatch(const void* x, void* y, const float* g, const float* b, int rows, int cols,
+                const int* map, int period, cudaStream_t st) {
+  const int blocks = (rows + 7) / 8;
+  const bool al = (cols % 128 == 0);
+  if (al && cols == 1024)
+    layernorm_rows<TI, TO, 8><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+  else if (al && cols == 512)
+    layernorm_rows<TI, TO, 4><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+  else if (al && cols == 256)
+    layernorm_rows<TI, TO, 2><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+  else if (al && cols == 128)
+    layernorm_rows<TI, TO, 1><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+  else if (al && cols == 2048)
+    layernorm_rows<TI, TO, 16><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+  else if (!map)
+    layernorm_rows_generic<TI, TO><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols);
+  else
+    return kErrShape;
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+// Patch-embed im2col: image planar CHW [3, img, img] (per image) ->
+// A[row, (ky*ps + kx)*3 + c] for the patch at raster position src_of_row[row
+// % np] (so rows come out in whatever token order the map gives), K padded
+// with zeros up to kpad.  Matches the OHWI weight layout of the reference's
+// NHWC conv path (image_encoder.c:554-597).
+template <int TO>
+__global__ void patch_im2col(const float* __restrict__ img, void* __restrict__ a, int n_img, int img_sz,
+                             int ps, int gs, int kpad, const int* __restrict__ src_of_row) {
+  const int np = gs * gs;
+  const int64_t total = static_cast<int64_t>(n_img) * np * kpad;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(i % kpad);
+    const int64_t row = i / kpad;
+    const int im = static_cast<int>(row / np);
+    int p = static_cast<int>(row % np);
+    if (src_of_row) p = src_of_row[p];
+    float v = 0.f;
+    const int kk = ps * ps * 3;
+    if (k < kk) {
+      const int c = k % 3, kx = (k / 3) % ps, ky = k / (3 * ps);
+      const int py = p / gs, px = p % gs;
+      v = img[((static_cast<int64_t>(im) * 3 + c) * img_sz + py * ps + ky) * img_sz + px * ps + kx];
+    }
+    if (TO == kBF16) static_cast<__nv_bfloat16*>(a)[i] = __float2bfloat16_rn(v);
+    else if (TO == kF16) static_cast<__half*>(a)[i] = __float2half_rn(v);
+    else static_cast<float*>(a)[i] = v;
+  }
+}
+
+// Row gather: dst[(r/period)*period + r%period] = src[(r/period)*period +
+// map[r%period]] for 16-byte vectors of `row_bytes`.
+__global__ void gather_rows(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
+                            int row_bytes, const int* __restrict__ map, int period) {
+  const int vec = row_bytes / 16;
+  const int64_t total = static_cast<int64_t>(rows) * vec;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / vec), v = static_cast<int>(i % vec);
+    const int sr = (r / period) * period + map[r % period];
+    reinterpret_cast<uint4*>(dst + static_cast<int64_t>(r) * row_bytes)[v] =
+        reinterpret_cast<const uint4*>(src + static_cast<int64_t>(sr) * row_bytes)[v];
+  }
+}
+
+// Q8_0 blocks {f32 scale; i8 q[32]} (quant.h:30-33) over a flattened [N,K]
+// weight, K % 32 == 0 -> int8 [N,K] + scales transposed [K/32, N].
+__global__ void q8_repack(const uint8_t* __restrict__ blocks, int8_t* __restrict__ q, float* __restrict__ sc,
+                          int N, int K) {
+  const int kb = K / 32;
+  const int64_t nblk = static_cast<int64_t>(N) * kb;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < nblk;
+       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* blk = blocks + b * 36;
+    const int n = static_cast<int>(b / kb), j = static_cast<int>(b % kb);
+    float s;
+    memcpy(&s, blk, 4);
+    sc[static_cast<int64_t>(j) * N + n] = s;
+    int8_t* dst = q + static_cast<int64_t>(n) * K + j * 32;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) dst[i] = static_cast<int8_t>(blk[4 + i]);
+  }
+}
+
+// sam3_q8_quantize (quant.c:67-131) on the device, one block of 32 per
+// thread: scale = absmax/127; q = roundf(x * (1/scale)) clamped to +-127;
+// zero tail; scale 0 -> zero block.  IEEE division and roundf give the same
+// bits as the reference's scalar path.
+__global__ void q8_quantize_kernel(const float* __restrict__ src, uint8_t* __restrict__ dst, int64_t n) {
+  const int64_t nb = (n + 31) / 32;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < nb;
+       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t off = b * 32;
+    const int cnt = static_cast<int>(n - off < 32 ? n - off : 32);
+    float amax = 0.f;
+    for (int i = 0; i < cnt; ++i) amax = fmaxf(amax, fabsf(src[off + i]));
+    const float scale = __fdiv_rn(amax, 127.0f);
+    uint8_t* blk = dst + b * 36;
+    memcpy(blk, &scale, 4);
+    const float inv = scale == 0.f ? 0.f : __fdiv_rn(1.0f, scale);
+    for (int i = 0; i < 32; ++i) {
+      int q = 0;
+      if (scale != 0.f && i < cnt) {
+        q = static_cast<int>(roundf(__fmul_rn(src[off + i], inv)));
+        q = q > 127 ? 127 : (q < -127 ? -127 : q);
+      }
+      blk[4 + i] = static_cast<uint8_t>(static_cast<int8_t>(q));
+    }
+  }
+}
+
+template <int TI, int TO>
+__global__ void cast_kernel(const void* __restrict__ x, void* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v;
+    if (TI == kF32) v = static_cast<const float*>(x)[i];
+    else if (TI == kBF16) v = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[i]);
+    else v = __half2float(static_cast<const __half*>(x)[i]);
+    if (TO == kF32) static_cast<float*>(y)[i] = v;
+    else if (TO == kBF16) static_cast<__nv_bfloat16*>(y)[i] = __float2bfloat16_rn(v);
+    else static_cast<__half*>(y)[i] = __float2half_rn(v);
+  }
+}
+
+int grid_for(int64_t n, int threads) {
+  int64_t g = (n + threads - 1) / threads;
+  int cap = num_sms() * 16;
+  return static_cast<int>(g < cap ? (g < 1 ? 1 : g) : cap);
+}
+
+}  // namespace
+
+int launch_layernorm(const void* x, int tin, void* y, int tout, const float* g, const float* b, int rows,
+                     int cols, const int* out_row_map, int out_row_period, cudaStream_t st) {
+  if (rows <= 0) return kOk;
+  if (cols <= 0) return kErrShape;
+  count_launches(1);
+#define S3_LN(TI, TO)                                                                       \
+  if (tin == TI && tout == TO)                                                              \
+    return ln_dispatch<TI, TO>(x, y, g, b, rows, cols, out_row_map, out_row_period, st);
+  S3_LN(kF32, kF32) S3_LN(kF32, kBF16) S3_LN(kF32, kF16)
+  S3_LN(kBF16, kF32) S3_LN(kBF16, kBF16) S3_LN(kF16, kF32) S3_LN(kF16, kF16)
+#undef S3_LN
+  return kErrDtype;
+}
+
+int launch_patch_im2col(const float* img, void* a, int tout, int n_img, int img_sz, int ps, int kpad,
+                        const int* src_of_row, cudaStream_t st) {
+  count_launches(1);
+  const int gs = img_sz / ps;
+  const int64_t total = static_cast<int64_t>(n_img) * gs * gs * kpad;
+  const int grid = grid_for(total, 256);
+  if (tout == kBF16) patch_im2col<kBF16><<<grid, 256, 0, st>>>(img, a, n_img, img_sz, ps, gs, kpad, src_of_row);
+  else if (tout == kF16) patch_im2col<kF16><<<grid, 256, 0, st>>>(img, a, n_img, img_sz, ps, gs, kpad, src_of_row);
+  else patch_im2col<kF32><<<grid, 256, 0, st>>>(img, a, n_img, img_sz, ps, gs, kpad, src_of_row);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int launch_gather_rows(const void* src, void* dst, int rows, int row_bytes, const int* map, int period,
+                       cudaStream_t st) {
+  count_launches(1);
+  if (row_bytes % 16) return kErrShape;
+  const int64_t total = static_cast<int64_t>(rows) * (row_bytes / 16);
+  gather_rows<<<grid_for(total, 256), 256, 0, st>>>(static_cast<const uint8_t*>(src),
+                                                     static_cast<uint8_t*>(dst), rows, row_bytes, map,
+                                                     period);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int launch_q8_repack(const void* blocks, int8_t* q, float* sc, int N, int K, cudaStream_t st) {
+  count_launches(1);
+  if (K % 32) return kErrShape;
+  const int64_t n = static_cast<int64_t>(N) * (K / 32);
+  q8_repack<<<grid_for(n, 256), 256, 0, st>>>(static_cast<const uint8_t*>(blocks), q, sc, N, K);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int launch_q8_quantize(const float* src, void* blocks, int64_t n, cudaStream_t st) {
+  count_launches(1);
+  q8_quantize_kernel<<<grid_for((n + 31) / 32, 256), 256, 0, st>>>(src, static_cast<uint8_t*>(blocks), n);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int launch_cast(const void* x, int tin, void* y, int tout, int64_t n, cudaStream_t st) {
+  count_launches(1);
+  const int grid = grid_for(n, 256);
+#define S3_CAST(TI, TO) \
+  if (tin == TI && tout == TO) { cast_kernel<TI, TO><<<grid, 256, 0, st>>>(x, y, n); return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch; }
+  S3_CAST(kF32, kBF16) S3_CAST(kF32, kF16) S3_CAST(kBF16, kF32) S3_CAST(kF16, kF32) S3_CAST(kF32, kF32)
+#undef S3_CAST
+  return kErrDtype;
+}
+
+}  // namespace s3

@@ -1,0 +1,19 @@
+// misc.cuh - launchers of the HBM-bound helper kernels (misc.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "sam3cu_internal.h"
+
+namespace s3 {
+
+int launch_layernorm(const void* x, int tin, void* y, int tout, const float* g, const float* b, int rows,
+                     int cols, const int* out_row_map, int out_row_period, cudaStream_t st);
+int launch_patch_im2col(const float* img, void* a, int tout, int n_img, int img_sz, int ps, int kpad,
+                        const int* src_of_row, cudaStream_t st);
+int launch_gather_rows(const void* src, void* dst, int rows, int row_bytes, const int* map, int period,
+                       cudaStream_t st);
+int launch_q8_repack(const void* blocks, int8_t* q, float* sc, int N, int K, cudaStream_t st);
+int launch_cast(const void* x, int tin, void* y, int tout, int64_t n, cudaStream_t st);
+
+}  // namespace s3

@@ -1,0 +1,260 @@
+"""Python host side of the B200 backend: ctypes bindings of include/sam3cu.h.
+
+This mirrors the per-op and encoder entry points of sam3.c that the CUDA
+library replaces (see the header for the reference file:line of each).  It
+loads ``lib/libsam3cu.so`` built in tree by ``build.py`` and raises if the
+library is missing: there is no CPU fallback.  Device buffers are passed as
+torch CUDA tensors (torch is used only for device memory and streams).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libsam3cu.so")
+
+F32, F16, BF16, Q8_0 = 0, 1, 2, 5
+ACT_NONE, ACT_GELU_TANH = 0, 1
+
+EXPORTS = (
+    "sam3cu_init", "sam3cu_strerror", "sam3cu_last_device_error",
+    "sam3cu_launch_count", "sam3cu_linear", "sam3cu_linear_q8",
+    "sam3cu_q8_repack", "sam3cu_q8_quantize", "sam3cu_layernorm",
+    "sam3cu_sdpa", "sam3cu_vit_create", "sam3cu_vit_destroy",
+    "sam3cu_vit_encode", "sam3cu_vit_encode_async", "sam3cu_vit_stream",
+    "sam3cu_vit_launches_per_encode",
+)
+
+_lib = None
+
+
+class Sam3cuError(RuntimeError):
+    pass
+
+
+def lib():
+    """Load libsam3cu.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise Sam3cuError(f"{LIB_PATH} not built: run `python sam3.c_b200/build.py`")
+        L = C.CDLL(LIB_PATH)
+        vp, i32, i64 = C.c_void_p, C.c_int, C.c_int64
+        L.sam3cu_strerror.restype = C.c_char_p
+        L.sam3cu_last_device_error.restype = C.c_uint
+        L.sam3cu_launch_count.restype = C.c_uint64
+        L.sam3cu_launch_count.argtypes = [i32]
+        L.sam3cu_linear.argtypes = [vp, i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]
+        L.sam3cu_linear_q8.argtypes = [vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]
+        L.sam3cu_q8_repack.argtypes = [vp, i32, i32, vp, vp, vp]
+        L.sam3cu_q8_quantize.argtypes = [vp, vp, i64, vp]
+        L.sam3cu_layernorm.argtypes = [vp, i32, vp, vp, vp, i32, i32, i32, vp]
+        L.sam3cu_sdpa.argtypes = [vp, vp, vp, i64, vp, i64, i32, i32, i32, i32, i32, vp]
+        L.sam3cu_vit_create.restype = vp
+        L.sam3cu_vit_create.argtypes = [vp, vp, i32, i32, C.POINTER(C.c_int)]
+        L.sam3cu_vit_destroy.argtypes = [vp]
+        L.sam3cu_vit_encode.argtypes = [vp, vp, i32, vp, i32]
+        L.sam3cu_vit_encode_async.argtypes = [vp, vp, i32, vp]
+        L.sam3cu_vit_stream.restype = vp
+        L.sam3cu_vit_stream.argtypes = [vp]
+        L.sam3cu_vit_launches_per_encode.argtypes = [vp, i32]
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = lib().sam3cu_strerror(rc).decode()
+        raise Sam3cuError(f"{what}: {msg} ({rc})")
+
+
+def init(device: int = 0) -> None:
+    check(lib().sam3cu_init(device), "sam3cu_init")
+
+
+def device_error() -> int:
+    return lib().sam3cu_last_device_error()
+
+
+def launch_count(reset: bool = False) -> int:
+    return lib().sam3cu_launch_count(1 if reset else 0)
+
+
+def _ptr(t) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    import torch
+    return torch.cuda.current_stream().cuda_stream
+
+
+_TORCH_CODE = None
+
+
+def dtype_code(t) -> int:
+    import torch
+    return {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}[t.dtype]
+
+
+# ------------------------------------------------------------------ ops
+def linear(x, w, bias=None, residual=None, act=ACT_NONE, out_dtype=None, out=None):
+    """y = act(x . w^T + bias) + residual (cuda tensors; x, w 16-bit)."""
+    import torch
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype or x.dtype, device=x.device)
+    check(lib().sam3cu_linear(_ptr(x), dtype_code(x), _ptr(w), _ptr(bias), _ptr(residual),
+                              _ptr(out), dtype_code(out), M, K, N, act, _stream()), "sam3cu_linear")
+    return out
+
+
+def q8_repack(blocks, N: int, K: int):
+    """Reference Q8_0 blocks (uint8 cuda tensor, 36 B each) -> (q, scales)."""
+    import torch
+    q = torch.empty((N, K), dtype=torch.int8, device=blocks.device)
+    sc = torch.empty((K // 32, N), dtype=torch.float32, device=blocks.device)
+    check(lib().sam3cu_q8_repack(_ptr(blocks), N, K, _ptr(q), _ptr(sc), _stream()), "q8_repack")
+    return q, sc
+
+
+def q8_quantize(src):
+    import torch
+    n = src.numel()
+    blocks = torch.empty(((n + 31) // 32) * 36, dtype=torch.uint8, device=src.device)
+    check(lib().sam3cu_q8_quantize(_ptr(src), _ptr(blocks), n, _stream()), "q8_quantize")
+    return blocks
+
+
+def linear_q8(x, q, scales, bias=None, residual=None, act=ACT_NONE, out_dtype=None, out=None):
+    import torch
+    M, K = x.shape
+    N = q.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype or x.dtype, device=x.device)
+    check(lib().sam3cu_linear_q8(_ptr(x), dtype_code(x), _ptr(q), _ptr(scales), _ptr(bias),
+                                 _ptr(residual), _ptr(out), dtype_code(out), M, K, N, act,
+                                 _stream()), "sam3cu_linear_q8")
+    return out
+
+
+def layernorm(x, gamma=None, beta=None, out_dtype=None, out=None):
+    import torch
+    rows, cols = x.reshape(-1, x.shape[-1]).shape
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    check(lib().sam3cu_layernorm(_ptr(x), dtype_code(x), _ptr(gamma), _ptr(beta), _ptr(out),
+                                 dtype_code(out), rows, cols, _stream()), "sam3cu_layernorm")
+    return out
+
+
+def sdpa_packed(qkv, n_groups: int, seq: int, heads: int, head_dim: int = 64, out=None):
+    """Attention over a fused [rows, 3*E] Q|K|V buffer -> [rows, E]."""
+    import torch
+    rows, three_e = qkv.shape
+    E = three_e // 3
+    if out is None:
+        out = torch.empty((rows, E), dtype=qkv.dtype, device=qkv.device)
+    base = qkv.data_ptr()
+    es = qkv.element_size()
+    check(lib().sam3cu_sdpa(base, base + E * es, base + 2 * E * es, three_e, _ptr(out), E,
+                            dtype_code(qkv), n_groups, seq, heads, head_dim, _stream()), "sam3cu_sdpa")
+    return out
+
+
+# ------------------------------------------------------------------ ViT
+class _Cfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("img_size", "patch_size", "embed_dim", "depth",
+                                       "n_heads", "window_size", "mlp_dim")]
+
+
+BLOCK_KEYS = ("ln1_w", "ln1_b", "qkv_w", "qkv_b", "proj_w", "proj_b", "ln2_w", "ln2_b",
+              "fc1_w", "fc1_b", "fc2_w", "fc2_b")
+
+
+class _Blk(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in BLOCK_KEYS]
+
+
+class _W(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("patch_w", "patch_b", "pos_raw", "ln_pre_w",
+                                          "ln_pre_b")] + [("blocks", _Blk * 32)]
+
+
+CFG_KEYS = ("img_size", "patch_size", "embed_dim", "depth", "n_heads", "window_size", "mlp_dim")
+
+
+class VitEncoder:
+    """sam3_vit_init + sam3_vit_load + sam3_vit_build on one B200.
+
+    ``weights`` is a dict of host float32 numpy arrays in the reference
+    layouts (see sam3cu_vit_weights); ``weight_dtype`` is BF16, F16 or Q8_0.
+    """
+
+    def __init__(self, cfg: dict, weights: dict, weight_dtype: int = BF16, max_batch: int = 1):
+        self.cfg = dict(cfg)
+        c = _Cfg(*(cfg[k] for k in CFG_KEYS))
+        w = _W()
+        keep = []
+
+        def put(obj, name, arr):
+            a = np.ascontiguousarray(arr, np.float32)
+            keep.append(a)
+            setattr(obj, name, a.ctypes.data)
+
+        for n in ("patch_w", "patch_b", "pos_raw", "ln_pre_w", "ln_pre_b"):
+            put(w, n, weights[n])
+        for i, blk in enumerate(weights["blocks"]):
+            for n in BLOCK_KEYS:
+                put(w.blocks[i], n, blk[n])
+        st = C.c_int(0)
+        h = lib().sam3cu_vit_create(C.byref(c), C.byref(w), weight_dtype, max_batch, C.byref(st))
+        del keep
+        if not h:
+            check(st.value or -1, "sam3cu_vit_create")
+        self.h = h
+        self.max_batch = max_batch
+        gs = cfg["img_size"] // cfg["patch_size"]
+        self.np = gs * gs
+
+    def close(self):
+        if self.h:
+            lib().sam3cu_vit_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        return lib().sam3cu_vit_stream(self.h)
+
+    def launches_per_encode(self, n: int) -> int:
+        return lib().sam3cu_vit_launches_per_encode(self.h, n)
+
+    def encode_host(self, images: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
+        """Host in, host out: [n,3,img,img] f32 -> [n, np, e] f32."""
+        images = np.ascontiguousarray(images, np.float32)
+        n = images.shape[0]
+        if out is None:
+            out = np.empty((n, self.np, self.cfg["embed_dim"]), np.float32)
+        check(lib().sam3cu_vit_encode(self.h, images.ctypes.data, n, out.ctypes.data, 0),
+              "sam3cu_vit_encode")
+        return out
+
+    def encode_ptr(self, images_ptr: int, n: int, out_ptr: int, on_device: bool) -> None:
+        check(lib().sam3cu_vit_encode(self.h, images_ptr, n, out_ptr, 1 if on_device else 0),
+              "sam3cu_vit_encode")
+
+    def encode_async(self, images, out) -> None:
+        """Device tensors; enqueue on the encoder's stream, no wait."""
+        check(lib().sam3cu_vit_encode_async(self.h, images.data_ptr(), images.shape[0],
+                                            out.data_ptr()), "sam3cu_vit_encode_async")

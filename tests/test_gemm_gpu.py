@@ -1,0 +1,103 @@
+"""GPU parity of the fused tcgen05 linear (sam3cu_linear / sam3cu_linear_q8)
+against the CPU oracle's restatement of gh_linear (+GELU, +residual).
+
+Inputs are rounded to the operand type first, so the oracle sees exactly the
+values the tensor cores see; what remains is FP32 accumulation order and the
+output rounding.  Tolerances (normwise max relative error): F32 output 1e-4
+... 2e-3 depending on K, 16-bit output 1e-2.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from _util import rel_err, to_np
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    (128, 64, 256),      # one tile
+    (257, 128, 320),     # M and N tails
+    (100, 200, 40),      # K not a multiple of 64, N % 32 != 0
+    (5184, 1024, 1024),  # ViT proj
+    (5184, 1024, 3072),  # ViT qkv
+]
+
+
+def _inputs(M, K, N, seed, dt):
+    import torch
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w = rng.standard_normal((N, K), dtype=np.float32) / np.sqrt(K)
+    b = rng.standard_normal(N, dtype=np.float32) / np.sqrt(K)
+    rnd = O.round_bf16 if dt == "bf16" else O.round_fp16
+    x, w = rnd(x), rnd(w)
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float16
+    dev = torch.device("cuda")
+    return (x, w, b, torch.from_numpy(x).to(dev, tdt), torch.from_numpy(w).to(dev, tdt),
+            torch.from_numpy(b).to(dev))
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_linear_bias_f32out(cuda, dt, M, K, N):
+    import torch
+    import sam3cu
+    x, w, b, tx, tw, tb = _inputs(M, K, N, 1, dt)
+    y = sam3cu.linear(tx, tw, bias=tb, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert sam3cu.device_error() == 0
+    ref = O.linear(x, w, b)
+    assert rel_err(to_np(y), ref) < 1e-4 * max(1.0, K / 256)
+
+
+@pytest.mark.parametrize("M,K,N", [(257, 128, 320), (5184, 1024, 4736)])
+def test_linear_gelu_bf16out(cuda, M, K, N):
+    import sam3cu
+    x, w, b, tx, tw, tb = _inputs(M, K, N, 2, "bf16")
+    y = sam3cu.linear(tx, tw, bias=tb, act=sam3cu.ACT_GELU_TANH)
+    ref = O.linear(x, w, b, act=1)
+    assert rel_err(to_np(y), ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,K,N", [(300, 256, 128), (5184, 4736, 1024)])
+def test_linear_residual_inplace(cuda, M, K, N):
+    import torch
+    import sam3cu
+    x, w, b, tx, tw, tb = _inputs(M, K, N, 3, "bf16")
+    res = np.random.default_rng(4).standard_normal((M, N), dtype=np.float32)
+    tres = torch.from_numpy(res).cuda()
+    sam3cu.linear(tx, tw, bias=tb, residual=tres, out=tres)  # x += linear(...)
+    ref = O.linear(x, w, b, res=res)
+    assert rel_err(to_np(tres), ref) < 2e-4 * max(1.0, K / 1024)
+
+
+def test_q8_quantize_bitexact(cuda):
+    import torch
+    import sam3cu
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal(4736 * 1024 + 17, dtype=np.float32) * 0.02)
+    w[:64] = 0.0  # zero blocks: scale 0
+    blocks = sam3cu.q8_quantize(torch.from_numpy(w).cuda())
+    ref = O.q8_quantize(w)
+    assert blocks.cpu().numpy().tobytes() == ref.tobytes()
+
+
+@pytest.mark.parametrize("M,K,N", [(257, 128, 320), (5184, 1024, 4736)])
+def test_linear_q8(cuda, M, K, N):
+    import torch
+    import sam3cu
+    rng = np.random.default_rng(6)
+    x = O.round_bf16(rng.standard_normal((M, K), dtype=np.float32))
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    b = rng.standard_normal(N, dtype=np.float32) * 0.01
+    blocks = O.q8_quantize(w)
+    wdq = O.q8_dequantize(blocks, N * K).reshape(N, K)
+    tb = torch.from_numpy(np.frombuffer(blocks.tobytes(), np.uint8).copy()).cuda()
+    q, sc = sam3cu.q8_repack(tb, N, K)
+    y = sam3cu.linear_q8(torch.from_numpy(x).cuda().bfloat16(), q, sc,
+                         bias=torch.from_numpy(b).cuda(), out_dtype=torch.float32)
+    # the dequantised weight is rounded to bf16 on chip: compare against the
+    # exact x . dequant(W)^T at the north-star tolerance, and against the
+    # bf16-rounded dequantised weight tightly
+    assert rel_err(to_np(y), O.linear(x, wdq, b)) < 1e-2
+    assert rel_err(to_np(y), O.linear(x, O.round_bf16(wdq), b)) < 1e-4 * max(1.0, K / 256)
