@@ -88,6 +88,14 @@ def _ptr(t) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+def _f32(t, what):
+    """bias / residual / gamma / beta must be contiguous float32 device tensors."""
+    import torch
+    if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or not t.is_cuda):
+        raise TypeError(f"{what} must be a contiguous float32 CUDA tensor")
+    return _ptr(t)
+
+
 def _stream():
     import torch
     return torch.cuda.current_stream().cuda_stream
@@ -109,7 +117,7 @@ def linear(x, w, bias=None, residual=None, act=ACT_NONE, out_dtype=None, out=Non
     N = w.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype or x.dtype, device=x.device)
-    check(lib().sam3cu_linear(_ptr(x), dtype_code(x), _ptr(w), _ptr(bias), _ptr(residual),
+    check(lib().sam3cu_linear(_ptr(x), dtype_code(x), _ptr(w), _f32(bias, 'bias'), _f32(residual, 'residual'),
                               _ptr(out), dtype_code(out), M, K, N, act, _stream()), "sam3cu_linear")
     return out
 
@@ -148,7 +156,7 @@ def layernorm(x, gamma=None, beta=None, out_dtype=None, out=None):
     rows, cols = x.reshape(-1, x.shape[-1]).shape
     if out is None:
         out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
-    check(lib().sam3cu_layernorm(_ptr(x), dtype_code(x), _ptr(gamma), _ptr(beta), _ptr(out),
+    check(lib().sam3cu_layernorm(_ptr(x), dtype_code(x), _f32(gamma, 'gamma'), _f32(beta, 'beta'), _ptr(out),
                                  dtype_code(out), rows, cols, _stream()), "sam3cu_layernorm")
     return out
 

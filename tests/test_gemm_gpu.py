@@ -27,8 +27,8 @@ def _inputs(M, K, N, seed, dt):
     import torch
     rng = np.random.default_rng(seed)
     x = rng.standard_normal((M, K), dtype=np.float32)
-    w = rng.standard_normal((N, K), dtype=np.float32) / np.sqrt(K)
-    b = rng.standard_normal(N, dtype=np.float32) / np.sqrt(K)
+    w = rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(K))
+    b = rng.standard_normal(N, dtype=np.float32) / np.float32(np.sqrt(K))
     rnd = O.round_bf16 if dt == "bf16" else O.round_fp16
     x, w = rnd(x), rnd(w)
     tdt = torch.bfloat16 if dt == "bf16" else torch.float16
@@ -75,7 +75,7 @@ def test_q8_quantize_bitexact(cuda):
     import torch
     import sam3cu
     rng = np.random.default_rng(5)
-    w = (rng.standard_normal(4736 * 1024 + 17, dtype=np.float32) * 0.02)
+    w = rng.standard_normal(4736 * 1024 + 17, dtype=np.float32) * np.float32(0.02)
     w[:64] = 0.0  # zero blocks: scale 0
     blocks = sam3cu.q8_quantize(torch.from_numpy(w).cuda())
     ref = O.q8_quantize(w)
@@ -88,8 +88,8 @@ def test_linear_q8(cuda, M, K, N):
     import sam3cu
     rng = np.random.default_rng(6)
     x = O.round_bf16(rng.standard_normal((M, K), dtype=np.float32))
-    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
-    b = rng.standard_normal(N, dtype=np.float32) * 0.01
+    w = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
+    b = rng.standard_normal(N, dtype=np.float32) * np.float32(0.01)
     blocks = O.q8_quantize(w)
     wdq = O.q8_dequantize(blocks, N * K).reshape(N, K)
     tb = torch.from_numpy(np.frombuffer(blocks.tobytes(), np.uint8).copy()).cuda()
