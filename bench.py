@@ -1,0 +1,331 @@
+"""Benchmark: 1008px Hiera-L image encodes per second on B200 (sam3.c's
+sam3_vit_build hot path), plus the encoder-GEMM TFLOP/s and the reference CPU
+backend timed on the same host.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference]
+
+Workload: a batch of 64 synthetic 1008x1008 images
+(seeded, see sam3.c_b200/synth.py) encoded by the 32-block ViT (width 1024,
+16 heads, MLP 4736, 24x24 windows, global blocks 7/15/23/31) with BF16
+weights ~N(0, 0.02), sharded by image over the N GPUs (one weight replica
+per GPU, no collective on the data path): strong scaling, total work fixed.
+One step = the 64-image batch.  Under torchrun every rank encodes its
+shard; the step time is the max over ranks of CUDA-event time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "sam3.c_b200"))
+
+import synth  # noqa: E402
+
+CFG = synth.HIERA_L
+ATTN_GFLOP_PER_IMAGE = 28 * 12.23 + 4 * 110.08
+TOTAL_GFLOP_PER_IMAGE = 5399.0
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def gemm_gflop_per_image(cfg=CFG):
+    gs = cfg["img_size"] // cfg["patch_size"]
+    M, e, m = gs * gs, cfg["embed_dim"], cfg["mlp_dim"]
+    per_block = 2 * M * e * (3 * e + e + m + m)
+    patch = 2 * M * cfg["patch_size"] ** 2 * 3 * e
+    return (cfg["depth"] * per_block + patch) / 1e9
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- reference arm
+def cpu_reference_sample(threads: int = 0):
+    """Time the UNMODIFIED reference CPU backend (oracle/_ref, sam3.c sources)
+    on a bounded sample of one 1008px image: sam3_vit_build with depth 0
+    (patch embed + pos-embed + ln_pre) and with depth 2 (two window blocks),
+    both through the reference's own graph and CPU kernels.  Per-image time
+    = embed + 28 window blocks + 4 global blocks, a global block costed at a
+    window block x (144.05 + 110.08) / (144.05 + 12.23) GFLOP (its extra
+    attention FLOPs at the window block's rate)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    if not O.ref_available():
+        return None
+    n = O.ref_set_threads(threads)
+    c0 = dict(CFG, depth=0)
+    c2 = dict(CFG, depth=2)
+    w = synth.vit_weights(c2, seed=0)
+    img = synth.images(CFG, 1, seed=100)[0]
+    t = time.perf_counter()
+    O.ref_vit_encode(c0, w, img)
+    t_embed = time.perf_counter() - t
+    t = time.perf_counter()
+    O.ref_vit_encode(c2, w, img)
+    t2 = time.perf_counter() - t
+    t_blk = max((t2 - t_embed) / 2, 1e-9)
+    g = (144.05 + 110.08) / (144.05 + 12.23)
+    t_img = t_embed + 28 * t_blk + 4 * g * t_blk
+    return {"value": 1.0 / t_img, "unit": "images/s", "cores": os.cpu_count() if n == 0 else n,
+            "kind": "reference",
+            "sample": (f"reference sam3_vit_build on its CPU backend (oracle/_ref), 1 image 1008px: "
+                       f"depth-0 run {t_embed:.2f}s + depth-2 run {t2:.2f}s -> "
+                       f"{t_blk:.2f}s/window block, extrapolated to 32 blocks = {t_img:.1f}s/image"),
+            "seconds_per_image": t_img}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_reference_sample(args.cpu_threads)
+        if r is None:
+            print(json.dumps({"impl": "reference",
+                              "unavailable": "oracle/_ref/libsam3_ref.so not built"}))
+            return 0
+        if i >= args.warmup:
+            vals.append(r)
+    v = float(np.median([r["value"] for r in vals]))
+    last = vals[-1]
+    line = {"impl": "reference", "metric": "images_per_sec_1008px_hiera_l", "value": v,
+            "unit": "images/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * args.images / v, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config4_batched_encode_64x1008px_hiera_l",
+                       "global_batch": args.images, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "images/s", "cores": last["cores"],
+                             "kind": "reference", "sample": last["sample"]},
+            "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import sam3cu
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl")
+    torch.cuda.set_device(local)
+    sam3cu.init(local)
+    dev = torch.device("cuda", local)
+
+    n_total = args.images
+    per = [n_total // world + (1 if r < n_total % world else 0) for r in range(world)]
+    n_local = per[rank]
+    first = sum(per[:rank])
+    B = min(args.batch, max(n_local, 1))
+    wdt = {"bf16": sam3cu.BF16, "f16": sam3cu.F16, "q8": sam3cu.Q8_0}[args.dtype]
+
+    w = synth.vit_weights(CFG, seed=0)
+    enc = sam3cu.VitEncoder(CFG, w, wdt, max_batch=B)
+    del w
+    s = CFG["img_size"]
+    np_ = enc.np
+    e = CFG["embed_dim"]
+    # this rank's images: image i of the job uses seed 100 + i
+    host_imgs = torch.empty((n_local, 3, s, s), dtype=torch.float32).pin_memory()
+    for i in range(n_local):
+        host_imgs[i] = torch.from_numpy(synth.images(CFG, 1, seed=100 + first + i)[0])
+    host_out = torch.empty((B, np_, e), dtype=torch.float32).pin_memory()
+    dev_imgs = host_imgs.to(dev)
+    dev_out = torch.empty((B, np_, e), dtype=torch.float32, device=dev)
+    stream = torch.cuda.ExternalStream(enc.stream, device=dev)
+    chunks = [(i, min(B, n_local - i)) for i in range(0, n_local, B)]
+
+    def step_device():
+        for i, n in chunks:
+            enc.encode_async(dev_imgs[i:i + n], dev_out[:n])
+
+    def step_e2e():
+        # public API with host buffers: H2D of the inputs and D2H of the
+        # features happen inside every call, on the encoder's stream
+        for i, n in chunks:
+            enc.encode_ptr(host_imgs[i].data_ptr(), n, host_out.data_ptr(), on_device=False)
+
+    def timed(fn, k):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(k):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = torch.tensor([a.elapsed_time(b)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    for _ in range(args.warmup):
+        step_device()
+    torch.cuda.synchronize()
+    sam3cu.launch_count(reset=True)
+    clk = ClockSampler(local)
+    clk.start()
+    ms = timed(step_device, args.steps)
+    clocks = clk.stop()
+    launches = sam3cu.launch_count()
+    assert sam3cu.device_error() == 0, "device-side error during the timed region"
+    ms_step = ms / args.steps
+    value = n_total / (ms_step / 1000.0)
+
+    # end-to-end through the public API with host buffers
+    for _ in range(max(1, args.warmup // 2)):
+        step_e2e()
+    ms_e2e = timed(step_e2e, max(1, args.steps // 2)) / max(1, args.steps // 2)
+    e2e_value = n_total / (ms_e2e / 1000.0)
+    h2d = n_total * 3 * s * s * 4
+    d2h = n_total * np_ * e * 4
+
+    # per-kernel-kind device time of one encode of B images (direct
+    # launches with events between them, same stream)
+    prof = enc.profile(dev_imgs[:B], dev_out)
+    gemm_ms, gemm_n = prof["gemm"]
+    attn_ms, attn_n = prof["attention"]
+    ln_ms, ln_n = prof["layernorm"]
+    gemm_tflops = gemm_gflop_per_image() * B / gemm_ms  # GFLOP/ms = TFLOP/s
+    attn_tflops = ATTN_GFLOP_PER_IMAGE * B / attn_ms
+    # LN1/LN2 read the f32 stream and write 16-bit; ln_pre reads and writes f32
+    ln_bytes = (2 * CFG["depth"] * np_ * e * (4 + 2) + np_ * e * 8) * B
+    pk, pk_src = peaks()
+    peak = pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_reference_sample(args.cpu_threads)
+            if cpu is not None:
+                cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        total = gemm_ms + attn_ms + ln_ms + prof["other"][0]
+        line = {
+            "metric": "images_per_sec_1008px_hiera_l", "value": value, "unit": "images/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": {"bf16": "bf16", "f16": "f16", "q8": "q8_0w+bf16"}[args.dtype],
+            "data": "synthetic (seeded images and random-init weights of the Hiera-L ViT)",
+            "config": {"workload": "config4_batched_encode_64x1008px_hiera_l",
+                       "global_batch": n_total, "images_per_encode_call": B, "seq_len": 5184,
+                       "parallelism": f"dp{world} (image shards, weight replica per GPU)",
+                       "l2": "inputs and weights larger than L2 (0.8 GB images, 0.9 GB weights)"},
+            "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05 linear + fused epilogue)",
+                         "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": gemm_tflops / peak, "traffic": None,
+                         "peak_source": f"{pk_src} bf16_tflops_sustained"},
+            "gemm_tflops": gemm_tflops,
+            "attention_tflops": attn_tflops,
+            "layernorm_gbs": ln_bytes / (ln_ms / 1000.0) / 1e9,
+            "kernel_share": {k: round(prof[k][0] / total, 4) for k in prof},
+            "kernel_launches_per_encode": {k: prof[k][1] for k in prof},
+            "model_tflops": TOTAL_GFLOP_PER_IMAGE * value / 1000.0,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line))
+    enc.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--images", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=8, help="images per encode call")
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16", "q8"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-threads", type=int, default=0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

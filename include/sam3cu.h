@@ -201,6 +201,17 @@ SAM3CU_API int sam3cu_vit_encode_async(sam3cu_vit *vit, const float *images,
 /* cudaStream_t of the encoder, as void *. */
 SAM3CU_API void *sam3cu_vit_stream(sam3cu_vit *vit);
 
+/*
+ * Run one encode with direct launches (no graph) and a CUDA event after
+ * every launch; ms[k] / counts[k] receive the total device time and launch
+ * count per kind: 0 GEMM, 1 attention, 2 LayerNorm, 3 other.  images/out
+ * device.  For measurement only: the per-launch events serialise nothing
+ * but add a little host overhead.
+ */
+SAM3CU_API int sam3cu_vit_profile(sam3cu_vit *vit, const float *images,
+				  int n_images, float *out, double *ms,
+				  int *counts);
+
 /* Kernel launches one encode of n_images enqueues. */
 SAM3CU_API int sam3cu_vit_launches_per_encode(sam3cu_vit *vit, int n_images);
 

@@ -242,8 +242,10 @@ int ref_vit_encode(int img_size, int patch_size, int embed_dim, int depth,
 		2ul * mlp_dim * embed_dim + 10ul * embed_dim + mlp_dim) +
 		(size_t)embed_dim * patch_size * patch_size * 3 +
 		577ul * embed_dim + 4ul * embed_dim + 4ul * np * 64);
-	size_t sbytes = 4ul * np * ((size_t)mlp_dim * 3 + embed_dim * 40) +
-			(64ul << 20);
+	/* per-block-batch scratch of sam3_vit_build (two blocks per graph on
+	 * the CPU backend, image_encoder.c:701-712), with headroom */
+	size_t sbytes = 4ul * np * ((size_t)mlp_dim * 24 + embed_dim * 160) +
+			(512ul << 20);
 	int rc = -1;
 	if (!vit || sam3_arena_init(&model, wbytes * 2 + (64ul << 20)) ||
 	    sam3_arena_init(&scratch, sbytes) ||

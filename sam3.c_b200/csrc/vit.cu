@@ -96,6 +96,9 @@ struct sam3cu_vit {
   std::vector<const float*> graph_in;
   std::vector<float*> graph_out;
   int launches_per_block = 7;
+  // optional per-launch profiling (sam3cu_vit_profile): kind of each launch
+  std::vector<int>* prof_kinds = nullptr;
+  std::vector<cudaEvent_t>* prof_events = nullptr;
 };
 
 namespace s3 {
@@ -160,6 +163,18 @@ int run_linear(sam3cu_vit* v, const Linear& L, const void* a, int lda, int M, co
   return launch_gemm(a, lda, L.w.p, L.K, nullptr, nullptr, v->act, shp, ep, v->stream, 0);
 }
 
+enum ProfKind { kProfGemm = 0, kProfAttn = 1, kProfLn = 2, kProfOther = 3, kProfKinds = 4 };
+
+// Record an event after a launch of the given kind (profiling runs only).
+void tick(sam3cu_vit* v, int kind) {
+  if (!v->prof_events) return;
+  cudaEvent_t e;
+  cudaEventCreate(&e);
+  cudaEventRecord(e, v->stream);
+  v->prof_events->push_back(e);
+  v->prof_kinds->push_back(kind);
+}
+
 // Enqueue the whole forward for n images: images (device, CHW f32) -> out
 // (device, [n, np, e] f32 raster order).
 int forward(sam3cu_vit* v, const float* images, int n, float* out) {
@@ -170,8 +185,10 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
   int rc;
   // ---- patch embed + bias + pos-embed (window order) -> x; ln_pre in place
   void* acol = v->h.p;  // im2col scratch aliases the MLP hidden buffer
+  tick(v, kProfOther);  // start marker
   if ((rc = launch_patch_im2col(images, acol, v->act, n, c.img_size, c.patch_size, v->kpad, w2r, v->stream)))
     return rc;
+  tick(v, kProfOther);
   {
     EpiParams ep = epi_default();
     ep.out = v->x.p;
@@ -182,10 +199,12 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
     ep.ldr = e;
     ep.res_row_period = np;
     if ((rc = run_linear(v, v->patch, acol, v->kpad, M, ep))) return rc;
+    tick(v, kProfGemm);
   }
   if ((rc = launch_layernorm(v->x.p, kF32, v->x.p, kF32, v->ln_pre_w.as<float>(), v->ln_pre_b.as<float>(), M, e,
                              nullptr, 0, v->stream)))
     return rc;
+  tick(v, kProfLn);
   if (c.depth == 0)
     return launch_gather_rows(v->x.p, out, M, e * 4, v->raster_to_win.as<int>(), np, v->stream);
   for (int i = 0; i < c.depth; ++i) {
@@ -195,6 +214,7 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
     if ((rc = launch_layernorm(v->x.p, kF32, v->xn.p, v->act, B.ln1_w.as<float>(), B.ln1_b.as<float>(), M, e,
                                nullptr, 0, v->stream)))
       return rc;
+    tick(v, kProfLn);
     {
       EpiParams ep = epi_default();
       ep.out = v->qkv.p;
@@ -213,6 +233,7 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
         ep.rope_period = ws * ws;
       }
       if ((rc = run_linear(v, B.qkv, v->xn.p, e, M, ep))) return rc;
+      tick(v, kProfGemm);
     }
     {
       const uint16_t* qkv = v->qkv.as<uint16_t>();
@@ -221,6 +242,7 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
       if ((rc = launch_attention(qkv, qkv + e, qkv + 2 * e, 3 * e, v->ao.p, e, v->act, groups, seq, c.n_heads, hd,
                                  v->stream)))
         return rc;
+      tick(v, kProfAttn);
     }
     {
       EpiParams ep = epi_default();
@@ -231,10 +253,12 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
       ep.residual = v->x.as<float>();
       ep.ldr = e;
       if ((rc = run_linear(v, B.proj, v->ao.p, e, M, ep))) return rc;
+      tick(v, kProfGemm);
     }
     if ((rc = launch_layernorm(v->x.p, kF32, v->xn.p, v->act, B.ln2_w.as<float>(), B.ln2_b.as<float>(), M, e,
                                nullptr, 0, v->stream)))
       return rc;
+    tick(v, kProfLn);
     {
       EpiParams ep = epi_default();
       ep.out = v->h.p;
@@ -243,6 +267,7 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
       ep.bias = B.fc1.bias.as<float>();
       ep.act = 1;
       if ((rc = run_linear(v, B.fc1, v->xn.p, e, M, ep))) return rc;
+      tick(v, kProfGemm);
     }
     {
       EpiParams ep = epi_default();
@@ -257,6 +282,7 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
         ep.out_row_period = np;
       }
       if ((rc = run_linear(v, B.fc2, v->h.p, c.mlp_dim, M, ep))) return rc;
+      tick(v, kProfGemm);
     }
   }
   return kOk;
@@ -409,6 +435,31 @@ void sam3cu_vit_destroy(sam3cu_vit* v) {
 }
 
 void* sam3cu_vit_stream(sam3cu_vit* v) { return v ? v->stream : nullptr; }
+
+int sam3cu_vit_profile(sam3cu_vit* v, const float* images, int n, float* out, double* ms, int* counts) {
+  if (!v || n <= 0 || n > v->max_batch || !images || !out || !ms || !counts) return SAM3CU_EINVAL;
+  std::vector<int> kinds;
+  std::vector<cudaEvent_t> evs;
+  v->prof_kinds = &kinds;
+  v->prof_events = &evs;
+  int rc = forward(v, images, n, out);
+  v->prof_kinds = nullptr;
+  v->prof_events = nullptr;
+  cudaError_t ce = cudaStreamSynchronize(v->stream);
+  for (int k = 0; k < kProfKinds; ++k) {
+    ms[k] = 0.0;
+    counts[k] = 0;
+  }
+  for (size_t i = 1; i < evs.size(); ++i) {
+    float t = 0.f;
+    cudaEventElapsedTime(&t, evs[i - 1], evs[i]);
+    ms[kinds[i]] += t;
+    counts[kinds[i]] += 1;
+  }
+  for (auto e : evs) cudaEventDestroy(e);
+  if (rc) return rc;
+  return ce == cudaSuccess ? kOk : kErrCuda;
+}
 
 int sam3cu_vit_launches_per_encode(sam3cu_vit* v, int n) {
   (void)n;

@@ -26,8 +26,10 @@ EXPORTS = (
     "sam3cu_q8_repack", "sam3cu_q8_quantize", "sam3cu_layernorm",
     "sam3cu_sdpa", "sam3cu_vit_create", "sam3cu_vit_destroy",
     "sam3cu_vit_encode", "sam3cu_vit_encode_async", "sam3cu_vit_stream",
-    "sam3cu_vit_launches_per_encode",
+    "sam3cu_vit_launches_per_encode", "sam3cu_vit_profile",
 )
+
+PROFILE_KINDS = ("gemm", "attention", "layernorm", "other")
 
 _lib = None
 
@@ -62,6 +64,7 @@ def lib():
         L.sam3cu_vit_stream.restype = vp
         L.sam3cu_vit_stream.argtypes = [vp]
         L.sam3cu_vit_launches_per_encode.argtypes = [vp, i32]
+        L.sam3cu_vit_profile.argtypes = [vp, vp, i32, vp, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         _lib = L
     return _lib
 
@@ -261,6 +264,15 @@ class VitEncoder:
     def encode_ptr(self, images_ptr: int, n: int, out_ptr: int, on_device: bool) -> None:
         check(lib().sam3cu_vit_encode(self.h, images_ptr, n, out_ptr, 1 if on_device else 0),
               "sam3cu_vit_encode")
+
+    def profile(self, images, out) -> dict:
+        """One direct-launch encode with an event after every launch: device
+        ms and launch count per kernel kind (device tensors in/out)."""
+        ms = (C.c_double * 4)()
+        cnt = (C.c_int * 4)()
+        check(lib().sam3cu_vit_profile(self.h, images.data_ptr(), images.shape[0], out.data_ptr(),
+                                       ms, cnt), "sam3cu_vit_profile")
+        return {k: (ms[i], cnt[i]) for i, k in enumerate(PROFILE_KINDS)}
 
     def encode_async(self, images, out) -> None:
         """Device tensors; enqueue on the encoder's stream, no wait."""
