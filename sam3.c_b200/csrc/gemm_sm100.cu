@@ -23,6 +23,15 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanhf(inner));
 }
 
+// Same formula with the SFU's tanh.approx.f32 (max relative error about
+// 2^-11, below the 2^-9 rounding of the 16-bit outputs it is used for).
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  float inner = 0.7978845608f * (x + 0.044715f * x * x * x);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
+  return 0.5f * x * (1.0f + t);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -32,10 +41,10 @@ __device__ __forceinline__ uint32_t pack_f16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Apply the fused epilogue to 32 consecutive columns [col0, col0+32) of one
-// output row and store them.
-__device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, float (&v)[32], int row,
-                                               int col0, int N) {
+// Bias, activation and RoPE on 32 consecutive columns [col0, col0+32) of
+// one output row, in registers.
+__device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32], int row, int col0,
+                                              int N) {
   const bool full = col0 + 32 <= N;
   if (ep.bias) {
     if (full) {
@@ -55,8 +64,13 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, float (&v)[3
     }
   }
   if (ep.act == 1) {
+    if (ep.out_type == kOutF32) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_fast(v[j]);
+    }
   }
   if (col0 < ep.rope_cols) {
     int p = row % ep.rope_period;
@@ -72,6 +86,12 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, float (&v)[3
       v[2 * i + 1] = x0 * s + x1 * c;
     }
   }
+}
+
+// Residual add and per-thread store of the same 32 columns (kEpiDirect).
+__device__ __forceinline__ void epilogue_store_direct(const EpiParams& ep, float (&v)[32], int row,
+                                                      int col0, int N) {
+  const bool full = col0 + 32 <= N;
   if (ep.residual) {
     int rr = ep.res_row_period > 0 ? row % ep.res_row_period : row;
     const float* r = ep.residual + static_cast<int64_t>(rr) * ep.ldr + col0;
@@ -136,6 +156,33 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, float (&v)[3
   }
 }
 
+// Write one thread's 32 values (row `lane` of a 32x32 chunk) into the
+// warp's staging buffer in the layout of the output tensor map: f32 rows of
+// 128 B with the 128-byte swizzle, or 16-bit rows of 64 B with the 64-byte
+// swizzle (16-byte chunk c of row r lands at c ^ (r & 7), resp.
+// c ^ ((r >> 1) & 3)), which keeps the 16-byte stores bank-conflict free.
+__device__ __forceinline__ void stage_chunk(uint8_t* buf, const float (&v)[32], int lane, int out_type) {
+  if (out_type == kOutF32) {
+    uint8_t* rowp = buf + lane * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(rowp + ((c ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  } else {
+    const bool bf = out_type == kOutBF16;
+    uint8_t* rowp = buf + lane * 64;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint4 w;
+      w.x = bf ? pack_bf16(v[8 * c], v[8 * c + 1]) : pack_f16(v[8 * c], v[8 * c + 1]);
+      w.y = bf ? pack_bf16(v[8 * c + 2], v[8 * c + 3]) : pack_f16(v[8 * c + 2], v[8 * c + 3]);
+      w.z = bf ? pack_bf16(v[8 * c + 4], v[8 * c + 5]) : pack_f16(v[8 * c + 4], v[8 * c + 5]);
+      w.w = bf ? pack_bf16(v[8 * c + 6], v[8 * c + 7]) : pack_f16(v[8 * c + 6], v[8 * c + 7]);
+      *reinterpret_cast<uint4*>(rowp + ((c ^ ((lane >> 1) & 3)) << 4)) = w;
+    }
+  }
+}
+
 // Dequantise one k-tile of Q8 W (int8 [kBN rows x 64] + scales [2][kBN]) to
 // 16-bit values in the 128-byte-swizzled K-major layout the MMA reads.
 // 128 threads; thread t handles 16-byte chunk (t & 7) of rows (t>>3)+16i.
@@ -168,13 +215,14 @@ __device__ __forceinline__ void q8_dequant_tile(const int8_t* q, const float* sc
 template <int kBMode>
 __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                const __grid_constant__ CUtensorMap tmap_s, GemmShape shp, EpiParams ep, uint32_t idesc,
-                int b_is_bf16) {
+                const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_o,
+                GemmShape shp, EpiParams ep, uint32_t idesc, int b_is_bf16, int epi_mode) {
   using Cfg = GemmCfg<kBMode>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* stage_out = smem + S * Cfg::kStageBytes;  // kEpiWarps x 4 KiB
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(stage_out + Cfg::kEpiWarps * Cfg::kStageOutBytes);
   uint64_t* empty_bar = full_bar + S;
   uint64_t* conv_bar = empty_bar + S;   // Q8: dequantised tile ready
   uint64_t* accf_bar = conv_bar + S;    // [2] accumulator committed
@@ -197,7 +245,7 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&accf_bar[a], 1);
-      mbar_init(&acce_bar[a], 4);
+      mbar_init(&acce_bar[a], Cfg::kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -227,8 +275,8 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % m_tiles) * kBM;
-        const int n0 = (tile / m_tiles) * kBN;
+        const int m0 = (tile / n_tiles) * kBM;  // N-fastest: A rows stay in L2
+        const int n0 = (tile % n_tiles) * kBN;
         for (int kt = 0; kt < k_iters; ++kt, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -276,13 +324,18 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
         if (ok) umma_commit(&accf_bar[acc]);
       }
     }
-  } else if (warp < 6) {
-    // ---------------- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1)
+  } else if (warp < 2 + Cfg::kEpiWarps) {
+    // ---------------- epilogue: warp w -> TMEM lane quarter w % 4, column
+    // range [half * kBN / H, (half + 1) * kBN / H) with H = kEpiWarps / 4
     const int quarter = warp & 3;
+    constexpr int kHalves = Cfg::kEpiWarps / 4;
+    constexpr int kChunks = kBN / 32 / kHalves;
+    const int half = (warp - 2) / 4;
+    uint8_t* my_stage = stage_out + (warp - 2) * Cfg::kStageOutBytes;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int m0 = (tile % m_tiles) * kBM;
-      const int n0 = (tile / m_tiles) * kBN;
+      const int m0 = (tile / n_tiles) * kBM;
+      const int n0 = (tile % n_tiles) * kBN;
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       // one lane waits, the warp follows its verdict (tcgen05.ld is .aligned)
@@ -294,25 +347,46 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
       const int row = m0 + quarter * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int cc = 0; cc < kChunks; ++cc) {
+        const int c = half * kChunks + cc;
         const int col0 = n0 + c * 32;
         uint32_t r[32];
         tmem_ld_32x32b_x32(taddr + c * 32, r);
         tmem_ld_wait();
-        if (row < shp.M && col0 < shp.N) {
-          float v[32];
+        if (col0 >= shp.N) continue;  // warp-uniform
+        float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          epilogue_chunk(ep, v, row, col0, shp.N);
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (epi_mode == kEpiDirect) {
+          if (row < shp.M) {
+            epilogue_math(ep, v, row, col0, shp.N);
+            epilogue_store_direct(ep, v, row, col0, shp.N);
+          }
+        } else {
+          // rows >= M and columns >= N are clipped by the TMA store
+          epilogue_math(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N);
+          if (lane == 0) bulk_wait_read<0>();  // previous chunk's smem read done
+          __syncwarp();
+          stage_chunk(my_stage, v, lane, epi_mode == kEpiTmaAdd ? kOutF32 : ep.out_type);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (epi_mode == kEpiTmaAdd)
+              tma_reduce_add_2d(&tmap_o, my_stage, col0, m0 + quarter * 32);
+            else
+              tma_store_2d(&tmap_o, my_stage, col0, m0 + quarter * 32);
+            bulk_commit();
+          }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
     }
+    if (lane == 0) bulk_wait<0>();  // all stores of this warp complete
   } else if (kBMode == kBQ8) {
     // ---------------- Q8 converters (warps 6..9, 128 threads)
-    const int t = threadIdx.x - 192;
+    const int t = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);
     uint32_t it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
@@ -385,6 +459,25 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
   int cap = max_ctas > 0 ? max_ctas : num_sms();
   if (grid > cap) grid = cap;
   const uint32_t idesc = make_idesc(bf ? 1u : 0u, kBM, kBN);
+  // epilogue write path (see EpiMode)
+  CUtensorMap to;
+  memset(&to, 0, sizeof(to));
+  int mode = kEpiDirect;
+  if (!ep.out_row_map && ep.res_row_period == 0) {
+    if (!ep.residual)
+      mode = kEpiTmaStore;
+    else if (ep.residual == ep.out && ep.out_type == kOutF32 && ep.ldr == ep.ldo)
+      mode = kEpiTmaAdd;
+  }
+  if (mode != kEpiDirect) {
+    const bool f32 = ep.out_type == kOutF32;
+    const CUtensorMapDataType odt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                        : (ep.out_type == kOutBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+    if (!make_tmap_2d(&to, ep.out, odt, f32 ? 4 : 2, shp.M, shp.N, ep.ldo, 32, 32,
+                      f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+      mode = kEpiDirect;  // e.g. an output base that is not 16-byte aligned
+  }
   count_launches(1);
   if (q8) {
     if (shp.K % 64 != 0) return kErrShape;
@@ -400,8 +493,8 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       cudaFuncSetAttribute(gemm_kernel<kBQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       attr = true;
     }
-    gemm_kernel<kBQ8><<<grid, GemmCfg<kBQ8>::kThreads, smem, stream>>>(ta, tb, ts, shp, ep, idesc,
-                                                                         bf ? 1 : 0);
+    gemm_kernel<kBQ8><<<grid, GemmCfg<kBQ8>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep, idesc,
+                                                                         bf ? 1 : 0, mode);
   } else {
     if (ldw % 8 != 0) return kErrShape;
     if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, kBN, kBK, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -412,8 +505,8 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       cudaFuncSetAttribute(gemm_kernel<kBTma16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       attr = true;
     }
-    gemm_kernel<kBTma16><<<grid, GemmCfg<kBTma16>::kThreads, smem, stream>>>(ta, tb, ts, shp, ep,
-                                                                              idesc, bf ? 1 : 0);
+    gemm_kernel<kBTma16><<<grid, GemmCfg<kBTma16>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep,
+                                                                              idesc, bf ? 1 : 0, mode);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
 }

@@ -12,7 +12,10 @@
 //   warp 0      TMA producer: A and W tiles -> kStages-deep smem ring
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma into TMEM;
 //               owns TMEM allocation (2 accumulators x BN fp32 columns)
-//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> fused ops -> HBM
+//   warps 2..    epilogue (8 warps; 4 with Q8 W): tcgen05.ld TMEM ->
+//               registers -> fused ops -> HBM.  Warp w reads TMEM lane
+//               quarter w % 4 (the hardware restriction) and, with 8 warps,
+//               one half of the tile's columns.
 // The two TMEM accumulators let the epilogue of tile i overlap the main loop
 // of tile i+1.
 //
@@ -33,6 +36,13 @@ namespace s3 {
 
 enum OutType : int { kOutF32 = 0, kOutF16 = 1, kOutBF16 = 2 };  // = sam3_dtype codes
 enum BMode : int { kBTma16 = 0, kBQ8 = 1 };
+
+// How the epilogue writes a chunk:
+//   kEpiDirect    per-thread vector stores (every fused op, any layout)
+//   kEpiTmaStore  swizzled smem staging + TMA bulk store (no residual / remap)
+//   kEpiTmaAdd    staging + TMA bulk reduce-add into the f32 output, which
+//                 is the residual (in-place x += linear(...))
+enum EpiMode : int { kEpiDirect = 0, kEpiTmaStore = 1, kEpiTmaAdd = 2 };
 
 // Fused epilogue description.  All pointers are device pointers.
 struct EpiParams {
@@ -74,11 +84,15 @@ constexpr int kTmemCols = 2 * kBN;           // 512: double-buffered accumulator
 
 template <int kBMode>
 struct GemmCfg {
-  static constexpr int kThreads = kBMode == kBQ8 ? 320 : 192;  // + 4 converter warps
+  // 16-bit W: 2 + 8 epilogue warps; Q8 W: 2 + 4 epilogue + 4 converter warps
+  static constexpr int kEpiWarps = kBMode == kBQ8 ? 4 : 8;
+  static constexpr int kThreads = 64 + kEpiWarps * 32 + (kBMode == kBQ8 ? 128 : 0);
   static constexpr int kStages = kBMode == kBQ8 ? kStagesQ8 : kStages16;
   static constexpr int kStageBytes =
       kATileBytes + kBTileBytes + (kBMode == kBQ8 ? kQ8TileBytes + kQ8ScaleBytes : 0);
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kStageOutBytes = 32 * 32 * 4;  // per epilogue warp: one 32x32 chunk
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kEpiWarps * kStageOutBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 }  // namespace s3
