@@ -12,7 +12,8 @@
 // 24x24 window (seq 576) when the token order is window-major, or a whole
 // image (seq 5184) for global blocks.
 //
-// This version computes on the warp-level bf16/fp16 MMA (m16n8k16, fp32
+// The production path is the tcgen05 kernel in attention_sm100.cu; this
+// version computes on the warp-level bf16/fp16 MMA (m16n8k16, fp32
 // accumulate): 4 warps x 16 query rows per CTA, 64-key tiles double-buffered
 // through cp.async with an XOR-swizzled shared-memory layout.
 #include <cuda_bf16.h>
@@ -20,6 +21,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 
 #include "attention.cuh"
 #include "sam3cu_internal.h"
@@ -246,8 +249,9 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const uint16_t* __restric
 
 }  // namespace
 
-int launch_attention(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,
-                     int n_groups, int seq, int heads, int head_dim, cudaStream_t st) {
+// Warp-MMA version (kept as the comparison baseline; SAM3CU_ATTN=mma selects it).
+int launch_attention_mma(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo,
+                         int dtype, int n_groups, int seq, int heads, int head_dim, cudaStream_t st) {
   if (head_dim != kHD) return kErrShape;
   if (ldq % 8 || ldo % 8) return kErrShape;
   if (n_groups <= 0 || seq <= 0 || heads <= 0) return kOk;
@@ -266,6 +270,16 @@ int launch_attention(const void* q, const void* k, const void* v, int64_t ldq, v
   else
     return kErrDtype;
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int launch_attention(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,
+                     int n_groups, int seq, int heads, int head_dim, cudaStream_t st) {
+  static const int use_mma = [] {
+    const char* e = getenv("SAM3CU_ATTN");
+    return e && strcmp(e, "mma") == 0 ? 1 : 0;
+  }();
+  if (use_mma) return launch_attention_mma(q, k, v, ldq, o, ldo, dtype, n_groups, seq, heads, head_dim, st);
+  return launch_attention_tc(q, k, v, ldq, o, ldo, dtype, n_groups, seq, heads, head_dim, st);
 }
 
 }  // namespace s3

@@ -1,0 +1,360 @@
+// attention_sm100.cu - tcgen05 flash attention, head_dim 64, bf16 / fp16.
+//
+//   O = softmax(Q K^T / 8) V   per (group of `seq` rows, head)
+//
+// The online-softmax algorithm of cpu_sdpa.c:49-159 (running max, running
+// sum, rescale of the partial output), evaluated on 128x128 tiles with the
+// fifth-generation tensor cores:
+//
+//   S_j   = Q K_j^T          tcgen05.mma 128x128x64 -> TMEM (128 columns)
+//   P_j   = exp2(S_j*c - m)  softmax warps: one thread per query row
+//   O    += P_j V_j          tcgen05.mma 128x64x128, A = P from shared memory,
+//                            B = V as stored (MN-major), accumulator in TMEM
+//
+// CTA = 6 warps, two CTAs per SM (112 KiB smem, 256 TMEM columns and
+// 192 threads x 168 registers each):
+//   warp 0     TMA (Q tile once, K_j / V_j through a 2-stage ring);
+//              allocates TMEM
+//   warp 1     MMA issue (one thread)
+//   warps 2-5  softmax and the output epilogue; warp w owns TMEM lane
+//              quarter w % 4, i.e. query rows 32*(w%4) .. +31
+// A softmax thread copies its S row to registers and releases S at once,
+// so S_{j+1} = Q K_{j+1}^T runs on the tensor cores during the softmax of
+// tile j; the two CTAs of an SM interleave on the exponential units.
+// The output is rescaled lazily: only when a row maximum grows by more than
+// 2^8 is O read back from TMEM, multiplied and stored (tcgen05.ld / st);
+// otherwise exponentials are taken against the stale maximum (values up to
+// 256 are exact enough in fp32 and bf16).  Every mbarrier wait is bounded.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "sam3cu_internal.h"
+#include "sm100_ptx.cuh"
+#include "tma_host.cuh"
+
+namespace s3 {
+
+S3_DEV_ERROR_ACCESSOR(dev_error_attn_tc)
+
+namespace {
+
+constexpr int kQ = 128;                  // query rows per CTA
+constexpr int kKV = 128;                 // keys per tile
+constexpr int kD = 64;                   // head dim
+constexpr int kTile = kQ * kD * 2;       // 16 KiB (Q, K or V tile)
+constexpr int kPBytes = kQ * kKV * 2;    // 32 KiB
+constexpr int kSmem = kTile * 5 + kPBytes;  // Q | K0 V0 | K1 V1 | P = 112 KiB
+constexpr int kTmemCols = 256;           // S: 0..127, O: 128..191
+constexpr int kThreads = 192;
+constexpr float kRescaleLog2 = 8.0f;     // lazy rescale threshold (x256)
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, bool bf) {
+  if (bf) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Bounded wait by lane 0, verdict broadcast to the warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsigned err, volatile int* abort_flag,
+                                          int lane) {
+  int ok = 0;
+  if (lane == 0) ok = mbar_wait(bar, parity, err, abort_flag) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// Two CTAs of 6 warps per SM put 3 warps on each SM sub-partition, whose
+// register file holds 16K entries: 168 registers per thread at most.
+template <bool kBf16>
+__global__ void __launch_bounds__(192, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, uint16_t* __restrict__ o, int64_t ldo, int seq,
+                   int q_tiles, float scale_log2) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint64_t bars[12];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag_s;
+  uint64_t* q_full = &bars[0];
+  uint64_t* kv_full = &bars[1];   // [2]
+  uint64_t* kv_empty = &bars[3];  // [2]
+  uint64_t* s_full = &bars[5];
+  uint64_t* s_empty = &bars[6];
+  uint64_t* p_full = &bars[7];
+  uint64_t* p_empty = &bars[8];
+  uint64_t* o_full = &bars[9];
+  volatile int* abort_flag = &abort_flag_s;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = blockIdx.x / q_tiles, qt = blockIdx.x % q_tiles, head = blockIdx.y;
+  const int row0 = group * seq;  // first row of the group in the [rows, ld] matrices
+  const int n_kv = (seq + kKV - 1) / kKV;
+
+  if ((smem_u32(smem) & 1023u) != 0) {  // the swizzled layouts need 1 KiB alignment
+    if (threadIdx.x == 0) atomicCAS(&g_dev_error, 0u, static_cast<unsigned>(kErrTmemAlloc));
+    return;
+  }
+  uint8_t* sQ = smem;
+  uint8_t* sK[2] = {smem + kTile, smem + 3 * kTile};
+  uint8_t* sV[2] = {smem + 2 * kTile, smem + 4 * kTile};
+  uint8_t* sP = smem + 5 * kTile;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 4);
+    mbar_init(p_full, 4);
+    mbar_init(p_empty, 1);
+    mbar_init(o_full, 1);
+    abort_flag_s = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  if (warp == 0) {
+    // TMA producer (one thread)
+    if (lane == 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      mbar_arrive_expect_tx(q_full, kTile);
+      tma_load_2d(sQ, &tq, q_full, head * kD, row0 + qt * kQ);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, kErrStageFree, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+        tma_load_2d(sK[st], &tk, &kv_full[st], head * kD, row0 + j * kKV);
+        tma_load_2d(sV[st], &tv, &kv_full[st], head * kD, row0 + j * kKV);
+      }
+    }
+  } else if (warp == 1) {
+    // MMA issuer (one thread)
+    if (lane == 0) {
+      const uint32_t fmt = kBf16 ? 1u : 0u;
+      const uint32_t idesc_pv = make_idesc(fmt, kQ, kD, 1u);
+      bool ok = mbar_wait(q_full, 0, kErrTmaWait, abort_flag);
+      const uint64_t qdesc = make_sdesc_sw128(smem_u32(sQ));
+      auto keys_in = [&](int j) {  // keys of tile j, rounded up to a multiple of 16
+        const int left = seq - j * kKV;
+        return left >= kKV ? kKV : ((left + 15) & ~15);
+      };
+      // S_j = Q K_j^T into TMEM once K_j landed and the softmax read S_{j-1}
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, kErrTmaWait, abort_flag)) return false;
+        if (!mbar_wait(s_empty, (j & 1) ^ 1, kErrAccFree, abort_flag)) return false;
+        tc_fence_after();
+        const uint64_t kdesc = make_sdesc_sw128(smem_u32(sK[st]));
+        const uint32_t idesc_s = make_idesc(fmt, kQ, keys_in(j));
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) umma_ss<0>(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
+        umma_commit(s_full);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        // the next S = Q K^T runs while the softmax of tile j is computed
+        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        if (!mbar_wait(p_full, j & 1, kErrAccFull, abort_flag)) break;
+        tc_fence_after();
+        const int st = j & 1, n = keys_in(j);
+        const uint32_t vbase = smem_u32(sV[st]), pbase = smem_u32(sP);
+        for (int kk = 0; kk < n / 16; ++kk) {
+          const uint64_t pdesc = make_sdesc_sw128(pbase + (kk >> 2) * 16384 + (kk & 3) * 32);
+          const uint64_t vdesc = make_sdesc_sw128_mn(vbase + kk * 2048);
+          umma_ss<0>(tO, pdesc, vdesc, idesc_pv, (j | kk) ? 1u : 0u);
+        }
+        umma_commit(p_empty);
+        umma_commit(&kv_empty[st]);
+      }
+      umma_commit(o_full);
+    }
+  } else {
+    // ------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row within the tile
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!warp_wait(s_full, j & 1, kErrAccFull, abort_flag, lane)) { ok = false; break; }
+      tc_fence_after();
+      // S row -> registers, then S is free for the next Q K^T
+      const int kb = j * kKV;
+      float sv[kKV];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(tS + lane_off + c * 32, u);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[i]);
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_empty);
+      if (kb + kKV > seq) {  // ragged last tile: keys >= seq do not exist
+#pragma unroll
+        for (int c = 0; c < kKV; ++c)
+          if (kb + c >= seq) sv[c] = -INFINITY;
+      }
+      // row max with 8 independent chains (a single chain is 128 dependent ops)
+      float m8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m8[i] = sv[i];
+#pragma unroll
+      for (int c = 8; c < kKV; ++c) m8[c & 7] = fmaxf(m8[c & 7], sv[c]);
+      const float mt = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      const bool need = (mt - m_used) * scale_log2 > kRescaleLog2;
+      // P buffer and O are free once the previous P.V finished
+      if (j > 0 && !warp_wait(p_empty, (j - 1) & 1, kErrAccFree, abort_flag, lane)) { ok = false; break; }
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_new = fmaxf(m_used, mt);
+        const float corr = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * scale_log2);
+        l *= corr;
+        m_used = m_new;
+        if (j > 0) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t u[32];
+            tmem_ld_32x32b_x32(tO + lane_off + c * 32, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
+            tmem_st_32x32b_x32(tO + lane_off + c * 32, u);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P = exp2(S*c - m) -> 16-bit, 128-byte-swizzled K-major rows
+      const float mb = m_used * scale_log2;
+      uint8_t* prow = sP + r * 128;
+      float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c8 = 0; c8 < kKV / 8; ++c8) {  // 16-byte chunks of 8 keys
+        float p[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          p[i] = ex2(fmaf(sv[c8 * 8 + i], scale_log2, -mb));
+          l8[i] += p[i];
+        }
+        uint4 w;
+        w.x = pack2(p[0], p[1], kBf16);
+        w.y = pack2(p[2], p[3], kBf16);
+        w.z = pack2(p[4], p[5], kBf16);
+        w.w = pack2(p[6], p[7], kBf16);
+        const int blk = c8 >> 3, cc = c8 & 7;
+        *reinterpret_cast<uint4*>(prow + blk * 16384 + ((cc ^ (r & 7)) << 4)) = w;
+      }
+      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && warp_wait(o_full, 0, kErrAccFull, abort_flag, lane)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int qrow = qt * kQ + r;
+      uint16_t* orow = o + static_cast<int64_t>(row0 + qrow) * ldo + head * kD;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(tO + lane_off + c * 32, u);
+        tmem_ld_wait();
+        if (qrow < seq) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 w;
+            w.x = pack2(__uint_as_float(u[q4 * 8 + 0]) * inv, __uint_as_float(u[q4 * 8 + 1]) * inv, kBf16);
+            w.y = pack2(__uint_as_float(u[q4 * 8 + 2]) * inv, __uint_as_float(u[q4 * 8 + 3]) * inv, kBf16);
+            w.z = pack2(__uint_as_float(u[q4 * 8 + 4]) * inv, __uint_as_float(u[q4 * 8 + 5]) * inv, kBf16);
+            w.w = pack2(__uint_as_float(u[q4 * 8 + 6]) * inv, __uint_as_float(u[q4 * 8 + 7]) * inv, kBf16);
+            *reinterpret_cast<uint4*>(orow + c * 32 + q4 * 8) = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+bool make_head_map(CUtensorMap* m, const void* base, int dtype, int64_t rows, int heads, int64_t ld) {
+  const CUtensorMapDataType dt = dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return make_tmap_2d(m, base, dt, 2, rows, static_cast<uint64_t>(heads) * kD, ld, kQ, kD,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <bool kBf16>
+void set_smem_attr() {
+  static bool done = false;
+  if (!done) {
+    cudaFuncSetAttribute(attn_tc_kernel<kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    // full shared-memory carveout, so two 114 KiB CTAs fit on one SM
+    cudaFuncSetAttribute(attn_tc_kernel<kBf16>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    done = true;
+  }
+}
+
+}  // namespace
+
+int launch_attention_tc(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,
+                        int n_groups, int seq, int heads, int head_dim, cudaStream_t st) {
+  if (head_dim != kD) return kErrShape;
+  if (dtype != kBF16 && dtype != kF16) return kErrDtype;
+  if (ldq % 8 || ldo % 8 || (reinterpret_cast<uintptr_t>(o) & 15)) return kErrShape;
+  if (n_groups <= 0 || seq <= 0 || heads <= 0) return kOk;
+  const int64_t rows = static_cast<int64_t>(n_groups) * seq;
+  if (rows > 0x7fffffffLL) return kErrShape;
+  CUtensorMap mq, mk, mv;
+  if (!make_head_map(&mq, q, dtype, rows, heads, ldq) || !make_head_map(&mk, k, dtype, rows, heads, ldq) ||
+      !make_head_map(&mv, v, dtype, rows, heads, ldq))
+    return kErrTma;
+  const int q_tiles = (seq + kQ - 1) / kQ;
+  dim3 grid(n_groups * q_tiles, heads);
+  const float scale_log2 = (1.0f / sqrtf(static_cast<float>(head_dim))) * 1.4426950408889634f;
+  count_launches(1);
+  if (dtype == kBF16) {
+    set_smem_attr<true>();
+    attn_tc_kernel<true><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, static_cast<uint16_t*>(o), ldo, seq, q_tiles,
+                                                        scale_log2);
+  } else {
+    set_smem_attr<false>();
+    attn_tc_kernel<false><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, static_cast<uint16_t*>(o), ldo, seq, q_tiles,
+                                                         scale_log2);
+  }
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+}  // namespace s3

@@ -67,8 +67,8 @@ const char* sam3cu_strerror(int s) {
 
 unsigned int sam3cu_last_device_error(void) {
   cudaDeviceSynchronize();
-  unsigned int a = dev_error_gemm(), b = dev_error_attn(), c = dev_error_misc();
-  return a ? a : (b ? b : c);
+  unsigned int a = dev_error_gemm(), b = dev_error_attn(), c = dev_error_misc(), d = dev_error_attn_tc();
+  return a ? a : (b ? b : (c ? c : d));
 }
 
 uint64_t sam3cu_launch_count(int reset) {

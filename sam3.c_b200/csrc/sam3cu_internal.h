@@ -30,6 +30,9 @@ int launch_q8_quantize(const float* src, void* blocks, int64_t n, cudaStream_t s
 unsigned int dev_error_gemm();
 unsigned int dev_error_attn();
 unsigned int dev_error_misc();
+int launch_attention_tc(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,
+                        int n_groups, int seq, int heads, int head_dim, cudaStream_t st);
+unsigned int dev_error_attn_tc();
 int launch_attention(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,
                      int n_groups, int seq, int heads, int head_dim, cudaStream_t st);
 int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8, const float* q8_scales,

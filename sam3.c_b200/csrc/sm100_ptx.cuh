@@ -75,10 +75,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -211,6 +211,22 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -230,11 +246,25 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16 / kind::tf32 with fp32 accumulate,
-// both operands K-major.  fmt: 0 = f16, 1 = bf16, 2 = tf32.
-__host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, int M, int N) {
+// Shared-memory descriptor for an MN-major operand whose MN extent is one
+// 128-byte swizzle row (64 16-bit elements): K rows of 128 B, 8-row groups
+// 1024 B apart (SBO); the next 64-wide MN block (LBO) is never reached.
+__device__ __forceinline__ uint64_t make_sdesc_sw128_mn(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(16384u >> 4) << 16;  // LBO (unused: one MN block)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;   // SBO: next 8 K-rows
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16 / kind::tf32 with fp32 accumulate.
+// fmt: 0 = f16, 1 = bf16, 2 = tf32.  b_mn_major selects an MN-major B.
+__host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, int M, int N, uint32_t b_mn_major = 0) {
   return (1u << 4)                                  // D format f32
          | (fmt << 7) | (fmt << 10)                 // A, B format
+         | (b_mn_major << 16)                       // B major-ness
          | (static_cast<uint32_t>(N >> 3) << 17)   // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);  // M / 16
 }
