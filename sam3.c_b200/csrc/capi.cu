@@ -17,7 +17,8 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 int linear_common(const void* x, int x_dtype, const void* w, const int8_t* q, const float* sc, const float* bias,
                   const float* residual, void* y, int y_dtype, int M, int K, int N, int act, void* stream) {
   if (!x || !y || (!w && !q) || M < 0 || K <= 0 || N <= 0) return SAM3CU_EINVAL;
-  if (x_dtype != SAM3CU_BF16 && x_dtype != SAM3CU_F16) return SAM3CU_EDTYPE;
+  if (x_dtype != SAM3CU_BF16 && x_dtype != SAM3CU_F16 && x_dtype != SAM3CU_F32) return SAM3CU_EDTYPE;
+  if (x_dtype == SAM3CU_F32 && q) return SAM3CU_EDTYPE;  // Q8 weights take 16-bit activations
   if (y_dtype != SAM3CU_F32 && y_dtype != SAM3CU_BF16 && y_dtype != SAM3CU_F16) return SAM3CU_EDTYPE;
   if (act != SAM3CU_ACT_NONE && act != SAM3CU_ACT_GELU_TANH) return SAM3CU_EINVAL;
   if (residual == y && y_dtype != SAM3CU_F32) return SAM3CU_EINVAL;

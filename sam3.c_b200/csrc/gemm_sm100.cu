@@ -183,6 +183,29 @@ __device__ __forceinline__ void stage_chunk(uint8_t* buf, const float (&v)[32], 
   }
 }
 
+// Split the F32 A and W tiles of one stage (16 KiB + 32 KiB, contiguous
+// at `hi`) in place into hi = x & ~0x1fff (a TF32 value) and lo = x - hi,
+// written at the same offset of the lo region (so the swizzled layout is
+// kept).  128 threads, 16-byte vectors.
+__device__ __forceinline__ void split_tf32_tile(uint8_t* hi, uint8_t* lo, int t) {
+  constexpr int kVec = (kATileBytes + kBTileBytes) / 16;
+#pragma unroll 4
+  for (int i = t; i < kVec; i += 128) {
+    float4 x = reinterpret_cast<float4*>(hi)[i];
+    float4 h, l;
+    h.x = __uint_as_float(__float_as_uint(x.x) & 0xffffe000u);
+    h.y = __uint_as_float(__float_as_uint(x.y) & 0xffffe000u);
+    h.z = __uint_as_float(__float_as_uint(x.z) & 0xffffe000u);
+    h.w = __uint_as_float(__float_as_uint(x.w) & 0xffffe000u);
+    l.x = x.x - h.x;
+    l.y = x.y - h.y;
+    l.z = x.z - h.z;
+    l.w = x.w - h.w;
+    reinterpret_cast<float4*>(hi)[i] = h;
+    reinterpret_cast<float4*>(lo)[i] = l;
+  }
+}
+
 // Dequantise one k-tile of Q8 W (int8 [kBN rows x 64] + scales [2][kBN]) to
 // 16-bit values in the 128-byte-swizzled K-major layout the MMA reads.
 // 128 threads; thread t handles 16-byte chunk (t & 7) of rows (t>>3)+16i.
@@ -235,7 +258,8 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
   const int m_tiles = (shp.M + kBM - 1) / kBM;
   const int n_tiles = (shp.N + kBN - 1) / kBN;
   const int num_tiles = m_tiles * n_tiles;
-  const int k_iters = (shp.K + kBK - 1) / kBK;
+  constexpr int BKe = Cfg::kBKe;
+  const int k_iters = (shp.K + BKe - 1) / BKe;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -288,8 +312,8 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
             tma_load_2d(stage_sc(s), &tmap_s, &full_bar[s], n0, kt * (kBK / 32));
           } else {
             mbar_arrive_expect_tx(&full_bar[s], kATileBytes + kBTileBytes);
-            tma_load_2d(stage_a(s), &tmap_a, &full_bar[s], kt * kBK, m0);
-            tma_load_2d(stage_b(s), &tmap_b, &full_bar[s], kt * kBK, n0);
+            tma_load_2d(stage_a(s), &tmap_a, &full_bar[s], kt * BKe, m0);
+            tma_load_2d(stage_b(s), &tmap_b, &full_bar[s], kt * BKe, n0);
           }
         }
       }
@@ -309,15 +333,27 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
         for (int kt = 0; kt < k_iters; ++kt, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
-          uint64_t* ready = kBMode == kBQ8 ? &conv_bar[s] : &full_bar[s];
+          uint64_t* ready = Cfg::kConv ? &conv_bar[s] : &full_bar[s];
           if (!mbar_wait(ready, ph, kErrTmaWait, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = make_sdesc_sw128(smem_u32(stage_a(s)));
           const uint64_t bdesc = make_sdesc_sw128(smem_u32(stage_b(s)));
+          if constexpr (kBMode == kBF32) {
+            // 3xTF32: lo terms first, hi.hi last; 8 TF32 = 32 bytes per MMA
+            const uint64_t aldesc = make_sdesc_sw128(smem_u32(stage_q(s)));
+            const uint64_t bldesc = make_sdesc_sw128(smem_u32(stage_q(s) + kATileBytes));
 #pragma unroll
-          for (int k = 0; k < kBK / kUmmaK; ++k) {
-            // advance 16 elements = 32 bytes = 2 (16-byte units) along K
-            umma_ss<0>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+            for (int k = 0; k < BKe / Cfg::kUmmaKe; ++k) {
+              umma_ss<1>(d_tmem, aldesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+              umma_ss<1>(d_tmem, adesc + 2 * k, bldesc + 2 * k, idesc, 1u);
+              umma_ss<1>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, 1u);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < BKe / Cfg::kUmmaKe; ++k) {
+              // advance 16 elements = 32 bytes = 2 (16-byte units) along K
+              umma_ss<0>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+            }
           }
           umma_commit(&empty_bar[s]);  // frees the smem stage when these MMAs finish
         }
@@ -384,8 +420,8 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
     }
     if (lane == 0) bulk_wait<0>();  // all stores of this warp complete
-  } else if (kBMode == kBQ8) {
-    // ---------------- Q8 converters (warps 6..9, 128 threads)
+  } else if (Cfg::kConv) {
+    // ---------------- converters (4 warps): Q8 dequant or TF32 hi/lo split
     const int t = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);
     uint32_t it = 0;
     bool ok = true;
@@ -394,12 +430,16 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
         const int s = it % S;
         const uint32_t ph = (it / S) & 1;
         if (!mbar_wait(&full_bar[s], ph, kErrTmaWait, abort_flag)) { ok = false; break; }
-        const int8_t* q = reinterpret_cast<const int8_t*>(stage_q(s));
-        const float* sc = reinterpret_cast<const float*>(stage_sc(s));
-        if (b_is_bf16)
-          q8_dequant_tile<true>(q, sc, stage_b(s), t);
-        else
-          q8_dequant_tile<false>(q, sc, stage_b(s), t);
+        if constexpr (kBMode == kBF32) {
+          split_tf32_tile(stage_a(s), stage_q(s), t);
+        } else {
+          const int8_t* q = reinterpret_cast<const int8_t*>(stage_q(s));
+          const float* sc = reinterpret_cast<const float*>(stage_sc(s));
+          if (b_is_bf16)
+            q8_dequant_tile<true>(q, sc, stage_b(s), t);
+          else
+            q8_dequant_tile<false>(q, sc, stage_b(s), t);
+        }
         fence_proxy_async_smem();  // make generic-proxy writes visible to tcgen05
         mbar_arrive(&conv_bar[s]);
       }
@@ -436,10 +476,12 @@ int num_sms() {
 // W: 16-bit [N, ldw] or (q8 != null) int8 [N, K] + scales [K/32, N].
 int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8, const float* q8_scales,
                 int ab_dtype, GemmShape shp, const EpiParams& ep, cudaStream_t stream, int max_ctas) {
-  if (ab_dtype != kBF16 && ab_dtype != kF16) return kErrDtype;
-  const bool bf = ab_dtype == kBF16;
+  if (ab_dtype != kBF16 && ab_dtype != kF16 && ab_dtype != kF32) return kErrDtype;
+  const bool bf = ab_dtype == kBF16, f32in = ab_dtype == kF32;
+  if (f32in && q8) return kErrDtype;
   if (shp.M <= 0 || shp.N <= 0 || shp.K <= 0) return 0;
-  if (shp.K % 8 != 0 || lda % 8 != 0) return kErrShape;
+  // TMA: 16-byte row pitch
+  if (f32in ? (shp.K % 4 != 0 || lda % 4 != 0) : (shp.K % 8 != 0 || lda % 8 != 0)) return kErrShape;
   if (ep.rope_cols > 0 && (ep.rope_period <= 0 || !ep.rope_cos || !ep.rope_sin)) return kErrShape;
   if (ep.out_row_map && ep.out_row_period <= 0) return kErrShape;
   // vector epilogue stores/loads: 16-byte aligned rows
@@ -448,17 +490,19 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
   if ((reinterpret_cast<uintptr_t>(ep.out) | reinterpret_cast<uintptr_t>(ep.residual) |
        reinterpret_cast<uintptr_t>(ep.bias)) & 15u)
     return kErrShape;
-  const CUtensorMapDataType dt =
-      bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt = f32in ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : (bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+  const int es = f32in ? 4 : 2;
+  const int bke = f32in ? GemmCfg<kBF32>::kBKe : kBK;  // 128-byte operand rows either way
   CUtensorMap ta, tb, ts;
   memset(&ts, 0, sizeof(ts));
-  if (!make_tmap_2d(&ta, A, dt, 2, shp.M, shp.K, lda, kBM, kBK, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!make_tmap_2d(&ta, A, dt, es, shp.M, shp.K, lda, kBM, bke, CU_TENSOR_MAP_SWIZZLE_128B))
     return kErrTma;
   const int m_tiles = (shp.M + kBM - 1) / kBM, n_tiles = (shp.N + kBN - 1) / kBN;
   int grid = m_tiles * n_tiles;
   int cap = max_ctas > 0 ? max_ctas : num_sms();
   if (grid > cap) grid = cap;
-  const uint32_t idesc = make_idesc(bf ? 1u : 0u, kBM, kBN);
+  const uint32_t idesc = make_idesc(f32in ? 2u : (bf ? 1u : 0u), kBM, kBN);
   // epilogue write path (see EpiMode)
   CUtensorMap to;
   memset(&to, 0, sizeof(to));
@@ -495,6 +539,18 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
     }
     gemm_kernel<kBQ8><<<grid, GemmCfg<kBQ8>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep, idesc,
                                                                          bf ? 1 : 0, mode);
+  } else if (f32in) {
+    if (ldw % 4 != 0) return kErrShape;
+    if (!make_tmap_2d(&tb, W, dt, 4, shp.N, shp.K, ldw, kBN, bke, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kErrTma;
+    constexpr int smem = GemmCfg<kBF32>::kSmemBytes;
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(gemm_kernel<kBF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      attr = true;
+    }
+    gemm_kernel<kBF32><<<grid, GemmCfg<kBF32>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep, idesc, 0,
+                                                                           mode);
   } else {
     if (ldw % 8 != 0) return kErrShape;
     if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, kBN, kBK, CU_TENSOR_MAP_SWIZZLE_128B))

@@ -26,6 +26,12 @@
 //            TMA brings the int8 tile and scales, four converter warps
 //            dequantise (q * scale -> bf16) straight into the swizzled
 //            operand layout in shared memory.
+//   kBF32    A and W are F32: "3xTF32".  TMA brings 32-wide F32 tiles
+//            (128-byte rows, same swizzle), four converter warps split
+//            every element x in place into hi = x with the low 13 mantissa
+//            bits cleared (exact in TF32) and lo = x - hi (exact in F32),
+//            and the MMA warp issues hi.hi + hi.lo + lo.hi with
+//            kind::tf32, an F32 product to about 2^-22 relative.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -35,7 +41,7 @@
 namespace s3 {
 
 enum OutType : int { kOutF32 = 0, kOutF16 = 1, kOutBF16 = 2 };  // = sam3_dtype codes
-enum BMode : int { kBTma16 = 0, kBQ8 = 1 };
+enum BMode : int { kBTma16 = 0, kBQ8 = 1, kBF32 = 2 };
 
 // How the epilogue writes a chunk:
 //   kEpiDirect    per-thread vector stores (every fused op, any layout)
@@ -85,11 +91,17 @@ constexpr int kTmemCols = 2 * kBN;           // 512: double-buffered accumulator
 template <int kBMode>
 struct GemmCfg {
   // 16-bit W: 2 + 8 epilogue warps; Q8 W: 2 + 4 epilogue + 4 converter warps
-  static constexpr int kEpiWarps = kBMode == kBQ8 ? 4 : 8;
-  static constexpr int kThreads = 64 + kEpiWarps * 32 + (kBMode == kBQ8 ? 128 : 0);
-  static constexpr int kStages = kBMode == kBQ8 ? kStagesQ8 : kStages16;
+  static constexpr bool kConv = kBMode != kBTma16;  // converter warps present
+  static constexpr int kEpiWarps = kConv ? 4 : 8;
+  static constexpr int kThreads = 64 + kEpiWarps * 32 + (kConv ? 128 : 0);
+  static constexpr int kStages = kBMode == kBQ8 ? kStagesQ8 : (kBMode == kBF32 ? 2 : kStages16);
+  // K elements per stage (always 128-byte operand rows) and per MMA
+  static constexpr int kBKe = kBMode == kBF32 ? 32 : 64;
+  static constexpr int kUmmaKe = kBMode == kBF32 ? 8 : 16;
+  // F32 stage: A_hi | W_hi | A_lo | W_lo (same byte sizes as the 16-bit tiles)
   static constexpr int kStageBytes =
-      kATileBytes + kBTileBytes + (kBMode == kBQ8 ? kQ8TileBytes + kQ8ScaleBytes : 0);
+      kATileBytes + kBTileBytes +
+      (kBMode == kBQ8 ? kQ8TileBytes + kQ8ScaleBytes : (kBMode == kBF32 ? kATileBytes + kBTileBytes : 0));
   static constexpr int kStageOutBytes = 32 * 32 * 4;  // per epilogue warp: one 32x32 chunk
   static constexpr int kSmemBytes =
       kStages * kStageBytes + kEpiWarps * kStageOutBytes + 1024 /*align*/ + 256 /*barriers*/;

@@ -101,3 +101,24 @@ def test_linear_q8(cuda, M, K, N):
     # bf16-rounded dequantised weight tightly
     assert rel_err(to_np(y), O.linear(x, wdq, b)) < 1e-2
     assert rel_err(to_np(y), O.linear(x, O.round_bf16(wdq), b)) < 1e-4 * max(1.0, K / 256)
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 32, 256), (257, 100, 320), (5184, 1024, 1024),
+                                   (5184, 4736, 1024)])
+def test_linear_f32_3xtf32(cuda, M, K, N):
+    """F32 x F32 (3xTF32 on the tensor cores) against the F32 oracle at the
+    north-star F32 bound 1e-4 (normwise), with bias and in-place residual."""
+    import torch
+    import sam3cu
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w = rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(K))
+    b = rng.standard_normal(N, dtype=np.float32)
+    y = sam3cu.linear(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(),
+                      bias=torch.from_numpy(b).cuda(), out_dtype=torch.float32)
+    assert rel_err(to_np(y), O.linear(x, w, b)) < 1e-4
+    res = rng.standard_normal((M, N), dtype=np.float32)
+    tres = torch.from_numpy(res).cuda()
+    sam3cu.linear(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), residual=tres, out=tres,
+                  act=sam3cu.ACT_GELU_TANH)
+    assert rel_err(to_np(tres), O.linear(x, w, None, res=res, act=1)) < 1e-4
