@@ -92,8 +92,9 @@ SAM3CU_API uint64_t sam3cu_launch_count(int reset);
 /*
  * y[M,N] = act(x[M,K] . w[N,K]^T + bias[N]) + residual[M,N]
  *
- * x, w: device, same 16-bit type (x_dtype = SAM3CU_BF16 or SAM3CU_F16),
- * row-major, K % 8 == 0.  bias/residual: device F32 or NULL; residual may
+ * x, w: device, same type: SAM3CU_BF16 or SAM3CU_F16 (K % 8 == 0), or
+ * SAM3CU_F32 (K % 4 == 0; computed as 3xTF32 on the tensor cores, about
+ * 2^-22 relative per product), row-major.  bias/residual: device F32 or NULL; residual may
  * equal y when y is F32.  y_dtype: SAM3CU_F32, _BF16 or _F16.  act: enum
  * sam3cu_act.  FP32 accumulation on the tensor cores.
  */
@@ -140,6 +141,62 @@ SAM3CU_API int sam3cu_layernorm(const void *x, int x_dtype, const float *gamma,
 SAM3CU_API int sam3cu_sdpa(const void *q, const void *k, const void *v, int64_t ld_qkv,
 		void *o, int64_t ld_o, int dtype, int n_groups, int seq,
 		int heads, int head_dim, void *stream);
+
+/* ------------------------------------------- per-node ops (backend vtable)
+ * Device helpers and the remaining encoder-graph ops, used by the
+ * sam3_backend_ops lowering in cuda_backend.c.  dtype arguments take
+ * SAM3CU_F32 / _F16 / _BF16; pointers are device pointers unless named
+ * host.  Each replaces the CPU kernel named beside it. */
+
+SAM3CU_API int sam3cu_dev_alloc(void **p, size_t bytes);
+SAM3CU_API int sam3cu_dev_free(void *p);
+SAM3CU_API int sam3cu_stream_create(void **stream);
+SAM3CU_API int sam3cu_stream_destroy(void *stream);
+SAM3CU_API int sam3cu_stream_sync(void *stream);
+SAM3CU_API int sam3cu_memcpy_h2d(void *dst, const void *host_src, size_t n, void *stream);
+SAM3CU_API int sam3cu_memcpy_d2h(void *host_dst, const void *src, size_t n, void *stream);
+SAM3CU_API int sam3cu_memcpy_d2d(void *dst, const void *src, size_t n, void *stream);
+
+/* TRANSPOSE / PERMUTE of up to 4 dims (cpu_transpose.c:312-387):
+ * out dims[i] = dims[perm[i]]; elem_size 1, 2 or 4 bytes. */
+SAM3CU_API int sam3cu_permute(const void *src, void *dst, int elem_size, int n_dims,
+			      const int *dims, const int *perm, void *stream);
+
+/* SLICE [start, end) along axis (cpu_slice.c). */
+SAM3CU_API int sam3cu_slice(const void *src, void *dst, int elem_size, int n_dims,
+			    const int *dims, int axis, int start, int end, void *stream);
+
+/* ADD out[i] = a[i] + b[i % nb] for nb = n, last dim or 1
+ * (cpu_elementwise.c:28-62, :472-495). */
+SAM3CU_API int sam3cu_add(const void *a, const void *b, void *out, int dtype, int64_t n,
+			  int64_t nb, void *stream);
+
+/* GELU, tanh form (cpu_gelu.c:23-36). */
+SAM3CU_API int sam3cu_gelu(const void *x, void *y, int dtype, int64_t n, void *stream);
+
+/* ROPE on [batch, seq, heads, hd] with F32 [seq, hd/2] cos/sin tables
+ * (cpu_rope.c:35-110). */
+SAM3CU_API int sam3cu_rope(const void *x, const float *cos_t, const float *sin_t, void *y,
+			   int dtype, int batch, int seq, int heads, int hd, void *stream);
+
+/* CAST between F32, F16 and BF16 (cpu_cast.c), round to nearest even. */
+SAM3CU_API int sam3cu_cast(const void *x, int x_dtype, void *y, int y_dtype, int64_t n,
+			   void *stream);
+
+/* F32 SDPA on contiguous [bh, s, hd] (hd 32 or 64) with an optional
+ * additive [sq, sk] mask (cpu_sdpa.c:216-288, same online softmax). */
+SAM3CU_API int sam3cu_sdpa_f32(const float *q, const float *k, const float *v,
+			       const float *mask, float *o, int bh, int sq, int sk, int hd,
+			       void *stream);
+
+/* NHWC im2col for CONV2D with OHWI weights (cpu_conv2d.c): rows (n,oy,ox),
+ * columns (ky,kx,c) zero-padded to kpad. */
+SAM3CU_API int sam3cu_im2col_nhwc(const void *x, void *a, int dtype, int n, int H, int W,
+				  int C, int kh, int kw, int stride, int pad, int kpad,
+				  void *stream);
+
+/* Q8_0 blocks -> F32 (sam3_q8_dequantize, quant.c:134-151). */
+SAM3CU_API int sam3cu_q8_dequantize(const void *blocks, float *out, int64_t n, void *stream);
 
 /* ---------------------------------------------------------------- ViT */
 

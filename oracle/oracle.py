@@ -276,6 +276,99 @@ def ref_sdpa(q, k, v):
     return o
 
 
+def ref_vit_encode_backend(cfg: dict, w: dict, image: np.ndarray, ops: int, be_size: int,
+                           be_type: int = 2) -> np.ndarray:
+    """The reference's own sam3_vit_build evaluated through another backend's
+    vtable (ops = address of its struct sam3_backend_ops)."""
+    gs = cfg["img_size"] // cfg["patch_size"]
+    out = np.empty((gs * gs, cfg["embed_dim"]), np.float32)
+    s, keep = _vit_struct(w)
+    image = np.ascontiguousarray(image, np.float32)
+    rc = ref().ref_vit_encode_backend(*(C.c_int(cfg[k]) for k in (
+        "img_size", "patch_size", "embed_dim", "depth", "n_heads",
+        "window_size", "mlp_dim")), C.byref(s), _p(image), _p(out), C.c_void_p(ops),
+        C.c_size_t(be_size), C.c_int(be_type))
+    del keep
+    if rc != 0:
+        raise RuntimeError(f"ref_vit_encode_backend failed rc={rc}")
+    return out
+
+
+DT = {"f32": 0, "f16": 1, "bf16": 2, "q8": 5}
+
+
+def _bits(a, dt):
+    """float32 array -> storage array of the reference dtype (bit patterns)."""
+    if dt == "f32":
+        return np.ascontiguousarray(a, np.float32)
+    if dt == "bf16":
+        return (np.ascontiguousarray(round_bf16(a)).view(np.uint32) >> 16).astype(np.uint16)
+    if dt == "f16":
+        return np.ascontiguousarray(a, np.float32).astype(np.float16).view(np.uint16)
+    raise ValueError(dt)
+
+
+def _unbits(a, dt):
+    if dt == "f32":
+        return a
+    if dt == "bf16":
+        return (a.astype(np.uint32) << 16).view(np.float32)
+    return a.view(np.float16).astype(np.float32)
+
+
+def ref_linear_graph(x, w, b, dt="f32", gelu=False, ops=None, be_size=0, be_type=2):
+    """gh_linear (+GELU) graph built by the reference helpers, evaluated by
+    the reference CPU backend (ops None) or another backend."""
+    M, K = x.shape
+    N = w.shape[0]
+    xs, ws = _bits(x, dt), _bits(w, dt)
+    bs = None if b is None else _bits(b, dt)
+    out = np.empty((M, N), np.float32 if dt == "f32" else np.uint16)
+    rc = ref().ref_linear_graph(DT[dt], _p(xs), _p(ws), _p(bs), _p(out), M, K, N,
+                                1 if gelu else 0, C.c_void_p(ops), C.c_size_t(be_size),
+                                C.c_int(be_type))
+    if rc != 0:
+        raise RuntimeError(f"ref_linear_graph failed rc={rc}")
+    return _unbits(out, dt)
+
+
+class _TDesc(C.Structure):
+    _fields_ = [("dtype", C.c_int), ("n_dims", C.c_int), ("dims", C.c_int * 4),
+                ("data", C.c_void_p)]
+
+
+def ref_node_graph(op, ins, out_dtype, out_shape, params=(0, 0, 0, 0), ops=None, be_size=0,
+                   be_type=2):
+    """Single-node graph; ins: list of (storage array, dtype name, shape)."""
+    descs = (_TDesc * 4)()
+    keep = []
+    for i, (arr, dt, shp) in enumerate(ins):
+        a = np.ascontiguousarray(arr)
+        keep.append(a)
+        descs[i].dtype = DT[dt]
+        descs[i].n_dims = len(shp)
+        for j, d in enumerate(shp):
+            descs[i].dims[j] = d
+        descs[i].data = a.ctypes.data
+    od = _TDesc()
+    od.dtype = DT[out_dtype]
+    od.n_dims = len(out_shape)
+    for j, d in enumerate(out_shape):
+        od.dims[j] = d
+    out = np.empty(out_shape, np.float32 if out_dtype == "f32" else np.uint16)
+    prm = (C.c_int * 4)(*params)
+    rc = ref().ref_node_graph(op, len(ins), descs, C.byref(od), _p(out), prm, C.c_void_p(ops),
+                              C.c_size_t(be_size), C.c_int(be_type))
+    del keep
+    if rc != 0:
+        raise RuntimeError(f"ref_node_graph(op={op}) failed rc={rc}")
+    return _unbits(out, out_dtype)
+
+
+OP = dict(MATMUL=1, ADD=2, GELU=6, LAYERNORM=7, CONV2D=8, RESHAPE=9, TRANSPOSE=10, CAST=11,
+          SLICE=13, ROPE=17, SDPA=21)
+
+
 def ref_vit_encode(cfg: dict, w: dict, image: np.ndarray) -> np.ndarray:
     gs = cfg["img_size"] // cfg["patch_size"]
     out = np.empty((gs * gs, cfg["embed_dim"]), np.float32)

@@ -231,9 +231,56 @@ static void put(struct sam3_tensor *t, const float *src)
 /* Full sam3_vit_build (image_encoder.c:513-963) on the reference CPU
  * backend.  image: planar CHW [3,img,img] F32, already normalised.
  * out: [np, e] F32.  Returns 0 on success. */
+static struct sam3_backend *make_backend(const struct sam3_backend_ops *ops,
+					 size_t be_size, int be_type)
+{
+	if (!ops)
+		return sam3_backend_init(SAM3_BACKEND_CPU);
+	/* what sam3_backend_init does for a registered type (backend.c:36-78) */
+	struct sam3_backend *be = calloc(1, be_size);
+	if (!be)
+		return NULL;
+	be->type = (enum sam3_backend_type)be_type;
+	be->ops = ops;
+	if (be->ops->init(be) != SAM3_OK) {
+		free(be);
+		return NULL;
+	}
+	return be;
+}
+
+static int vit_encode_impl(int img_size, int patch_size, int embed_dim,
+			   int depth, int n_heads, int window_size, int mlp_dim,
+			   const struct ref_vit_w *w, const float *image,
+			   float *out, const struct sam3_backend_ops *ops,
+			   size_t be_size, int be_type);
+
 int ref_vit_encode(int img_size, int patch_size, int embed_dim, int depth,
 		   int n_heads, int window_size, int mlp_dim,
 		   const struct ref_vit_w *w, const float *image, float *out)
+{
+	return vit_encode_impl(img_size, patch_size, embed_dim, depth, n_heads,
+			       window_size, mlp_dim, w, image, out, NULL, 0, 0);
+}
+
+/* The reference's own sam3_vit_build driving another backend through its
+ * vtable (ops = sam3_cuda_backend_ops(), be_size = its instance size). */
+int ref_vit_encode_backend(int img_size, int patch_size, int embed_dim,
+			   int depth, int n_heads, int window_size,
+			   int mlp_dim, const struct ref_vit_w *w,
+			   const float *image, float *out, const void *ops,
+			   size_t be_size, int be_type)
+{
+	return vit_encode_impl(img_size, patch_size, embed_dim, depth, n_heads,
+			       window_size, mlp_dim, w, image, out, ops,
+			       be_size, be_type);
+}
+
+static int vit_encode_impl(int img_size, int patch_size, int embed_dim,
+			   int depth, int n_heads, int window_size, int mlp_dim,
+			   const struct ref_vit_w *w, const float *image,
+			   float *out, const struct sam3_backend_ops *ops,
+			   size_t be_size, int be_type)
 {
 	struct sam3_arena model, scratch, persist;
 	struct sam3_vit *vit = calloc(1, sizeof(*vit));
@@ -251,7 +298,7 @@ int ref_vit_encode(int img_size, int patch_size, int embed_dim, int depth,
 	    sam3_arena_init(&scratch, sbytes) ||
 	    sam3_arena_init(&persist, 8ul * np * embed_dim + (16ul << 20)))
 		return -2;
-	struct sam3_backend *be = sam3_backend_init(SAM3_BACKEND_CPU);
+	struct sam3_backend *be = make_backend(ops, be_size, be_type);
 	if (!be)
 		goto done;
 	sam3_vit_init(vit, img_size, patch_size, embed_dim, depth, n_heads,
@@ -293,11 +340,119 @@ int ref_vit_encode(int img_size, int patch_size, int embed_dim, int depth,
 		rc = 0;
 	}
 done:
-	if (be)
-		sam3_backend_free(be);
+	if (be) {
+		if (ops) {
+			be->ops->free(be);
+			free(be);
+		} else {
+			sam3_backend_free(be);
+		}
+	}
 	sam3_arena_free(&model);
 	sam3_arena_free(&scratch);
 	sam3_arena_free(&persist);
 	free(vit);
+	return rc;
+}
+
+/* gh_linear (TRANSPOSE(W) -> MATMUL -> ADD(bias)) and optionally tanh-GELU,
+ * built by the reference's graph helpers on tensors of dtype dt (0 F32,
+ * 1 F16, 2 BF16; 16-bit data as bit patterns), evaluated by the given
+ * backend (NULL ops = the reference CPU backend).  x [M,K], w [N,K],
+ * b [N] (or NULL), y [M,N].  Returns 0 on success. */
+int ref_linear_graph(int dt, const void *x, const void *wt, const void *b,
+		     void *y, int M, int K, int N, int gelu, const void *ops,
+		     size_t be_size, int be_type)
+{
+	static const enum sam3_dtype map[3] = {SAM3_DTYPE_F32, SAM3_DTYPE_F16,
+					       SAM3_DTYPE_BF16};
+	size_t es = dt == 0 ? 4 : 2;
+	struct sam3_arena a;
+	if (sam3_arena_init(&a, 64ul << 20))
+		return -2;
+	struct sam3_graph *g = calloc(1, sizeof(*g));
+	struct sam3_backend *be = make_backend(ops, be_size, be_type);
+	int rc = -1;
+	if (!g || !be)
+		goto out;
+	sam3_graph_init(g);
+	struct sam3_tensor *tx = gh_tensor_wrap(&a, map[dt], 2, (int[]){M, K}, (void *)x);
+	struct sam3_tensor *tw = gh_tensor_wrap(&a, map[dt], 2, (int[]){N, K}, (void *)wt);
+	struct sam3_tensor *tb = b ? gh_tensor_wrap(&a, map[dt], 1, (int[]){N}, (void *)b) : NULL;
+	struct sam3_tensor *r = gh_linear(g, &a, tx, tw, tb);
+	if (r && gelu) {
+		struct sam3_tensor *o = gh_alloc_tensor(&a, map[dt], 2, (int[]){M, N});
+		r = o ? sam3_graph_add_op(g, SAM3_OP_GELU, (struct sam3_tensor *[]){r}, 1, o) : NULL;
+	}
+	if (!r)
+		goto out;
+	if (be->ops->graph_eval(be, g) != SAM3_OK)
+		goto out;
+	memcpy(y, r->data, es * (size_t)M * N);
+	rc = 0;
+out:
+	if (be) {
+		if (ops) {
+			be->ops->free(be);
+			free(be);
+		} else {
+			sam3_backend_free(be);
+		}
+	}
+	free(g);
+	sam3_arena_free(&a);
+	return rc;
+}
+
+/* A single-node graph of `op` (LAYERNORM with gamma/beta, SDPA [B,H,S,hd],
+ * ROPE [B,S,H,hd] + [S,hd/2] tables, MATMUL A[M,K].B[K,N] incl. F32 x
+ * Q8_0, SLICE, TRANSPOSE 4-D permute, CONV2D NHWC x OHWI, ADD) evaluated
+ * by the given backend.  ins: up to 4 host tensors described by dtype /
+ * n_dims / dims; params: node params.  Output shape/dtype given. */
+struct ref_tdesc {
+	int dtype, n_dims, dims[4];
+	const void *data;
+};
+
+int ref_node_graph(int op, int n_in, const struct ref_tdesc *ins,
+		   const struct ref_tdesc *outd, void *out_data,
+		   const int *params, const void *ops, size_t be_size,
+		   int be_type)
+{
+	struct sam3_arena a;
+	if (sam3_arena_init(&a, 16ul << 20))
+		return -2;
+	struct sam3_graph *g = calloc(1, sizeof(*g));
+	struct sam3_backend *be = make_backend(ops, be_size, be_type);
+	int rc = -1;
+	if (!g || !be)
+		goto out;
+	sam3_graph_init(g);
+	struct sam3_tensor *in[4] = {0};
+	for (int i = 0; i < n_in; i++)
+		in[i] = gh_tensor_wrap(&a, (enum sam3_dtype)ins[i].dtype,
+				       ins[i].n_dims, ins[i].dims,
+				       (void *)ins[i].data);
+	struct sam3_tensor *o = gh_alloc_tensor(&a, (enum sam3_dtype)outd->dtype,
+						outd->n_dims, outd->dims);
+	if (!o || !sam3_graph_add_op(g, (enum sam3_op)op, in, n_in, o))
+		goto out;
+	for (int i = 0; i < 4; i++)
+		g->nodes[0].params[i] = params ? params[i] : 0;
+	if (be->ops->graph_eval(be, g) != SAM3_OK)
+		goto out;
+	memcpy(out_data, o->data, o->nbytes);
+	rc = 0;
+out:
+	if (be) {
+		if (ops) {
+			be->ops->free(be);
+			free(be);
+		} else {
+			sam3_backend_free(be);
+		}
+	}
+	free(g);
+	sam3_arena_free(&a);
 	return rc;
 }

@@ -1,0 +1,843 @@
+/*
+ * cuda_backend.c - struct sam3_backend_ops for the B200 (C11).
+ *
+ * The drop-in for sam3.c's backend vtable (src/backend/backend.h:29-56):
+ * graph_eval walks the graph in array order, as cpu_graph_eval does
+ * (cpu_backend.c:175-202), and lowers each (op, dtype) to the device entry
+ * points of include/sam3cu.h.  Three peepholes remove the reference's
+ * per-linear glue: TRANSPOSE(W) feeding MATMUL is not materialised (the
+ * GEMM reads W [N,K] K-major), an ADD of a [N] bias to a MATMUL output and
+ * a following GELU are fused into the GEMM epilogue.
+ *
+ * Memory: graph inputs are copied host->device from t->data (non-ephemeral
+ * ones once, then cached by header address); node outputs get device
+ * buffers for the duration of graph_eval (RESHAPE aliases its input);
+ * outputs no later node consumes are copied back to t->data.
+ */
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../../include/sam3cu_backend.h"
+
+/* ------------------------------------------------------------------ state */
+
+struct devent {                   /* device copy of a host tensor */
+	const struct sam3_tensor *t;
+	const void               *data;   /* t->data when copied */
+	size_t                    nbytes;
+	void                     *dptr;
+	int                       kind;   /* 0 empty, 1 cached input, 2 graph-local */
+	const void               *aux;    /* derived buffer (f32 bias, q8 repack...) */
+};
+
+struct hostblk {
+	struct hostblk *next;
+};
+
+struct impl {
+	void            *stream;
+	struct devent   *map;             /* open addressing on tensor address */
+	size_t           cap, used;
+	struct hostblk  *host;            /* alloc_tensor buffers */
+	void           **tmp;             /* graph-local device allocations */
+	size_t           ntmp, captmp;
+	/* per-graph scratch tables, sized to n_nodes */
+	int             *uses;
+	int             *flags;
+	int              nflags;
+};
+
+enum { F_SKIP = 1, F_LAZY_T = 2, F_BIAS_FUSED = 4, F_GELU_FUSED = 8 };
+
+static size_t dsize(enum sam3_dtype d)
+{
+	switch (d) {
+	case SAM3_DTYPE_F32: return 4;
+	case SAM3_DTYPE_F16: return 2;
+	case SAM3_DTYPE_BF16: return 2;
+	case SAM3_DTYPE_I32: return 4;
+	case SAM3_DTYPE_I8: return 1;
+	default: return 0;
+	}
+}
+
+static int64_t nelems(const struct sam3_tensor *t)
+{
+	int64_t n = 1;
+	for (int i = 0; i < t->n_dims; i++)
+		n *= t->dims[i];
+	return n;
+}
+
+static size_t tbytes(const struct sam3_tensor *t)
+{
+	if (t->dtype == SAM3_DTYPE_Q8_0)
+		return (size_t)((nelems(t) + 31) / 32) * 36;
+	return (size_t)nelems(t) * dsize(t->dtype);
+}
+
+static struct impl *IM(struct sam3_backend *be)
+{
+	return (struct impl *)((struct sam3_cuda_backend *)be)->impl;
+}
+
+static enum sam3_error st(int rc)
+{
+	if (rc == 0)
+		return SAM3_OK;
+	if (rc >= -7)
+		return (enum sam3_error)rc;
+	if (rc == SAM3CU_EDTYPE2)
+		return SAM3_EDTYPE;
+	if (rc == SAM3CU_ENOMEM2)
+		return SAM3_ENOMEM;
+	if (rc == SAM3CU_ESHAPE)
+		return SAM3_EINVAL;
+	return SAM3_EBACKEND;
+}
+
+#define TRY(x) do { enum sam3_error e_ = st(x); if (e_ != SAM3_OK) { \
+	fprintf(stderr, "[sam3cu] %s:%d: %s failed: %s\n", __FILE__, __LINE__, #x, \
+		sam3cu_strerror(x)); return e_; } } while (0)
+
+/* ------------------------------------------------------------------ map */
+
+static size_t hptr(const void *p, size_t cap)
+{
+	uintptr_t x = (uintptr_t)p;
+	x ^= x >> 17;
+	x *= 0x9E3779B97F4A7C15ull;
+	return (size_t)(x >> 20) & (cap - 1);
+}
+
+static struct devent *map_find(struct impl *m, const struct sam3_tensor *t)
+{
+	if (!m->cap)
+		return NULL;
+	size_t i = hptr(t, m->cap);
+	for (size_t k = 0; k < m->cap; k++, i = (i + 1) & (m->cap - 1)) {
+		if (m->map[i].kind == 0)
+			return NULL;
+		if (m->map[i].t == t && m->map[i].kind > 0)
+			return &m->map[i];
+	}
+	return NULL;
+}
+
+static void devent_free(struct devent *e)
+{
+	if (e->dptr && e->kind == 1)
+		sam3cu_dev_free(e->dptr);
+	if (e->aux)
+		sam3cu_dev_free((void *)e->aux);
+	e->dptr = NULL;
+	e->aux = NULL;
+}
+
+static enum sam3_error map_rehash(struct impl *m, size_t ncap);
+
+static struct devent *map_insert(struct impl *m, const struct sam3_tensor *t)
+{
+	if ((m->used + 1) * 2 > m->cap &&
+	    map_rehash(m, m->cap ? m->cap * 2 : 1024) != SAM3_OK)
+		return NULL;
+	size_t i = hptr(t, m->cap);
+	while (m->map[i].kind != 0 && m->map[i].t != t)
+		i = (i + 1) & (m->cap - 1);
+	if (m->map[i].kind == 0)
+		m->used++;
+	else
+		devent_free(&m->map[i]);
+	memset(&m->map[i], 0, sizeof(m->map[i]));
+	m->map[i].t = t;
+	return &m->map[i];
+}
+
+static enum sam3_error map_rehash(struct impl *m, size_t ncap)
+{
+	struct devent *old = m->map;
+	size_t ocap = m->cap;
+	struct devent *nm = calloc(ncap, sizeof(*nm));
+	if (!nm)
+		return SAM3_ENOMEM;
+	m->map = nm;
+	m->cap = ncap;
+	m->used = 0;
+	for (size_t i = 0; i < ocap; i++) {
+		if (old[i].kind <= 0)
+			continue;
+		size_t j = hptr(old[i].t, ncap);
+		while (nm[j].kind != 0)
+			j = (j + 1) & (ncap - 1);
+		nm[j] = old[i];
+		m->used++;
+	}
+	free(old);
+	return SAM3_OK;
+}
+
+/* remove graph-local entries (kind 2), keep cached inputs */
+static void map_drop_local(struct impl *m)
+{
+	int any = 0;
+	for (size_t i = 0; i < m->cap; i++)
+		if (m->map[i].kind == 2) {
+			if (m->map[i].aux)
+				sam3cu_dev_free((void *)m->map[i].aux);
+			m->map[i].kind = -1; /* tombstone */
+			any = 1;
+		}
+	if (any)
+		map_rehash(m, m->cap);
+}
+
+static enum sam3_error tmp_alloc(struct impl *m, size_t bytes, void **p)
+{
+	if (m->ntmp == m->captmp) {
+		size_t nc = m->captmp ? m->captmp * 2 : 256;
+		void **n = realloc(m->tmp, nc * sizeof(void *));
+		if (!n)
+			return SAM3_ENOMEM;
+		m->tmp = n;
+		m->captmp = nc;
+	}
+	TRY(sam3cu_dev_alloc(p, (bytes + 255) & ~(size_t)255));
+	m->tmp[m->ntmp++] = *p;
+	return SAM3_OK;
+}
+
+static void tmp_free_all(struct impl *m)
+{
+	for (size_t i = 0; i < m->ntmp; i++)
+		sam3cu_dev_free(m->tmp[i]);
+	m->ntmp = 0;
+}
+
+/* ------------------------------------------------------------------ vtable */
+
+static enum sam3_error cu_init(struct sam3_backend *be)
+{
+	struct sam3_cuda_backend *cb = (struct sam3_cuda_backend *)be;
+	if (sam3cu_init(cb->device) != 0)
+		return SAM3_EBACKEND;
+	struct impl *m = calloc(1, sizeof(*m));
+	if (!m)
+		return SAM3_ENOMEM;
+	if (sam3cu_stream_create(&m->stream) != 0) {
+		free(m);
+		return SAM3_EBACKEND;
+	}
+	cb->impl = m;
+	return SAM3_OK;
+}
+
+static void host_free_all(struct impl *m)
+{
+	while (m->host) {
+		struct hostblk *n = m->host->next;
+		free(m->host);
+		m->host = n;
+	}
+}
+
+static void cu_free(struct sam3_backend *be)
+{
+	struct impl *m = IM(be);
+	if (!m)
+		return;
+	sam3cu_stream_sync(m->stream);
+	tmp_free_all(m);
+	for (size_t i = 0; i < m->cap; i++)
+		if (m->map[i].kind > 0)
+			devent_free(&m->map[i]);
+	free(m->map);
+	free(m->tmp);
+	free(m->uses);
+	free(m->flags);
+	host_free_all(m);
+	sam3cu_stream_destroy(m->stream);
+	free(m);
+	((struct sam3_cuda_backend *)be)->impl = NULL;
+}
+
+static enum sam3_error cu_alloc_tensor(struct sam3_backend *be,
+				       struct sam3_tensor *t)
+{
+	struct impl *m = IM(be);
+	if (!t || t->n_dims < 1 || t->n_dims > SAM3_MAX_DIMS)
+		return SAM3_EINVAL;
+	size_t nb = tbytes(t);
+	if (!nb)
+		return SAM3_EINVAL;
+	struct hostblk *b = aligned_alloc(64, (sizeof(*b) + 63) / 64 * 64 + ((nb + 63) / 64 * 64));
+	if (!b)
+		return SAM3_ENOMEM;
+	b->next = m->host;
+	m->host = b;
+	t->data = (char *)b + (sizeof(*b) + 63) / 64 * 64;
+	t->nbytes = nb;
+	t->strides[t->n_dims - 1] = 1;
+	for (int i = t->n_dims - 2; i >= 0; i--)
+		t->strides[i] = t->strides[i + 1] * t->dims[i + 1];
+	return SAM3_OK;
+}
+
+static void cu_arena_reset(struct sam3_backend *be)
+{
+	struct impl *m = IM(be);
+	sam3cu_stream_sync(m->stream);
+	tmp_free_all(m);
+	map_drop_local(m);
+	host_free_all(m);
+}
+
+static void cu_cache_invalidate(struct sam3_backend *be, const void *start,
+				size_t len)
+{
+	struct impl *m = IM(be);
+	const char *lo = start, *hi = (const char *)start + len;
+	int any = 0;
+	sam3cu_stream_sync(m->stream);
+	for (size_t i = 0; i < m->cap; i++) {
+		struct devent *e = &m->map[i];
+		if (e->kind != 1)
+			continue;
+		const char *a = (const char *)e->t, *d = e->data;
+		if ((a >= lo && a < hi) || (d && d >= lo && d < hi)) {
+			devent_free(e);
+			e->kind = -1;
+			any = 1;
+		}
+	}
+	if (any)
+		map_rehash(m, m->cap);
+}
+
+/* device pointer of a tensor that is produced in this graph or is an input */
+static enum sam3_error dev_of(struct impl *m, const struct sam3_tensor *t,
+			      int produced, void **p)
+{
+	struct devent *e = map_find(m, t);
+	if (e && (e->kind == 2 || (e->data == t->data && e->nbytes == tbytes(t)))) {
+		*p = e->dptr;
+		return SAM3_OK;
+	}
+	if (produced) {
+		fprintf(stderr, "[sam3cu] tensor %p used before its producer ran\n",
+			(const void *)t);
+		return SAM3_EINVAL;
+	}
+	if (!t->data) {
+		fprintf(stderr, "[sam3cu] graph input %p has no host data\n",
+			(const void *)t);
+		return SAM3_EINVAL;
+	}
+	size_t nb = tbytes(t);
+	void *d = NULL;
+	if (t->ephemeral) {
+		TRY(tmp_alloc(m, nb, &d));
+	} else {
+		TRY(sam3cu_dev_alloc(&d, nb));
+	}
+	TRY(sam3cu_memcpy_h2d(d, t->data, nb, m->stream));
+	e = map_insert(m, t);
+	if (!e)
+		return SAM3_ENOMEM;
+	e->data = t->data;
+	e->nbytes = nb;
+	e->dptr = d;
+	e->kind = t->ephemeral ? 2 : 1;
+	*p = d;
+	return SAM3_OK;
+}
+
+static enum sam3_error out_buf(struct impl *m, const struct sam3_tensor *t,
+			       void **p)
+{
+	TRY(tmp_alloc(m, tbytes(t), p));
+	struct devent *e = map_insert(m, t);
+	if (!e)
+		return SAM3_ENOMEM;
+	e->data = t->data;
+	e->nbytes = tbytes(t);
+	e->dptr = *p;
+	e->kind = 2;
+	return SAM3_OK;
+}
+
+static int is_16(enum sam3_dtype d)
+{
+	return d == SAM3_DTYPE_F16 || d == SAM3_DTYPE_BF16;
+}
+
+/* f32 copy of a small (bias / gamma / beta) tensor, cached on its entry */
+static enum sam3_error f32_view(struct impl *m, const struct sam3_tensor *t,
+				int produced, const float **out)
+{
+	void *d;
+	TRY(dev_of(m, t, produced, &d));
+	if (t->dtype == SAM3_DTYPE_F32) {
+		*out = d;
+		return SAM3_OK;
+	}
+	if (!is_16(t->dtype))
+		return SAM3_EDTYPE;
+	struct devent *e = map_find(m, t);
+	if (e && e->aux) {
+		*out = e->aux;
+		return SAM3_OK;
+	}
+	void *f;
+	TRY(sam3cu_dev_alloc(&f, (size_t)nelems(t) * 4));
+	TRY(sam3cu_cast(d, t->dtype, f, SAM3_DTYPE_F32, nelems(t), m->stream));
+	if (e)
+		e->aux = f;
+	*out = f;
+	return SAM3_OK;
+}
+
+/* ------------------------------------------------------------------ ops */
+
+static int produced_in(struct sam3_graph *g, int upto, const struct sam3_tensor *t)
+{
+	for (int i = 0; i < upto; i++)
+		if (g->nodes[i].output == t)
+			return 1;
+	return 0;
+}
+
+/* MATMUL (+ fused bias / GELU): cpu_kernel_matmul family, gh_linear */
+static enum sam3_error op_matmul(struct impl *m, struct sam3_graph *g, int ni)
+{
+	struct sam3_node *nd = &g->nodes[ni];
+	struct sam3_tensor *a = nd->inputs[0], *b = nd->inputs[1];
+	struct sam3_tensor *out = nd->output;
+	const struct sam3_tensor *w = NULL;  /* [N,K] K-major */
+	int lazy = 0;
+	/* B produced by a lazy TRANSPOSE of a 2-D W in this graph? */
+	for (int j = 0; j < ni; j++)
+		if (g->nodes[j].output == b && (m->flags[j] & F_LAZY_T)) {
+			w = g->nodes[j].inputs[0];
+			lazy = 1;
+		}
+	if (!lazy && b->n_dims != 2)
+		return SAM3_EINVAL;
+	int K = a->dims[a->n_dims - 1];
+	int64_t M = nelems(a) / K;
+	int N = b->n_dims == 1 ? 1 : b->dims[b->n_dims - 1];
+	if (lazy)
+		N = w->dims[0];
+	if ((lazy ? w->dims[1] : b->dims[b->n_dims - 2]) != K || M > 0x7fffffff)
+		return SAM3_EINVAL;
+	/* epilogue fusion target: the ADD / GELU output if fused */
+	struct sam3_tensor *dst = out;
+	const struct sam3_tensor *bias = NULL;
+	int act = 0;
+	if (m->flags[ni] & F_BIAS_FUSED) {
+		for (int j = ni + 1; j < g->n_nodes; j++)
+			if (g->nodes[j].op == SAM3_OP_ADD && g->nodes[j].inputs[0] == out) {
+				bias = g->nodes[j].inputs[1];
+				dst = g->nodes[j].output;
+				if (m->flags[j] & F_GELU_FUSED) {
+					for (int k = j + 1; k < g->n_nodes; k++)
+						if (g->nodes[k].op == SAM3_OP_GELU &&
+						    g->nodes[k].inputs[0] == dst) {
+							dst = g->nodes[k].output;
+							act = SAM3CU_ACT_GELU_TANH;
+							break;
+						}
+				}
+				break;
+			}
+	}
+	void *pa, *pw, *py;
+	const float *pb = NULL;
+	TRY(dev_of(m, a, produced_in(g, ni, a), &pa));
+	if (bias)
+		TRY(f32_view(m, bias, produced_in(g, ni, bias), &pb));
+	TRY(out_buf(m, dst, &py));
+	enum sam3_dtype wt = lazy ? w->dtype : b->dtype;
+
+	if (wt == SAM3_DTYPE_Q8_0 && a->dtype == SAM3_DTYPE_F32) {
+		if (lazy) {
+			/* F32 x Q8_0 -> F32: activations to BF16, weight dequantised on chip */
+			void *abf;
+			TRY(tmp_alloc(m, (size_t)M * K * 2, &abf));
+			TRY(sam3cu_cast(pa, SAM3_DTYPE_F32, abf, SAM3_DTYPE_BF16, M * K, m->stream));
+			/* W [N,K] quantised along K: repack once per weight */
+			void *pq;
+			TRY(dev_of(m, w, produced_in(g, ni, w), &pq));
+			struct devent *e = map_find(m, w);
+			if (!e->aux) {
+				void *q;
+				TRY(sam3cu_dev_alloc(&q, (size_t)N * K + (size_t)(K / 32) * N * 4));
+				TRY(sam3cu_q8_repack(pq, N, K, q, (float *)((char *)q + (size_t)N * K),
+						     m->stream));
+				e->aux = q;
+			}
+			const int8_t *q = e->aux;
+			TRY(sam3cu_linear_q8(abf, SAM3CU_BF16, q, (const float *)(q + (size_t)N * K), pb,
+					     NULL, py, SAM3CU_F32, (int)M, K, N, act, m->stream));
+			return SAM3_OK;
+		}
+		/* single-op convention: B [K,N] quantised flat (cpu_matmul_q8.c:28-35) */
+		void *pq, *bf, *bt;
+		TRY(dev_of(m, b, produced_in(g, ni, b), &pq));
+		TRY(tmp_alloc(m, (size_t)K * N * 4, &bf));
+		TRY(tmp_alloc(m, (size_t)K * N * 4, &bt));
+		TRY(sam3cu_q8_dequantize(pq, bf, (int64_t)K * N, m->stream));
+		int dims[2] = {K, N}, perm[2] = {1, 0};
+		TRY(sam3cu_permute(bf, bt, 4, 2, dims, perm, m->stream));
+		TRY(sam3cu_linear(pa, SAM3CU_F32, bt, pb, NULL, py, SAM3CU_F32, (int)M, K, N, act,
+				  m->stream));
+		return SAM3_OK;
+	}
+	if (a->dtype != wt || (a->dtype != SAM3_DTYPE_F32 && !is_16(a->dtype)))
+		return SAM3_EDTYPE;
+	if (lazy) {
+		TRY(dev_of(m, w, produced_in(g, ni, w), &pw));
+	} else {
+		/* B [K,N] -> [N,K] */
+		void *pbk;
+		TRY(dev_of(m, b, produced_in(g, ni, b), &pbk));
+		TRY(tmp_alloc(m, (size_t)K * N * dsize(b->dtype), &pw));
+		int dims[2] = {K, N}, perm[2] = {1, 0};
+		TRY(sam3cu_permute(pbk, pw, (int)dsize(b->dtype), 2, dims, perm, m->stream));
+	}
+	TRY(sam3cu_linear(pa, a->dtype, pw, pb, NULL, py, dst->dtype, (int)M, K, N, act,
+			  m->stream));
+	return SAM3_OK;
+}
+
+static enum sam3_error op_node(struct impl *m, struct sam3_graph *g, int ni)
+{
+	struct sam3_node *nd = &g->nodes[ni];
+	struct sam3_tensor *out = nd->output;
+	struct sam3_tensor *x = nd->inputs[0];
+	void *px = NULL, *py = NULL;
+	if (!out || !x)
+		return SAM3_EINVAL;
+
+	switch (nd->op) {
+	case SAM3_OP_MATMUL:
+		return op_matmul(m, g, ni);
+
+	case SAM3_OP_RESHAPE: {  /* alias (cpu_reshape.c:20-38) */
+		if (tbytes(out) != tbytes(x))
+			return SAM3_EINVAL;
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		struct devent *e = map_insert(m, out);
+		if (!e)
+			return SAM3_ENOMEM;
+		e->data = out->data;
+		e->nbytes = tbytes(out);
+		e->dptr = px;
+		e->kind = 2;
+		return SAM3_OK;
+	}
+
+	case SAM3_OP_TRANSPOSE: {
+		size_t es = dsize(x->dtype);
+		if (!es)
+			return SAM3_EDTYPE;
+		int axes[4], has = 0, nd_ = x->n_dims;
+		for (int i = 0; i < nd_; i++) {
+			axes[i] = nd->params[i];
+			if (axes[i])
+				has = 1;
+		}
+		if (!has) {  /* legacy: swap the last two dims (cpu_transpose.c:330-348) */
+			for (int i = 0; i < nd_; i++)
+				axes[i] = i;
+			if (nd_ >= 2) {
+				axes[nd_ - 2] = nd_ - 1;
+				axes[nd_ - 1] = nd_ - 2;
+			}
+		}
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_permute(px, py, (int)es, nd_, x->dims, axes, m->stream));
+		return SAM3_OK;
+	}
+
+	case SAM3_OP_SLICE: {
+		size_t es = dsize(x->dtype);
+		if (!es)
+			return SAM3_EDTYPE;
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_slice(px, py, (int)es, x->n_dims, x->dims, nd->params[0],
+				 nd->params[1], nd->params[2], m->stream));
+		return SAM3_OK;
+	}
+
+	case SAM3_OP_ADD: {
+		struct sam3_tensor *y = nd->inputs[1];
+		void *pyy;
+		if (!y || x->dtype != y->dtype ||
+		    (x->dtype != SAM3_DTYPE_F32 && !is_16(x->dtype)))
+			return SAM3_EDTYPE;
+		int64_t n = nelems(x), nb = nelems(y);
+		if (!(nb == n || nb == 1 || nb == x->dims[x->n_dims - 1]))
+			return SAM3_EINVAL;
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(dev_of(m, y, produced_in(g, ni, y), &pyy));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_add(px, pyy, py, x->dtype, n, nb, m->stream));
+		return SAM3_OK;
+	}
+
+	case SAM3_OP_GELU:
+		if (x->dtype != SAM3_DTYPE_F32 && !is_16(x->dtype))
+			return SAM3_EDTYPE;
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_gelu(px, py, x->dtype, nelems(x), m->stream));
+		return SAM3_OK;
+
+	case SAM3_OP_CAST:
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_cast(px, x->dtype, py, out->dtype, nelems(x), m->stream));
+		return SAM3_OK;
+
+	case SAM3_OP_LAYERNORM: {  /* cpu_layernorm.c:210-254; gamma/beta optional */
+		const float *gm = NULL, *bt = NULL;
+		int cols = x->dims[x->n_dims - 1];
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		if (nd->n_inputs > 1 && nd->inputs[1])
+			TRY(f32_view(m, nd->inputs[1], produced_in(g, ni, nd->inputs[1]), &gm));
+		if (nd->n_inputs > 2 && nd->inputs[2])
+			TRY(f32_view(m, nd->inputs[2], produced_in(g, ni, nd->inputs[2]), &bt));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_layernorm(px, x->dtype, gm, bt, py, out->dtype, (int)(nelems(x) / cols),
+				     cols, m->stream));
+		return SAM3_OK;
+	}
+
+	case SAM3_OP_ROPE: {
+		struct sam3_tensor *cs = nd->inputs[1], *sn = nd->inputs[2];
+		void *pc, *ps;
+		if (x->n_dims != 4 || !cs || !sn || cs->dtype != SAM3_DTYPE_F32 ||
+		    sn->dtype != SAM3_DTYPE_F32)
+			return SAM3_EINVAL;
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(dev_of(m, cs, produced_in(g, ni, cs), &pc));
+		TRY(dev_of(m, sn, produced_in(g, ni, sn), &ps));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_rope(px, pc, ps, py, x->dtype, x->dims[0], x->dims[1], x->dims[2],
+				x->dims[3], m->stream));
+		return SAM3_OK;
+	}
+
+	case SAM3_OP_SDPA: {  /* [S,hd] or [B,H,S,hd], optional mask [Sq,Sk] */
+		struct sam3_tensor *k = nd->inputs[1], *v = nd->inputs[2];
+		struct sam3_tensor *mk = nd->n_inputs > 3 ? nd->inputs[3] : NULL;
+		void *pk, *pv, *pm = NULL;
+		int hd = x->dims[x->n_dims - 1];
+		int sq = x->dims[x->n_dims - 2], sk = k->dims[k->n_dims - 2];
+		int bh = (int)(nelems(x) / ((int64_t)sq * hd));
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(dev_of(m, k, produced_in(g, ni, k), &pk));
+		TRY(dev_of(m, v, produced_in(g, ni, v), &pv));
+		if (mk)
+			TRY(dev_of(m, mk, produced_in(g, ni, mk), &pm));
+		TRY(out_buf(m, out, &py));
+		if (x->dtype == SAM3_DTYPE_F32) {
+			TRY(sam3cu_sdpa_f32(px, pk, pv, pm, py, bh, sq, sk, hd, m->stream));
+			return SAM3_OK;
+		}
+		if (is_16(x->dtype) && !mk && sq == sk && hd == 64) {
+			TRY(sam3cu_sdpa(px, pk, pv, 64, py, 64, x->dtype, bh, sq, 1, 64, m->stream));
+			return SAM3_OK;
+		}
+		return SAM3_EDTYPE;
+	}
+
+	case SAM3_OP_CONV2D: {  /* NHWC x OHWI, groups 1 (cpu_conv2d.c:296-400) */
+		struct sam3_tensor *w = nd->inputs[1];
+		int stride = nd->params[0] > 0 ? nd->params[0] : 1, pad = nd->params[1];
+		int groups = nd->params[2] > 0 ? nd->params[2] : 1;
+		if (!w || x->n_dims != 4 || w->n_dims != 4 || groups != 1 ||
+		    (nd->params[3] && nd->params[3] != pad) || w->dims[3] != x->dims[3] ||
+		    w->dtype != x->dtype)
+			return SAM3_EDTYPE;
+		int N = x->dims[0], H = x->dims[1], W = x->dims[2], C = x->dims[3];
+		int OC = w->dims[0], KH = w->dims[1], KW = w->dims[2];
+		int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+		int kk = KH * KW * C, al = x->dtype == SAM3_DTYPE_F32 ? 4 : 8;
+		int kpad = (kk + al - 1) / al * al;
+		size_t es = dsize(x->dtype);
+		void *pw, *col, *wpad;
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(dev_of(m, w, produced_in(g, ni, w), &pw));
+		TRY(tmp_alloc(m, (size_t)N * OH * OW * kpad * es, &col));
+		TRY(sam3cu_im2col_nhwc(px, col, x->dtype, N, H, W, C, KH, KW, stride, pad, kpad,
+				       m->stream));
+		if (kpad != kk) {  /* weight rows padded to kpad: im2col of a 1x1 "image" */
+			TRY(tmp_alloc(m, (size_t)OC * kpad * es, &wpad));
+			TRY(sam3cu_im2col_nhwc(pw, wpad, x->dtype, OC, 1, 1, kk, 1, 1, 1, 0, kpad,
+					       m->stream));
+		} else {
+			wpad = pw;
+		}
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_linear(col, x->dtype, wpad, NULL, NULL, py, out->dtype, N * OH * OW, kpad,
+				  OC, 0, m->stream));
+		return SAM3_OK;
+	}
+
+	default:
+		fprintf(stderr, "[sam3cu] op %d (dtype %d) is not supported on CUDA\n",
+			(int)nd->op, (int)x->dtype);
+		return SAM3_EDTYPE;
+	}
+}
+
+static int count_uses(struct sam3_graph *g, int from, const struct sam3_tensor *t)
+{
+	int n = 0;
+	for (int i = from; i < g->n_nodes; i++)
+		for (int k = 0; k < g->nodes[i].n_inputs; k++)
+			if (g->nodes[i].inputs[k] == t)
+				n++;
+	return n;
+}
+
+/* mark the peepholes: lazy W transposes, bias / GELU fusion into MATMUL */
+static void plan(struct impl *m, struct sam3_graph *g)
+{
+	memset(m->flags, 0, sizeof(int) * (size_t)g->n_nodes);
+	for (int i = 0; i < g->n_nodes; i++) {
+		struct sam3_node *nd = &g->nodes[i];
+		if (nd->op == SAM3_OP_TRANSPOSE && nd->inputs[0] && nd->inputs[0]->n_dims == 2 &&
+		    (nd->params[0] | nd->params[1]) == 0 &&
+		    nd->inputs[0]->dtype != SAM3_DTYPE_I32) {
+			/* every consumer must be a MATMUL using it as B */
+			int ok = 1, any = 0;
+			for (int j = i + 1; j < g->n_nodes && ok; j++)
+				for (int k = 0; k < g->nodes[j].n_inputs; k++)
+					if (g->nodes[j].inputs[k] == nd->output) {
+						any = 1;
+						if (g->nodes[j].op != SAM3_OP_MATMUL || k != 1)
+							ok = 0;
+					}
+			if (ok && any)
+				m->flags[i] |= F_LAZY_T | F_SKIP;
+		}
+		if (nd->op == SAM3_OP_MATMUL && count_uses(g, i + 1, nd->output) == 1) {
+			for (int j = i + 1; j < g->n_nodes; j++) {
+				struct sam3_node *ad = &g->nodes[j];
+				if (ad->op != SAM3_OP_ADD || ad->inputs[0] != nd->output)
+					continue;
+				struct sam3_tensor *b = ad->inputs[1];
+				int N = nd->output->dims[nd->output->n_dims - 1];
+				if (b && nelems(b) == N && N > 1 && (N % 8) == 0 &&
+				    b->dtype == nd->output->dtype) {
+					m->flags[i] |= F_BIAS_FUSED;
+					m->flags[j] |= F_SKIP;
+					if (count_uses(g, j + 1, ad->output) == 1) {
+						for (int k = j + 1; k < g->n_nodes; k++)
+							if (g->nodes[k].op == SAM3_OP_GELU &&
+							    g->nodes[k].inputs[0] == ad->output) {
+								m->flags[j] |= F_GELU_FUSED;
+								m->flags[k] |= F_SKIP;
+								break;
+							}
+					}
+				}
+				break;
+			}
+		}
+	}
+}
+
+static enum sam3_error cu_graph_eval(struct sam3_backend *be,
+				     struct sam3_graph *g)
+{
+	struct impl *m = IM(be);
+	enum sam3_error err = SAM3_OK;
+	if (!g || g->n_nodes < 0)
+		return SAM3_EINVAL;
+	if (g->n_nodes > m->nflags) {
+		int *f = realloc(m->flags, sizeof(int) * (size_t)g->n_nodes);
+		if (!f)
+			return SAM3_ENOMEM;
+		m->flags = f;
+		m->nflags = g->n_nodes;
+	}
+	plan(m, g);
+	for (int i = 0; i < g->n_nodes; i++) {
+		if (m->flags[i] & F_SKIP)
+			continue;
+		err = op_node(m, g, i);
+		if (err != SAM3_OK) {
+			fprintf(stderr, "[sam3cu] graph_eval: node %d (op=%d) failed (%d)\n", i,
+				(int)g->nodes[i].op, (int)err);
+			break;
+		}
+	}
+	/* outputs nobody in this graph consumes go back to host (or stay cached) */
+	for (int i = 0; err == SAM3_OK && i < g->n_nodes; i++) {
+		struct sam3_tensor *t = g->nodes[i].output;
+		if (m->flags[i] & F_SKIP)
+			continue;
+		if (count_uses(g, i + 1, t))
+			continue;
+		/* a fused MATMUL writes the final ADD/GELU tensor: find what it wrote */
+		struct devent *e = map_find(m, t);
+		if ((m->flags[i] & F_BIAS_FUSED))
+			continue;  /* its ADD (skipped) output is handled below */
+		if (!e)
+			continue;
+		if (g->no_readback) {
+			e->kind = 1;  /* keep resident for the next graph */
+			e->data = t->data;
+			void *keep;
+			if (sam3cu_dev_alloc(&keep, e->nbytes) == 0) {
+				sam3cu_memcpy_d2d(keep, e->dptr, e->nbytes, m->stream);
+				e->dptr = keep;
+			}
+		} else if (t->data) {
+			if (sam3cu_memcpy_d2h(t->data, e->dptr, tbytes(t), m->stream) != 0)
+				err = SAM3_EBACKEND;
+		}
+	}
+	/* fused outputs (the ADD / GELU tensors written by a MATMUL) */
+	for (int i = 0; err == SAM3_OK && i < g->n_nodes; i++) {
+		if (!(m->flags[i] & F_SKIP) || g->nodes[i].op == SAM3_OP_TRANSPOSE)
+			continue;
+		struct sam3_tensor *t = g->nodes[i].output;
+		if (count_uses(g, i + 1, t))
+			continue;
+		if ((m->flags[i] & F_GELU_FUSED))
+			continue;  /* the GELU node holds the result */
+		struct devent *e = map_find(m, t);
+		if (!e || !t->data || g->no_readback)
+			continue;
+		if (sam3cu_memcpy_d2h(t->data, e->dptr, tbytes(t), m->stream) != 0)
+			err = SAM3_EBACKEND;
+	}
+	if (sam3cu_stream_sync(m->stream) != 0 && err == SAM3_OK)
+		err = SAM3_EBACKEND;
+	if (err == SAM3_OK && sam3cu_last_device_error() != 0)
+		err = SAM3_EBACKEND;
+	tmp_free_all(m);
+	map_drop_local(m);
+	return err;
+}
+
+static const struct sam3_backend_ops cuda_ops = {
+	.init             = cu_init,
+	.free             = cu_free,
+	.alloc_tensor     = cu_alloc_tensor,
+	.graph_eval       = cu_graph_eval,
+	.arena_reset      = cu_arena_reset,
+	.cache_invalidate = cu_cache_invalidate,
+};
+
+const struct sam3_backend_ops *sam3_cuda_backend_ops(void)
+{
+	return &cuda_ops;
+}

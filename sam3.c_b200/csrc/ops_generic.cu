@@ -1,0 +1,353 @@
+// ops_generic.cu - the remaining graph ops of the encoder path as device
+// kernels, for the per-node lowering of the backend vtable (cuda_backend.c):
+// permute/transpose, slice, broadcast add, GELU, RoPE, cast, an F32
+// attention (with the optional additive mask of SAM3_OP_SDPA), NHWC im2col
+// for CONV2D and Q8_0 dequantisation.  Plus the device-memory and stream
+// helpers the C11 backend shell calls.  These are HBM-bound elementwise
+// kernels; the hot GEMM / attention / LayerNorm work lives in the fused
+// kernels.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cstdint>
+
+#include "../../include/sam3cu.h"
+#include "sam3cu_internal.h"
+
+using namespace s3;
+
+namespace {
+
+template <int T>
+__device__ __forceinline__ float ld(const void* p, int64_t i) {
+  if (T == kF32) return static_cast<const float*>(p)[i];
+  if (T == kBF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+template <int T>
+__device__ __forceinline__ void st(void* p, int64_t i, float v) {
+  if (T == kF32) static_cast<float*>(p)[i] = v;
+  else if (T == kBF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else static_cast<__half*>(p)[i] = __float2half_rn(v);
+}
+
+int grid_for(int64_t n, int threads) {
+  int64_t g = (n + threads - 1) / threads;
+  const int cap = num_sms() * 16;
+  return static_cast<int>(g < 1 ? 1 : (g < cap ? g : cap));
+}
+
+int rc_launch() { return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch; }
+
+cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+#define GRID_LOOP(i, n)                                                                   \
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < (n); \
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+
+// out[o] = in[src(o)] for a permutation of up to 4 dims (cpu_transpose.c).
+template <typename E>
+__global__ void permute_kernel(const E* __restrict__ in, E* __restrict__ out, int64_t n, int4 odims, int4 istr) {
+  GRID_LOOP(o, n) {
+    int64_t r = o;
+    const int c3 = static_cast<int>(r % odims.w); r /= odims.w;
+    const int c2 = static_cast<int>(r % odims.z); r /= odims.z;
+    const int c1 = static_cast<int>(r % odims.y); r /= odims.y;
+    const int c0 = static_cast<int>(r);
+    out[o] = in[static_cast<int64_t>(c0) * istr.x + static_cast<int64_t>(c1) * istr.y +
+                static_cast<int64_t>(c2) * istr.z + static_cast<int64_t>(c3) * istr.w];
+  }
+}
+
+// Slice along an axis: view as [outer, len, inner] (cpu_slice.c).
+template <typename E>
+__global__ void slice_kernel(const E* __restrict__ in, E* __restrict__ out, int64_t n, int64_t inner,
+                             int64_t len_out, int64_t len_in, int64_t start) {
+  GRID_LOOP(o, n) {
+    const int64_t i = o % inner, r = o / inner;
+    const int64_t k = r % len_out, outer = r / len_out;
+    out[o] = in[(outer * len_in + start + k) * inner + i];
+  }
+}
+
+// out[i] = a[i] + b[i % nb]  (same shape, row [N] broadcast, scalar;
+// cpu_elementwise.c:28-62 / :472-495)
+template <int T>
+__global__ void add_kernel(const void* a, const void* b, void* out, int64_t n, int64_t nb) {
+  GRID_LOOP(i, n) st<T>(out, i, ld<T>(a, i) + ld<T>(b, i % nb));
+}
+
+// tanh-GELU (cpu_gelu.c:23-36)
+template <int T>
+__global__ void gelu_kernel(const void* x, void* y, int64_t n) {
+  GRID_LOOP(i, n) {
+    const float v = ld<T>(x, i);
+    const float inner = 0.7978845608f * (v + 0.044715f * v * v * v);
+    st<T>(y, i, 0.5f * v * (1.0f + tanhf(inner)));
+  }
+}
+
+// RoPE on [batch, seq, heads, hd] with F32 [seq, hd/2] tables (cpu_rope.c)
+template <int T>
+__global__ void rope_kernel(const void* x, const float* __restrict__ cs, const float* __restrict__ sn, void* y,
+                            int64_t npairs, int seq, int heads, int half) {
+  GRID_LOOP(p, npairs) {
+    const int d = static_cast<int>(p % half);
+    const int64_t bsh = p / half;
+    const int s = static_cast<int>((bsh / heads) % seq);
+    const float c = cs[s * half + d], si = sn[s * half + d];
+    const float x0 = ld<T>(x, 2 * p), x1 = ld<T>(x, 2 * p + 1);
+    st<T>(y, 2 * p, x0 * c - x1 * si);
+    st<T>(y, 2 * p + 1, x0 * si + x1 * c);
+  }
+}
+
+template <int TI, int TO>
+__global__ void cast_any(const void* x, void* y, int64_t n) {
+  GRID_LOOP(i, n) st<TO>(y, i, ld<TI>(x, i));
+}
+
+// F32 attention, one thread per query row (online softmax exactly as
+// cpu_sdpa.c:49-159, in k order, expf), 64 queries per block; K and V tiles
+// of 64 keys staged in shared memory and read as broadcasts.
+template <int HD>
+__global__ void __launch_bounds__(64) sdpa_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                      const float* __restrict__ v, const float* __restrict__ mask,
+                                                      float* __restrict__ o, int sq, int sk, float scale) {
+  __shared__ float ks[64][HD];
+  __shared__ float vs[64][HD];
+  const int bh = blockIdx.y;
+  const int qi = blockIdx.x * 64 + threadIdx.x;
+  const float* qr = q + (static_cast<int64_t>(bh) * sq + (qi < sq ? qi : 0)) * HD;
+  float qv[HD], acc[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    qv[d] = qr[d];
+    acc[d] = 0.f;
+  }
+  float mx = -FLT_MAX, sum = 0.f;
+  const float* kb = k + static_cast<int64_t>(bh) * sk * HD;
+  const float* vb = v + static_cast<int64_t>(bh) * sk * HD;
+  for (int t0 = 0; t0 < sk; t0 += 64) {
+    const int nt = sk - t0 < 64 ? sk - t0 : 64;
+    __syncthreads();
+    for (int e = threadIdx.x; e < nt * HD; e += 64) {
+      ks[e / HD][e % HD] = kb[static_cast<int64_t>(t0) * HD + e];
+      vs[e / HD][e % HD] = vb[static_cast<int64_t>(t0) * HD + e];
+    }
+    __syncthreads();
+    for (int j = 0; j < nt; ++j) {
+      float s = 0.f;
+#pragma unroll
+      for (int d = 0; d < HD; ++d) s += qv[d] * ks[j][d];
+      s *= scale;
+      if (mask && qi < sq) s += mask[static_cast<int64_t>(qi) * sk + t0 + j];
+      if (s > mx) {
+        const float corr = expf(mx - s);
+        sum *= corr;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) acc[d] *= corr;
+        mx = s;
+      }
+      const float w = expf(s - mx);
+#pragma unroll
+      for (int d = 0; d < HD; ++d) acc[d] += w * vs[j][d];
+      sum += w;
+    }
+  }
+  if (qi < sq) {
+    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+    float* orow = o + (static_cast<int64_t>(bh) * sq + qi) * HD;
+#pragma unroll
+    for (int d = 0; d < HD; ++d) orow[d] = acc[d] * inv;
+  }
+}
+
+// NHWC im2col for CONV2D with OHWI weights (cpu_conv2d.c): row (n, oy, ox),
+// column (ky, kx, c), zero padding, K padded with zeros to kpad.
+template <int T>
+__global__ void im2col_nhwc(const void* x, void* a, int64_t n, int H, int W, int C, int kh, int kw, int stride,
+                            int pad, int OH, int OW, int kpad) {
+  GRID_LOOP(i, n) {
+    const int kcol = static_cast<int>(i % kpad);
+    const int64_t row = i / kpad;
+    const int ox = static_cast<int>(row % OW);
+    const int oy = static_cast<int>((row / OW) % OH);
+    const int64_t b = row / (static_cast<int64_t>(OW) * OH);
+    float val = 0.f;
+    if (kcol < kh * kw * C) {
+      const int c = kcol % C, kx = (kcol / C) % kw, ky = kcol / (C * kw);
+      const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+      if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+        val = ld<T>(x, ((b * H + iy) * W + ix) * C + c);
+    }
+    st<T>(a, i, val);
+  }
+}
+
+// Q8_0 blocks -> F32 (quant.c:134-151)
+__global__ void q8_dequant_kernel(const uint8_t* __restrict__ blocks, float* __restrict__ out, int64_t n) {
+  GRID_LOOP(i, n) {
+    const uint8_t* blk = blocks + (i / 32) * 36;
+    float s;
+    memcpy(&s, blk, 4);
+    out[i] = static_cast<float>(static_cast<int8_t>(blk[4 + i % 32])) * s;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int sam3cu_dev_alloc(void** p, size_t bytes) {
+  return cudaMalloc(p, bytes ? bytes : 16) == cudaSuccess ? SAM3CU_OK : SAM3CU_ENOMEM;
+}
+int sam3cu_dev_free(void* p) { return cudaFree(p) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA; }
+int sam3cu_stream_create(void** s) {
+  cudaStream_t st;
+  if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return SAM3CU_ECUDA;
+  *s = st;
+  return SAM3CU_OK;
+}
+int sam3cu_stream_destroy(void* s) { return cudaStreamDestroy(S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA; }
+int sam3cu_stream_sync(void* s) { return cudaStreamSynchronize(S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA; }
+int sam3cu_memcpy_h2d(void* dst, const void* src, size_t n, void* s) {
+  return cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA;
+}
+int sam3cu_memcpy_d2h(void* dst, const void* src, size_t n, void* s) {
+  return cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToHost, S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA;
+}
+int sam3cu_memcpy_d2d(void* dst, const void* src, size_t n, void* s) {
+  return cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToDevice, S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA;
+}
+
+int sam3cu_permute(const void* src, void* dst, int elem_size, int n_dims, const int* dims, const int* perm,
+                   void* stream) {
+  if (!src || !dst || n_dims < 1 || n_dims > 4) return SAM3CU_EINVAL;
+  int d[4] = {1, 1, 1, 1}, p[4] = {0, 1, 2, 3};
+  const int off = 4 - n_dims;
+  for (int i = 0; i < n_dims; ++i) {
+    d[off + i] = dims[i];
+    if (perm[i] < 0 || perm[i] >= n_dims) return SAM3CU_EINVAL;
+    p[off + i] = perm[i] + off;
+  }
+  int64_t istride[4];
+  istride[3] = 1;
+  for (int i = 2; i >= 0; --i) istride[i] = istride[i + 1] * d[i + 1];
+  int4 odims = make_int4(d[p[0]], d[p[1]], d[p[2]], d[p[3]]);
+  int4 istr = make_int4(static_cast<int>(istride[p[0]]), static_cast<int>(istride[p[1]]),
+                        static_cast<int>(istride[p[2]]), static_cast<int>(istride[p[3]]));
+  const int64_t n = static_cast<int64_t>(d[0]) * d[1] * d[2] * d[3];
+  if (n >= (1ll << 31)) return SAM3CU_ESHAPE;
+  count_launches(1);
+  const int g = grid_for(n, 256);
+  if (elem_size == 4) permute_kernel<uint32_t><<<g, 256, 0, S(stream)>>>(static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst), n, odims, istr);
+  else if (elem_size == 2) permute_kernel<uint16_t><<<g, 256, 0, S(stream)>>>(static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), n, odims, istr);
+  else if (elem_size == 1) permute_kernel<uint8_t><<<g, 256, 0, S(stream)>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), n, odims, istr);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_slice(const void* src, void* dst, int elem_size, int n_dims, const int* dims, int axis, int start,
+                 int end, void* stream) {
+  if (!src || !dst || n_dims < 1 || n_dims > 4 || axis < 0 || axis >= n_dims) return SAM3CU_EINVAL;
+  if (start < 0 || end > dims[axis] || start >= end) return SAM3CU_EINVAL;
+  int64_t inner = 1, outer = 1;
+  for (int i = axis + 1; i < n_dims; ++i) inner *= dims[i];
+  for (int i = 0; i < axis; ++i) outer *= dims[i];
+  const int64_t n = outer * (end - start) * inner;
+  count_launches(1);
+  const int g = grid_for(n, 256);
+  if (elem_size == 4) slice_kernel<uint32_t><<<g, 256, 0, S(stream)>>>(static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst), n, inner, end - start, dims[axis], start);
+  else if (elem_size == 2) slice_kernel<uint16_t><<<g, 256, 0, S(stream)>>>(static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), n, inner, end - start, dims[axis], start);
+  else if (elem_size == 1) slice_kernel<uint8_t><<<g, 256, 0, S(stream)>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), n, inner, end - start, dims[axis], start);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_add(const void* a, const void* b, void* out, int dtype, int64_t n, int64_t nb, void* stream) {
+  if (!a || !b || !out || n < 0 || nb <= 0 || n % nb) return SAM3CU_EINVAL;
+  if (n == 0) return SAM3CU_OK;
+  count_launches(1);
+  const int g = grid_for(n, 256);
+  if (dtype == kF32) add_kernel<kF32><<<g, 256, 0, S(stream)>>>(a, b, out, n, nb);
+  else if (dtype == kBF16) add_kernel<kBF16><<<g, 256, 0, S(stream)>>>(a, b, out, n, nb);
+  else if (dtype == kF16) add_kernel<kF16><<<g, 256, 0, S(stream)>>>(a, b, out, n, nb);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_gelu(const void* x, void* y, int dtype, int64_t n, void* stream) {
+  if (!x || !y || n < 0) return SAM3CU_EINVAL;
+  if (n == 0) return SAM3CU_OK;
+  count_launches(1);
+  const int g = grid_for(n, 256);
+  if (dtype == kF32) gelu_kernel<kF32><<<g, 256, 0, S(stream)>>>(x, y, n);
+  else if (dtype == kBF16) gelu_kernel<kBF16><<<g, 256, 0, S(stream)>>>(x, y, n);
+  else if (dtype == kF16) gelu_kernel<kF16><<<g, 256, 0, S(stream)>>>(x, y, n);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_rope(const void* x, const float* cos_t, const float* sin_t, void* y, int dtype, int batch, int seq,
+                int heads, int hd, void* stream) {
+  if (!x || !y || !cos_t || !sin_t || hd % 2 || batch <= 0 || seq <= 0 || heads <= 0) return SAM3CU_EINVAL;
+  const int64_t np = static_cast<int64_t>(batch) * seq * heads * (hd / 2);
+  count_launches(1);
+  const int g = grid_for(np, 256);
+  if (dtype == kF32) rope_kernel<kF32><<<g, 256, 0, S(stream)>>>(x, cos_t, sin_t, y, np, seq, heads, hd / 2);
+  else if (dtype == kBF16) rope_kernel<kBF16><<<g, 256, 0, S(stream)>>>(x, cos_t, sin_t, y, np, seq, heads, hd / 2);
+  else if (dtype == kF16) rope_kernel<kF16><<<g, 256, 0, S(stream)>>>(x, cos_t, sin_t, y, np, seq, heads, hd / 2);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_cast(const void* x, int xdt, void* y, int ydt, int64_t n, void* stream) {
+  if (!x || !y || n < 0) return SAM3CU_EINVAL;
+  if (n == 0) return SAM3CU_OK;
+  count_launches(1);
+  const int g = grid_for(n, 256);
+#define S3_C(A, B) if (xdt == A && ydt == B) { cast_any<A, B><<<g, 256, 0, S(stream)>>>(x, y, n); return rc_launch(); }
+  S3_C(kF32, kF32) S3_C(kF32, kBF16) S3_C(kF32, kF16) S3_C(kBF16, kF32) S3_C(kBF16, kBF16) S3_C(kBF16, kF16)
+  S3_C(kF16, kF32) S3_C(kF16, kBF16) S3_C(kF16, kF16)
+#undef S3_C
+  return SAM3CU_EDTYPE;
+}
+
+int sam3cu_sdpa_f32(const float* q, const float* k, const float* v, const float* mask, float* o, int bh, int sq,
+                    int sk, int hd, void* stream) {
+  if (!q || !k || !v || !o || bh <= 0 || sq <= 0 || sk <= 0) return SAM3CU_EINVAL;
+  dim3 grid((sq + 63) / 64, bh);
+  const float scale = 1.0f / sqrtf(static_cast<float>(hd));
+  count_launches(1);
+  if (hd == 64) sdpa_f32_kernel<64><<<grid, 64, 0, S(stream)>>>(q, k, v, mask, o, sq, sk, scale);
+  else if (hd == 32) sdpa_f32_kernel<32><<<grid, 64, 0, S(stream)>>>(q, k, v, mask, o, sq, sk, scale);
+  else return SAM3CU_ESHAPE;
+  return rc_launch();
+}
+
+int sam3cu_im2col_nhwc(const void* x, void* a, int dtype, int n, int H, int W, int C, int kh, int kw, int stride,
+                       int pad, int kpad, void* stream) {
+  if (!x || !a || stride <= 0 || kh <= 0 || kw <= 0 || kpad < kh * kw * C) return SAM3CU_EINVAL;
+  const int OH = (H + 2 * pad - kh) / stride + 1, OW = (W + 2 * pad - kw) / stride + 1;
+  if (OH <= 0 || OW <= 0) return SAM3CU_EINVAL;
+  const int64_t total = static_cast<int64_t>(n) * OH * OW * kpad;
+  count_launches(1);
+  const int g = grid_for(total, 256);
+  if (dtype == kF32) im2col_nhwc<kF32><<<g, 256, 0, S(stream)>>>(x, a, total, H, W, C, kh, kw, stride, pad, OH, OW, kpad);
+  else if (dtype == kBF16) im2col_nhwc<kBF16><<<g, 256, 0, S(stream)>>>(x, a, total, H, W, C, kh, kw, stride, pad, OH, OW, kpad);
+  else if (dtype == kF16) im2col_nhwc<kF16><<<g, 256, 0, S(stream)>>>(x, a, total, H, W, C, kh, kw, stride, pad, OH, OW, kpad);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_q8_dequantize(const void* blocks, float* out, int64_t n, void* stream) {
+  if (!blocks || !out || n <= 0) return SAM3CU_EINVAL;
+  count_launches(1);
+  q8_dequant_kernel<<<grid_for(n, 256), 256, 0, S(stream)>>>(static_cast<const uint8_t*>(blocks), out, n);
+  return rc_launch();
+}
+
+}  // extern "C"

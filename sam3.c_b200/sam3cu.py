@@ -27,7 +27,12 @@ EXPORTS = (
     "sam3cu_sdpa", "sam3cu_vit_create", "sam3cu_vit_destroy",
     "sam3cu_vit_encode", "sam3cu_vit_encode_async", "sam3cu_vit_stream",
     "sam3cu_vit_launches_per_encode", "sam3cu_vit_profile",
+    "sam3_cuda_backend_ops",
 )
+
+# sizeof(struct sam3_cuda_backend): {enum type; ops*} + int device + void *impl
+CUDA_BACKEND_SIZE = 32
+CUDA_BACKEND_TYPE = 2
 
 PROFILE_KINDS = ("gemm", "attention", "layernorm", "other")
 
@@ -67,6 +72,13 @@ def lib():
         L.sam3cu_vit_profile.argtypes = [vp, vp, i32, vp, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         _lib = L
     return _lib
+
+
+def backend_ops() -> int:
+    """Address of the struct sam3_backend_ops of the CUDA backend."""
+    f = lib().sam3_cuda_backend_ops
+    f.restype = C.c_void_p
+    return f()
 
 
 def check(rc: int, what: str = "") -> None:

@@ -51,8 +51,8 @@ def test_bad_arguments_rejected_on_host():
     L = sam3cu.lib()
     # null operands, bad dtype, bad activation: rejected before any launch
     assert L.sam3cu_linear(None, 2, None, None, None, None, 0, 4, 8, 8, 0, None) == -1
-    assert L.sam3cu_linear(C.c_void_p(16), 0, C.c_void_p(16), None, None, C.c_void_p(16), 0, 4, 8, 8, 0,
-                           None) == -6
+    assert L.sam3cu_linear(C.c_void_p(16), 3, C.c_void_p(16), None, None, C.c_void_p(16), 0, 4, 8, 8, 0,
+                           None) == -6  # I32 operands
     assert L.sam3cu_linear(C.c_void_p(16), 2, C.c_void_p(16), None, None, C.c_void_p(16), 0, 4, 8, 8, 9,
                            None) == -1
     assert L.sam3cu_sdpa(None, None, None, 0, None, 0, 2, 1, 1, 1, 64, None) == -1
