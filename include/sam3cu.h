@@ -68,6 +68,7 @@ enum sam3cu_status {
 	SAM3CU_EDEVICE   = -105, /* a device-side bounded wait gave up */
 	SAM3CU_EDTYPE2   = -106, /* unsupported dtype combination */
 	SAM3CU_ENOMEM2   = -107, /* device allocation failed */
+	SAM3CU_ESCRATCH  = -108, /* request exceeds a fixed static scratch buffer */
 };
 
 /* Activation fused into a linear's epilogue. */
@@ -194,6 +195,26 @@ SAM3CU_API int sam3cu_sdpa_f32(const float *q, const float *k, const float *v,
 SAM3CU_API int sam3cu_im2col_nhwc(const void *x, void *a, int dtype, int n, int H, int W,
 				  int C, int kh, int kw, int stride, int pad, int kpad,
 				  void *stream);
+
+/*
+ * CONV2D without any device allocation.  No counterpart in the reference:
+ * it exists for callers that cannot let a library allocate device memory
+ * (hosts that reserve all GPU memory in their own pool, fixed-budget
+ * deployments, latency-critical loops where cudaMalloc/cudaFree would
+ * synchronise the device).  Same computation as the backend's CONV2D
+ * lowering: NHWC input x [n,H,W,C], OHWI weight w [OC,kh,kw,C], groups 1,
+ * optional F32 bias [OC], output y [n,OH,OW,OC]; dtype F32, BF16 or F16
+ * (all device pointers).  The im2col column buffer lives in a static 32 MiB
+ * device array that every GPU loading the library holds until exit;
+ * requests that need more return SAM3CU_ESCRATCH (split the batch).  All
+ * calls share that array: calls that can overlap on the GPU race, so order
+ * them on one stream.  The first call on a device resolves the array's
+ * address (cudaGetSymbolAddress); make it before any stream capture.
+ */
+SAM3CU_API int sam3cu_conv2d_nhwc_noalloc(const void *x, const void *w, const float *bias,
+					  void *y, int dtype, int n, int H, int W, int C,
+					  int OC, int kh, int kw, int stride, int pad,
+					  void *stream);
 
 /* Q8_0 blocks -> F32 (sam3_q8_dequantize, quant.c:134-151). */
 SAM3CU_API int sam3cu_q8_dequantize(const void *blocks, float *out, int64_t n, void *stream);

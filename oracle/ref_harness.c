@@ -420,7 +420,7 @@ int ref_node_graph(int op, int n_in, const struct ref_tdesc *ins,
 		   int be_type)
 {
 	struct sam3_arena a;
-	if (sam3_arena_init(&a, 16ul << 20))
+	if (sam3_arena_init(&a, 512ul << 20))
 		return -2;
 	struct sam3_graph *g = calloc(1, sizeof(*g));
 	struct sam3_backend *be = make_backend(ops, be_size, be_type);

@@ -62,6 +62,7 @@ const char* sam3cu_strerror(int s) {
     case SAM3CU_EDEVICE: return "device-side wait timed out";
     case SAM3CU_EDTYPE2: return "unsupported dtype combination";
     case SAM3CU_ENOMEM2: return "device allocation failed";
+    case SAM3CU_ESCRATCH: return "request exceeds the fixed static scratch buffer";
     default: return "unknown status";
   }
 }

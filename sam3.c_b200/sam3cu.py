@@ -27,7 +27,7 @@ EXPORTS = (
     "sam3cu_sdpa", "sam3cu_vit_create", "sam3cu_vit_destroy",
     "sam3cu_vit_encode", "sam3cu_vit_encode_async", "sam3cu_vit_stream",
     "sam3cu_vit_launches_per_encode", "sam3cu_vit_profile",
-    "sam3_cuda_backend_ops",
+    "sam3_cuda_backend_ops", "sam3cu_conv2d_nhwc_noalloc",
 )
 
 # sizeof(struct sam3_cuda_backend): {enum type; ops*} + int device + void *impl
@@ -69,6 +69,7 @@ def lib():
         L.sam3cu_vit_stream.restype = vp
         L.sam3cu_vit_stream.argtypes = [vp]
         L.sam3cu_vit_launches_per_encode.argtypes = [vp, i32]
+        L.sam3cu_conv2d_nhwc_noalloc.argtypes = [vp, vp, vp, vp] + [i32] * 10 + [vp]
         L.sam3cu_vit_profile.argtypes = [vp, vp, i32, vp, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         _lib = L
     return _lib
@@ -187,6 +188,22 @@ def sdpa_packed(qkv, n_groups: int, seq: int, heads: int, head_dim: int = 64, ou
     es = qkv.element_size()
     check(lib().sam3cu_sdpa(base, base + E * es, base + 2 * E * es, three_e, _ptr(out), E,
                             dtype_code(qkv), n_groups, seq, heads, head_dim, _stream()), "sam3cu_sdpa")
+    return out
+
+
+def conv2d_nhwc_noalloc(x, w, bias=None, stride=1, pad=0, out=None):
+    """CONV2D (NHWC x OHWI, groups 1) through the entry point that allocates
+    no device memory (its column buffer is a static device array)."""
+    import torch
+    n, H, W, C = x.shape
+    OC, kh, kw, C2 = w.shape
+    assert C == C2
+    OH, OW = (H + 2 * pad - kh) // stride + 1, (W + 2 * pad - kw) // stride + 1
+    if out is None:
+        out = torch.empty((n, OH, OW, OC), dtype=x.dtype, device=x.device)
+    check(lib().sam3cu_conv2d_nhwc_noalloc(_ptr(x), _ptr(w), _f32(bias, 'bias'), _ptr(out),
+                                           dtype_code(x), n, H, W, C, OC, kh, kw, stride, pad,
+                                           _stream()), "sam3cu_conv2d_nhwc_noalloc")
     return out
 
 
