@@ -27,6 +27,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "sam3.c_b200"))
 
+import dp  # noqa: E402
 import synth  # noqa: E402
 
 CFG = synth.HIERA_L
@@ -187,9 +188,7 @@ def run_ours(args):
     dev = torch.device("cuda", local)
 
     n_total = args.images
-    per = [n_total // world + (1 if r < n_total % world else 0) for r in range(world)]
-    n_local = per[rank]
-    first = sum(per[:rank])
+    first, n_local = dp.shard_range(n_total, world, rank)
     B = min(args.batch, max(n_local, 1))
     wdt = {"bf16": sam3cu.BF16, "f16": sam3cu.F16, "q8": sam3cu.Q8_0}[args.dtype]
 
@@ -202,7 +201,7 @@ def run_ours(args):
     # this rank's images: image i of the job uses seed 100 + i
     host_imgs = torch.empty((n_local, 3, s, s), dtype=torch.float32).pin_memory()
     for i in range(n_local):
-        host_imgs[i] = torch.from_numpy(synth.images(CFG, 1, seed=100 + first + i)[0])
+        host_imgs[i] = torch.from_numpy(synth.images(CFG, 1, seed=dp.image_seed(first + i))[0])
     host_out = torch.empty((B, np_, e), dtype=torch.float32).pin_memory()
     dev_imgs = host_imgs.to(dev)
     dev_out = torch.empty((B, np_, e), dtype=torch.float32, device=dev)
@@ -230,10 +229,7 @@ def run_ours(args):
             fn()
         b.record(stream)
         torch.cuda.synchronize()
-        ms = torch.tensor([a.elapsed_time(b)], device=dev)
-        if world > 1:
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        return float(ms.item())
+        return dp.max_over_ranks(a.elapsed_time(b), device=dev)
 
     for _ in range(args.warmup):
         step_device()
