@@ -49,9 +49,11 @@ constexpr int kD = 64;                   // head dim
 constexpr int kTile = kQ * kD * 2;       // 16 KiB (Q, K or V tile)
 constexpr int kPBytes = kQ * kKV * 2;    // 32 KiB
 constexpr int kSmem = kTile * 5 + kPBytes;  // Q | K0 V0 | K1 V1 | P = 112 KiB
-constexpr int kTmemCols = 256;           // S: 0..127, O: 128..191
-constexpr int kThreads = 192;
+constexpr int kTmemCols = 256;           // S: 0..127, O: 128..191, exchange: 192..193
+constexpr int kThreads = 320;          // 2 control + 8 softmax warps
+constexpr int kHalf = kKV / 2;           // columns per softmax warp
 constexpr float kRescaleLog2 = 8.0f;     // lazy rescale threshold (x256)
+constexpr int kFmaExp = 0;               // of every 8 exponentials, this many on the FMA pipe
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf) {
   if (bf) {
@@ -68,6 +70,41 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, so part of the exponentials leave the SFU: Cody-Waite
+// range reduction x = n + f, n = round(x) obtained by adding 1.5*2^23, f in
+// [-1/2, 1/2]; 2^f from a degree-3 polynomial fitted here to minimax
+// relative error on that interval (max 7.5e-5, below the 2^-9 rounding of
+// the 16-bit P it feeds); 2^n added to the exponent field.  x >= -126.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.0f);
+  const float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float t = x + kMagic;
+  const float f = x - (t - kMagic);
+  float p = fmaf(0.055171653628349304f, f, 0.2426111400127411f);
+  p = fmaf(p, f, 0.6932609677314758f);
+  p = fmaf(p, f, 0.9999280571937561f);
+  const int n = __float_as_int(t) - __float_as_int(kMagic);
+  return __int_as_float(__float_as_int(p) + (n << 23));
+}
+
+// Swap one float per row with the warp holding the other column half of
+// the same rows (TMEM column tX + half, then read tX + (half ^ 1)).  The two
+// named-barrier passes order the store before the partner's load and the
+// load before the next store.
+__device__ __forceinline__ float pair_exchange(uint32_t tX, uint32_t lane_off, int half, float v, int quarter) {
+  tmem_st_32x32b_x1(tX + lane_off + half, __float_as_uint(v));
+  tmem_st_wait();
+  tc_fence_before();
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+  tc_fence_after();
+  const float other = __uint_as_float(tmem_ld_32x32b_x1(tX + lane_off + (half ^ 1)));
+  tmem_ld_wait();
+  tc_fence_before();
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+  tc_fence_after();
+  return other;
+}
+
 // Bounded wait by lane 0, verdict broadcast to the warp.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsigned err, volatile int* abort_flag,
                                           int lane) {
@@ -76,10 +113,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsign
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// Two CTAs of 6 warps per SM put 3 warps on each SM sub-partition, whose
-// register file holds 16K entries: 168 registers per thread at most.
+// Two CTAs of 10 warps per SM: 5 warps per SM sub-partition, whose
+// register file holds 16K entries: about 100 registers per thread.
 template <bool kBf16>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(320, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, uint16_t* __restrict__ o, int64_t ldo, int seq,
                    int q_tiles, float scale_log2) {
@@ -107,8 +144,8 @@ __global__ void __launch_bounds__(192, 2)
     return;
   }
   uint8_t* sQ = smem;
-  uint8_t* sK[2] = {smem + kTile, smem + 3 * kTile};
-  uint8_t* sV[2] = {smem + 2 * kTile, smem + 4 * kTile};
+  auto sK = [&](int st) { return smem + (1 + 2 * st) * kTile; };
+  auto sV = [&](int st) { return smem + (2 + 2 * st) * kTile; };
   uint8_t* sP = smem + 5 * kTile;
 
   if (threadIdx.x == 0) {
@@ -118,8 +155,8 @@ __global__ void __launch_bounds__(192, 2)
       mbar_init(&kv_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_empty, 4);
-    mbar_init(p_full, 4);
+    mbar_init(s_empty, 8);
+    mbar_init(p_full, 8);
     mbar_init(p_empty, 1);
     mbar_init(o_full, 1);
     abort_flag_s = 0;
@@ -133,7 +170,7 @@ __global__ void __launch_bounds__(192, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tS = tmem, tO = tmem + 128, tX = tmem + 192;  // tX: 2 exchange columns
 
   if (warp == 0) {
     // TMA producer (one thread)
@@ -147,8 +184,8 @@ __global__ void __launch_bounds__(192, 2)
         const int st = j & 1;
         if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, kErrStageFree, abort_flag)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
-        tma_load_2d(sK[st], &tk, &kv_full[st], head * kD, row0 + j * kKV);
-        tma_load_2d(sV[st], &tv, &kv_full[st], head * kD, row0 + j * kKV);
+        tma_load_2d(sK(st), &tk, &kv_full[st], head * kD, row0 + j * kKV);
+        tma_load_2d(sV(st), &tv, &kv_full[st], head * kD, row0 + j * kKV);
       }
     }
   } else if (warp == 1) {
@@ -168,7 +205,7 @@ __global__ void __launch_bounds__(192, 2)
         if (!mbar_wait(&kv_full[st], (j >> 1) & 1, kErrTmaWait, abort_flag)) return false;
         if (!mbar_wait(s_empty, (j & 1) ^ 1, kErrAccFree, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t kdesc = make_sdesc_sw128(smem_u32(sK[st]));
+        const uint64_t kdesc = make_sdesc_sw128(smem_u32(sK(st)));
         const uint32_t idesc_s = make_idesc(fmt, kQ, keys_in(j));
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) umma_ss<0>(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
@@ -182,7 +219,7 @@ __global__ void __launch_bounds__(192, 2)
         if (!mbar_wait(p_full, j & 1, kErrAccFull, abort_flag)) break;
         tc_fence_after();
         const int st = j & 1, n = keys_in(j);
-        const uint32_t vbase = smem_u32(sV[st]), pbase = smem_u32(sP);
+        const uint32_t vbase = smem_u32(sV(st)), pbase = smem_u32(sP);
         for (int kk = 0; kk < n / 16; ++kk) {
           const uint64_t pdesc = make_sdesc_sw128(pbase + (kk >> 2) * 16384 + (kk & 3) * 32);
           const uint64_t vdesc = make_sdesc_sw128_mn(vbase + kk * 2048);
@@ -195,73 +232,73 @@ __global__ void __launch_bounds__(192, 2)
     }
   } else {
     // ------------------------------------------------ softmax + epilogue
+    // warp w: TMEM lane quarter w % 4 (hardware rule), column half (w-2)/4
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t scol = half * kHalf;  // first S column / key of this warp
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       if (!warp_wait(s_full, j & 1, kErrAccFull, abort_flag, lane)) { ok = false; break; }
       tc_fence_after();
-      // S row -> registers, then S is free for the next Q K^T
-      const int kb = j * kKV;
-      float sv[kKV];
+      // this warp's 64 S columns -> registers, then release S
+      const int kb = j * kKV + scol;
+      uint32_t su[kHalf];  // S bits, loaded in place
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(tS + lane_off + c * 32, u);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[i]);
-      }
+      for (int c = 0; c < kHalf / 32; ++c)
+        tmem_ld_32x32b_x32(tS + lane_off + scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
       tmem_ld_wait();
+      float* sv = reinterpret_cast<float*>(su);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_empty);
-      if (kb + kKV > seq) {  // ragged last tile: keys >= seq do not exist
+      if (kb + kHalf > seq) {  // ragged last tile: keys >= seq do not exist
 #pragma unroll
-        for (int c = 0; c < kKV; ++c)
+        for (int c = 0; c < kHalf; ++c)
           if (kb + c >= seq) sv[c] = -INFINITY;
       }
-      // row max with 8 independent chains (a single chain is 128 dependent ops)
       float m8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) m8[i] = sv[i];
 #pragma unroll
-      for (int c = 8; c < kKV; ++c) m8[c & 7] = fmaxf(m8[c & 7], sv[c]);
-      const float mt = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      for (int c = 8; c < kHalf; ++c) m8[c & 7] = fmaxf(m8[c & 7], sv[c]);
+      float mt = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      // combine with the other half of the row: exchange through TMEM
+      // column 192 + half (same lane quarter), named barrier of the 2 warps
+      mt = fmaxf(mt, pair_exchange(tX, lane_off, half, mt, quarter));
       const bool need = (mt - m_used) * scale_log2 > kRescaleLog2;
       // P buffer and O are free once the previous P.V finished
       if (j > 0 && !warp_wait(p_empty, (j - 1) & 1, kErrAccFree, abort_flag, lane)) { ok = false; break; }
       tc_fence_after();
-      if (__any_sync(0xffffffffu, need)) {
+      if (__any_sync(0xffffffffu, need)) {  // same rows, same verdict in both halves
         const float m_new = fmaxf(m_used, mt);
         const float corr = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * scale_log2);
         l *= corr;
         m_used = m_new;
-        if (j > 0) {
+        if (j > 0) {  // this half rescales O columns [32*half, 32*half+32)
+          uint32_t u[32];
+          tmem_ld_32x32b_x32(tO + lane_off + half * 32, u);
+          tmem_ld_wait();
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t u[32];
-            tmem_ld_32x32b_x32(tO + lane_off + c * 32, u);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
-            tmem_st_32x32b_x32(tO + lane_off + c * 32, u);
-          }
+          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
+          tmem_st_32x32b_x32(tO + lane_off + half * 32, u);
           tmem_st_wait();
         }
       }
-      // P = exp2(S*c - m) -> 16-bit, 128-byte-swizzled K-major rows
+      // P = exp2(S*c - m) -> 16-bit into swizzle block `half` of this row
       const float mb = m_used * scale_log2;
-      uint8_t* prow = sP + r * 128;
+      uint8_t* prow = sP + half * 16384 + r * 128;
       float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c8 = 0; c8 < kKV / 8; ++c8) {  // 16-byte chunks of 8 keys
+      for (int cc = 0; cc < kHalf / 8; ++cc) {  // 16-byte chunks of 8 keys
         float p[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          p[i] = ex2(fmaf(sv[c8 * 8 + i], scale_log2, -mb));
+          const float e = fmaf(sv[cc * 8 + i], scale_log2, -mb);
+          p[i] = i < kFmaExp ? exp2_fma(e) : ex2(e);  // split SFU / FMA pipe
           l8[i] += p[i];
         }
         uint4 w;
@@ -269,8 +306,7 @@ __global__ void __launch_bounds__(192, 2)
         w.y = pack2(p[2], p[3], kBf16);
         w.z = pack2(p[4], p[5], kBf16);
         w.w = pack2(p[6], p[7], kBf16);
-        const int blk = c8 >> 3, cc = c8 & 7;
-        *reinterpret_cast<uint4*>(prow + blk * 16384 + ((cc ^ (r & 7)) << 4)) = w;
+        *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) = w;
       }
       l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
       fence_proxy_async_smem();
@@ -278,26 +314,25 @@ __global__ void __launch_bounds__(192, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
+    // row sums of the two halves
+    l += pair_exchange(tX, lane_off, half, l, quarter);
     if (ok && warp_wait(o_full, 0, kErrAccFull, abort_flag, lane)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int qrow = qt * kQ + r;
-      uint16_t* orow = o + static_cast<int64_t>(row0 + qrow) * ldo + head * kD;
+      uint16_t* orow = o + static_cast<int64_t>(row0 + qrow) * ldo + head * kD + half * 32;
+      uint32_t u[32];
+      tmem_ld_32x32b_x32(tO + lane_off + half * 32, u);
+      tmem_ld_wait();
+      if (qrow < seq) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(tO + lane_off + c * 32, u);
-        tmem_ld_wait();
-        if (qrow < seq) {
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint4 w;
-            w.x = pack2(__uint_as_float(u[q4 * 8 + 0]) * inv, __uint_as_float(u[q4 * 8 + 1]) * inv, kBf16);
-            w.y = pack2(__uint_as_float(u[q4 * 8 + 2]) * inv, __uint_as_float(u[q4 * 8 + 3]) * inv, kBf16);
-            w.z = pack2(__uint_as_float(u[q4 * 8 + 4]) * inv, __uint_as_float(u[q4 * 8 + 5]) * inv, kBf16);
-            w.w = pack2(__uint_as_float(u[q4 * 8 + 6]) * inv, __uint_as_float(u[q4 * 8 + 7]) * inv, kBf16);
-            *reinterpret_cast<uint4*>(orow + c * 32 + q4 * 8) = w;
-          }
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 w;
+          w.x = pack2(__uint_as_float(u[q4 * 8 + 0]) * inv, __uint_as_float(u[q4 * 8 + 1]) * inv, kBf16);
+          w.y = pack2(__uint_as_float(u[q4 * 8 + 2]) * inv, __uint_as_float(u[q4 * 8 + 3]) * inv, kBf16);
+          w.z = pack2(__uint_as_float(u[q4 * 8 + 4]) * inv, __uint_as_float(u[q4 * 8 + 5]) * inv, kBf16);
+          w.w = pack2(__uint_as_float(u[q4 * 8 + 6]) * inv, __uint_as_float(u[q4 * 8 + 7]) * inv, kBf16);
+          *reinterpret_cast<uint4*>(orow + q4 * 8) = w;
         }
       }
     }
