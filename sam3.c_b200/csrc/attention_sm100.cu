@@ -259,13 +259,10 @@ __global__ void __launch_bounds__(320, 2)
         for (int c = 0; c < kHalf; ++c)
           if (kb + c >= seq) sv[c] = -INFINITY;
       }
-      float m8[8];
+      float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = sv[i];
-#pragma unroll
-      for (int c = 8; c < kHalf; ++c) m8[c & 7] = fmaxf(m8[c & 7], sv[c]);
-      float mt = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      for (int c = 4; c < kHalf; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
+      float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       // combine with the other half of the row: exchange through TMEM
       // column 192 + half (same lane quarter), named barrier of the 2 warps
       mt = fmaxf(mt, pair_exchange(tX, lane_off, half, mt, quarter));
@@ -279,28 +276,31 @@ __global__ void __launch_bounds__(320, 2)
         l *= corr;
         m_used = m_new;
         if (j > 0) {  // this half rescales O columns [32*half, 32*half+32)
-          uint32_t u[32];
-          tmem_ld_32x32b_x32(tO + lane_off + half * 32, u);
-          tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
-          tmem_st_32x32b_x32(tO + lane_off + half * 32, u);
+          for (int c = 0; c < 4; ++c) {  // 8 columns at a time: few live registers
+            uint32_t u[8];
+            tmem_ld_32x32b_x8(tO + lane_off + half * 32 + c * 8, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
+            tmem_st_32x32b_x8(tO + lane_off + half * 32 + c * 8, u);
+          }
           tmem_st_wait();
         }
       }
       // P = exp2(S*c - m) -> 16-bit into swizzle block `half` of this row
       const float mb = m_used * scale_log2;
       uint8_t* prow = sP + half * 16384 + r * 128;
-      float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int cc = 0; cc < kHalf / 8; ++cc) {  // 16-byte chunks of 8 keys
-        float p[8];
+      for (int cc = 0; cc < kHalf / 8; ++cc) {  // 16-byte chunks of 8 keys, exps in place
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float e = fmaf(sv[cc * 8 + i], scale_log2, -mb);
-          p[i] = i < kFmaExp ? exp2_fma(e) : ex2(e);  // split SFU / FMA pipe
-          l8[i] += p[i];
+          sv[cc * 8 + i] = i < kFmaExp ? exp2_fma(e) : ex2(e);  // split SFU / FMA pipe
+          l4[i & 3] += sv[cc * 8 + i];
         }
+        const float* p = sv + cc * 8;
         uint4 w;
         w.x = pack2(p[0], p[1], kBf16);
         w.y = pack2(p[2], p[3], kBf16);
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(320, 2)
         w.w = pack2(p[6], p[7], kBf16);
         *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) = w;
       }
-      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
