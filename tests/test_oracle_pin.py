@@ -135,3 +135,17 @@ def test_vit_forward_vs_reference():
     w = synth.vit_weights(cfg, seed=3)
     img = synth.images(cfg, 1, seed=4)[0]
     assert rel_err(O.vit_forward(cfg, w, img), O.ref_vit_encode(cfg, w, img)) < 1e-5
+
+
+def test_oracle_vit_vs_reference_golden_fixture():
+    """The restated full forward at 1008 px (8 blocks, one global) against
+    the committed outputs of the reference sam3_vit_build (~1 min)."""
+    import os
+    import synth
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "vit_1008_depth8.npz"))
+    cfg = dict(zip(("img_size", "patch_size", "embed_dim", "depth", "n_heads", "window_size", "mlp_dim"),
+                   (int(v) for v in g["cfg"])))
+    w = synth.vit_weights(cfg, seed=int(g["seeds"][0]))
+    img = synth.images(cfg, 1, seed=int(g["seeds"][1]))[0]
+    y = O.vit_forward(cfg, w, img).ravel()
+    assert rel_err(y[g["idx"]], g["f32_sample"]) < 1e-5
