@@ -69,8 +69,9 @@ const char* sam3cu_strerror(int s) {
 
 unsigned int sam3cu_last_device_error(void) {
   cudaDeviceSynchronize();
-  unsigned int a = dev_error_gemm(), b = dev_error_attn(), c = dev_error_misc(), d = dev_error_attn_tc();
-  return a ? a : (b ? b : (c ? c : d));
+  unsigned int a = dev_error_gemm(), b = dev_error_attn(), c = dev_error_misc(), d = dev_error_attn_tc(),
+               e = dev_error_gemm2();
+  return a ? a : (b ? b : (c ? c : (d ? d : e)));
 }
 
 uint64_t sam3cu_launch_count(int reset) {

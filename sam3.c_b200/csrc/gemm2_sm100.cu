@@ -1,0 +1,240 @@
+// gemm2_sm100.cu - the 16-bit linear on CTA pairs (tcgen05 cta_group::2).
+//
+// Same contract and fused epilogue as gemm_kernel<kBTma16> (gemm_sm100.cu),
+// but every output tile is 256 x 256 and is computed by a pair of CTAs on
+// two SMs (a cluster of 2):
+//   * each CTA TMA-loads its own 128 rows of A and its own 128 rows (N) of
+//     W into its shared memory; the transaction bytes of both CTAs count on
+//     the leader's (cluster rank 0) barrier;
+//   * the leader's MMA thread issues tcgen05.mma.cta_group::2 256x256x16:
+//     A rows and W halves are read from both CTAs' shared memory at the
+//     same offsets, each CTA's TMEM receives its 128 rows x 256 columns;
+//   * commits release the stage / accumulator in both CTAs.
+// Per SM this halves the W bytes that shared memory must deliver per MMA
+// (the reason a 1-SM 128x256 tile cannot run the tensor core at its rate),
+// and with 32 KiB stages the ring is 6 deep.  No multicast loads are used.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "gemm_epilogue.cuh"
+#include "gemm_sm100.cuh"
+#include "sam3cu_internal.h"
+#include "tma_host.cuh"
+
+namespace s3 {
+
+S3_DEV_ERROR_ACCESSOR(dev_error_gemm2)
+
+namespace {
+
+constexpr int kPM = 128;                 // rows per CTA (256 per pair)
+constexpr int kPN = 256;                 // output columns per tile
+constexpr int kPK = 64;
+constexpr int kPStages = 6;
+constexpr int kPTile = kPM * kPK * 2;    // 16 KiB: A tile or W half-tile
+constexpr int kPStage = 2 * kPTile;
+constexpr int kPEpiWarps = 8;
+constexpr int kPThreads = 64 + kPEpiWarps * 32;
+constexpr int kPOut = 32 * 32 * 4;
+constexpr int kPSmem = kPStages * kPStage + kPEpiWarps * kPOut + 1024 + 256;
+constexpr int kPTmemCols = 2 * kPN;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                 const __grid_constant__ CUtensorMap tmap_o, GemmShape shp, EpiParams ep, uint32_t idesc,
+                 int epi_mode) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_out = smem + kPStages * kPStage;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(stage_out + kPEpiWarps * kPOut);
+  uint64_t* empty_bar = full_bar + kPStages;
+  uint64_t* accf_bar = empty_bar + kPStages;  // [2]
+  uint64_t* acce_bar = accf_bar + 2;          // [2] (leader's counts both CTAs)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int m_tiles = (shp.M + 2 * kPM - 1) / (2 * kPM);
+  const int n_tiles = (shp.N + kPN - 1) / kPN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_iters = (shp.K + kPK - 1) / kPK;
+  auto stage_a = [&](int s) { return smem + s * kPStage; };
+  auto stage_b = [&](int s) { return smem + s * kPStage + kPTile; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf_bar[a], 1);
+      mbar_init(&acce_bar[a], 2 * kPEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kPTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers and TMEM exist before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs): own A rows, own W half
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_a);
+      tma_prefetch_desc(&tmap_b);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int m0 = (tile / n_tiles) * 2 * kPM + rank * kPM;
+        const int n0 = (tile % n_tiles) * kPN + rank * (kPN / 2);
+        for (int kt = 0; kt < k_iters; ++kt, ++it) {
+          const int s = it % kPStages;
+          const uint32_t ph = (it / kPStages) & 1;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kPStage);  // both CTAs' bytes
+          const uint32_t lead_full = mapa_shared(smem_u32(&full_bar[s]), 0);
+          tma_load_2d_pair(stage_a(s), &tmap_a, lead_full, kt * kPK, m0);
+          tma_load_2d_pair(stage_b(s), &tmap_b, lead_full, kt * kPK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: the pair leader only
+    if (lane == 0 && rank == 0) {
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&acce_bar[acc], aph ^ 1, kErrAccFree, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kPN;
+        for (int kt = 0; kt < k_iters; ++kt, ++it) {
+          const int s = it % kPStages;
+          const uint32_t ph = (it / kPStages) & 1;
+          if (!mbar_wait(&full_bar[s], ph, kErrTmaWait, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = make_sdesc_sw128(smem_u32(stage_a(s)));
+          const uint64_t bdesc = make_sdesc_sw128(smem_u32(stage_b(s)));
+#pragma unroll
+          for (int k = 0; k < kPK / kUmmaK; ++k)
+            umma_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+          // free the stage in both CTAs once these MMAs have read it
+          umma_commit_pair(mapa_shared(smem_u32(&empty_bar[s]), 0));
+          umma_commit_pair(mapa_shared(smem_u32(&empty_bar[s]), 1));
+        }
+        if (ok) {
+          umma_commit_pair(mapa_shared(smem_u32(&accf_bar[acc]), 0));
+          umma_commit_pair(mapa_shared(smem_u32(&accf_bar[acc]), 1));
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows
+    const int quarter = warp & 3;
+    constexpr int kChunks = kPN / 32 / (kPEpiWarps / 4);
+    const int half = (warp - 2) / 4;
+    uint8_t* my_stage = stage_out + (warp - 2) * kPOut;
+    const uint32_t lead_acce0 = mapa_shared(smem_u32(&acce_bar[0]), 0);
+    const uint32_t lead_acce1 = mapa_shared(smem_u32(&acce_bar[1]), 0);
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
+      const int m0 = (tile / n_tiles) * 2 * kPM + rank * kPM;
+      const int n0 = (tile % n_tiles) * kPN;
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      int got = 0;
+      if (lane == 0) got = mbar_wait(&accf_bar[acc], aph, kErrAccFull, abort_flag) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
+      tc_fence_after();
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kPN;
+#pragma unroll 1
+      for (int cc = 0; cc < kChunks; ++cc) {
+        const int c = half * kChunks + cc;
+        const int col0 = n0 + c * 32;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (col0 >= shp.N) continue;  // warp-uniform
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (epi_mode == kEpiDirect) {
+          if (row < shp.M) {
+            epilogue_math(ep, v, row, col0, shp.N);
+            epilogue_store_direct(ep, v, row, col0, shp.N);
+          }
+        } else {
+          epilogue_math(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N);
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+          stage_chunk(my_stage, v, lane, epi_mode == kEpiTmaAdd ? kOutF32 : ep.out_type);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (epi_mode == kEpiTmaAdd)
+              tma_reduce_add_2d(&tmap_o, my_stage, col0, m0 + quarter * 32);
+            else
+              tma_store_2d(&tmap_o, my_stage, col0, m0 + quarter * 32);
+            bulk_commit();
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(&acce_bar[acc]);
+        else
+          mbar_arrive_cluster(acc ? lead_acce1 : lead_acce0);
+      }
+    }
+    if (lane == 0) bulk_wait<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kPTmemCols);
+  }
+}
+
+}  // namespace
+
+// Pair launch of the 16-bit linear; the caller has validated shapes and
+// alignment (launch_gemm).  Returns kOk, kErrTma or kErrLaunch.
+int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, GemmShape shp, const EpiParams& ep,
+                     const CUtensorMap& to, int mode, cudaStream_t stream, int max_ctas) {
+  const CUtensorMapDataType dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, A, dt, 2, shp.M, shp.K, lda, kPM, kPK, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
+  if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, kPN / 2, kPK, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
+  const int m_tiles = (shp.M + 2 * kPM - 1) / (2 * kPM), n_tiles = (shp.N + kPN - 1) / kPN;
+  int pairs = m_tiles * n_tiles;
+  const int cap = (max_ctas > 0 ? max_ctas : num_sms()) / 2;
+  if (pairs > cap) pairs = cap;
+  const uint32_t idesc = make_idesc(bf ? 1u : 0u, 2 * kPM, kPN);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
+    attr = true;
+  }
+  gemm2_kernel<<<2 * pairs, kPThreads, kPSmem, stream>>>(ta, tb, to, shp, ep, idesc, mode);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+}  // namespace s3

@@ -6,8 +6,10 @@
 
 #include <atomic>
 #include <cstring>
+#include <cstdlib>
 
 #include "gemm_sm100.cuh"
+#include "gemm_epilogue.cuh"
 #include "sam3cu_internal.h"
 #include "tma_host.cuh"
 
@@ -16,172 +18,6 @@ namespace s3 {
 S3_DEV_ERROR_ACCESSOR(dev_error_gemm)
 
 namespace {
-
-__device__ __forceinline__ float gelu_tanh(float x) {
-  // 0.5*x*(1+tanh(sqrt(2/pi)*(x+0.044715x^3))), cpu_gelu.c:23-36
-  float inner = 0.7978845608f * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(inner));
-}
-
-// Same formula with the SFU's tanh.approx.f32 (max relative error about
-// 2^-11, below the 2^-9 rounding of the 16-bit outputs it is used for).
-__device__ __forceinline__ float gelu_tanh_fast(float x) {
-  float inner = 0.7978845608f * (x + 0.044715f * x * x * x);
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
-  return 0.5f * x * (1.0f + t);
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
-  __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// Bias, activation and RoPE on 32 consecutive columns [col0, col0+32) of
-// one output row, in registers.
-__device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32], int row, int col0,
-                                              int N) {
-  const bool full = col0 + 32 <= N;
-  if (ep.bias) {
-    if (full) {
-      const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float4 b = __ldg(b4 + j);
-        v[4 * j] += b.x;
-        v[4 * j + 1] += b.y;
-        v[4 * j + 2] += b.z;
-        v[4 * j + 3] += b.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) v[j] += __ldg(ep.bias + col0 + j);
-    }
-  }
-  if (ep.act == 1) {
-    if (ep.out_type == kOutF32) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_fast(v[j]);
-    }
-  }
-  if (col0 < ep.rope_cols) {
-    int p = row % ep.rope_period;
-    if (ep.rope_pos) p = __ldg(ep.rope_pos + p);
-    const int d0 = (col0 & 63) >> 1;  // first pair index within the head
-    const float* cs = ep.rope_cos + p * 32 + d0;
-    const float* sn = ep.rope_sin + p * 32 + d0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float c = __ldg(cs + i), s = __ldg(sn + i);
-      float x0 = v[2 * i], x1 = v[2 * i + 1];
-      v[2 * i] = x0 * c - x1 * s;
-      v[2 * i + 1] = x0 * s + x1 * c;
-    }
-  }
-}
-
-// Residual add and per-thread store of the same 32 columns (kEpiDirect).
-__device__ __forceinline__ void epilogue_store_direct(const EpiParams& ep, float (&v)[32], int row,
-                                                      int col0, int N) {
-  const bool full = col0 + 32 <= N;
-  if (ep.residual) {
-    int rr = ep.res_row_period > 0 ? row % ep.res_row_period : row;
-    const float* r = ep.residual + static_cast<int64_t>(rr) * ep.ldr + col0;
-    if (full) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float4 x = *reinterpret_cast<const float4*>(r + 4 * j);
-        v[4 * j] += x.x;
-        v[4 * j + 1] += x.y;
-        v[4 * j + 2] += x.z;
-        v[4 * j + 3] += x.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) v[j] += r[j];
-    }
-  }
-  int orow = row;
-  if (ep.out_row_map) {
-    int per = ep.out_row_period;
-    orow = (row / per) * per + __ldg(ep.out_row_map + row % per);
-  }
-  const int64_t off = static_cast<int64_t>(orow) * ep.ldo + col0;
-  if (ep.out_type == kOutF32) {
-    float* o = static_cast<float*>(ep.out) + off;
-    if (full) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        reinterpret_cast<float4*>(o)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else {
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) o[j] = v[j];
-    }
-  } else {
-    const bool bf = ep.out_type == kOutBF16;
-    uint16_t* o = static_cast<uint16_t*>(ep.out) + off;
-    if (full) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint4 w;
-        w.x = bf ? pack_bf16(v[8 * j], v[8 * j + 1]) : pack_f16(v[8 * j], v[8 * j + 1]);
-        w.y = bf ? pack_bf16(v[8 * j + 2], v[8 * j + 3]) : pack_f16(v[8 * j + 2], v[8 * j + 3]);
-        w.z = bf ? pack_bf16(v[8 * j + 4], v[8 * j + 5]) : pack_f16(v[8 * j + 4], v[8 * j + 5]);
-        w.w = bf ? pack_bf16(v[8 * j + 6], v[8 * j + 7]) : pack_f16(v[8 * j + 6], v[8 * j + 7]);
-        reinterpret_cast<uint4*>(o)[j] = w;
-      }
-    } else {
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) {
-          uint16_t h;
-          if (bf) {
-            __nv_bfloat16 t = __float2bfloat16_rn(v[j]);
-            h = *reinterpret_cast<uint16_t*>(&t);
-          } else {
-            __half t = __float2half_rn(v[j]);
-            h = *reinterpret_cast<uint16_t*>(&t);
-          }
-          o[j] = h;
-        }
-    }
-  }
-}
-
-// Write one thread's 32 values (row `lane` of a 32x32 chunk) into the
-// warp's staging buffer in the layout of the output tensor map: f32 rows of
-// 128 B with the 128-byte swizzle, or 16-bit rows of 64 B with the 64-byte
-// swizzle (16-byte chunk c of row r lands at c ^ (r & 7), resp.
-// c ^ ((r >> 1) & 3)), which keeps the 16-byte stores bank-conflict free.
-__device__ __forceinline__ void stage_chunk(uint8_t* buf, const float (&v)[32], int lane, int out_type) {
-  if (out_type == kOutF32) {
-    uint8_t* rowp = buf + lane * 128;
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-      *reinterpret_cast<float4*>(rowp + ((c ^ (lane & 7)) << 4)) =
-          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-  } else {
-    const bool bf = out_type == kOutBF16;
-    uint8_t* rowp = buf + lane * 64;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint4 w;
-      w.x = bf ? pack_bf16(v[8 * c], v[8 * c + 1]) : pack_f16(v[8 * c], v[8 * c + 1]);
-      w.y = bf ? pack_bf16(v[8 * c + 2], v[8 * c + 3]) : pack_f16(v[8 * c + 2], v[8 * c + 3]);
-      w.z = bf ? pack_bf16(v[8 * c + 4], v[8 * c + 5]) : pack_f16(v[8 * c + 4], v[8 * c + 5]);
-      w.w = bf ? pack_bf16(v[8 * c + 6], v[8 * c + 7]) : pack_f16(v[8 * c + 6], v[8 * c + 7]);
-      *reinterpret_cast<uint4*>(rowp + ((c ^ ((lane >> 1) & 3)) << 4)) = w;
-    }
-  }
-}
 
 // Split the F32 A and W tiles of one stage (16 KiB + 32 KiB, contiguous
 // at `hi`) in place into hi = x & ~0x1fff (a TF32 value) and lo = x - hi,
@@ -455,6 +291,18 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
 }
 
 int g_num_sms = 0;
+
+// 2-SM pair tiles (gemm2_sm100.cu) for the 16-bit path unless SAM3CU_GEMM=1sm
+// or the problem is too small to keep the SMs busy with 256x256 tiles.
+bool use_pair_gemm(const GemmShape& shp) {
+  static const int mode = [] {
+    const char* e = getenv("SAM3CU_GEMM");
+    return e && strcmp(e, "1sm") == 0 ? 0 : 1;
+  }();
+  if (!mode) return false;
+  const long pairs = static_cast<long>((shp.M + 255) / 256) * ((shp.N + 255) / 256);
+  return pairs >= num_sms();  // at least two waves of pairs
+}
 std::atomic<uint64_t> g_launches{0};
 
 }  // namespace
@@ -523,6 +371,10 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       mode = kEpiDirect;  // e.g. an output base that is not 16-byte aligned
   }
   count_launches(1);
+  if (!q8 && !f32in && use_pair_gemm(shp)) {
+    if (ldw % 8 != 0) return kErrShape;
+    return launch_gemm_pair(A, lda, W, ldw, bf, shp, ep, to, mode, stream, max_ctas);
+  }
   if (q8) {
     if (shp.K % 64 != 0) return kErrShape;
     if (!make_tmap_2d(&tb, q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, shp.N, shp.K, shp.K, kBN, kBK,

@@ -33,6 +33,7 @@
 //            and the MMA warp issues hi.hi + hi.lo + lo.hi with
 //            kind::tf32, an F32 product to about 2^-22 relative.
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -106,5 +107,9 @@ struct GemmCfg {
   static constexpr int kSmemBytes =
       kStages * kStageBytes + kEpiWarps * kStageOutBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
+
+// 2-SM pair launch (gemm2_sm100.cu); shapes validated by launch_gemm.
+int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, GemmShape shp, const EpiParams& ep,
+                     const CUtensorMap& to, int mode, cudaStream_t stream, int max_ctas);
 
 }  // namespace s3

@@ -33,6 +33,7 @@ unsigned int dev_error_misc();
 int launch_attention_tc(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,
                         int n_groups, int seq, int heads, int head_dim, cudaStream_t st);
 unsigned int dev_error_attn_tc();
+unsigned int dev_error_gemm2();
 int launch_attention(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,
                      int n_groups, int seq, int heads, int head_dim, cudaStream_t st);
 int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8, const float* q8_scales,
