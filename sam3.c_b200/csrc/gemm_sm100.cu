@@ -42,9 +42,23 @@ __device__ __forceinline__ void split_tf32_tile(uint8_t* hi, uint8_t* lo, int t)
   }
 }
 
+// float(q) for the 4 signed bytes of `raw`, without int->float conversion
+// instructions (they issue at a quarter rate): each byte, offset by 128,
+// is permuted into the low mantissa byte of 2^23 and 2^23 + 128 is
+// subtracted; exact for every int8.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t raw, float (&f)[4]) {
+  const uint32_t u = raw ^ 0x80808080u;  // b + 128 as unsigned bytes
+  f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
+  f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
+  f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
+  f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+}
+
 // Dequantise one k-tile of Q8 W (int8 [kBN rows x 64] + scales [2][kBN]) to
-// 16-bit values in the 128-byte-swizzled K-major layout the MMA reads.
-// 128 threads; thread t handles 16-byte chunk (t & 7) of rows (t>>3)+16i.
+// 16-bit values in the 128-byte-swizzled K-major layout the MMA reads:
+// value = float(q) * scale rounded to nearest even (as sam3_q8_dequantize
+// then an RNE cast).  128 threads; thread t handles 16-byte chunk (t & 7)
+// of rows (t>>3)+16i.
 template <bool kBf16>
 __device__ __forceinline__ void q8_dequant_tile(const int8_t* q, const float* sc, uint8_t* dst,
                                                 int t) {
@@ -54,18 +68,22 @@ __device__ __forceinline__ void q8_dequant_tile(const int8_t* q, const float* sc
     const int n = (t >> 3) + 16 * i;
     const uint2 raw = *reinterpret_cast<const uint2*>(q + n * kBK + c * 8);
     const float s = sc[(c >> 2) * kBN + n];
-    const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+    float f[8];
+    i8x4_to_f32(raw.x, *reinterpret_cast<float(*)[4]>(f));
+    i8x4_to_f32(raw.y, *reinterpret_cast<float(*)[4]>(f + 4));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) f[k] *= s;
     uint4 w;
-    if (kBf16) {
-      w.x = pack_bf16(b[0] * s, b[1] * s);
-      w.y = pack_bf16(b[2] * s, b[3] * s);
-      w.z = pack_bf16(b[4] * s, b[5] * s);
-      w.w = pack_bf16(b[6] * s, b[7] * s);
+    if (kBf16) {  // one cvt.rn.bf16x2.f32 per pair (integer rounding would load the ALU pipe)
+      w.x = pack_bf16(f[0], f[1]);
+      w.y = pack_bf16(f[2], f[3]);
+      w.z = pack_bf16(f[4], f[5]);
+      w.w = pack_bf16(f[6], f[7]);
     } else {
-      w.x = pack_f16(b[0] * s, b[1] * s);
-      w.y = pack_f16(b[2] * s, b[3] * s);
-      w.z = pack_f16(b[4] * s, b[5] * s);
-      w.w = pack_f16(b[6] * s, b[7] * s);
+      w.x = pack_f16(f[0], f[1]);
+      w.y = pack_f16(f[2], f[3]);
+      w.z = pack_f16(f[4], f[5]);
+      w.w = pack_f16(f[6], f[7]);
     }
     *reinterpret_cast<uint4*>(dst + n * 128 + ((c ^ (n & 7)) << 4)) = w;
   }
@@ -80,11 +98,13 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stage_out = smem + S * Cfg::kStageBytes;  // kEpiWarps x 4 KiB
+  uint8_t* bring = smem + S * Cfg::kStageBytes;                  // Q8: dequantised W ring
+  uint8_t* stage_out = bring + Cfg::kBRing * kBTileBytes;       // kEpiWarps x 4 KiB
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(stage_out + Cfg::kEpiWarps * Cfg::kStageOutBytes);
   uint64_t* empty_bar = full_bar + S;
-  uint64_t* conv_bar = empty_bar + S;   // Q8: dequantised tile ready
-  uint64_t* accf_bar = conv_bar + S;    // [2] accumulator committed
+  uint64_t* conv_bar = empty_bar + S;   // F32: stage split; Q8: [2] ring slot ready
+  uint64_t* bemp_bar = conv_bar + S;    // Q8: [2] ring slot consumed by the MMAs
+  uint64_t* accf_bar = bemp_bar + 2;    // [2] accumulator committed
   uint64_t* acce_bar = accf_bar + 2;    // [2] accumulator drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -103,6 +123,7 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
       mbar_init(&empty_bar[s], 1);
       mbar_init(&conv_bar[s], 128);
     }
+    for (int b = 0; b < 2; ++b) mbar_init(&bemp_bar[b], 1);
     for (int a = 0; a < 2; ++a) {
       mbar_init(&accf_bar[a], 1);
       mbar_init(&acce_bar[a], Cfg::kEpiWarps);
@@ -120,11 +141,14 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   auto stage_a = [&](int s) { return smem + s * Cfg::kStageBytes; };
+  // W operand of k-iteration `it`: in the stage, or (Q8) in ring slot it & 1
   auto stage_b = [&](int s) { return smem + s * Cfg::kStageBytes + kATileBytes; };
-  auto stage_q = [&](int s) { return smem + s * Cfg::kStageBytes + kATileBytes + kBTileBytes; };
-  auto stage_sc = [&](int s) {
-    return smem + s * Cfg::kStageBytes + kATileBytes + kBTileBytes + kQ8TileBytes;
+  auto ring_b = [&](uint32_t it) { return bring + (it & 1) * kBTileBytes; };
+  // F32: lo half of the stage; Q8: int8 tile and scales
+  auto stage_q = [&](int s) {
+    return smem + s * Cfg::kStageBytes + kATileBytes + (kBMode == kBQ8 ? 0 : kBTileBytes);
   };
+  auto stage_sc = [&](int s) { return smem + s * Cfg::kStageBytes + kATileBytes + kQ8TileBytes; };
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -169,11 +193,12 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
         for (int kt = 0; kt < k_iters; ++kt, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
-          uint64_t* ready = Cfg::kConv ? &conv_bar[s] : &full_bar[s];
-          if (!mbar_wait(ready, ph, kErrTmaWait, abort_flag)) { ok = false; break; }
+          uint64_t* ready = kBMode == kBQ8 ? &conv_bar[it & 1] : (Cfg::kConv ? &conv_bar[s] : &full_bar[s]);
+          const uint32_t rph = kBMode == kBQ8 ? (it >> 1) & 1 : ph;
+          if (!mbar_wait(ready, rph, kErrTmaWait, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = make_sdesc_sw128(smem_u32(stage_a(s)));
-          const uint64_t bdesc = make_sdesc_sw128(smem_u32(stage_b(s)));
+          const uint64_t bdesc = make_sdesc_sw128(smem_u32(kBMode == kBQ8 ? ring_b(it) : stage_b(s)));
           if constexpr (kBMode == kBF32) {
             // 3xTF32: lo terms first, hi.hi last; 8 TF32 = 32 bytes per MMA
             const uint64_t aldesc = make_sdesc_sw128(smem_u32(stage_q(s)));
@@ -192,6 +217,7 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
             }
           }
           umma_commit(&empty_bar[s]);  // frees the smem stage when these MMAs finish
+          if (kBMode == kBQ8) umma_commit(&bemp_bar[it & 1]);  // and the ring slot
         }
         if (ok) umma_commit(&accf_bar[acc]);
       }
@@ -268,16 +294,20 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
         if (!mbar_wait(&full_bar[s], ph, kErrTmaWait, abort_flag)) { ok = false; break; }
         if constexpr (kBMode == kBF32) {
           split_tf32_tile(stage_a(s), stage_q(s), t);
+          fence_proxy_async_smem();  // make generic-proxy writes visible to tcgen05
+          mbar_arrive(&conv_bar[s]);
         } else {
+          // ring slot free once the MMAs of iteration it - 2 finished
+          if (!mbar_wait(&bemp_bar[it & 1], ((it >> 1) & 1) ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
           const int8_t* q = reinterpret_cast<const int8_t*>(stage_q(s));
           const float* sc = reinterpret_cast<const float*>(stage_sc(s));
           if (b_is_bf16)
-            q8_dequant_tile<true>(q, sc, stage_b(s), t);
+            q8_dequant_tile<true>(q, sc, ring_b(it), t);
           else
-            q8_dequant_tile<false>(q, sc, stage_b(s), t);
+            q8_dequant_tile<false>(q, sc, ring_b(it), t);
+          fence_proxy_async_smem();  // make generic-proxy writes visible to tcgen05
+          mbar_arrive(&conv_bar[it & 1]);
         }
-        fence_proxy_async_smem();  // make generic-proxy writes visible to tcgen05
-        mbar_arrive(&conv_bar[s]);
       }
     }
   }

@@ -81,7 +81,7 @@ constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;          // 64 x 16-bit = 128 B rows (SWIZZLE_128B)
 constexpr int kStages16 = 4;      // smem ring depth, 16-bit W
-constexpr int kStagesQ8 = 3;      // smem ring depth, Q8 W (bigger stages)
+constexpr int kStagesQ8 = 4;      // smem ring depth, Q8 W (A + int8 + scales per stage)
 constexpr int kUmmaK = 16;
 constexpr int kATileBytes = kBM * kBK * 2;   // 16 KiB
 constexpr int kBTileBytes = kBN * kBK * 2;   // 32 KiB
@@ -99,13 +99,16 @@ struct GemmCfg {
   // K elements per stage (always 128-byte operand rows) and per MMA
   static constexpr int kBKe = kBMode == kBF32 ? 32 : 64;
   static constexpr int kUmmaKe = kBMode == kBF32 ? 8 : 16;
-  // F32 stage: A_hi | W_hi | A_lo | W_lo (same byte sizes as the 16-bit tiles)
+  // 16-bit stage: A | W.  F32 stage: A_hi | W_hi | A_lo | W_lo.  Q8 stage:
+  // A | int8 W | scales (34 KiB); the dequantised 16-bit W tiles live in a
+  // separate 2-deep ring so conversion is decoupled from the TMA ring.
   static constexpr int kStageBytes =
-      kATileBytes + kBTileBytes +
-      (kBMode == kBQ8 ? kQ8TileBytes + kQ8ScaleBytes : (kBMode == kBF32 ? kATileBytes + kBTileBytes : 0));
+      kBMode == kBQ8 ? kATileBytes + kQ8TileBytes + kQ8ScaleBytes
+                     : kATileBytes + kBTileBytes + (kBMode == kBF32 ? kATileBytes + kBTileBytes : 0);
+  static constexpr int kBRing = kBMode == kBQ8 ? 2 : 0;
   static constexpr int kStageOutBytes = 32 * 32 * 4;  // per epilogue warp: one 32x32 chunk
-  static constexpr int kSmemBytes =
-      kStages * kStageBytes + kEpiWarps * kStageOutBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBRing * kBTileBytes + kEpiWarps * kStageOutBytes +
+                                    1024 /*align*/ + 256 /*barriers*/;
 };
 
 // 2-SM pair launch (gemm2_sm100.cu); shapes validated by launch_gemm.
