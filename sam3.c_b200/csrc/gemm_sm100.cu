@@ -57,15 +57,15 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t raw, float (&f)[4]) {
 // Dequantise one k-tile of Q8 W (int8 [kBN rows x 64] + scales [2][kBN]) to
 // 16-bit values in the 128-byte-swizzled K-major layout the MMA reads:
 // value = float(q) * scale rounded to nearest even (as sam3_q8_dequantize
-// then an RNE cast).  128 threads; thread t handles 16-byte chunk (t & 7)
-// of rows (t>>3)+16i.
-template <bool kBf16>
+// then an RNE cast).  kT threads; thread t handles 16-byte chunk (t & 7)
+// of rows (t>>3)+(kT/8)i for kT threads.
+template <bool kBf16, int kT>
 __device__ __forceinline__ void q8_dequant_tile(const int8_t* q, const float* sc, uint8_t* dst,
                                                 int t) {
   const int c = t & 7;
 #pragma unroll 4
-  for (int i = 0; i < kBN / 16; ++i) {
-    const int n = (t >> 3) + 16 * i;
+  for (int i = 0; i < kBN / (kT / 8); ++i) {
+    const int n = (t >> 3) + (kT / 8) * i;
     const uint2 raw = *reinterpret_cast<const uint2*>(q + n * kBK + c * 8);
     const float s = sc[(c >> 2) * kBN + n];
     float f[8];
@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
-      mbar_init(&conv_bar[s], 128);
+      mbar_init(&conv_bar[s], Cfg::kConvThreads);
     }
     for (int b = 0; b < 2; ++b) mbar_init(&bemp_bar[b], 1);
     for (int a = 0; a < 2; ++a) {
@@ -302,9 +302,9 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
           const int8_t* q = reinterpret_cast<const int8_t*>(stage_q(s));
           const float* sc = reinterpret_cast<const float*>(stage_sc(s));
           if (b_is_bf16)
-            q8_dequant_tile<true>(q, sc, ring_b(it), t);
+            q8_dequant_tile<true, Cfg::kConvThreads>(q, sc, ring_b(it), t);
           else
-            q8_dequant_tile<false>(q, sc, ring_b(it), t);
+            q8_dequant_tile<false, Cfg::kConvThreads>(q, sc, ring_b(it), t);
           fence_proxy_async_smem();  // make generic-proxy writes visible to tcgen05
           mbar_arrive(&conv_bar[it & 1]);
         }

@@ -94,7 +94,8 @@ struct GemmCfg {
   // 16-bit W: 2 + 8 epilogue warps; Q8 W: 2 + 4 epilogue + 4 converter warps
   static constexpr bool kConv = kBMode != kBTma16;  // converter warps present
   static constexpr int kEpiWarps = kConv ? 4 : 8;
-  static constexpr int kThreads = 64 + kEpiWarps * 32 + (kConv ? 128 : 0);
+  static constexpr int kConvThreads = kBMode == kBQ8 ? 256 : (kConv ? 128 : 0);
+  static constexpr int kThreads = 64 + kEpiWarps * 32 + kConvThreads;
   static constexpr int kStages = kBMode == kBQ8 ? kStagesQ8 : (kBMode == kBF32 ? 2 : kStages16);
   // K elements per stage (always 128-byte operand rows) and per MMA
   static constexpr int kBKe = kBMode == kBF32 ? 32 : 64;
