@@ -66,17 +66,14 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32
     }
   }
   if (col0 < ep.rope_cols) {
-    int p = row % ep.rope_period;
-    if (ep.rope_pos) p = __ldg(ep.rope_pos + p);
-    const int d0 = (col0 & 63) >> 1;  // first pair index within the head
-    const float* cs = ep.rope_cos + p * 32 + d0;
-    const float* sn = ep.rope_sin + p * 32 + d0;
+    const int p = row % ep.rope_period;
+    const float2* cs = ep.rope_cs + static_cast<int64_t>((col0 & 63) >> 1) * ep.rope_period + p;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      float c = __ldg(cs + i), s = __ldg(sn + i);
-      float x0 = v[2 * i], x1 = v[2 * i + 1];
-      v[2 * i] = x0 * c - x1 * s;
-      v[2 * i + 1] = x0 * s + x1 * c;
+      const float2 t = __ldg(cs + static_cast<int64_t>(i) * ep.rope_period);
+      const float x0 = v[2 * i], x1 = v[2 * i + 1];
+      v[2 * i] = x0 * t.x - x1 * t.y;
+      v[2 * i + 1] = x0 * t.y + x1 * t.x;
     }
   }
 }

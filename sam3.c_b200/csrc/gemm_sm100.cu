@@ -360,7 +360,7 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
   if (shp.M <= 0 || shp.N <= 0 || shp.K <= 0) return 0;
   // TMA: 16-byte row pitch
   if (f32in ? (shp.K % 4 != 0 || lda % 4 != 0) : (shp.K % 8 != 0 || lda % 8 != 0)) return kErrShape;
-  if (ep.rope_cols > 0 && (ep.rope_period <= 0 || !ep.rope_cos || !ep.rope_sin)) return kErrShape;
+  if (ep.rope_cols > 0 && (ep.rope_period <= 0 || !ep.rope_cs)) return kErrShape;
   if (ep.out_row_map && ep.out_row_period <= 0) return kErrShape;
   // vector epilogue stores/loads: 16-byte aligned rows
   if (ep.ldo % (ep.out_type == kOutF32 ? 4 : 8) != 0) return kErrShape;

@@ -62,12 +62,13 @@ struct EpiParams {
   int ldr;
   int res_row_period;    // >0: residual row = row % period (pos-embed tiling)
   // RoPE on output columns [0, rope_cols): interleaved pairs within 64-wide
-  // heads rotated by cos/sin[pos, 32] (cpu_rope.c:35-110).
-  const float* rope_cos;
-  const float* rope_sin;
+  // heads rotated by (cos, sin) of row p = row % rope_period
+  // (cpu_rope.c:35-110).  The table is pair-major, rope_cs[d * period + p]
+  // for pair d in [0, 32), so that the 32 lanes of a warp (32 consecutive
+  // rows) read one contiguous 256-byte run per pair.
+  const float2* rope_cs;
   int rope_cols;
-  int rope_period;       // position index p = row % rope_period
-  const int* rope_pos;   // optional: position = rope_pos[p]
+  int rope_period;
   // Output row remap: stored row = (row / period) * period + map[row % period]
   const int* out_row_map;
   int out_row_period;

@@ -85,7 +85,7 @@ struct sam3cu_vit {
   s3::Block blocks[s3::kMaxLayers];
   s3::Linear patch;
   s3::DevBuf ln_pre_w, ln_pre_b, pos_win;        // pos_win: tiled pos-embed [np, e] f32, window order
-  s3::DevBuf rope_win_cos, rope_win_sin, rope_glo_cos, rope_glo_sin;
+  s3::DevBuf rope_win, rope_glo;  // float2 (cos, sin), pair-major: [32][positions]
   s3::DevBuf win_to_raster;                      // int [np]
   s3::DevBuf raster_to_win;                      // int [np]
   std::vector<int> graph_nodes;                  // kernel nodes per captured graph
@@ -223,13 +223,10 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
       ep.bias = B.qkv.bias.as<float>();
       ep.rope_cols = 2 * e;
       if (glob) {
-        ep.rope_cos = v->rope_glo_cos.as<float>();
-        ep.rope_sin = v->rope_glo_sin.as<float>();
+        ep.rope_cs = v->rope_glo.as<float2>();
         ep.rope_period = np;
-        ep.rope_pos = w2r;
       } else {
-        ep.rope_cos = v->rope_win_cos.as<float>();
-        ep.rope_sin = v->rope_win_sin.as<float>();
+        ep.rope_cs = v->rope_win.as<float2>();
         ep.rope_period = ws * ws;
       }
       if ((rc = run_linear(v, B.qkv, v->xn.p, e, M, ep))) return rc;
@@ -335,12 +332,25 @@ int vit_setup(sam3cu_vit* v, const sam3cu_vit_weights* w) {
   if ((rc = ck(cudaStreamSynchronize(st)))) return rc;
   // RoPE tables: window-local (scale 1) and global (scale ws/gs)
   std::vector<float> cs, sn;
+  // Epilogue layout: (cos, sin) pairs, pair-major, indexed by the GEMM row
+  // (window-local slot, resp. the window-major token index of a global block).
+  const int half = e / c.n_heads / 2;
+  std::vector<float> tab;
+  auto pair_major = [&](int n, const int* row_pos) {
+    tab.assign(static_cast<size_t>(half) * n * 2, 0.f);
+    for (int d = 0; d < half; ++d)
+      for (int r = 0; r < n; ++r) {
+        const int p = row_pos ? row_pos[r] : r;
+        tab[(static_cast<size_t>(d) * n + r) * 2] = cs[static_cast<size_t>(p) * half + d];
+        tab[(static_cast<size_t>(d) * n + r) * 2 + 1] = sn[static_cast<size_t>(p) * half + d];
+      }
+  };
   host_rope_table(ws * ws, ws, e / c.n_heads, 1.0f, cs, sn);
-  if ((rc = upload_f32(v->rope_win_cos, cs.data(), cs.size(), st))) return rc;
-  if ((rc = upload_f32(v->rope_win_sin, sn.data(), sn.size(), st))) return rc;
+  pair_major(ws * ws, nullptr);
+  if ((rc = upload_f32(v->rope_win, tab.data(), tab.size(), st))) return rc;
   host_rope_table(np, gs, e / c.n_heads, static_cast<float>(ws) / static_cast<float>(gs), cs, sn);
-  if ((rc = upload_f32(v->rope_glo_cos, cs.data(), cs.size(), st))) return rc;
-  if ((rc = upload_f32(v->rope_glo_sin, sn.data(), sn.size(), st))) return rc;
+  pair_major(np, w2r.data());
+  if ((rc = upload_f32(v->rope_glo, tab.data(), tab.size(), st))) return rc;
   if ((rc = cudaStreamSynchronize(st) == cudaSuccess ? kOk : kErrCuda)) return rc;
   // tiled pos-embed in window order (tile_pos_embed, image_encoder.c:167-218)
   {
