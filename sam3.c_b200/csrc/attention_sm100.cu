@@ -7,17 +7,26 @@
 // fifth-generation tensor cores:
 //
 //   S_j   = Q K_j^T          tcgen05.mma 128x128x64 -> TMEM (128 columns)
-//   P_j   = exp2(S_j*c - m)  softmax warps: one thread per query row
-//   O    += P_j V_j          tcgen05.mma 128x64x128, A = P from shared memory,
+//   P_j   = exp2(S_j*c - m)  softmax warps: one thread per query row, P
+//                            packed to 16-bit pairs in TMEM (64 columns)
+//   O    += P_j V_j          tcgen05.mma 128x64x128, A = P from TMEM,
 //                            B = V as stored (MN-major), accumulator in TMEM
 //
-// CTA = 6 warps, two CTAs per SM (112 KiB smem, 256 TMEM columns and
-// 192 threads x 168 registers each):
-//   warp 0     TMA (Q tile once, K_j / V_j through a 2-stage ring);
+// Keeping P in TMEM leaves shared memory to Q and the K/V ring: per 128-key
+// tile the tensor cores read 48 KiB of operands from shared memory (Q, K,
+// V) instead of 80 KiB plus the 32 KiB P store, and shared-memory bandwidth
+// is what limits a head_dim-64 tile.
+//
+// CTA = 10 warps, two CTAs per SM (112 KiB smem, 256 TMEM columns and
+// 320 threads x 96 registers each):
+//   warp 0     TMA (Q tile once, K_j / V_j through a 3-stage ring);
 //              allocates TMEM
 //   warp 1     MMA issue (one thread)
-//   warps 2-5  softmax and the output epilogue; warp w owns TMEM lane
-//              quarter w % 4, i.e. query rows 32*(w%4) .. +31
+//   warps 2-9  softmax and the output epilogue; warp w owns TMEM lane
+//              quarter w % 4, i.e. query rows 32*(w%4) .. +31, and key
+//              half (w-2)/4 of every tile: it reads the whole S row for the
+//              row maximum, exponentiates its 64 keys and writes their P;
+//              the two warps of a quarter add their row sums at the end
 // A softmax thread copies its S row to registers and releases S at once,
 // so S_{j+1} = Q K_{j+1}^T runs on the tensor cores during the softmax of
 // tile j; the two CTAs of an SM interleave on the exponential units.
@@ -47,13 +56,20 @@ constexpr int kQ = 128;                  // query rows per CTA
 constexpr int kKV = 128;                 // keys per tile
 constexpr int kD = 64;                   // head dim
 constexpr int kTile = kQ * kD * 2;       // 16 KiB (Q, K or V tile)
-constexpr int kPBytes = kQ * kKV * 2;    // 32 KiB
-constexpr int kSmem = kTile * 5 + kPBytes;  // Q | K0 V0 | K1 V1 | P = 112 KiB
-constexpr int kTmemCols = 256;           // S: 0..127, O: 128..191, exchange: 192..193
+#ifndef S3_ATTN_STAGES
+#define S3_ATTN_STAGES 3
+#endif
+constexpr int kStages = S3_ATTN_STAGES;  // K/V ring depth
+constexpr int kSmem = kTile * (1 + 2 * kStages);  // Q | K0 V0 | K1 V1 | ...
+constexpr int kTmemCols = 256;           // S: 0..127, O: 128..191, P: 192..255
 constexpr int kThreads = 320;          // 2 control + 8 softmax warps
 constexpr int kHalf = kKV / 2;           // columns per softmax warp
 constexpr float kRescaleLog2 = 8.0f;     // lazy rescale threshold (x256)
-constexpr int kFmaExp = 0;               // of every 8 exponentials, this many on the FMA pipe
+#ifndef S3_ATTN_FMA_EXP
+#define S3_ATTN_FMA_EXP 0
+#endif
+constexpr int kFmaExp = S3_ATTN_FMA_EXP;  // of every 8 exponentials, this many on the FMA pipe
+
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf) {
   if (bf) {
@@ -88,7 +104,8 @@ __device__ __forceinline__ float exp2_fma(float x) {
 }
 
 // Swap one float per row with the warp holding the other column half of
-// the same rows (TMEM column tX + half, then read tX + (half ^ 1)).  The two
+// the same rows (TMEM column tX + half, then read tX + (half ^ 1)); tX is
+// any two free columns.  The two
 // named-barrier passes order the store before the partner's load and the
 // load before the next store.
 __device__ __forceinline__ float pair_exchange(uint32_t tX, uint32_t lane_off, int half, float v, int quarter) {
@@ -121,17 +138,17 @@ __global__ void __launch_bounds__(320, 2)
                    const __grid_constant__ CUtensorMap tv, uint16_t* __restrict__ o, int64_t ldo, int seq,
                    int q_tiles, float scale_log2) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ uint64_t bars[12];
+  __shared__ uint64_t bars[8 + 2 * kStages];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag_s;
   uint64_t* q_full = &bars[0];
-  uint64_t* kv_full = &bars[1];   // [2]
-  uint64_t* kv_empty = &bars[3];  // [2]
-  uint64_t* s_full = &bars[5];
-  uint64_t* s_empty = &bars[6];
-  uint64_t* p_full = &bars[7];
-  uint64_t* p_empty = &bars[8];
-  uint64_t* o_full = &bars[9];
+  uint64_t* s_full = &bars[1];
+  uint64_t* s_empty = &bars[2];
+  uint64_t* p_full = &bars[3];
+  uint64_t* p_empty = &bars[4];
+  uint64_t* o_full = &bars[5];
+  uint64_t* kv_full = &bars[6];              // [kStages]
+  uint64_t* kv_empty = &bars[6 + kStages];   // [kStages]
   volatile int* abort_flag = &abort_flag_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -146,11 +163,10 @@ __global__ void __launch_bounds__(320, 2)
   uint8_t* sQ = smem;
   auto sK = [&](int st) { return smem + (1 + 2 * st) * kTile; };
   auto sV = [&](int st) { return smem + (2 + 2 * st) * kTile; };
-  uint8_t* sP = smem + 5 * kTile;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
@@ -170,7 +186,7 @@ __global__ void __launch_bounds__(320, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128, tX = tmem + 192;  // tX: 2 exchange columns
+  const uint32_t tS = tmem, tO = tmem + 128, tP = tmem + 192;
 
   if (warp == 0) {
     // TMA producer (one thread)
@@ -181,8 +197,8 @@ __global__ void __launch_bounds__(320, 2)
       mbar_arrive_expect_tx(q_full, kTile);
       tma_load_2d(sQ, &tq, q_full, head * kD, row0 + qt * kQ);
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, kErrStageFree, abort_flag)) break;
+        const int st = j % kStages;
+        if (!mbar_wait(&kv_empty[st], ((j / kStages) & 1) ^ 1, kErrStageFree, abort_flag)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
         tma_load_2d(sK(st), &tk, &kv_full[st], head * kD, row0 + j * kKV);
         tma_load_2d(sV(st), &tv, &kv_full[st], head * kD, row0 + j * kKV);
@@ -201,8 +217,8 @@ __global__ void __launch_bounds__(320, 2)
       };
       // S_j = Q K_j^T into TMEM once K_j landed and the softmax read S_{j-1}
       auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, kErrTmaWait, abort_flag)) return false;
+        const int st = j % kStages;
+        if (!mbar_wait(&kv_full[st], (j / kStages) & 1, kErrTmaWait, abort_flag)) return false;
         if (!mbar_wait(s_empty, (j & 1) ^ 1, kErrAccFree, abort_flag)) return false;
         tc_fence_after();
         const uint64_t kdesc = make_sdesc_sw128(smem_u32(sK(st)));
@@ -218,12 +234,11 @@ __global__ void __launch_bounds__(320, 2)
         if (j + 1 < n_kv && !issue_s(j + 1)) break;
         if (!mbar_wait(p_full, j & 1, kErrAccFull, abort_flag)) break;
         tc_fence_after();
-        const int st = j & 1, n = keys_in(j);
-        const uint32_t vbase = smem_u32(sV(st)), pbase = smem_u32(sP);
-        for (int kk = 0; kk < n / 16; ++kk) {
-          const uint64_t pdesc = make_sdesc_sw128(pbase + (kk >> 2) * 16384 + (kk & 3) * 32);
+        const int st = j % kStages, n = keys_in(j);
+        const uint32_t vbase = smem_u32(sV(st));
+        for (int kk = 0; kk < n / 16; ++kk) {  // A = P from TMEM: 16 keys = 8 columns
           const uint64_t vdesc = make_sdesc_sw128_mn(vbase + kk * 2048);
-          umma_ss<0>(tO, pdesc, vdesc, idesc_pv, (j | kk) ? 1u : 0u);
+          umma_ts(tO, tP + kk * 8, vdesc, idesc_pv, (j | kk) ? 1u : 0u);
         }
         umma_commit(p_empty);
         umma_commit(&kv_empty[st]);
@@ -239,33 +254,60 @@ __global__ void __launch_bounds__(320, 2)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t scol = half * kHalf;  // first S column / key of this warp
     float m_used = -INFINITY, l = 0.f;
+    // A warp whose 32 query rows all lie past the group end (the last query
+    // tile of a 576-token window) only keeps the barrier protocol going.
+    const bool rows_live = qt * kQ + quarter * 32 < seq;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       if (!warp_wait(s_full, j & 1, kErrAccFull, abort_flag, lane)) { ok = false; break; }
       tc_fence_after();
-      // this warp's 64 S columns -> registers, then release S
       const int kb = j * kKV + scol;
+      // keys of this half exist (the ragged last tile of a window has none
+      // in its upper half; P.V then reads only the lower half of P)
+      const bool live = rows_live && kb < seq;
       uint32_t su[kHalf];  // S bits, loaded in place
-#pragma unroll
-      for (int c = 0; c < kHalf / 32; ++c)
-        tmem_ld_32x32b_x32(tS + lane_off + scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
-      tmem_ld_wait();
       float* sv = reinterpret_cast<float*>(su);
+      float mt = -INFINITY;
+      if (rows_live) {
+        // maximum of the other key half first (its values are discarded)
+        const int kbo = j * kKV + (scol ^ kHalf);
+        if (kbo < seq) {
+#pragma unroll
+          for (int c = 0; c < kHalf / 32; ++c)
+            tmem_ld_32x32b_x32(tS + lane_off + (scol ^ kHalf) + c * 32,
+                               *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
+          tmem_ld_wait();
+          if (kbo + kHalf > seq) {
+#pragma unroll
+            for (int c = 0; c < kHalf; ++c)
+              if (kbo + c >= seq) sv[c] = -INFINITY;
+          }
+          float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+          for (int c = 4; c < kHalf; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
+          mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        }
+      }
+      if (live) {  // this warp's 64 S columns -> registers
+#pragma unroll
+        for (int c = 0; c < kHalf / 32; ++c)
+          tmem_ld_32x32b_x32(tS + lane_off + scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
+        tmem_ld_wait();
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty);
-      if (kb + kHalf > seq) {  // ragged last tile: keys >= seq do not exist
+      if (lane == 0) mbar_arrive(s_empty);  // S may be overwritten
+      if (live) {
+        if (kb + kHalf > seq) {  // ragged last tile: keys >= seq do not exist
 #pragma unroll
-        for (int c = 0; c < kHalf; ++c)
-          if (kb + c >= seq) sv[c] = -INFINITY;
+          for (int c = 0; c < kHalf; ++c)
+            if (kb + c >= seq) sv[c] = -INFINITY;
+        }
+        float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+        for (int c = 4; c < kHalf; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
+        mt = fmaxf(mt, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
       }
-      float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
-#pragma unroll
-      for (int c = 4; c < kHalf; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
-      float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      // combine with the other half of the row: exchange through TMEM
-      // column 192 + half (same lane quarter), named barrier of the 2 warps
-      mt = fmaxf(mt, pair_exchange(tX, lane_off, half, mt, quarter));
       const bool need = (mt - m_used) * scale_log2 > kRescaleLog2;
       // P buffer and O are free once the previous P.V finished
       if (j > 0 && !warp_wait(p_empty, (j - 1) & 1, kErrAccFree, abort_flag, lane)) { ok = false; break; }
@@ -288,36 +330,37 @@ __global__ void __launch_bounds__(320, 2)
           tmem_st_wait();
         }
       }
-      // P = exp2(S*c - m) -> 16-bit into swizzle block `half` of this row
-      const float mb = m_used * scale_log2;
-      uint8_t* prow = sP + half * 16384 + r * 128;
-      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+      // P = exp2(S*c - m) -> 16-bit pairs into TMEM columns 192 + 32*half
+      if (live) {
+        const float mb = m_used * scale_log2;
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int cc = 0; cc < kHalf / 8; ++cc) {  // 16-byte chunks of 8 keys, exps in place
+        for (int c0 = 0; c0 < kHalf; c0 += 16) {  // 16 keys -> 8 columns at a time: few live registers
+          uint32_t pk[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float e = fmaf(sv[cc * 8 + i], scale_log2, -mb);
-          sv[cc * 8 + i] = i < kFmaExp ? exp2_fma(e) : ex2(e);  // split SFU / FMA pipe
-          l4[i & 3] += sv[cc * 8 + i];
+          for (int c = c0; c < c0 + 16; c += 2) {
+            const float e0 = fmaf(sv[c], scale_log2, -mb), e1 = fmaf(sv[c + 1], scale_log2, -mb);
+            const float p0 = (c & 7) < kFmaExp ? exp2_fma(e0) : ex2(e0);  // split SFU / FMA pipe
+            const float p1 = ((c + 1) & 7) < kFmaExp ? exp2_fma(e1) : ex2(e1);
+            l4[c & 3] += p0;
+            l4[(c + 1) & 3] += p1;
+            pk[(c - c0) / 2] = pack2(p0, p1, kBf16);
+          }
+          tmem_st_32x32b_x8(tP + lane_off + half * (kHalf / 2) + c0 / 2, pk);
         }
-        const float* p = sv + cc * 8;
-        uint4 w;
-        w.x = pack2(p[0], p[1], kBf16);
-        w.y = pack2(p[2], p[3], kBf16);
-        w.z = pack2(p[4], p[5], kBf16);
-        w.w = pack2(p[6], p[7], kBf16);
-        *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) = w;
+        l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+        tmem_st_wait();
       }
-      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // row sums of the two halves
-    l += pair_exchange(tX, lane_off, half, l, quarter);
-    if (ok && warp_wait(o_full, 0, kErrAccFull, abort_flag, lane)) {
-      tc_fence_after();
+    // all MMAs done: O complete, S columns free for the row-sum exchange
+    // (both warps of a quarter reach the exchange, also after an abort)
+    const bool o_ok = ok && warp_wait(o_full, 0, kErrAccFull, abort_flag, lane);
+    tc_fence_after();
+    if (rows_live) l += pair_exchange(tS, lane_off, half, l, quarter);
+    if (o_ok) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int qrow = qt * kQ + r;
       uint16_t* orow = o + static_cast<int64_t>(row0 + qrow) * ldo + head * kD + half * 32;
