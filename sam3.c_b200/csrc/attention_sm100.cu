@@ -103,6 +103,68 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
+// Two f32 lanes in one 64-bit register for the packed f32x2 operations.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// exp2_fma (below) on two lanes with packed f32x2 arithmetic.
+__device__ __forceinline__ void exp2_fma_x2(uint64_t x2, float& y0, float& y1) {
+  float x0, x1;
+  f2unpack(x2, x0, x1);
+  x2 = f2pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t magic = f2pack(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+  const uint64_t t = fadd2(x2, magic);
+  const uint64_t f = fsub2(x2, fsub2(t, magic));
+  uint64_t p = ffma2(f2pack(0.055171653628349304f, 0.055171653628349304f), f,
+                     f2pack(0.2426111400127411f, 0.2426111400127411f));
+  p = ffma2(p, f, f2pack(0.6932609677314758f, 0.6932609677314758f));
+  p = ffma2(p, f, f2pack(0.9999280571937561f, 0.9999280571937561f));
+  float p0, p1, t0, t1;
+  f2unpack(p, p0, p1);
+  f2unpack(t, t0, t1);
+  // 2^n into the exponent field: bits(p) + (bits(t) - bits(magic)) * 2^23
+  y0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(t0) - 0x4B400000) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(t1) - 0x4B400000) << 23));
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Maximum of 64 values: four chains of three-input max.
+__device__ __forceinline__ float max64(const float* v) {
+  float m[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+  for (int c = 4; c < 64; c += 8) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) m[k] = max3(m[k], v[c + 2 * k], v[c + 2 * k + 1]);
+  }
+  return fmaxf(max3(m[0], m[1], m[2]), m[3]);
+}
+
 // Swap one float per row with the warp holding the other column half of
 // the same rows (TMEM column tX + half, then read tX + (half ^ 1)); tX is
 // any two free columns.  The two
@@ -205,46 +267,49 @@ __global__ void __launch_bounds__(320, 2)
       }
     }
   } else if (warp == 1) {
-    // MMA issuer (one thread)
-    if (lane == 0) {
-      const uint32_t fmt = kBf16 ? 1u : 0u;
-      const uint32_t idesc_pv = make_idesc(fmt, kQ, kD, 1u);
-      bool ok = mbar_wait(q_full, 0, kErrTmaWait, abort_flag);
-      const uint64_t qdesc = make_sdesc_sw128(smem_u32(sQ));
-      auto keys_in = [&](int j) {  // keys of tile j, rounded up to a multiple of 16
-        const int left = seq - j * kKV;
-        return left >= kKV ? kKV : ((left + 15) & ~15);
-      };
-      // S_j = Q K_j^T into TMEM once K_j landed and the softmax read S_{j-1}
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % kStages;
-        if (!mbar_wait(&kv_full[st], (j / kStages) & 1, kErrTmaWait, abort_flag)) return false;
-        if (!mbar_wait(s_empty, (j & 1) ^ 1, kErrAccFree, abort_flag)) return false;
-        tc_fence_after();
-        const uint64_t kdesc = make_sdesc_sw128(smem_u32(sK(st)));
-        const uint32_t idesc_s = make_idesc(fmt, kQ, keys_in(j));
+    // MMA issuer: the whole warp runs the loop (operands stay warp-uniform),
+    // one elected lane issues each tcgen05.mma / commit
+    const uint32_t fmt = kBf16 ? 1u : 0u;
+    const uint32_t idesc_pv = make_idesc(fmt, kQ, kD, 1u);
+    bool ok = mbar_wait_warp(q_full, 0, kErrTmaWait, abort_flag);
+    const uint64_t qdesc = make_sdesc_sw128(smem_u32(sQ));
+    auto keys_in = [&](int j) {  // keys of tile j, rounded up to a multiple of 16
+      const int left = seq - j * kKV;
+      return left >= kKV ? kKV : ((left + 15) & ~15);
+    };
+    // S_j = Q K_j^T into TMEM once K_j landed and the softmax read S_{j-1}
+    auto issue_s = [&](int j) -> bool {
+      const int st = j % kStages;
+      if (!mbar_wait_warp(&kv_full[st], (j / kStages) & 1, kErrTmaWait, abort_flag)) return false;
+      if (!mbar_wait_warp(s_empty, (j & 1) ^ 1, kErrAccFree, abort_flag)) return false;
+      tc_fence_after();
+      const uint64_t kdesc = make_sdesc_sw128(smem_u32(sK(st)));
+      const uint32_t idesc_s = make_idesc(fmt, kQ, keys_in(j));
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) umma_ss<0>(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
-        umma_commit(s_full);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        // the next S = Q K^T runs while the softmax of tile j is computed
-        if (j + 1 < n_kv && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full, j & 1, kErrAccFull, abort_flag)) break;
-        tc_fence_after();
-        const int st = j % kStages, n = keys_in(j);
-        const uint32_t vbase = smem_u32(sV(st));
-        for (int kk = 0; kk < n / 16; ++kk) {  // A = P from TMEM: 16 keys = 8 columns
-          const uint64_t vdesc = make_sdesc_sw128_mn(vbase + kk * 2048);
-          umma_ts(tO, tP + kk * 8, vdesc, idesc_pv, (j | kk) ? 1u : 0u);
-        }
-        umma_commit(p_empty);
-        umma_commit(&kv_empty[st]);
+      for (int kk = 0; kk < kD / 16; ++kk) umma_ss_warp(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
+      umma_commit_warp(s_full);
+      return true;
+    };
+    if (ok) ok = issue_s(0);
+    for (int j = 0; ok && j < n_kv; ++j) {
+      // the next S = Q K^T runs while the softmax of tile j is computed
+      if (j + 1 < n_kv && !issue_s(j + 1)) break;
+      if (!mbar_wait_warp(p_full, j & 1, kErrAccFull, abort_flag)) break;
+      tc_fence_after();
+      const int st = j % kStages, n = keys_in(j);
+      const uint64_t vdesc = make_sdesc_sw128_mn(smem_u32(sV(st)));
+      if (n == kKV) {
+#pragma unroll
+        for (int kk = 0; kk < kKV / 16; ++kk)  // A = P from TMEM: 16 keys = 8 columns
+          umma_ts_warp(tO, tP + kk * 8, vdesc + kk * (2048 >> 4), idesc_pv, (j | kk) ? 1u : 0u);
+      } else {
+        for (int kk = 0; kk < n / 16; ++kk)
+          umma_ts_warp(tO, tP + kk * 8, vdesc + kk * (2048 >> 4), idesc_pv, (j | kk) ? 1u : 0u);
       }
-      umma_commit(o_full);
+      umma_commit_warp(p_empty);
+      umma_commit_warp(&kv_empty[st]);
     }
+    umma_commit_warp(o_full);
   } else {
     // ------------------------------------------------ softmax + epilogue
     // warp w: TMEM lane quarter w % 4 (hardware rule), column half (w-2)/4
@@ -282,10 +347,7 @@ __global__ void __launch_bounds__(320, 2)
             for (int c = 0; c < kHalf; ++c)
               if (kbo + c >= seq) sv[c] = -INFINITY;
           }
-          float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
-#pragma unroll
-          for (int c = 4; c < kHalf; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
-          mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+          mt = max64(sv);
         }
       }
       if (live) {  // this warp's 64 S columns -> registers
@@ -303,10 +365,7 @@ __global__ void __launch_bounds__(320, 2)
           for (int c = 0; c < kHalf; ++c)
             if (kb + c >= seq) sv[c] = -INFINITY;
         }
-        float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
-#pragma unroll
-        for (int c = 4; c < kHalf; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
-        mt = fmaxf(mt, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+        mt = fmaxf(mt, max64(sv));
       }
       const bool need = (mt - m_used) * scale_log2 > kRescaleLog2;
       // P buffer and O are free once the previous P.V finished
@@ -333,22 +392,32 @@ __global__ void __launch_bounds__(320, 2)
       // P = exp2(S*c - m) -> 16-bit pairs into TMEM columns 192 + 32*half
       if (live) {
         const float mb = m_used * scale_log2;
-        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+        // e = S*c - m and the row sums on packed f32x2 lanes (keys c, c+1)
+        const uint64_t sc2 = f2pack(scale_log2, scale_log2), nmb2 = f2pack(-mb, -mb);
+        uint64_t l2[2] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
 #pragma unroll
         for (int c0 = 0; c0 < kHalf; c0 += 16) {  // 16 keys -> 8 columns at a time: few live registers
           uint32_t pk[8];
 #pragma unroll
           for (int c = c0; c < c0 + 16; c += 2) {
-            const float e0 = fmaf(sv[c], scale_log2, -mb), e1 = fmaf(sv[c + 1], scale_log2, -mb);
-            const float p0 = (c & 7) < kFmaExp ? exp2_fma(e0) : ex2(e0);  // split SFU / FMA pipe
-            const float p1 = ((c + 1) & 7) < kFmaExp ? exp2_fma(e1) : ex2(e1);
-            l4[c & 3] += p0;
-            l4[(c + 1) & 3] += p1;
+            const uint64_t e2 = ffma2(f2pack(sv[c], sv[c + 1]), sc2, nmb2);
+            float p0, p1;
+            if ((c & 7) < kFmaExp) {  // split SFU / FMA pipe
+              exp2_fma_x2(e2, p0, p1);
+            } else {
+              float e0, e1;
+              f2unpack(e2, e0, e1);
+              p0 = ex2(e0);
+              p1 = ex2(e1);
+            }
+            l2[(c >> 1) & 1] = fadd2(l2[(c >> 1) & 1], f2pack(p0, p1));
             pk[(c - c0) / 2] = pack2(p0, p1, kBf16);
           }
           tmem_st_32x32b_x8(tP + lane_off + half * (kHalf / 2) + c0 / 2, pk);
         }
-        l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+        float a0, a1, b0, b1;
+        f2unpack(fadd2(l2[0], l2[1]), a0, a1);
+        l += a0 + a1;
         tmem_st_wait();
       }
       tc_fence_before();
@@ -395,14 +464,18 @@ bool make_head_map(CUtensorMap* m, const void* base, int dtype, int64_t rows, in
 }
 
 template <bool kBf16>
-void set_smem_attr() {
+int launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, void* o, int64_t ldo,
+                   int seq, int q_tiles, dim3 grid, float scale_log2, cudaStream_t st) {
   static bool done = false;
   if (!done) {
     cudaFuncSetAttribute(attn_tc_kernel<kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    // full shared-memory carveout, so two 114 KiB CTAs fit on one SM
+    // full shared-memory carveout, so two CTAs fit on one SM
     cudaFuncSetAttribute(attn_tc_kernel<kBf16>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     done = true;
   }
+  attn_tc_kernel<kBf16><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, static_cast<uint16_t*>(o), ldo, seq, q_tiles,
+                                                        scale_log2);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 }  // namespace
@@ -423,16 +496,8 @@ int launch_attention_tc(const void* q, const void* k, const void* v, int64_t ldq
   dim3 grid(n_groups * q_tiles, heads);
   const float scale_log2 = (1.0f / sqrtf(static_cast<float>(head_dim))) * 1.4426950408889634f;
   count_launches(1);
-  if (dtype == kBF16) {
-    set_smem_attr<true>();
-    attn_tc_kernel<true><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, static_cast<uint16_t*>(o), ldo, seq, q_tiles,
-                                                        scale_log2);
-  } else {
-    set_smem_attr<false>();
-    attn_tc_kernel<false><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, static_cast<uint16_t*>(o), ldo, seq, q_tiles,
-                                                         scale_log2);
-  }
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+  if (dtype == kBF16) return launch_variant<true>(mq, mk, mv, o, ldo, seq, q_tiles, grid, scale_log2, st);
+  return launch_variant<false>(mq, mk, mv, o, ldo, seq, q_tiles, grid, scale_log2, st);
 }
 
 }  // namespace s3

@@ -108,34 +108,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer: the pair leader only
-    if (lane == 0 && rank == 0) {
+    // ---------------- MMA issuer: the pair leader's whole warp runs the loop
+    // (operands stay warp-uniform), one elected lane issues each MMA / commit
+    if (rank == 0) {
       uint32_t it = 0;
       int local = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1;
-        if (!mbar_wait(&acce_bar[acc], aph ^ 1, kErrAccFree, abort_flag)) break;
+        if (!mbar_wait_warp(&acce_bar[acc], aph ^ 1, kErrAccFree, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kPN;
         for (int kt = 0; kt < k_iters; ++kt, ++it) {
           const int s = it % kPStages;
           const uint32_t ph = (it / kPStages) & 1;
-          if (!mbar_wait(&full_bar[s], ph, kErrTmaWait, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_warp(&full_bar[s], ph, kErrTmaWait, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = make_sdesc_sw128(smem_u32(stage_a(s)));
           const uint64_t bdesc = make_sdesc_sw128(smem_u32(stage_b(s)));
 #pragma unroll
           for (int k = 0; k < kPK / kUmmaK; ++k)
-            umma_ss_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+            umma_ss_pair_warp(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
           // free the stage in both CTAs once these MMAs have read it
-          umma_commit_pair(mapa_shared(smem_u32(&empty_bar[s]), 0));
-          umma_commit_pair(mapa_shared(smem_u32(&empty_bar[s]), 1));
+          umma_commit_pair_warp(mapa_shared(smem_u32(&empty_bar[s]), 0));
+          umma_commit_pair_warp(mapa_shared(smem_u32(&empty_bar[s]), 1));
         }
         if (ok) {
-          umma_commit_pair(mapa_shared(smem_u32(&accf_bar[acc]), 0));
-          umma_commit_pair(mapa_shared(smem_u32(&accf_bar[acc]), 1));
+          umma_commit_pair_warp(mapa_shared(smem_u32(&accf_bar[acc]), 0));
+          umma_commit_pair_warp(mapa_shared(smem_u32(&accf_bar[acc]), 1));
         }
       }
     }

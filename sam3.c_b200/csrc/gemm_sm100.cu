@@ -179,15 +179,16 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
+    // ---------------- MMA issuer: the whole warp runs the loop (operands
+    // stay warp-uniform), one elected lane issues each MMA / commit
+    {
       uint32_t it = 0;
       int local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1;
-        if (!mbar_wait(&acce_bar[acc], aph ^ 1, kErrAccFree, abort_flag)) break;
+        if (!mbar_wait_warp(&acce_bar[acc], aph ^ 1, kErrAccFree, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
         for (int kt = 0; kt < k_iters; ++kt, ++it) {
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
           const uint32_t ph = (it / S) & 1;
           uint64_t* ready = kBMode == kBQ8 ? &conv_bar[it & 1] : (Cfg::kConv ? &conv_bar[s] : &full_bar[s]);
           const uint32_t rph = kBMode == kBQ8 ? (it >> 1) & 1 : ph;
-          if (!mbar_wait(ready, rph, kErrTmaWait, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_warp(ready, rph, kErrTmaWait, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = make_sdesc_sw128(smem_u32(stage_a(s)));
           const uint64_t bdesc = make_sdesc_sw128(smem_u32(kBMode == kBQ8 ? ring_b(it) : stage_b(s)));
@@ -205,21 +206,21 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
             const uint64_t bldesc = make_sdesc_sw128(smem_u32(stage_q(s) + kATileBytes));
 #pragma unroll
             for (int k = 0; k < BKe / Cfg::kUmmaKe; ++k) {
-              umma_ss<1>(d_tmem, aldesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
-              umma_ss<1>(d_tmem, adesc + 2 * k, bldesc + 2 * k, idesc, 1u);
-              umma_ss<1>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, 1u);
+              umma_ss_warp<1>(d_tmem, aldesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+              umma_ss_warp<1>(d_tmem, adesc + 2 * k, bldesc + 2 * k, idesc, 1u);
+              umma_ss_warp<1>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, 1u);
             }
           } else {
 #pragma unroll
             for (int k = 0; k < BKe / Cfg::kUmmaKe; ++k) {
               // advance 16 elements = 32 bytes = 2 (16-byte units) along K
-              umma_ss<0>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+              umma_ss_warp<0>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
             }
           }
-          umma_commit(&empty_bar[s]);  // frees the smem stage when these MMAs finish
-          if (kBMode == kBQ8) umma_commit(&bemp_bar[it & 1]);  // and the ring slot
+          umma_commit_warp(&empty_bar[s]);  // frees the smem stage when these MMAs finish
+          if (kBMode == kBQ8) umma_commit_warp(&bemp_bar[it & 1]);  // and the ring slot
         }
-        if (ok) umma_commit(&accf_bar[acc]);
+        if (ok) umma_commit_warp(&accf_bar[acc]);
       }
     }
   } else if (warp < 2 + Cfg::kEpiWarps) {
