@@ -251,20 +251,24 @@ __global__ void __launch_bounds__(320, 2)
   const uint32_t tS = tmem, tO = tmem + 128, tP = tmem + 192;
 
   if (warp == 0) {
-    // TMA producer (one thread)
-    if (lane == 0) {
+    // TMA producer: the whole warp runs the loop, one elected lane issues
+    if (elect_one()) {
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
       mbar_arrive_expect_tx(q_full, kTile);
       tma_load_2d(sQ, &tq, q_full, head * kD, row0 + qt * kQ);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % kStages;
-        if (!mbar_wait(&kv_empty[st], ((j / kStages) & 1) ^ 1, kErrStageFree, abort_flag)) break;
+    }
+    __syncwarp();
+    for (int j = 0; j < n_kv; ++j) {
+      const int st = j % kStages;
+      if (!mbar_wait_warp(&kv_empty[st], ((j / kStages) & 1) ^ 1, kErrStageFree, abort_flag)) break;
+      if (elect_one()) {
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
         tma_load_2d(sK(st), &tk, &kv_full[st], head * kD, row0 + j * kKV);
         tma_load_2d(sV(st), &tv, &kv_full[st], head * kD, row0 + j * kKV);
       }
+      __syncwarp();
     }
   } else if (warp == 1) {
     // MMA issuer: the whole warp runs the loop (operands stay warp-uniform),

@@ -87,10 +87,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer (both CTAs): own A rows, own W half
-    if (lane == 0) {
-      tma_prefetch_desc(&tmap_a);
-      tma_prefetch_desc(&tmap_b);
+    // ---------------- TMA producer (both CTAs): own A rows, own W half; the
+    // whole warp runs the loop, one elected lane issues the copies
+    {
+      if (elect_one()) {
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+      }
+      __syncwarp();
       uint32_t it = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
@@ -99,11 +103,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         for (int kt = 0; kt < k_iters; ++kt, ++it) {
           const int s = it % kPStages;
           const uint32_t ph = (it / kPStages) & 1;
-          if (!mbar_wait(&empty_bar[s], ph ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
-          if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kPStage);  // both CTAs' bytes
+          if (!mbar_wait_warp(&empty_bar[s], ph ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
           const uint32_t lead_full = mapa_shared(smem_u32(&full_bar[s]), 0);
-          tma_load_2d_pair(stage_a(s), &tmap_a, lead_full, kt * kPK, m0);
-          tma_load_2d_pair(stage_b(s), &tmap_b, lead_full, kt * kPK, n0);
+          if (elect_one()) {
+            if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kPStage);  // both CTAs' bytes
+            tma_load_2d_pair(stage_a(s), &tmap_a, lead_full, kt * kPK, m0);
+            tma_load_2d_pair(stage_b(s), &tmap_b, lead_full, kt * kPK, n0);
+          }
+          __syncwarp();
         }
       }
     }

@@ -151,11 +151,15 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
   auto stage_sc = [&](int s) { return smem + s * Cfg::kStageBytes + kATileBytes + kQ8TileBytes; };
 
   if (warp == 0) {
-    // ---------------- TMA producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tmap_a);
-      tma_prefetch_desc(&tmap_b);
-      if (kBMode == kBQ8) tma_prefetch_desc(&tmap_s);
+    // ---------------- TMA producer: the whole warp runs the loop, one
+    // elected lane issues the copies
+    {
+      if (elect_one()) {
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+        if (kBMode == kBQ8) tma_prefetch_desc(&tmap_s);
+      }
+      __syncwarp();
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
@@ -164,17 +168,20 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
         for (int kt = 0; kt < k_iters; ++kt, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
-          if (!mbar_wait(&empty_bar[s], ph ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
-          if (kBMode == kBQ8) {
-            mbar_arrive_expect_tx(&full_bar[s], kATileBytes + kQ8TileBytes + kQ8ScaleBytes);
-            tma_load_2d(stage_a(s), &tmap_a, &full_bar[s], kt * kBK, m0);
-            tma_load_2d(stage_q(s), &tmap_b, &full_bar[s], kt * kBK, n0);
-            tma_load_2d(stage_sc(s), &tmap_s, &full_bar[s], n0, kt * (kBK / 32));
-          } else {
-            mbar_arrive_expect_tx(&full_bar[s], kATileBytes + kBTileBytes);
-            tma_load_2d(stage_a(s), &tmap_a, &full_bar[s], kt * BKe, m0);
-            tma_load_2d(stage_b(s), &tmap_b, &full_bar[s], kt * BKe, n0);
+          if (!mbar_wait_warp(&empty_bar[s], ph ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
+          if (elect_one()) {
+            if (kBMode == kBQ8) {
+              mbar_arrive_expect_tx(&full_bar[s], kATileBytes + kQ8TileBytes + kQ8ScaleBytes);
+              tma_load_2d(stage_a(s), &tmap_a, &full_bar[s], kt * kBK, m0);
+              tma_load_2d(stage_q(s), &tmap_b, &full_bar[s], kt * kBK, n0);
+              tma_load_2d(stage_sc(s), &tmap_s, &full_bar[s], n0, kt * (kBK / 32));
+            } else {
+              mbar_arrive_expect_tx(&full_bar[s], kATileBytes + kBTileBytes);
+              tma_load_2d(stage_a(s), &tmap_a, &full_bar[s], kt * BKe, m0);
+              tma_load_2d(stage_b(s), &tmap_b, &full_bar[s], kt * BKe, n0);
+            }
           }
+          __syncwarp();
         }
       }
     }

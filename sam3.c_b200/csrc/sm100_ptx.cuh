@@ -103,6 +103,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// True in exactly one lane of the (converged, full) warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p;
+  asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.u32 %0, 1, 0, e;\n\t}" : "=r"(p));
+  return p != 0;
+}
+
 // mbar_wait executed by every lane of a warp; the verdict is made uniform
 // (and the warp reconverged) before the caller's warp-wide elect.sync.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, unsigned err,
