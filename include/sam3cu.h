@@ -25,6 +25,10 @@
  *       sam3_vit_init / sam3_vit_load / sam3_vit_build
  *       (src/model/image_encoder.h:112-173, image_encoder.c:513-963): the
  *       whole encoder forward lowered to fused kernels on one GPU.
+ *   sam3cu_tvit_*
+ *       the TinyViT hot ops of image_encoder_tinyvit.c: the relative
+ *       position bias expansion (expand_attention_bias :265-335), the window
+ *       attention after the qkv linear (tvit_window_attention :790-866).
  *   sam3_cuda_backend_ops (include/sam3cu_backend.h)
  *       the backend vtable struct sam3_backend_ops (src/backend/backend.h:29-56).
  *
@@ -142,6 +146,33 @@ SAM3CU_API int sam3cu_layernorm(const void *x, int x_dtype, const float *gamma,
 SAM3CU_API int sam3cu_sdpa(const void *q, const void *k, const void *v, int64_t ld_qkv,
 		void *o, int64_t ld_o, int dtype, int n_groups, int seq,
 		int heads, int head_dim, void *stream);
+
+/* ------------------------------------------------------------- TinyViT */
+
+/*
+ * Expand TinyViT's compact relative position bias [heads, n_offsets]
+ * (n_offsets = distinct (|dy|, |dx|) pairs of a ws x ws window, numbered in
+ * first-seen order) into the dense [heads, ws*ws, out_ld] table, as
+ * expand_attention_bias (image_encoder_tinyvit.c:265-335) does for
+ * out_ld = ws*ws.  Host memory; out_ld >= ws*ws, extra columns are zeroed.
+ * Returns SAM3CU_EINVAL if n_offsets does not match ws.
+ */
+SAM3CU_API int sam3cu_tvit_expand_bias(const float *compact, int heads, int n_offsets, int ws,
+		float *out, int out_ld);
+
+/*
+ * TinyViT window attention after the qkv linear (tvit_window_attention,
+ * image_encoder_tinyvit.c:790-866): qkv [n_windows * n_tokens, ld_qkv] in
+ * the per-head interleaved layout (head h: q, k, v at columns
+ * h*3*hd + {0, hd, 2*hd}), scores (q/sqrt(hd))·kᵀ + bias[h], softmax,
+ * ·v, written to out [n_windows * n_tokens, ld_out] with head h at columns
+ * h*hd (the permute-back layout before proj).  bias: device f32
+ * [heads, n_tokens, bias_ld] (sam3cu_tvit_expand_bias), bias_ld a multiple
+ * of 4, or NULL.  dtype F16 or BF16, head_dim 32 or 64; device pointers.
+ */
+SAM3CU_API int sam3cu_tvit_window_attention(const void *qkv, int64_t ld_qkv, void *out, int64_t ld_out,
+		int dtype, int n_windows, int n_tokens, int heads, int head_dim,
+		const float *bias, int bias_ld, void *stream);
 
 /* ------------------------------------------- per-node ops (backend vtable)
  * Device helpers and the remaining encoder-graph ops, used by the

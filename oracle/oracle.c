@@ -547,3 +547,204 @@ void orc_vit_forward(const struct orc_vit_cfg *c,
 				      gc, gsn, wc, wsn);
 	free(gc); free(gsn); free(wc); free(wsn);
 }
+
+/* ---- TinyViT (src/model/image_encoder_tinyvit.c) ------------------------ */
+
+/* expand_attention_bias (:265-335): compact [heads, n_off] -> dense
+ * [heads, N, N], N = ws*ws; offsets (|dy|, |dx|) numbered in the order the
+ * position pairs (p1, p2), both row-major, first meet them.  Returns the
+ * number of distinct offsets found (the caller checks it against n_off). */
+int orc_tvit_expand_bias(const float *compact, int heads, int n_off, int ws,
+			 float *out)
+{
+	int N = ws * ws, count = 0;
+	int *idx = malloc(sizeof(int) * (size_t)N);
+	for (int i = 0; i < N; i++)
+		idx[i] = -1;
+	for (int p1 = 0; p1 < N; p1++)
+		for (int p2 = 0; p2 < N; p2++) {
+			int key = abs(p1 / ws - p2 / ws) * ws +
+				  abs(p1 % ws - p2 % ws);
+			if (idx[key] < 0)
+				idx[key] = count++;
+		}
+	if (count == n_off)
+		for (int h = 0; h < heads; h++)
+			for (int p1 = 0; p1 < N; p1++)
+				for (int p2 = 0; p2 < N; p2++) {
+					int key = abs(p1 / ws - p2 / ws) * ws +
+						  abs(p1 % ws - p2 % ws);
+					out[((int64_t)h * N + p1) * N + p2] =
+						compact[(int64_t)h * n_off +
+							idx[key]];
+				}
+	free(idx);
+	return count;
+}
+
+/* Row softmax (cpu_softmax.c:29-47): max, expf(x - max), sum, * 1/sum. */
+static void softmax_row(float *x, int n)
+{
+	float mx = -FLT_MAX, sum = 0.0f;
+	for (int j = 0; j < n; j++)
+		if (x[j] > mx)
+			mx = x[j];
+	for (int j = 0; j < n; j++) {
+		x[j] = expf(x[j] - mx);
+		sum += x[j];
+	}
+	float inv = 1.0f / sum;
+	for (int j = 0; j < n; j++)
+		x[j] *= inv;
+}
+
+/* tvit_window_attention (:790-866) after the qkv linear.  qkv
+ * [nw*N, 3*heads*hd] in the per-head interleaved layout (reshape to
+ * [nw, N, heads, 3*hd], slices at 0, hd, 2*hd on the last dim :796-809);
+ * Q scaled by 1/sqrt(hd) (:823-833), scores Q.K^T + bias[h] (:836-846),
+ * softmax (:849), .V (:854), permuted back to out [nw*N, heads*hd]. */
+void orc_tvit_window_attention(const float *qkv, int nw, int N, int heads,
+			       int hd, const float *bias, float *out)
+{
+	const int C = heads * hd, ld = 3 * C;
+	const float scale = 1.0f / sqrtf((float)hd);
+#pragma omp parallel for schedule(dynamic, 1)
+	for (int64_t wh = 0; wh < (int64_t)nw * heads; wh++) {
+		const int w = (int)(wh / heads), h = (int)(wh % heads);
+		const float *base = qkv + (int64_t)w * N * ld + h * 3 * hd;
+		float *q = malloc(sizeof(float) * (size_t)N * hd);
+		float *s = malloc(sizeof(float) * (size_t)N);
+		for (int i = 0; i < N; i++)
+			for (int d = 0; d < hd; d++)
+				q[i * hd + d] = base[(int64_t)i * ld + d] * scale;
+		for (int i = 0; i < N; i++) {
+			for (int j = 0; j < N; j++) {
+				float acc = 0.0f;
+				const float *kr = base + (int64_t)j * ld + hd;
+				for (int d = 0; d < hd; d++)
+					acc += q[i * hd + d] * kr[d];
+				s[j] = acc + (bias ? bias[((int64_t)h * N + i) * N + j] : 0.0f);
+			}
+			softmax_row(s, N);
+			float *o = out + ((int64_t)w * N + i) * C + h * hd;
+			for (int d = 0; d < hd; d++) {
+				float acc = 0.0f;
+				for (int j = 0; j < N; j++)
+					acc += s[j] * base[(int64_t)j * ld + 2 * hd + d];
+				o[d] = acc;
+			}
+		}
+		free(q);
+		free(s);
+	}
+}
+
+/* tvit_conv_bn (:655-674) for the depthwise 3x3 convs: conv2d NHWC with
+ * OHWI weight [C,3,3,1], stride 1, pad 1, groups C (cpu_conv2d.c:320-420),
+ * optional conv bias, then eval BatchNorm (cpu_batchnorm.c: (x - mean) *
+ * 1/sqrtf(var + 1e-5) * gamma + beta), then tanh-GELU if gelu. */
+void orc_dwconv3x3_bn(const float *x, int B, int H, int W, int C,
+		      const float *w, const float *cb, const float *bn_w,
+		      const float *bn_b, const float *bn_mean,
+		      const float *bn_var, int gelu, float *y)
+{
+#pragma omp parallel for schedule(static)
+	for (int64_t p = 0; p < (int64_t)B * H * W; p++) {
+		int b = (int)(p / ((int64_t)H * W)), yy = (int)(p / W % H),
+		    xx = (int)(p % W);
+		for (int c = 0; c < C; c++) {
+			float acc = 0.0f;
+			for (int ky = 0; ky < 3; ky++)
+				for (int kx = 0; kx < 3; kx++) {
+					int iy = yy + ky - 1, ix = xx + kx - 1;
+					if (iy < 0 || iy >= H || ix < 0 || ix >= W)
+						continue;
+					acc += x[(((int64_t)b * H + iy) * W + ix) * C + c] *
+					       w[(c * 3 + ky) * 3 + kx];
+				}
+			if (cb)
+				acc += cb[c];
+			if (bn_mean) {
+				float inv = 1.0f / sqrtf(bn_var[c] + 1e-5f);
+				acc = (acc - bn_mean[c]) * inv;
+				if (bn_w)
+					acc *= bn_w[c];
+				if (bn_b)
+					acc += bn_b[c];
+			}
+			y[p * C + c] = gelu ? gelu_tanh(acc) : acc;
+		}
+	}
+}
+
+/* Weights of one TinyViTBlock (image_encoder_tinyvit.h: sam3_tvit_block),
+ * F32, linears [out, in]; attn_bias is the expanded [heads, N, N]. */
+struct orc_tvit_block {
+	const float *attn_norm_w, *attn_norm_b, *qkv_w, *qkv_b, *proj_w,
+		*proj_b, *attn_bias;
+	const float *lc_w, *lc_b, *lc_bn_w, *lc_bn_b, *lc_bn_mean, *lc_bn_var;
+	const float *mlp_norm_w, *mlp_norm_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+};
+
+/* tvit_block_forward (:896-1052) on x [H, W, C] (one image, NHWC), in
+ * place: zero-pad to multiples of ws (:916-956), window partition, window
+ * attention with its pre-LN (:767-771), unpartition, unpad, residual add;
+ * 3x3 depthwise conv + BN; LN -> fc1 -> GELU -> fc2, residual add. */
+void orc_tvit_block_forward(const struct orc_tvit_block *bw, float *x, int H,
+			    int W, int C, int heads, int ws, int mlp)
+{
+	const int Hp = (H + ws - 1) / ws * ws, Wp = (W + ws - 1) / ws * ws;
+	const int nwy = Hp / ws, nwx = Wp / ws, nw = nwy * nwx, N = ws * ws;
+	const int64_t T = (int64_t)nw * N;
+	float *win = calloc((size_t)T * C, sizeof(float));
+	float *ln = malloc(sizeof(float) * (size_t)T * C);
+	float *qkv = malloc(sizeof(float) * (size_t)T * 3 * C);
+	float *att = malloc(sizeof(float) * (size_t)T * C);
+	float *prj = malloc(sizeof(float) * (size_t)T * C);
+	/* pad + partition: window (wy, wx), token (cy, cx) */
+	for (int wy = 0; wy < nwy; wy++)
+		for (int wx = 0; wx < nwx; wx++)
+			for (int t = 0; t < N; t++) {
+				int py = wy * ws + t / ws, px = wx * ws + t % ws;
+				if (py < H && px < W)
+					memcpy(win + ((int64_t)(wy * nwx + wx) * N + t) * C,
+					       x + ((int64_t)py * W + px) * C,
+					       sizeof(float) * C);
+			}
+	orc_layernorm(win, bw->attn_norm_w, bw->attn_norm_b, ln, T, C);
+	orc_linear(ln, bw->qkv_w, bw->qkv_b, NULL, qkv, T, C, 3 * C, 0);
+	orc_tvit_window_attention(qkv, nw, N, heads, C / heads, bw->attn_bias,
+				  att);
+	orc_linear(att, bw->proj_w, bw->proj_b, NULL, prj, T, C, C, 0);
+	/* unpartition + unpad + residual */
+	for (int wy = 0; wy < nwy; wy++)
+		for (int wx = 0; wx < nwx; wx++)
+			for (int t = 0; t < N; t++) {
+				int py = wy * ws + t / ws, px = wx * ws + t % ws;
+				if (py >= H || px >= W)
+					continue;
+				const float *s = prj + ((int64_t)(wy * nwx + wx) * N + t) * C;
+				float *d = x + ((int64_t)py * W + px) * C;
+				for (int c = 0; c < C; c++)
+					d[c] = s[c] + d[c];
+			}
+	free(win);
+	free(qkv);
+	free(att);
+	free(prj);
+	/* local conv: 3x3 depthwise + BN (:1015) */
+	const int64_t HW = (int64_t)H * W;
+	float *lc = malloc(sizeof(float) * (size_t)HW * C);
+	orc_dwconv3x3_bn(x, 1, H, W, C, bw->lc_w, bw->lc_b, bw->lc_bn_w,
+			 bw->lc_bn_b, bw->lc_bn_mean, bw->lc_bn_var, 0, lc);
+	/* MLP with residual (:1027-1046) */
+	float *h1 = malloc(sizeof(float) * (size_t)HW * mlp);
+	free(ln);
+	ln = malloc(sizeof(float) * (size_t)HW * C);
+	orc_layernorm(lc, bw->mlp_norm_w, bw->mlp_norm_b, ln, HW, C);
+	orc_linear(ln, bw->fc1_w, bw->fc1_b, NULL, h1, HW, C, mlp, 1);
+	orc_linear(h1, bw->fc2_w, bw->fc2_b, lc, x, HW, mlp, C, 0);
+	free(lc);
+	free(h1);
+	free(ln);
+}

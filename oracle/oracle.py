@@ -340,7 +340,9 @@ class _TDesc(C.Structure):
 def ref_node_graph(op, ins, out_dtype, out_shape, params=(0, 0, 0, 0), ops=None, be_size=0,
                    be_type=2):
     """Single-node graph; ins: list of (storage array, dtype name, shape)."""
-    descs = (_TDesc * 4)()
+    if len(ins) > 6:
+        raise ValueError("at most 6 inputs")
+    descs = (_TDesc * 6)()
     keep = []
     for i, (arr, dt, shp) in enumerate(ins):
         a = np.ascontiguousarray(arr)
@@ -365,8 +367,8 @@ def ref_node_graph(op, ins, out_dtype, out_shape, params=(0, 0, 0, 0), ops=None,
     return _unbits(out, out_dtype)
 
 
-OP = dict(MATMUL=1, ADD=2, GELU=6, LAYERNORM=7, CONV2D=8, RESHAPE=9, TRANSPOSE=10, CAST=11,
-          SLICE=13, ROPE=17, SDPA=21)
+OP = dict(MATMUL=1, ADD=2, MUL=3, SOFTMAX=4, GELU=6, LAYERNORM=7, CONV2D=8, RESHAPE=9,
+          TRANSPOSE=10, CAST=11, SLICE=13, ROPE=17, SDPA=21, BIAS_ADD=22, BATCHNORM=24)
 
 
 def ref_vit_encode(cfg: dict, w: dict, image: np.ndarray) -> np.ndarray:
@@ -381,3 +383,136 @@ def ref_vit_encode(cfg: dict, w: dict, image: np.ndarray) -> np.ndarray:
     if rc != 0:
         raise RuntimeError(f"ref_vit_encode failed rc={rc}")
     return out
+
+
+# ---------------------------------------------------------------- TinyViT
+def tvit_n_offsets(ws: int) -> int:
+    """Distinct (|dy|, |dx|) offsets of a ws x ws window."""
+    return ws * ws
+
+
+def tvit_expand_bias(compact: np.ndarray, ws: int) -> np.ndarray:
+    """Restatement of expand_attention_bias: [heads, n_off] -> [heads, N, N]."""
+    compact = np.ascontiguousarray(compact, np.float32)
+    heads, n_off = compact.shape
+    out = np.empty((heads, ws * ws, ws * ws), np.float32)
+    n = orc().orc_tvit_expand_bias(_p(compact), heads, n_off, ws, _p(out))
+    if n != n_off:
+        raise ValueError(f"{n} offsets for ws={ws}, table has {n_off}")
+    return out
+
+
+def ref_tvit_expand_bias(compact: np.ndarray, ws: int) -> np.ndarray:
+    """The reference's own expand_attention_bias (compiled from its source)."""
+    compact = np.ascontiguousarray(compact, np.float32)
+    heads, n_off = compact.shape
+    out = np.empty((heads, ws * ws, ws * ws), np.float32)
+    if ref().ref_tvit_expand_bias(_p(compact), heads, n_off, ws, _p(out)) != 0:
+        raise RuntimeError("ref_tvit_expand_bias failed")
+    return out
+
+
+def tvit_window_attention(qkv: np.ndarray, nw: int, N: int, heads: int, hd: int,
+                          bias: np.ndarray | None) -> np.ndarray:
+    """Restatement of tvit_window_attention after the qkv linear."""
+    qkv = np.ascontiguousarray(qkv, np.float32)
+    out = np.empty((nw * N, heads * hd), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    orc().orc_tvit_window_attention(_p(qkv), nw, N, heads, hd, _p(b), _p(out))
+    return out
+
+
+def ref_tvit_window_attention(qkv: np.ndarray, nw: int, N: int, heads: int, hd: int,
+                              bias: np.ndarray | None) -> np.ndarray:
+    """tvit_window_attention evaluated by the reference CPU kernels, one
+    (window, head) slice at a time (the CPU MATMUL is 2-D only): MUL by the
+    [1] scale tensor, TRANSPOSE, MATMUL, ADD bias, SOFTMAX, MATMUL.  The
+    reshape / slice / permute nodes are exact copies, done here in numpy."""
+    C = heads * hd
+    x = np.ascontiguousarray(qkv, np.float32).reshape(nw, N, heads, 3 * hd)
+    scale = np.array([1.0 / np.sqrt(np.float32(hd))], np.float32)
+    out = np.empty((nw, N, heads, hd), np.float32)
+    for w in range(nw):
+        for h in range(heads):
+            q = np.ascontiguousarray(x[w, :, h, :hd])
+            k = np.ascontiguousarray(x[w, :, h, hd:2 * hd])
+            v = np.ascontiguousarray(x[w, :, h, 2 * hd:])
+            qs = ref_node_graph(OP["MUL"], [(q, "f32", (N, hd)), (scale, "f32", (1,))], "f32",
+                                (N, hd))
+            kt = ref_node_graph(OP["TRANSPOSE"], [(k, "f32", (N, hd))], "f32", (hd, N),
+                                params=(1, 0, 0, 0))
+            s = ref_node_graph(OP["MATMUL"], [(qs, "f32", (N, hd)), (kt, "f32", (hd, N))], "f32",
+                               (N, N))
+            if bias is not None:
+                s = ref_node_graph(OP["ADD"], [(s, "f32", (N, N)),
+                                               (np.ascontiguousarray(bias[h]), "f32", (N, N))],
+                                   "f32", (N, N))
+            p = ref_node_graph(OP["SOFTMAX"], [(s, "f32", (N, N))], "f32", (N, N))
+            out[w, :, h] = ref_node_graph(OP["MATMUL"], [(p, "f32", (N, N)), (v, "f32", (N, hd))],
+                                          "f32", (N, hd))
+    return out.reshape(nw * N, C)
+
+
+def dwconv3x3_bn(x: np.ndarray, w: np.ndarray, cb=None, bn=None, gelu=False) -> np.ndarray:
+    """Restatement of a depthwise 3x3 tvit_conv_bn on NHWC x [B, H, W, C];
+    w [C, 3, 3, 1]; bn = (gamma, beta, mean, var) or None."""
+    x = np.ascontiguousarray(x, np.float32)
+    B, H, W, Cc = x.shape
+    y = np.empty_like(x)
+    g = b = m = v = None
+    if bn is not None:
+        g, b, m, v = (np.ascontiguousarray(t, np.float32) for t in bn)
+    wc = np.ascontiguousarray(w, np.float32)
+    cbc = None if cb is None else np.ascontiguousarray(cb, np.float32)
+    orc().orc_dwconv3x3_bn(_p(x), B, H, W, Cc, _p(wc), _p(cbc), _p(g), _p(b), _p(m), _p(v),
+                           1 if gelu else 0, _p(y))
+    return y
+
+
+def ref_dwconv3x3_bn(x: np.ndarray, w: np.ndarray, cb=None, bn=None) -> np.ndarray:
+    """The reference CONV2D (groups = C, stride 1, pad 1), BIAS_ADD and
+    BATCHNORM kernels on the same inputs, as gh_conv2d + gh_batchnorm chain
+    them (graph_helpers.c:1360-1395, image_encoder_tinyvit.c:655-674)."""
+    x = np.ascontiguousarray(x, np.float32)
+    B, H, W, Cc = x.shape
+    ins = [(x, "f32", (B, H, W, Cc)), (np.ascontiguousarray(w, np.float32), "f32", (Cc, 3, 3, 1))]
+    y = ref_node_graph(OP["CONV2D"], ins, "f32", (B, H, W, Cc), params=(1, 1, Cc, 0))
+    if cb is not None:  # gh_conv2d adds the conv bias as a BIAS_ADD node (graph_helpers.c:1392)
+        y = ref_node_graph(OP["BIAS_ADD"], [(y, "f32", (B, H, W, Cc)),
+                                             (np.ascontiguousarray(cb, np.float32), "f32", (Cc,))],
+                           "f32", (B, H, W, Cc))
+    if bn is not None:
+        g, b, m, v = (np.ascontiguousarray(t, np.float32) for t in bn)
+        y = ref_node_graph(OP["BATCHNORM"], [(y, "f32", (B, H, W, Cc)), (g, "f32", (Cc,)),
+                                              (b, "f32", (Cc,)), (m, "f32", (Cc,)),
+                                              (v, "f32", (Cc,))], "f32", (B, H, W, Cc))
+    return y
+
+
+TVIT_BLOCK_KEYS = ("attn_norm_w", "attn_norm_b", "qkv_w", "qkv_b", "proj_w", "proj_b",
+                   "attn_bias", "lc_w", "lc_b", "lc_bn_w", "lc_bn_b", "lc_bn_mean", "lc_bn_var",
+                   "mlp_norm_w", "mlp_norm_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b")
+
+
+class _TvitBlk(C.Structure):
+    _fields_ = [(n, VP) for n in TVIT_BLOCK_KEYS]
+
+
+def tvit_block_forward(w: dict, x: np.ndarray, heads: int, ws: int) -> np.ndarray:
+    """Restatement of tvit_block_forward on one NHWC image x [H, W, C];
+    w['attn_bias'] is the expanded [heads, N, N] table."""
+    x = np.array(x, np.float32, copy=True, order="C")
+    H, W, Cc = x.shape
+    s = _TvitBlk()
+    keep = []
+    for n in TVIT_BLOCK_KEYS:
+        if w.get(n) is None:
+            setattr(s, n, None)
+            continue
+        a = np.ascontiguousarray(w[n], np.float32)
+        keep.append(a)
+        setattr(s, n, a.ctypes.data)
+    mlp = w["fc1_w"].shape[0]
+    orc().orc_tvit_block_forward(C.byref(s), _p(x), H, W, Cc, heads, ws, mlp)
+    del keep
+    return x

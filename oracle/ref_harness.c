@@ -428,7 +428,7 @@ int ref_node_graph(int op, int n_in, const struct ref_tdesc *ins,
 	if (!g || !be)
 		goto out;
 	sam3_graph_init(g);
-	struct sam3_tensor *in[4] = {0};
+	struct sam3_tensor *in[6] = {0};
 	for (int i = 0; i < n_in; i++)
 		in[i] = gh_tensor_wrap(&a, (enum sam3_dtype)ins[i].dtype,
 				       ins[i].n_dims, ins[i].dims,

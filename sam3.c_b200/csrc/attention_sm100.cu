@@ -54,21 +54,22 @@ namespace {
 
 constexpr int kQ = 128;                  // query rows per CTA
 constexpr int kKV = 128;                 // keys per tile
-constexpr int kD = 64;                   // head dim
-constexpr int kTile = kQ * kD * 2;       // 16 KiB (Q, K or V tile)
-#ifndef S3_ATTN_STAGES
-#define S3_ATTN_STAGES 3
-#endif
-constexpr int kStages = S3_ATTN_STAGES;  // K/V ring depth
-constexpr int kSmem = kTile * (1 + 2 * kStages);  // Q | K0 V0 | K1 V1 | ...
-constexpr int kTmemCols = 256;           // S: 0..127, O: 128..191, P: 192..255
+constexpr int kStages = 3;               // K/V ring depth
+constexpr int kTmemCols = 256;           // S: 0..127, O: 128.., P: 192..255
+
+// Per head dimension: a Q, K or V tile is 128 rows of kD 16-bit elements,
+// 128-byte rows (kD 64, 128-byte swizzle) or 64-byte rows (kD 32, 64-byte
+// swizzle).
+template <int kD>
+struct HeadCfg {
+  static constexpr int kRowBytes = kD * 2;
+  static constexpr int kTile = kQ * kRowBytes;
+  static constexpr int kSmem = kTile * (1 + 2 * kStages);  // Q | K0 V0 | K1 V1 | ...
+  static_assert(kD == 32 || kD == 64, "head_dim 32 or 64");
+};
 constexpr int kThreads = 320;          // 2 control + 8 softmax warps
 constexpr int kHalf = kKV / 2;           // columns per softmax warp
 constexpr float kRescaleLog2 = 8.0f;     // lazy rescale threshold (x256)
-#ifndef S3_ATTN_FMA_EXP
-#define S3_ATTN_FMA_EXP 0
-#endif
-constexpr int kFmaExp = S3_ATTN_FMA_EXP;  // of every 8 exponentials, this many on the FMA pipe
 
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf) {
@@ -84,23 +85,6 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA pipe, so part of the exponentials leave the SFU: Cody-Waite
-// range reduction x = n + f, n = round(x) obtained by adding 1.5*2^23, f in
-// [-1/2, 1/2]; 2^f from a degree-3 polynomial fitted here to minimax
-// relative error on that interval (max 7.5e-5, below the 2^-9 rounding of
-// the 16-bit P it feeds); 2^n added to the exponent field.  x >= -126.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -126.0f);
-  const float kMagic = 12582912.0f;  // 1.5 * 2^23
-  const float t = x + kMagic;
-  const float f = x - (t - kMagic);
-  float p = fmaf(0.055171653628349304f, f, 0.2426111400127411f);
-  p = fmaf(p, f, 0.6932609677314758f);
-  p = fmaf(p, f, 0.9999280571937561f);
-  const int n = __float_as_int(t) - __float_as_int(kMagic);
-  return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
 // Two f32 lanes in one 64-bit register for the packed f32x2 operations.
@@ -122,32 +106,6 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-// exp2_fma (below) on two lanes with packed f32x2 arithmetic.
-__device__ __forceinline__ void exp2_fma_x2(uint64_t x2, float& y0, float& y1) {
-  float x0, x1;
-  f2unpack(x2, x0, x1);
-  x2 = f2pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
-  const uint64_t magic = f2pack(12582912.0f, 12582912.0f);  // 1.5 * 2^23
-  const uint64_t t = fadd2(x2, magic);
-  const uint64_t f = fsub2(x2, fsub2(t, magic));
-  uint64_t p = ffma2(f2pack(0.055171653628349304f, 0.055171653628349304f), f,
-                     f2pack(0.2426111400127411f, 0.2426111400127411f));
-  p = ffma2(p, f, f2pack(0.6932609677314758f, 0.6932609677314758f));
-  p = ffma2(p, f, f2pack(0.9999280571937561f, 0.9999280571937561f));
-  float p0, p1, t0, t1;
-  f2unpack(p, p0, p1);
-  f2unpack(t, t0, t1);
-  // 2^n into the exponent field: bits(p) + (bits(t) - bits(magic)) * 2^23
-  y0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(t0) - 0x4B400000) << 23));
-  y1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(t1) - 0x4B400000) << 23));
-}
-
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -192,13 +150,32 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsign
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// Kernel arguments beyond the tensor maps.
+struct AttnParams {
+  uint16_t* o;         // output rows [groups * seq, ldo]; head h at column h * o_hstride
+  int64_t ldo;
+  int o_hstride;
+  int in_hstride;      // column distance between heads in the Q/K/V maps
+  int seq;             // rows (tokens) per group
+  int q_tiles;         // ceil(seq / 128)
+  float scale;         // softmax scale (1/sqrt(head_dim))
+  float scale_log2;    // scale * log2(e)
+  const float* bias;   // optional additive bias [heads, seq, bias_ld] f32
+  int bias_ld;         // multiple of 4
+};
+
 // Two CTAs of 10 warps per SM: 5 warps per SM sub-partition, whose
 // register file holds 16K entries: about 100 registers per thread.
-template <bool kBf16>
+// kBf16: Q/K/V/P/O are bf16, else f16.  kD: head dim.  kBias: an additive
+// f32 bias [head, query, key] joins the scaled scores before the softmax
+// (TinyViT's relative position bias, image_encoder_tinyvit.c:842-846).
+template <bool kBf16, int kD, bool kBias>
 __global__ void __launch_bounds__(320, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                   const __grid_constant__ CUtensorMap tv, uint16_t* __restrict__ o, int64_t ldo, int seq,
-                   int q_tiles, float scale_log2) {
+                   const __grid_constant__ CUtensorMap tv, const AttnParams prm) {
+  using HC = HeadCfg<kD>;
+  constexpr int kTile = HC::kTile;
+  constexpr int kOHalf = kD / 2;  // O columns per softmax warp
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ uint64_t bars[8 + 2 * kStages];
   __shared__ uint32_t tmem_slot;
@@ -213,10 +190,12 @@ __global__ void __launch_bounds__(320, 2)
   uint64_t* kv_empty = &bars[6 + kStages];   // [kStages]
   volatile int* abort_flag = &abort_flag_s;
 
+  const int seq = prm.seq;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int group = blockIdx.x / q_tiles, qt = blockIdx.x % q_tiles, head = blockIdx.y;
+  const int group = blockIdx.x / prm.q_tiles, qt = blockIdx.x % prm.q_tiles, head = blockIdx.y;
   const int row0 = group * seq;  // first row of the group in the [rows, ld] matrices
   const int n_kv = (seq + kKV - 1) / kKV;
+  const int hx = head * prm.in_hstride;  // column of this head in the Q/K/V maps
 
   if ((smem_u32(smem) & 1023u) != 0) {  // the swizzled layouts need 1 KiB alignment
     if (threadIdx.x == 0) atomicCAS(&g_dev_error, 0u, static_cast<unsigned>(kErrTmemAlloc));
@@ -225,6 +204,8 @@ __global__ void __launch_bounds__(320, 2)
   uint8_t* sQ = smem;
   auto sK = [&](int st) { return smem + (1 + 2 * st) * kTile; };
   auto sV = [&](int st) { return smem + (2 + 2 * st) * kTile; };
+  auto sdesc_k = [](uint32_t a) { return kD == 64 ? make_sdesc_sw128(a) : make_sdesc_sw64(a); };
+  auto sdesc_mn = [](uint32_t a) { return kD == 64 ? make_sdesc_sw128_mn(a) : make_sdesc_sw64_mn(a); };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -257,7 +238,7 @@ __global__ void __launch_bounds__(320, 2)
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
       mbar_arrive_expect_tx(q_full, kTile);
-      tma_load_2d(sQ, &tq, q_full, head * kD, row0 + qt * kQ);
+      tma_load_2d(sQ, &tq, q_full, hx, row0 + qt * kQ);
     }
     __syncwarp();
     for (int j = 0; j < n_kv; ++j) {
@@ -265,8 +246,8 @@ __global__ void __launch_bounds__(320, 2)
       if (!mbar_wait_warp(&kv_empty[st], ((j / kStages) & 1) ^ 1, kErrStageFree, abort_flag)) break;
       if (elect_one()) {
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
-        tma_load_2d(sK(st), &tk, &kv_full[st], head * kD, row0 + j * kKV);
-        tma_load_2d(sV(st), &tv, &kv_full[st], head * kD, row0 + j * kKV);
+        tma_load_2d(sK(st), &tk, &kv_full[st], hx, row0 + j * kKV);
+        tma_load_2d(sV(st), &tv, &kv_full[st], hx, row0 + j * kKV);
       }
       __syncwarp();
     }
@@ -276,7 +257,7 @@ __global__ void __launch_bounds__(320, 2)
     const uint32_t fmt = kBf16 ? 1u : 0u;
     const uint32_t idesc_pv = make_idesc(fmt, kQ, kD, 1u);
     bool ok = mbar_wait_warp(q_full, 0, kErrTmaWait, abort_flag);
-    const uint64_t qdesc = make_sdesc_sw128(smem_u32(sQ));
+    const uint64_t qdesc = sdesc_k(smem_u32(sQ));
     auto keys_in = [&](int j) {  // keys of tile j, rounded up to a multiple of 16
       const int left = seq - j * kKV;
       return left >= kKV ? kKV : ((left + 15) & ~15);
@@ -287,10 +268,11 @@ __global__ void __launch_bounds__(320, 2)
       if (!mbar_wait_warp(&kv_full[st], (j / kStages) & 1, kErrTmaWait, abort_flag)) return false;
       if (!mbar_wait_warp(s_empty, (j & 1) ^ 1, kErrAccFree, abort_flag)) return false;
       tc_fence_after();
-      const uint64_t kdesc = make_sdesc_sw128(smem_u32(sK(st)));
+      const uint64_t kdesc = sdesc_k(smem_u32(sK(st)));
       const uint32_t idesc_s = make_idesc(fmt, kQ, keys_in(j));
 #pragma unroll
-      for (int kk = 0; kk < kD / 16; ++kk) umma_ss_warp(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
+      for (int kk = 0; kk < kD / 16; ++kk)  // 16 elements = 32 bytes along K
+        umma_ss_warp(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
       umma_commit_warp(s_full);
       return true;
     };
@@ -301,14 +283,15 @@ __global__ void __launch_bounds__(320, 2)
       if (!mbar_wait_warp(p_full, j & 1, kErrAccFull, abort_flag)) break;
       tc_fence_after();
       const int st = j % kStages, n = keys_in(j);
-      const uint64_t vdesc = make_sdesc_sw128_mn(smem_u32(sV(st)));
+      const uint64_t vdesc = sdesc_mn(smem_u32(sV(st)));
+      constexpr uint32_t kVStep = 16 * HC::kRowBytes >> 4;  // 16 keys of V, in descriptor units
       if (n == kKV) {
 #pragma unroll
         for (int kk = 0; kk < kKV / 16; ++kk)  // A = P from TMEM: 16 keys = 8 columns
-          umma_ts_warp(tO, tP + kk * 8, vdesc + kk * (2048 >> 4), idesc_pv, (j | kk) ? 1u : 0u);
+          umma_ts_warp(tO, tP + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
       } else {
         for (int kk = 0; kk < n / 16; ++kk)
-          umma_ts_warp(tO, tP + kk * 8, vdesc + kk * (2048 >> 4), idesc_pv, (j | kk) ? 1u : 0u);
+          umma_ts_warp(tO, tP + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
       }
       umma_commit_warp(p_empty);
       umma_commit_warp(&kv_empty[st]);
@@ -322,6 +305,39 @@ __global__ void __launch_bounds__(320, 2)
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t scol = half * kHalf;  // first S column / key of this warp
+    // With a bias the scores are scaled (and biased) on load; the softmax
+    // then works on them with the plain log2(e) factor.
+    const float sl2 = kBias ? 1.4426950408889634f : prm.scale_log2;
+    const float* brow = nullptr;
+    if constexpr (kBias) {
+      const int q = min(qt * kQ + r, seq - 1);
+      brow = prm.bias + (static_cast<int64_t>(head) * seq + q) * prm.bias_ld;
+    }
+    // S columns [c0, c0+64) of key tile j -> sv (scaled and biased if kBias,
+    // keys >= seq set to -inf)
+    auto load_s = [&](float* sv, uint32_t* su, uint32_t c0, int kfirst) {
+#pragma unroll
+      for (int c = 0; c < kHalf / 32; ++c)
+        tmem_ld_32x32b_x32(tS + lane_off + c0 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
+      tmem_ld_wait();
+      if constexpr (kBias) {
+#pragma unroll
+        for (int c = 0; c < kHalf; c += 4) {
+          if (kfirst + c < seq) {  // bias rows are padded to a multiple of 4
+            const float4 b = __ldg(reinterpret_cast<const float4*>(brow + kfirst + c));
+            sv[c] = fmaf(sv[c], prm.scale, b.x);
+            sv[c + 1] = fmaf(sv[c + 1], prm.scale, b.y);
+            sv[c + 2] = fmaf(sv[c + 2], prm.scale, b.z);
+            sv[c + 3] = fmaf(sv[c + 3], prm.scale, b.w);
+          }
+        }
+      }
+      if (kfirst + kHalf > seq) {  // ragged last tile: keys >= seq do not exist
+#pragma unroll
+        for (int c = 0; c < kHalf; ++c)
+          if (kfirst + c >= seq) sv[c] = -INFINITY;
+      }
+    };
     float m_used = -INFINITY, l = 0.f;
     // A warp whose 32 query rows all lie past the group end (the last query
     // tile of a 576-token window) only keeps the barrier protocol going.
@@ -341,85 +357,57 @@ __global__ void __launch_bounds__(320, 2)
         // maximum of the other key half first (its values are discarded)
         const int kbo = j * kKV + (scol ^ kHalf);
         if (kbo < seq) {
-#pragma unroll
-          for (int c = 0; c < kHalf / 32; ++c)
-            tmem_ld_32x32b_x32(tS + lane_off + (scol ^ kHalf) + c * 32,
-                               *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
-          tmem_ld_wait();
-          if (kbo + kHalf > seq) {
-#pragma unroll
-            for (int c = 0; c < kHalf; ++c)
-              if (kbo + c >= seq) sv[c] = -INFINITY;
-          }
+          load_s(sv, su, scol ^ kHalf, kbo);
           mt = max64(sv);
         }
       }
-      if (live) {  // this warp's 64 S columns -> registers
-#pragma unroll
-        for (int c = 0; c < kHalf / 32; ++c)
-          tmem_ld_32x32b_x32(tS + lane_off + scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
-        tmem_ld_wait();
-      }
+      if (live) load_s(sv, su, scol, kb);  // this warp's 64 S columns
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_empty);  // S may be overwritten
-      if (live) {
-        if (kb + kHalf > seq) {  // ragged last tile: keys >= seq do not exist
-#pragma unroll
-          for (int c = 0; c < kHalf; ++c)
-            if (kb + c >= seq) sv[c] = -INFINITY;
-        }
-        mt = fmaxf(mt, max64(sv));
-      }
-      const bool need = (mt - m_used) * scale_log2 > kRescaleLog2;
+      if (live) mt = fmaxf(mt, max64(sv));
+      const bool need = (mt - m_used) * sl2 > kRescaleLog2;
       // P buffer and O are free once the previous P.V finished
       if (j > 0 && !warp_wait(p_empty, (j - 1) & 1, kErrAccFree, abort_flag, lane)) { ok = false; break; }
       tc_fence_after();
       if (__any_sync(0xffffffffu, need)) {  // same rows, same verdict in both halves
         const float m_new = fmaxf(m_used, mt);
-        const float corr = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * scale_log2);
+        const float corr = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * sl2);
         l *= corr;
         m_used = m_new;
-        if (j > 0) {  // this half rescales O columns [32*half, 32*half+32)
+        if (j > 0) {  // this half rescales O columns [kOHalf*half, kOHalf*(half+1))
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {  // 8 columns at a time: few live registers
+          for (int c = 0; c < kOHalf / 8; ++c) {  // 8 columns at a time: few live registers
             uint32_t u[8];
-            tmem_ld_32x32b_x8(tO + lane_off + half * 32 + c * 8, u);
+            tmem_ld_32x32b_x8(tO + lane_off + half * kOHalf + c * 8, u);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 8; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * corr);
-            tmem_st_32x32b_x8(tO + lane_off + half * 32 + c * 8, u);
+            tmem_st_32x32b_x8(tO + lane_off + half * kOHalf + c * 8, u);
           }
           tmem_st_wait();
         }
       }
       // P = exp2(S*c - m) -> 16-bit pairs into TMEM columns 192 + 32*half
       if (live) {
-        const float mb = m_used * scale_log2;
+        const float mb = m_used * sl2;
         // e = S*c - m and the row sums on packed f32x2 lanes (keys c, c+1)
-        const uint64_t sc2 = f2pack(scale_log2, scale_log2), nmb2 = f2pack(-mb, -mb);
+        const uint64_t sc2 = f2pack(sl2, sl2), nmb2 = f2pack(-mb, -mb);
         uint64_t l2[2] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
 #pragma unroll
         for (int c0 = 0; c0 < kHalf; c0 += 16) {  // 16 keys -> 8 columns at a time: few live registers
           uint32_t pk[8];
 #pragma unroll
           for (int c = c0; c < c0 + 16; c += 2) {
-            const uint64_t e2 = ffma2(f2pack(sv[c], sv[c + 1]), sc2, nmb2);
-            float p0, p1;
-            if ((c & 7) < kFmaExp) {  // split SFU / FMA pipe
-              exp2_fma_x2(e2, p0, p1);
-            } else {
-              float e0, e1;
-              f2unpack(e2, e0, e1);
-              p0 = ex2(e0);
-              p1 = ex2(e1);
-            }
+            float e0, e1;
+            f2unpack(ffma2(f2pack(sv[c], sv[c + 1]), sc2, nmb2), e0, e1);
+            const float p0 = ex2(e0), p1 = ex2(e1);
             l2[(c >> 1) & 1] = fadd2(l2[(c >> 1) & 1], f2pack(p0, p1));
             pk[(c - c0) / 2] = pack2(p0, p1, kBf16);
           }
           tmem_st_32x32b_x8(tP + lane_off + half * (kHalf / 2) + c0 / 2, pk);
         }
-        float a0, a1, b0, b1;
+        float a0, a1;
         f2unpack(fadd2(l2[0], l2[1]), a0, a1);
         l += a0 + a1;
         tmem_st_wait();
@@ -436,13 +424,16 @@ __global__ void __launch_bounds__(320, 2)
     if (o_ok) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int qrow = qt * kQ + r;
-      uint16_t* orow = o + static_cast<int64_t>(row0 + qrow) * ldo + head * kD + half * 32;
-      uint32_t u[32];
-      tmem_ld_32x32b_x32(tO + lane_off + half * 32, u);
+      uint16_t* orow = prm.o + static_cast<int64_t>(row0 + qrow) * prm.ldo + head * prm.o_hstride + half * kOHalf;
+      uint32_t u[kOHalf];
+      if constexpr (kD == 64)
+        tmem_ld_32x32b_x32(tO + lane_off + half * kOHalf, u);
+      else
+        tmem_ld_32x32b_x16(tO + lane_off + half * kOHalf, u);
       tmem_ld_wait();
       if (qrow < seq) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
+        for (int q4 = 0; q4 < kOHalf / 8; ++q4) {
           uint4 w;
           w.x = pack2(__uint_as_float(u[q4 * 8 + 0]) * inv, __uint_as_float(u[q4 * 8 + 1]) * inv, kBf16);
           w.y = pack2(__uint_as_float(u[q4 * 8 + 2]) * inv, __uint_as_float(u[q4 * 8 + 3]) * inv, kBf16);
@@ -461,47 +452,93 @@ __global__ void __launch_bounds__(320, 2)
   }
 }
 
-bool make_head_map(CUtensorMap* m, const void* base, int dtype, int64_t rows, int heads, int64_t ld) {
+// [rows, width] 16-bit matrix of row pitch ld, boxes of 128 rows x head_dim
+// columns (128- or 64-byte swizzle, matching the kernel's descriptors).
+bool make_head_map(CUtensorMap* m, const void* base, int dtype, int64_t rows, int64_t width, int64_t ld,
+                   int head_dim) {
   const CUtensorMapDataType dt = dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return make_tmap_2d(m, base, dt, 2, rows, static_cast<uint64_t>(heads) * kD, ld, kQ, kD,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
+  return make_tmap_2d(m, base, dt, 2, rows, width, ld, kQ, head_dim,
+                      head_dim == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
-template <bool kBf16>
-int launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, void* o, int64_t ldo,
-                   int seq, int q_tiles, dim3 grid, float scale_log2, cudaStream_t st) {
+template <bool kBf16, int kD, bool kBias>
+int launch_variant(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& prm,
+                   dim3 grid, cudaStream_t st) {
+  constexpr int smem = HeadCfg<kD>::kSmem;
   static bool done = false;
   if (!done) {
-    cudaFuncSetAttribute(attn_tc_kernel<kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaFuncSetAttribute(attn_tc_kernel<kBf16, kD, kBias>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     // full shared-memory carveout, so two CTAs fit on one SM
-    cudaFuncSetAttribute(attn_tc_kernel<kBf16>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(attn_tc_kernel<kBf16, kD, kBias>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     done = true;
   }
-  attn_tc_kernel<kBf16><<<grid, kThreads, kSmem, st>>>(mq, mk, mv, static_cast<uint16_t*>(o), ldo, seq, q_tiles,
-                                                        scale_log2);
+  attn_tc_kernel<kBf16, kD, kBias><<<grid, kThreads, smem, st>>>(mq, mk, mv, prm);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 }  // namespace
 
+int launch_attention_tc_ex(const AttnArgs& a, cudaStream_t st) {
+  if (a.head_dim != 64 && a.head_dim != 32) return kErrShape;
+  if (a.dtype != kBF16 && a.dtype != kF16) return kErrDtype;
+  const int in_hs = a.in_hstride > 0 ? a.in_hstride : a.head_dim;
+  const int o_hs = a.o_hstride > 0 ? a.o_hstride : a.head_dim;
+  // TMA: 16-byte row pitch and column starts; vector output stores
+  if (a.ldq % 8 || a.ldo % 8 || in_hs % 8 || o_hs % 8 || (reinterpret_cast<uintptr_t>(a.o) & 15)) return kErrShape;
+  if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v)) & 15)
+    return kErrShape;
+  if (a.bias && (a.bias_ld % 4 || a.bias_ld < a.seq || (reinterpret_cast<uintptr_t>(a.bias) & 15))) return kErrShape;
+  if (a.n_groups <= 0 || a.seq <= 0 || a.heads <= 0) return kOk;
+  const int64_t rows = static_cast<int64_t>(a.n_groups) * a.seq;
+  if (rows > 0x7fffffffLL) return kErrShape;
+  const int64_t width = static_cast<int64_t>(a.heads - 1) * in_hs + a.head_dim;  // last head ends here
+  CUtensorMap mq, mk, mv;
+  if (!make_head_map(&mq, a.q, a.dtype, rows, width, a.ldq, a.head_dim) ||
+      !make_head_map(&mk, a.k, a.dtype, rows, width, a.ldq, a.head_dim) ||
+      !make_head_map(&mv, a.v, a.dtype, rows, width, a.ldq, a.head_dim))
+    return kErrTma;
+  AttnParams prm;
+  prm.o = static_cast<uint16_t*>(a.o);
+  prm.ldo = a.ldo;
+  prm.o_hstride = o_hs;
+  prm.in_hstride = in_hs;
+  prm.seq = a.seq;
+  prm.q_tiles = (a.seq + kQ - 1) / kQ;
+  prm.scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf(static_cast<float>(a.head_dim));
+  prm.scale_log2 = prm.scale * 1.4426950408889634f;
+  prm.bias = a.bias;
+  prm.bias_ld = a.bias_ld;
+  dim3 grid(a.n_groups * prm.q_tiles, a.heads);
+  count_launches(1);
+  const bool bf = a.dtype == kBF16, b = a.bias != nullptr;
+  if (a.head_dim == 64) {
+    if (b) return bf ? launch_variant<true, 64, true>(mq, mk, mv, prm, grid, st)
+                     : launch_variant<false, 64, true>(mq, mk, mv, prm, grid, st);
+    return bf ? launch_variant<true, 64, false>(mq, mk, mv, prm, grid, st)
+              : launch_variant<false, 64, false>(mq, mk, mv, prm, grid, st);
+  }
+  if (b) return bf ? launch_variant<true, 32, true>(mq, mk, mv, prm, grid, st)
+                   : launch_variant<false, 32, true>(mq, mk, mv, prm, grid, st);
+  return bf ? launch_variant<true, 32, false>(mq, mk, mv, prm, grid, st)
+            : launch_variant<false, 32, false>(mq, mk, mv, prm, grid, st);
+}
+
 int launch_attention_tc(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,
                         int n_groups, int seq, int heads, int head_dim, cudaStream_t st) {
-  if (head_dim != kD) return kErrShape;
-  if (dtype != kBF16 && dtype != kF16) return kErrDtype;
-  if (ldq % 8 || ldo % 8 || (reinterpret_cast<uintptr_t>(o) & 15)) return kErrShape;
-  if (n_groups <= 0 || seq <= 0 || heads <= 0) return kOk;
-  const int64_t rows = static_cast<int64_t>(n_groups) * seq;
-  if (rows > 0x7fffffffLL) return kErrShape;
-  CUtensorMap mq, mk, mv;
-  if (!make_head_map(&mq, q, dtype, rows, heads, ldq) || !make_head_map(&mk, k, dtype, rows, heads, ldq) ||
-      !make_head_map(&mv, v, dtype, rows, heads, ldq))
-    return kErrTma;
-  const int q_tiles = (seq + kQ - 1) / kQ;
-  dim3 grid(n_groups * q_tiles, heads);
-  const float scale_log2 = (1.0f / sqrtf(static_cast<float>(head_dim))) * 1.4426950408889634f;
-  count_launches(1);
-  if (dtype == kBF16) return launch_variant<true>(mq, mk, mv, o, ldo, seq, q_tiles, grid, scale_log2, st);
-  return launch_variant<false>(mq, mk, mv, o, ldo, seq, q_tiles, grid, scale_log2, st);
+  AttnArgs a;
+  memset(&a, 0, sizeof(a));
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.ldq = ldq;
+  a.o = o;
+  a.ldo = ldo;
+  a.dtype = dtype;
+  a.n_groups = n_groups;
+  a.seq = seq;
+  a.heads = heads;
+  a.head_dim = head_dim;
+  return launch_attention_tc_ex(a, st);
 }
 
 }  // namespace s3

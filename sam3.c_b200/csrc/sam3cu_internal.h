@@ -32,6 +32,24 @@ unsigned int dev_error_attn();
 unsigned int dev_error_misc();
 int launch_attention_tc(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,
                         int n_groups, int seq, int heads, int head_dim, cudaStream_t st);
+// General form of the tcgen05 attention: head_dim 32 or 64, heads at any
+// column stride in Q/K/V (in_hstride, e.g. 3*head_dim for a per-head
+// interleaved q|k|v layout) and in O (o_hstride), an optional additive f32
+// bias [heads, seq, bias_ld] and an explicit scale (<= 0: 1/sqrt(head_dim)).
+struct AttnArgs {
+  const void *q, *k, *v;
+  int64_t ldq;
+  int in_hstride;
+  void* o;
+  int64_t ldo;
+  int o_hstride;
+  int dtype;
+  int n_groups, seq, heads, head_dim;
+  const float* bias;
+  int bias_ld;
+  float scale;
+};
+int launch_attention_tc_ex(const AttnArgs& a, cudaStream_t st);
 unsigned int dev_error_attn_tc();
 unsigned int dev_error_gemm2();
 int launch_attention(const void* q, const void* k, const void* v, int64_t ldq, void* o, int64_t ldo, int dtype,

@@ -344,6 +344,15 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -389,6 +398,28 @@ __device__ __forceinline__ void tmem_ld_wait() {
 // start>>4 in [0,14), LBO (unused for swizzled K-major, 1) in [16,30),
 // SBO = 1024 B between 8-row groups in [32,46), version 1 at bit 46,
 // layout SWIZZLE_128B = 2 in [61,64).
+// K-major operand, 64-byte swizzle (rows of 32 16-bit elements): 8-row
+// groups 512 bytes apart.
+__device__ __forceinline__ uint64_t make_sdesc_sw64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;
+  return d;
+}
+// MN-major operand with 64-byte rows (N = 32 16-bit elements, one swizzle
+// atom wide), 64-byte swizzle: 8 K-rows per 512-byte group.
+__device__ __forceinline__ uint64_t make_sdesc_sw64_mn(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(8192u >> 4) << 16;  // LBO (unused: one MN block)
+  d |= static_cast<uint64_t>(512u >> 4) << 32;   // SBO: next 8 K-rows
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;
+  return d;
+}
 __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);

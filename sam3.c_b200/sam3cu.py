@@ -28,6 +28,7 @@ EXPORTS = (
     "sam3cu_vit_encode", "sam3cu_vit_encode_async", "sam3cu_vit_stream",
     "sam3cu_vit_launches_per_encode", "sam3cu_vit_profile",
     "sam3_cuda_backend_ops", "sam3cu_conv2d_nhwc_noalloc",
+    "sam3cu_tvit_expand_bias", "sam3cu_tvit_window_attention",
 )
 
 # sizeof(struct sam3_cuda_backend): {enum type; ops*} + int device + void *impl
@@ -71,6 +72,9 @@ def lib():
         L.sam3cu_vit_launches_per_encode.argtypes = [vp, i32]
         L.sam3cu_conv2d_nhwc_noalloc.argtypes = [vp, vp, vp, vp] + [i32] * 10 + [vp]
         L.sam3cu_vit_profile.argtypes = [vp, vp, i32, vp, C.POINTER(C.c_double), C.POINTER(C.c_int)]
+        L.sam3cu_tvit_expand_bias.argtypes = [vp, i32, i32, i32, vp, i32]
+        L.sam3cu_tvit_window_attention.argtypes = [vp, i64, vp, i64, i32, i32, i32, i32, i32, vp, i32,
+                                                   vp]
         _lib = L
     return _lib
 
@@ -307,3 +311,39 @@ class VitEncoder:
         """Device tensors; enqueue on the encoder's stream, no wait."""
         check(lib().sam3cu_vit_encode_async(self.h, images.data_ptr(), images.shape[0],
                                             out.data_ptr()), "sam3cu_vit_encode_async")
+
+
+# ---------------------------------------------------------------- TinyViT
+def tvit_expand_bias(compact, ws: int, ld: int = 0):
+    """Host expansion of a compact [heads, ws*ws] TinyViT bias table into a
+    dense float32 numpy array [heads, ws*ws, ld] (ld rounded up to a
+    multiple of 4 by default, as the attention kernel needs)."""
+    import numpy as np
+    compact = np.ascontiguousarray(compact, np.float32)
+    heads, n_off = compact.shape
+    n = ws * ws
+    ld = ld or (n + 3) // 4 * 4
+    out = np.empty((heads, n, ld), np.float32)
+    check(lib().sam3cu_tvit_expand_bias(compact.ctypes.data, heads, n_off, ws, out.ctypes.data, ld),
+          "sam3cu_tvit_expand_bias")
+    return out
+
+
+def tvit_window_attention(qkv, n_windows: int, n_tokens: int, heads: int, head_dim: int,
+                          bias=None, out=None):
+    """TinyViT window attention on a per-head interleaved [T, 3*C] qkv
+    device tensor; bias: float32 device tensor [heads, n_tokens, ld]."""
+    import torch
+    rows, ld_qkv = qkv.shape
+    C_ = heads * head_dim
+    if out is None:
+        out = torch.empty((rows, C_), dtype=qkv.dtype, device=qkv.device)
+    bias_ld = 0
+    if bias is not None:
+        _f32(bias, "bias")
+        bias_ld = bias.shape[-1]
+    check(lib().sam3cu_tvit_window_attention(qkv.data_ptr(), ld_qkv, out.data_ptr(), out.shape[1],
+                                             dtype_code(qkv), n_windows, n_tokens, heads, head_dim,
+                                             _ptr(bias), bias_ld, _stream()),
+          "sam3cu_tvit_window_attention")
+    return out
