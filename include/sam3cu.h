@@ -28,7 +28,9 @@
  *   sam3cu_tvit_*
  *       the TinyViT hot ops of image_encoder_tinyvit.c: the relative
  *       position bias expansion (expand_attention_bias :265-335), the window
- *       attention after the qkv linear (tvit_window_attention :790-866).
+ *       attention after the qkv linear (tvit_window_attention :790-866),
+ *       the TinyViTBlock (tvit_block_forward :896-1052) and the MBConv
+ *       block (tvit_mbconv_forward :682-720).
  *   sam3_cuda_backend_ops (include/sam3cu_backend.h)
  *       the backend vtable struct sam3_backend_ops (src/backend/backend.h:29-56).
  *
@@ -173,6 +175,49 @@ SAM3CU_API int sam3cu_tvit_expand_bias(const float *compact, int heads, int n_of
 SAM3CU_API int sam3cu_tvit_window_attention(const void *qkv, int64_t ld_qkv, void *out, int64_t ld_out,
 		int dtype, int n_windows, int n_tokens, int heads, int head_dim,
 		const float *bias, int bias_ld, void *stream);
+
+/*
+ * One TinyViTBlock (tvit_block_forward, image_encoder_tinyvit.c:896-1052)
+ * on device: x [n_images, H, W, dim] NHWC f32, updated in place.  Weights
+ * are host F32 in the reference's layouts (sam3_tvit_block): linears
+ * [out, in], attn_bias the compact [heads, attn_bias_offsets] table,
+ * lc_w the depthwise [dim, 3, 3, 1] (OHWI) conv with its BatchNorm.
+ * Any pointer but qkv_w, proj_w, lc_w, fc1_w, fc2_w may be NULL (absent).
+ * dtype (BF16 / F16) is the type of the GEMM and attention operands;
+ * accumulation and the residual stream stay f32.
+ */
+struct sam3cu_tvit_block_weights {
+	const float *attn_norm_w, *attn_norm_b, *qkv_w, *qkv_b, *proj_w, *proj_b;
+	const float *attn_bias;
+	int attn_bias_offsets;
+	const float *lc_w, *lc_b, *lc_bn_w, *lc_bn_b, *lc_bn_mean, *lc_bn_var;
+	const float *mlp_norm_w, *mlp_norm_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+};
+typedef struct sam3cu_tvit_block sam3cu_tvit_block;
+SAM3CU_API sam3cu_tvit_block *sam3cu_tvit_block_create(int dim, int heads, int window_size,
+		int mlp_dim, int dtype, const struct sam3cu_tvit_block_weights *w, int *status);
+SAM3CU_API int sam3cu_tvit_block_forward(sam3cu_tvit_block *blk, float *x, int n_images,
+		int H, int W, void *stream);
+SAM3CU_API void sam3cu_tvit_block_destroy(sam3cu_tvit_block *blk);
+
+/*
+ * One MBConv block (tvit_mbconv_forward, image_encoder_tinyvit.c:682-720)
+ * on device: conv1 1x1 + BN, GELU, depthwise 3x3 + BN, GELU, conv3 1x1 +
+ * BN, + shortcut, GELU; x [n_images, H, W, dim] NHWC f32 in place.  conv1_w
+ * [mid, 1, 1, dim], conv2_w [mid, 3, 3, 1], conv3_w [dim, 1, 1, mid]
+ * (OHWI); conv biases and BN tensors may be NULL.
+ */
+struct sam3cu_tvit_mbconv_weights {
+	const float *conv1_w, *conv1_b, *bn1_w, *bn1_b, *bn1_mean, *bn1_var;
+	const float *conv2_w, *conv2_b, *bn2_w, *bn2_b, *bn2_mean, *bn2_var;
+	const float *conv3_w, *conv3_b, *bn3_w, *bn3_b, *bn3_mean, *bn3_var;
+};
+typedef struct sam3cu_tvit_mbconv sam3cu_tvit_mbconv;
+SAM3CU_API sam3cu_tvit_mbconv *sam3cu_tvit_mbconv_create(int dim, int mid_dim, int dtype,
+		const struct sam3cu_tvit_mbconv_weights *w, int *status);
+SAM3CU_API int sam3cu_tvit_mbconv_forward(sam3cu_tvit_mbconv *mb, float *x, int n_images,
+		int H, int W, void *stream);
+SAM3CU_API void sam3cu_tvit_mbconv_destroy(sam3cu_tvit_mbconv *mb);
 
 /* ------------------------------------------- per-node ops (backend vtable)
  * Device helpers and the remaining encoder-graph ops, used by the

@@ -748,3 +748,55 @@ void orc_tvit_block_forward(const struct orc_tvit_block *bw, float *x, int H,
 	free(h1);
 	free(ln);
 }
+
+/* 1x1 conv (NHWC, OHWI [O,1,1,I] == linear [O, I]) + optional conv bias +
+ * eval BatchNorm + optional GELU: tvit_conv_bn (:655-674) for the MBConv
+ * pointwise convs.  x [P, I] -> y [P, O]. */
+static void conv1x1_bn(const float *x, int64_t P, int I, int O, const float *w,
+		       const float *cb, const float *g, const float *be,
+		       const float *mean, const float *var, int gelu, float *y)
+{
+	orc_linear(x, w, cb, NULL, y, (int)P, I, O, 0);
+#pragma omp parallel for schedule(static)
+	for (int64_t p = 0; p < P; p++)
+		for (int o = 0; o < O; o++) {
+			float v = y[p * O + o];
+			if (mean) {
+				v = (v - mean[o]) * (1.0f / sqrtf(var[o] + 1e-5f));
+				if (g)
+					v *= g[o];
+				if (be)
+					v += be[o];
+			}
+			y[p * O + o] = gelu ? gelu_tanh(v) : v;
+		}
+}
+
+struct orc_tvit_mbconv {
+	const float *conv1_w, *conv1_b, *bn1_w, *bn1_b, *bn1_mean, *bn1_var;
+	const float *conv2_w, *conv2_b, *bn2_w, *bn2_b, *bn2_mean, *bn2_var;
+	const float *conv3_w, *conv3_b, *bn3_w, *bn3_b, *bn3_mean, *bn3_var;
+};
+
+/* tvit_mbconv_forward (:682-720) on x [B, H, W, C] NHWC, in place: conv1
+ * 1x1 + BN, GELU; depthwise 3x3 + BN, GELU; conv3 1x1 + BN; + shortcut;
+ * GELU. */
+void orc_tvit_mbconv_forward(const struct orc_tvit_mbconv *m, float *x, int B,
+			     int H, int W, int C, int mid)
+{
+	const int64_t P = (int64_t)B * H * W;
+	float *h = malloc(sizeof(float) * (size_t)P * mid);
+	float *h2 = malloc(sizeof(float) * (size_t)P * mid);
+	float *o = malloc(sizeof(float) * (size_t)P * C);
+	conv1x1_bn(x, P, C, mid, m->conv1_w, m->conv1_b, m->bn1_w, m->bn1_b,
+		   m->bn1_mean, m->bn1_var, 1, h);
+	orc_dwconv3x3_bn(h, B, H, W, mid, m->conv2_w, m->conv2_b, m->bn2_w,
+			 m->bn2_b, m->bn2_mean, m->bn2_var, 1, h2);
+	conv1x1_bn(h2, P, mid, C, m->conv3_w, m->conv3_b, m->bn3_w, m->bn3_b,
+		   m->bn3_mean, m->bn3_var, 0, o);
+	for (int64_t i = 0; i < P * C; i++)
+		x[i] = gelu_tanh(o[i] + x[i]);
+	free(h);
+	free(h2);
+	free(o);
+}

@@ -516,3 +516,32 @@ def tvit_block_forward(w: dict, x: np.ndarray, heads: int, ws: int) -> np.ndarra
     orc().orc_tvit_block_forward(C.byref(s), _p(x), H, W, Cc, heads, ws, mlp)
     del keep
     return x
+
+
+TVIT_MBCONV_KEYS = tuple(f"{c}{i}_{k}" if c == "bn" else f"conv{i}_{k}"
+                         for i in (1, 2, 3) for c, ks in (("conv", ("w", "b")),
+                                                          ("bn", ("w", "b", "mean", "var")))
+                         for k in ks)
+
+
+class _TvitMb(C.Structure):
+    _fields_ = [(n, VP) for n in TVIT_MBCONV_KEYS]
+
+
+def tvit_mbconv_forward(w: dict, x: np.ndarray) -> np.ndarray:
+    """Restatement of tvit_mbconv_forward on NHWC x [B, H, W, C]."""
+    x = np.array(x, np.float32, copy=True, order="C")
+    B, H, W, Cc = x.shape
+    s = _TvitMb()
+    keep = []
+    for n in TVIT_MBCONV_KEYS:
+        if w.get(n) is None:
+            setattr(s, n, None)
+            continue
+        a = np.ascontiguousarray(w[n], np.float32)
+        keep.append(a)
+        setattr(s, n, a.ctypes.data)
+    mid = w["conv1_w"].shape[0]
+    orc().orc_tvit_mbconv_forward(C.byref(s), _p(x), B, H, W, Cc, mid)
+    del keep
+    return x

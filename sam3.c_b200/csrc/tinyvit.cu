@@ -5,21 +5,319 @@
 //                                qkv linear: the reshape / slice / permute
 //                                / scale / QK^T / +bias / softmax / .V /
 //                                permute-back nodes as one tcgen05 kernel
+// sam3cu_tvit_block_*            tvit_block_forward (:896-1052)
+// sam3cu_tvit_mbconv_*           tvit_mbconv_forward (:682-720)
+//
+// The residual stream is NHWC f32 [images * H * W, C] in raster order, as
+// in the reference.  Per TinyViTBlock (T = 16-bit activation type):
+//   LN-gather  x -> xn T, rows in window-major order over the zero-padded
+//              image (pad tokens are LayerNorm(0) = beta, as after the
+//              reference's concat-with-zeros, :916-956)
+//   QKV GEMM   xn . Wqkv^T + b -> qkv T [Tw, 3C] (per-head interleaved)
+//   ATTN       window attention + relative position bias -> ao T [Tw, C]
+//   PROJ GEMM  ao . Wproj^T + b -> p f32 [Tw, C]
+//   UNPART     x[raster(t)] += p[t] for the tokens inside the image
+//   DWCONV     3x3 depthwise conv of x with the BatchNorm folded into its
+//              weights and bias -> lc f32
+//   LN         lc -> xn T
+//   FC1        xn . Wfc1^T + b, tanh-GELU -> h T
+//   FC2        h . Wfc2^T + b + lc -> x f32
+// Per MBConv (x f32 and its 16-bit copy xa):
+//   CONV1      xa . W1'^T + b1', GELU -> h T        (1x1 conv, BN folded)
+//   DWCONV     3x3 depthwise, BN folded, GELU -> h2 T
+//   CONV3      h2 . W3'^T + b3' + x -> x f32        (in place, TMA reduce-add)
+//   GELU       x = GELU(x), xa = T(x)
+// BatchNorm folding: w' = w * s, b' = (b - mean) * s + beta with
+// s = gamma / sqrtf(var + 1e-5) (cpu_batchnorm.c, eps 1e-5).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
 
 #include "../../include/sam3cu.h"
+#include "devbuf.cuh"
+#include "gemm_sm100.cuh"
+#include "io.cuh"
+#include "misc.cuh"
 #include "sam3cu_internal.h"
 
 using namespace s3;
 
 namespace {
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int ck(cudaError_t e) { return e == cudaSuccess ? kOk : kErrCuda; }
+
+int grid_1d(int64_t n, int block) {
+  int64_t g = (n + block - 1) / block;
+  return static_cast<int>(g < 1 ? 1 : (g > (1 << 30) ? (1 << 30) : g));
+}
+
+// Window-major padded token t of image b -> raster row of the unpadded
+// image, or -1 for a padding token.
+struct WinMap {
+  int H, W, ws, nwx, n_tok, per_img;  // per_img = windows * ws * ws
+  __device__ __forceinline__ int64_t src_row(int64_t t) const {
+    const int64_t b = t / per_img;
+    const int r = static_cast<int>(t - b * per_img);
+    const int w = r / n_tok, k = r - w * n_tok;
+    const int py = (w / nwx) * ws + k / ws, px = (w % nwx) * ws + k % ws;
+    if (py >= H || px >= W) return -1;
+    return (b * H + py) * W + px;
+  }
+};
+
+// LayerNorm of C-wide f32 rows (cpu_layernorm.c:31-64: mean, sum of squared
+// deviations, 1/sqrtf(var/C + 1e-5), gamma, beta), one warp per output row;
+// lane l holds columns l, l+32, ... (NE = C/32 of them).  With a window map
+// the output row t reads source row map.src_row(t) (a zero row if -1).
+template <int TO, int NE>
+__global__ void __launch_bounds__(256) ln_rows_tvit(const float* __restrict__ x, void* __restrict__ y,
+                                                    const float* __restrict__ g, const float* __restrict__ b,
+                                                    int64_t rows, int C, WinMap map, int use_map) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t src = use_map ? map.src_row(row) : row;
+  float v[NE];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NE; ++i) {
+    v[i] = src >= 0 ? x[src * C + i * 32 + lane] : 0.f;
+    s += v[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / static_cast<float>(C);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NE; ++i) {
+    const float d = v[i] - mean;
+    q += d * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float inv_std = 1.0f / sqrtf(q / static_cast<float>(C) + 1e-5f);
+#pragma unroll
+  for (int i = 0; i < NE; ++i) {
+    const int c = i * 32 + lane;
+    float r = (v[i] - mean) * inv_std;
+    if (g) r *= __ldg(g + c);
+    if (b) r += __ldg(b + c);
+    if (TO == kBF16)
+      static_cast<__nv_bfloat16*>(y)[row * C + c] = __float2bfloat16_rn(r);
+    else if (TO == kF16)
+      static_cast<__half*>(y)[row * C + c] = __float2half_rn(r);
+    else
+      static_cast<float*>(y)[row * C + c] = r;
+  }
+}
+
+template <int TO>
+int ln_tvit_dispatch(const float* x, void* y, const float* g, const float* b, int64_t rows, int C,
+                     const WinMap& m, int use_map, cudaStream_t st) {
+  const int grid = grid_1d(rows * 32, 256);
+  switch (C / 32) {
+#define S3_CASE(NE)                                                                             case NE:                                                                                        ln_rows_tvit<TO, NE><<<grid, 256, 0, st>>>(x, y, g, b, rows, C, m, use_map);               break;
+    S3_CASE(2) S3_CASE(3) S3_CASE(4) S3_CASE(6) S3_CASE(8) S3_CASE(9) S3_CASE(12) S3_CASE(16)
+    S3_CASE(18) S3_CASE(24) S3_CASE(32)
+#undef S3_CASE
+    default:
+      return kErrShape;
+  }
+  return ck(cudaGetLastError()) ? kErrLaunch : kOk;
+}
+
+int launch_ln_tvit(const float* x, void* y, int tout, const float* g, const float* b, int64_t rows, int C,
+                   const WinMap* m, cudaStream_t st) {
+  if (C % 32) return kErrShape;
+  count_launches(1);
+  WinMap mm{};
+  if (m) mm = *m;
+  const int use = m ? 1 : 0;
+  if (tout == kBF16) return ln_tvit_dispatch<kBF16>(x, y, g, b, rows, C, mm, use, st);
+  if (tout == kF16) return ln_tvit_dispatch<kF16>(x, y, g, b, rows, C, mm, use, st);
+  return ln_tvit_dispatch<kF32>(x, y, g, b, rows, C, mm, use, st);
+}
+
+// x[map.src_row(t)] += p[t] for the tokens inside the image (f32, C % 4 == 0).
+__global__ void unpartition_add(float* __restrict__ x, const float* __restrict__ p, int64_t rows, int C,
+                                WinMap map) {
+  const int c4 = C / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * c4) return;
+  const int64_t t = i / c4;
+  const int c = static_cast<int>(i - t * c4) * 4;
+  const int64_t dst = map.src_row(t);
+  if (dst < 0) return;
+  const float4 a = *reinterpret_cast<const float4*>(p + t * C + c);
+  float4* o = reinterpret_cast<float4*>(x + dst * C + c);
+  float4 v = *o;
+  v.x += a.x;
+  v.y += a.y;
+  v.z += a.z;
+  v.w += a.w;
+  *o = v;
+}
+
+__device__ __forceinline__ float gelu_f(float v) {
+  // 0.5*x*(1+tanh(sqrt(2/pi)*(x+0.044715x^3))), cpu_gelu.c:23-36
+  return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
+}
+
+// 3x3 depthwise conv, stride 1, zero padding 1, NHWC, four channels per
+// thread; w9 [9][C] (tap-major, BatchNorm folded), bias [C]; optional GELU.
+template <int TI, int TO, bool kGelu>
+__global__ void dwconv3x3(const void* __restrict__ x, void* __restrict__ y, const float* __restrict__ w9,
+                          const float* __restrict__ bias, int B, int H, int W, int C) {
+  const int c4 = C / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = static_cast<int64_t>(B) * H * W * c4;
+  if (i >= total) return;
+  const int c = static_cast<int>(i % c4) * 4;
+  const int64_t p = i / c4;
+  const int xx = static_cast<int>(p % W), yy = static_cast<int>((p / W) % H);
+  const int64_t img = p / (static_cast<int64_t>(H) * W);
+  float4 acc = __ldg(reinterpret_cast<const float4*>(bias + c));
+#pragma unroll
+  for (int ky = 0; ky < 3; ++ky) {
+    const int iy = yy + ky - 1;
+    if (iy < 0 || iy >= H) continue;
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx) {
+      const int ix = xx + kx - 1;
+      if (ix < 0 || ix >= W) continue;
+      const float4 v = IO<TI>::ld4(x, ((img * H + iy) * W + ix) * C + c);
+      const float4 k = __ldg(reinterpret_cast<const float4*>(w9 + (ky * 3 + kx) * C + c));
+      acc.x = fmaf(v.x, k.x, acc.x);
+      acc.y = fmaf(v.y, k.y, acc.y);
+      acc.z = fmaf(v.z, k.z, acc.z);
+      acc.w = fmaf(v.w, k.w, acc.w);
+    }
+  }
+  if (kGelu) {
+    acc.x = gelu_f(acc.x);
+    acc.y = gelu_f(acc.y);
+    acc.z = gelu_f(acc.z);
+    acc.w = gelu_f(acc.w);
+  }
+  IO<TO>::st4(y, p * C + c, acc);
+}
+
+int launch_dwconv3x3(const void* x, int tin, void* y, int tout, const float* w9, const float* bias, int B,
+                     int H, int W, int C, bool gelu, cudaStream_t st) {
+  if (C % 4) return kErrShape;
+  count_launches(1);
+  const int64_t total = static_cast<int64_t>(B) * H * W * (C / 4);
+  const int grid = grid_1d(total, 256);
+#define S3_DW(TI, TO)                                                                            if (tin == TI && tout == TO) {                                                                   if (gelu)                                                                                        dwconv3x3<TI, TO, true><<<grid, 256, 0, st>>>(x, y, w9, bias, B, H, W, C);                   else                                                                                             dwconv3x3<TI, TO, false><<<grid, 256, 0, st>>>(x, y, w9, bias, B, H, W, C);                  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;                                 }
+  S3_DW(kF32, kF32) S3_DW(kBF16, kBF16) S3_DW(kF16, kF16) S3_DW(kF32, kBF16) S3_DW(kF32, kF16)
+#undef S3_DW
+  return kErrDtype;
+}
+
+// x = GELU(x) in place (f32) and xa = x as 16-bit.
+template <int TO>
+__global__ void gelu_cast(float* __restrict__ x, void* __restrict__ xa, int64_t n4) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  float4 v = reinterpret_cast<float4*>(x)[i];
+  v.x = gelu_f(v.x);
+  v.y = gelu_f(v.y);
+  v.z = gelu_f(v.z);
+  v.w = gelu_f(v.w);
+  reinterpret_cast<float4*>(x)[i] = v;
+  IO<TO>::st4(xa, i * 4, v);
+}
+
+// Fold eval-mode BatchNorm into a conv/linear with out_ch output rows of
+// `per` weights each: w[o][...] *= s_o, b_o = (b_o - mean_o) * s_o + beta_o.
+void fold_bn(std::vector<float>& w, std::vector<float>& b, int out_ch, int per, const float* cb,
+             const float* gamma, const float* beta, const float* mean, const float* var) {
+  b.assign(out_ch, 0.f);
+  for (int o = 0; o < out_ch; ++o) {
+    float bias = cb ? cb[o] : 0.f;
+    float s = 1.f;
+    if (mean && var) {
+      s = 1.0f / sqrtf(var[o] + 1e-5f);
+      if (gamma) s *= gamma[o];
+      bias = (bias - mean[o]) * s + (beta ? beta[o] : 0.f);
+    }
+    for (int k = 0; k < per; ++k) w[static_cast<size_t>(o) * per + k] *= s;
+    b[o] = bias;
+  }
+}
+
+int upload(DevBuf& d, const void* h, size_t bytes, cudaStream_t st) {
+  if (!d.alloc(bytes)) return kErrNoMem;
+  return ck(cudaMemcpyAsync(d.p, h, bytes, cudaMemcpyHostToDevice, st));
+}
+
+// f32 host [N, K] -> device 16-bit [N, K]
+int upload_w16(DevBuf& d, const float* h, int N, int K, int dt, cudaStream_t st) {
+  DevBuf tmp;
+  const size_t n = static_cast<size_t>(N) * K;
+  int rc = upload(tmp, h, n * 4, st);
+  if (rc) return rc;
+  if (!d.alloc(n * 2)) return kErrNoMem;
+  if ((rc = launch_cast(tmp.p, kF32, d.p, dt, static_cast<int64_t>(n), st))) return rc;
+  return ck(cudaStreamSynchronize(st));
+}
+
+// Depthwise 3x3 weights [C,3,3,1] (OHWI) with BN folded -> device [9][C].
+int upload_dw(DevBuf& w9, DevBuf& bias, int C, const float* w, const float* cb, const float* g, const float* be,
+              const float* mean, const float* var, cudaStream_t st) {
+  std::vector<float> wf(w, w + static_cast<size_t>(C) * 9), bf;
+  fold_bn(wf, bf, C, 9, cb, g, be, mean, var);
+  std::vector<float> t(static_cast<size_t>(9) * C);
+  for (int c = 0; c < C; ++c)
+    for (int k = 0; k < 9; ++k) t[static_cast<size_t>(k) * C + c] = wf[static_cast<size_t>(c) * 9 + k];
+  int rc = upload(w9, t.data(), t.size() * 4, st);
+  if (rc) return rc;
+  if ((rc = upload(bias, bf.data(), bf.size() * 4, st))) return rc;
+  return ck(cudaStreamSynchronize(st));
+}
+
+EpiParams epi(void* out, int out_type, int ldo, const float* bias) {
+  EpiParams e;
+  memset(&e, 0, sizeof(e));
+  e.out = out;
+  e.out_type = out_type;
+  e.ldo = ldo;
+  e.bias = bias;
+  return e;
+}
+
+// Grow-only scratch buffer.
+int ensure(DevBuf& d, size_t bytes) {
+  if (d.p && d.bytes >= bytes) return kOk;
+  if (d.p) {
+    cudaFree(d.p);
+    d.p = nullptr;
+  }
+  return d.alloc(bytes) ? kOk : kErrNoMem;
+}
+
 }  // namespace
+
+struct sam3cu_tvit_block {
+  int C = 0, heads = 0, ws = 0, mlp = 0, act = kBF16;
+  DevBuf ln1_w, ln1_b, qkv_w, qkv_b, proj_w, proj_b, bias;  // bias [heads, N, bias_ld]
+  int bias_ld = 0;
+  DevBuf dw_w9, dw_b, ln2_w, ln2_b, fc1_w, fc1_b, fc2_w, fc2_b;
+  DevBuf xn, qkv, ao, pr, lc, h;  // scratch
+};
+
+struct sam3cu_tvit_mbconv {
+  int C = 0, mid = 0, act = kBF16;
+  DevBuf w1, b1, dw_w9, dw_b, w3, b3;
+  DevBuf xa, h, h2;  // scratch
+};
 
 extern "C" {
 
@@ -75,6 +373,191 @@ int sam3cu_tvit_window_attention(const void* qkv, int64_t ld_qkv, void* out, int
   a.bias_ld = bias_ld;
   a.scale = 0.f;  // 1/sqrt(head_dim), applied to the scores (the reference scales q)
   return launch_attention_tc_ex(a, as_stream(stream));
+}
+
+sam3cu_tvit_block* sam3cu_tvit_block_create(int dim, int heads, int ws, int mlp_dim, int dtype,
+                                            const struct sam3cu_tvit_block_weights* w, int* status) {
+  int rc = SAM3CU_OK;
+  auto fail = [&](int r) -> sam3cu_tvit_block* {
+    if (status) *status = r;
+    return nullptr;
+  };
+  if (!w || dim <= 0 || heads <= 0 || dim % heads || ws <= 0 || ws > 16 || mlp_dim <= 0) return fail(SAM3CU_EINVAL);
+  if (dtype != SAM3CU_BF16 && dtype != SAM3CU_F16) return fail(SAM3CU_EDTYPE);
+  const int hd = dim / heads;
+  if ((hd != 32 && hd != 64) || dim % 32 || mlp_dim % 8) return fail(SAM3CU_EINVAL);
+  if (!w->qkv_w || !w->proj_w || !w->lc_w || !w->fc1_w || !w->fc2_w) return fail(SAM3CU_EINVAL);
+  auto* b = new sam3cu_tvit_block();
+  b->C = dim;
+  b->heads = heads;
+  b->ws = ws;
+  b->mlp = mlp_dim;
+  b->act = dtype == SAM3CU_F16 ? kF16 : kBF16;
+  cudaStream_t st = nullptr;
+  const int C = dim, N = ws * ws;
+  auto vec = [&](DevBuf& d, const float* h, int n) {  // optional f32 vector (nullptr -> null buffer)
+    if (!h || rc) return;
+    rc = upload(d, h, static_cast<size_t>(n) * 4, st);
+  };
+  vec(b->ln1_w, w->attn_norm_w, C);
+  vec(b->ln1_b, w->attn_norm_b, C);
+  vec(b->qkv_b, w->qkv_b, 3 * C);
+  vec(b->proj_b, w->proj_b, C);
+  vec(b->ln2_w, w->mlp_norm_w, C);
+  vec(b->ln2_b, w->mlp_norm_b, C);
+  vec(b->fc1_b, w->fc1_b, mlp_dim);
+  vec(b->fc2_b, w->fc2_b, C);
+  if (!rc) rc = upload_w16(b->qkv_w, w->qkv_w, 3 * C, C, b->act, st);
+  if (!rc) rc = upload_w16(b->proj_w, w->proj_w, C, C, b->act, st);
+  if (!rc) rc = upload_w16(b->fc1_w, w->fc1_w, mlp_dim, C, b->act, st);
+  if (!rc) rc = upload_w16(b->fc2_w, w->fc2_w, C, mlp_dim, b->act, st);
+  if (!rc) rc = upload_dw(b->dw_w9, b->dw_b, C, w->lc_w, w->lc_b, w->lc_bn_w, w->lc_bn_b, w->lc_bn_mean,
+                          w->lc_bn_var, st);
+  if (!rc && w->attn_bias) {
+    b->bias_ld = (N + 3) / 4 * 4;
+    std::vector<float> dense(static_cast<size_t>(heads) * N * b->bias_ld);
+    rc = sam3cu_tvit_expand_bias(w->attn_bias, heads, w->attn_bias_offsets, ws, dense.data(), b->bias_ld);
+    if (!rc) rc = upload(b->bias, dense.data(), dense.size() * 4, st);
+  }
+  if (!rc) rc = ck(cudaDeviceSynchronize());
+  if (rc) {
+    delete b;
+    return fail(rc);
+  }
+  if (status) *status = SAM3CU_OK;
+  return b;
+}
+
+void sam3cu_tvit_block_destroy(sam3cu_tvit_block* b) { delete b; }
+
+int sam3cu_tvit_block_forward(sam3cu_tvit_block* b, float* x, int n_images, int H, int W, void* stream) {
+  if (!b || !x || n_images <= 0 || H <= 0 || W <= 0) return SAM3CU_EINVAL;
+  cudaStream_t st = as_stream(stream);
+  const int C = b->C, ws = b->ws, N = ws * ws, hd = C / b->heads;
+  const int nwy = (H + ws - 1) / ws, nwx = (W + ws - 1) / ws;
+  const int64_t per_img = static_cast<int64_t>(nwy) * nwx * N;
+  const int64_t Tw = per_img * n_images, Th = static_cast<int64_t>(n_images) * H * W;
+  if (Tw > 0x7fffffffLL || Th * b->mlp > (1LL << 40)) return SAM3CU_EINVAL;
+  const size_t es = 2;
+  int rc;
+  if ((rc = ensure(b->xn, static_cast<size_t>(std::max(Tw, Th)) * C * es)) ||
+      (rc = ensure(b->qkv, static_cast<size_t>(Tw) * 3 * C * es)) ||
+      (rc = ensure(b->ao, static_cast<size_t>(Tw) * C * es)) || (rc = ensure(b->pr, static_cast<size_t>(Tw) * C * 4)) ||
+      (rc = ensure(b->lc, static_cast<size_t>(Th) * C * 4)) ||
+      (rc = ensure(b->h, static_cast<size_t>(Th) * b->mlp * es)))
+    return rc;
+  WinMap m{H, W, ws, nwx, N, static_cast<int>(per_img)};
+  // window attention half (tvit_window_attention inside tvit_block_forward)
+  if ((rc = launch_ln_tvit(x, b->xn.p, b->act, b->ln1_w.as<float>(), b->ln1_b.as<float>(), Tw, C, &m, st)))
+    return rc;
+  EpiParams e = epi(b->qkv.p, b->act, 3 * C, b->qkv_b.as<float>());
+  if ((rc = launch_gemm(b->xn.p, C, b->qkv_w.p, C, nullptr, nullptr, b->act, GemmShape{static_cast<int>(Tw), 3 * C, C},
+                        e, st, 0)))
+    return rc;
+  if ((rc = sam3cu_tvit_window_attention(b->qkv.p, 3 * C, b->ao.p, C, b->act == kF16 ? SAM3CU_F16 : SAM3CU_BF16,
+                                         static_cast<int>(Tw / N), N, b->heads, hd, b->bias.as<float>(),
+                                         b->bias_ld, stream)))
+    return rc;
+  e = epi(b->pr.p, kOutF32, C, b->proj_b.as<float>());
+  if ((rc = launch_gemm(b->ao.p, C, b->proj_w.p, C, nullptr, nullptr, b->act, GemmShape{static_cast<int>(Tw), C, C},
+                        e, st, 0)))
+    return rc;
+  count_launches(1);
+  unpartition_add<<<grid_1d(Tw * (C / 4), 256), 256, 0, st>>>(x, b->pr.as<float>(), Tw, C, m);
+  if ((rc = ck(cudaGetLastError()))) return kErrLaunch;
+  // local conv (3x3 depthwise + BN) and the MLP
+  if ((rc = launch_dwconv3x3(x, kF32, b->lc.p, kF32, b->dw_w9.as<float>(), b->dw_b.as<float>(), n_images, H, W, C,
+                             false, st)))
+    return rc;
+  if ((rc = launch_ln_tvit(b->lc.as<float>(), b->xn.p, b->act, b->ln2_w.as<float>(), b->ln2_b.as<float>(), Th, C,
+                           nullptr, st)))
+    return rc;
+  e = epi(b->h.p, b->act, b->mlp, b->fc1_b.as<float>());
+  e.act = 1;
+  if ((rc = launch_gemm(b->xn.p, C, b->fc1_w.p, C, nullptr, nullptr, b->act,
+                        GemmShape{static_cast<int>(Th), b->mlp, C}, e, st, 0)))
+    return rc;
+  e = epi(x, kOutF32, C, b->fc2_b.as<float>());
+  e.residual = b->lc.as<float>();
+  e.ldr = C;
+  return launch_gemm(b->h.p, b->mlp, b->fc2_w.p, b->mlp, nullptr, nullptr, b->act,
+                     GemmShape{static_cast<int>(Th), C, b->mlp}, e, st, 0);
+}
+
+sam3cu_tvit_mbconv* sam3cu_tvit_mbconv_create(int dim, int mid_dim, int dtype,
+                                              const struct sam3cu_tvit_mbconv_weights* w, int* status) {
+  auto fail = [&](int r) -> sam3cu_tvit_mbconv* {
+    if (status) *status = r;
+    return nullptr;
+  };
+  if (!w || dim <= 0 || mid_dim <= 0 || dim % 8 || mid_dim % 8) return fail(SAM3CU_EINVAL);
+  if (!w->conv1_w || !w->conv2_w || !w->conv3_w) return fail(SAM3CU_EINVAL);
+  if (dtype != SAM3CU_BF16 && dtype != SAM3CU_F16) return fail(SAM3CU_EDTYPE);
+  auto* m = new sam3cu_tvit_mbconv();
+  m->C = dim;
+  m->mid = mid_dim;
+  m->act = dtype == SAM3CU_F16 ? kF16 : kBF16;
+  cudaStream_t st = nullptr;
+  int rc = kOk;
+  std::vector<float> wf, bf;
+  // conv1 1x1 [mid, 1, 1, C] == linear [mid, C]; conv3 [C, 1, 1, mid]
+  wf.assign(w->conv1_w, w->conv1_w + static_cast<size_t>(mid_dim) * dim);
+  fold_bn(wf, bf, mid_dim, dim, w->conv1_b, w->bn1_w, w->bn1_b, w->bn1_mean, w->bn1_var);
+  rc = upload_w16(m->w1, wf.data(), mid_dim, dim, m->act, st);
+  if (!rc) rc = upload(m->b1, bf.data(), bf.size() * 4, st);
+  if (!rc) {
+    wf.assign(w->conv3_w, w->conv3_w + static_cast<size_t>(dim) * mid_dim);
+    fold_bn(wf, bf, dim, mid_dim, w->conv3_b, w->bn3_w, w->bn3_b, w->bn3_mean, w->bn3_var);
+    rc = upload_w16(m->w3, wf.data(), dim, mid_dim, m->act, st);
+  }
+  if (!rc) rc = upload(m->b3, bf.data(), bf.size() * 4, st);
+  if (!rc) rc = upload_dw(m->dw_w9, m->dw_b, mid_dim, w->conv2_w, w->conv2_b, w->bn2_w, w->bn2_b, w->bn2_mean,
+                          w->bn2_var, st);
+  if (!rc) rc = ck(cudaDeviceSynchronize());
+  if (rc) {
+    delete m;
+    return fail(rc);
+  }
+  if (status) *status = SAM3CU_OK;
+  return m;
+}
+
+void sam3cu_tvit_mbconv_destroy(sam3cu_tvit_mbconv* m) { delete m; }
+
+int sam3cu_tvit_mbconv_forward(sam3cu_tvit_mbconv* m, float* x, int n_images, int H, int W, void* stream) {
+  if (!m || !x || n_images <= 0 || H <= 0 || W <= 0) return SAM3CU_EINVAL;
+  cudaStream_t st = as_stream(stream);
+  const int64_t Th = static_cast<int64_t>(n_images) * H * W;
+  if (Th > 0x7fffffffLL) return SAM3CU_EINVAL;
+  const size_t es = 2;
+  int rc;
+  if ((rc = ensure(m->xa, static_cast<size_t>(Th) * m->C * es)) ||
+      (rc = ensure(m->h, static_cast<size_t>(Th) * m->mid * es)) ||
+      (rc = ensure(m->h2, static_cast<size_t>(Th) * m->mid * es)))
+    return rc;
+  const int M = static_cast<int>(Th);
+  if ((rc = launch_cast(x, kF32, m->xa.p, m->act, Th * m->C, st))) return rc;
+  EpiParams e = epi(m->h.p, m->act, m->mid, m->b1.as<float>());
+  e.act = 1;
+  if ((rc = launch_gemm(m->xa.p, m->C, m->w1.p, m->C, nullptr, nullptr, m->act, GemmShape{M, m->mid, m->C}, e, st,
+                        0)))
+    return rc;
+  if ((rc = launch_dwconv3x3(m->h.p, m->act, m->h2.p, m->act, m->dw_w9.as<float>(), m->dw_b.as<float>(), n_images,
+                             H, W, m->mid, true, st)))
+    return rc;
+  e = epi(x, kOutF32, m->C, m->b3.as<float>());
+  e.residual = x;  // in place: x += conv3(...) (TMA reduce-add)
+  e.ldr = m->C;
+  if ((rc = launch_gemm(m->h2.p, m->mid, m->w3.p, m->mid, nullptr, nullptr, m->act, GemmShape{M, m->C, m->mid}, e,
+                        st, 0)))
+    return rc;
+  count_launches(1);
+  const int64_t n4 = Th * m->C / 4;
+  if (m->act == kF16)
+    gelu_cast<kF16><<<grid_1d(n4, 256), 256, 0, st>>>(x, m->xa.p, n4);
+  else
+    gelu_cast<kBF16><<<grid_1d(n4, 256), 256, 0, st>>>(x, m->xa.p, n4);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 }  // extern "C"

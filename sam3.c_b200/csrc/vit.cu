@@ -32,6 +32,7 @@
 #include <vector>
 
 #include "../../include/sam3cu.h"
+#include "devbuf.cuh"
 #include "gemm_sm100.cuh"
 #include "misc.cuh"
 #include "sam3cu_internal.h"
@@ -43,21 +44,6 @@ constexpr int kMaxLayers = 32;
 
 bool is_global_block(int i) { return i == 7 || i == 15 || i == 23 || i == 31; }
 
-struct DevBuf {
-  void* p = nullptr;
-  size_t bytes = 0;
-  ~DevBuf() {
-    if (p) cudaFree(p);
-  }
-  bool alloc(size_t n) {
-    bytes = n;
-    return cudaMalloc(&p, n ? n : 16) == cudaSuccess;
-  }
-  template <class T>
-  T* as() const {
-    return static_cast<T*>(p);
-  }
-};
 
 struct Linear {
   DevBuf w;      // 16-bit [N, K] (or unused for Q8)

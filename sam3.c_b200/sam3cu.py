@@ -29,6 +29,8 @@ EXPORTS = (
     "sam3cu_vit_launches_per_encode", "sam3cu_vit_profile",
     "sam3_cuda_backend_ops", "sam3cu_conv2d_nhwc_noalloc",
     "sam3cu_tvit_expand_bias", "sam3cu_tvit_window_attention",
+    "sam3cu_tvit_block_create", "sam3cu_tvit_block_forward", "sam3cu_tvit_block_destroy",
+    "sam3cu_tvit_mbconv_create", "sam3cu_tvit_mbconv_forward", "sam3cu_tvit_mbconv_destroy",
 )
 
 # sizeof(struct sam3_cuda_backend): {enum type; ops*} + int device + void *impl
@@ -75,6 +77,14 @@ def lib():
         L.sam3cu_tvit_expand_bias.argtypes = [vp, i32, i32, i32, vp, i32]
         L.sam3cu_tvit_window_attention.argtypes = [vp, i64, vp, i64, i32, i32, i32, i32, i32, vp, i32,
                                                    vp]
+        L.sam3cu_tvit_block_create.restype = vp
+        L.sam3cu_tvit_block_create.argtypes = [i32, i32, i32, i32, i32, vp, C.POINTER(C.c_int)]
+        L.sam3cu_tvit_block_forward.argtypes = [vp, vp, i32, i32, i32, vp]
+        L.sam3cu_tvit_block_destroy.argtypes = [vp]
+        L.sam3cu_tvit_mbconv_create.restype = vp
+        L.sam3cu_tvit_mbconv_create.argtypes = [i32, i32, i32, vp, C.POINTER(C.c_int)]
+        L.sam3cu_tvit_mbconv_forward.argtypes = [vp, vp, i32, i32, i32, vp]
+        L.sam3cu_tvit_mbconv_destroy.argtypes = [vp]
         _lib = L
     return _lib
 
@@ -347,3 +357,92 @@ def tvit_window_attention(qkv, n_windows: int, n_tokens: int, heads: int, head_d
                                              _ptr(bias), bias_ld, _stream()),
           "sam3cu_tvit_window_attention")
     return out
+
+
+class _TvitBlockW(C.Structure):
+    """struct sam3cu_tvit_block_weights (include/sam3cu.h)."""
+    _fields_ = ([(n, C.c_void_p) for n in ("attn_norm_w", "attn_norm_b", "qkv_w", "qkv_b", "proj_w",
+                                           "proj_b", "attn_bias")]
+                + [("attn_bias_offsets", C.c_int)]
+                + [(n, C.c_void_p) for n in ("lc_w", "lc_b", "lc_bn_w", "lc_bn_b", "lc_bn_mean",
+                                             "lc_bn_var", "mlp_norm_w", "mlp_norm_b", "fc1_w",
+                                             "fc1_b", "fc2_w", "fc2_b")])
+
+
+class _TvitMbW(C.Structure):
+    """struct sam3cu_tvit_mbconv_weights (include/sam3cu.h)."""
+    _fields_ = [(f"{c}{i}_{k}" if c == "bn" else f"conv{i}_{k}", C.c_void_p)
+                for i in (1, 2, 3) for c, ks in (("conv", ("w", "b")), ("bn", ("w", "b", "mean", "var")))
+                for k in ks]
+
+
+def _fill(struct, w: dict, keep: list):
+    import numpy as np
+    for name, ctype in struct._fields_:
+        if ctype is not C.c_void_p:
+            continue
+        a = w.get(name)
+        if a is None:
+            continue
+        a = np.ascontiguousarray(a, np.float32)
+        keep.append(a)
+        setattr(struct, name, a.ctypes.data)
+
+
+class TvitBlock:
+    """One TinyViTBlock on device (sam3cu_tvit_block_*).  w: host float32
+    arrays keyed as struct sam3cu_tvit_block_weights ('attn_bias' is the
+    compact [heads, ws*ws] table)."""
+
+    def __init__(self, dim, heads, ws, mlp_dim, w: dict, dtype=BF16):
+        s = _TvitBlockW()
+        keep = []
+        _fill(s, w, keep)
+        if w.get("attn_bias") is not None:
+            s.attn_bias_offsets = int(w["attn_bias"].shape[-1])
+        st = C.c_int(0)
+        self._h = lib().sam3cu_tvit_block_create(dim, heads, ws, mlp_dim, dtype, C.byref(s), C.byref(st))
+        del keep
+        if not self._h:
+            check(st.value or -1, "sam3cu_tvit_block_create")
+
+    def forward(self, x):
+        """x: float32 CUDA tensor [n_images, H, W, dim], updated in place."""
+        n, H, W, _ = x.shape
+        check(lib().sam3cu_tvit_block_forward(self._h, x.data_ptr(), n, H, W, _stream()),
+              "sam3cu_tvit_block_forward")
+        return x
+
+    def close(self):
+        if self._h:
+            lib().sam3cu_tvit_block_destroy(self._h)
+            self._h = None
+
+    __del__ = close
+
+
+class TvitMBConv:
+    """One MBConv block on device (sam3cu_tvit_mbconv_*)."""
+
+    def __init__(self, dim, mid_dim, w: dict, dtype=BF16):
+        s = _TvitMbW()
+        keep = []
+        _fill(s, w, keep)
+        st = C.c_int(0)
+        self._h = lib().sam3cu_tvit_mbconv_create(dim, mid_dim, dtype, C.byref(s), C.byref(st))
+        del keep
+        if not self._h:
+            check(st.value or -1, "sam3cu_tvit_mbconv_create")
+
+    def forward(self, x):
+        n, H, W, _ = x.shape
+        check(lib().sam3cu_tvit_mbconv_forward(self._h, x.data_ptr(), n, H, W, _stream()),
+              "sam3cu_tvit_mbconv_forward")
+        return x
+
+    def close(self):
+        if self._h:
+            lib().sam3cu_tvit_mbconv_destroy(self._h)
+            self._h = None
+
+    __del__ = close
