@@ -34,6 +34,12 @@ CFG = synth.HIERA_L
 ATTN_GFLOP_PER_IMAGE = 28 * 12.23 + 4 * 110.08
 TOTAL_GFLOP_PER_IMAGE = 5399.0
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) per launch of the dominant kernel, gemm2_kernel,
+# averaged over the four GEMMs of one ViT block at 8 images: one ncu capture
+# of `python bench.py --images 8 --batch 8 --steps 1 --warmup 1
+# --no-cpu-baseline` with --metrics dram__bytes_read.sum,dram__bytes_write.sum
+# -k regex:gemm2_kernel -s 4 -c 4 (per launch: 746.0, 292.8, 363.7, 434.6 MB).
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 459.3e6
 
 
 def gemm_gflop_per_image(cfg=CFG):
@@ -285,9 +291,12 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
-            "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05 linear + fused epilogue)",
+            "roofline": {"bound": "tensor",
+                         "kernel": "gemm2_kernel (2-SM tcgen05 linear + fused epilogue)",
                          "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
-                         "frac": gemm_tflops / peak, "traffic": None,
+                         "frac": gemm_tflops / peak,
+                         "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH if args.dtype != "q8" else None,
+                         "traffic_unit": "bytes per launch (ncu, 8 images, BF16)",
                          "peak_source": f"{pk_src} bf16_tflops_sustained"},
             "gemm_tflops": gemm_tflops,
             "attention_tflops": attn_tflops,
