@@ -149,6 +149,16 @@ SAM3CU_API int sam3cu_sdpa(const void *q, const void *k, const void *v, int64_t 
 		void *o, int64_t ld_o, int dtype, int n_groups, int seq,
 		int heads, int head_dim, void *stream);
 
+/*
+ * Failure-path self test (no reference counterpart).  Launches one CTA that
+ * waits on an mbarrier nothing ever arrives on, bounded by limit_ns
+ * (clamped to [1 ms, 2 s]).  On return *timed_out is 1 when the wait gave up,
+ * recorded its device error code and let the kernel finish, i.e. the path
+ * every pipeline wait in the library takes instead of hanging.  The device
+ * error word is cleared again, and the context stays usable.
+ */
+SAM3CU_API int sam3cu_selftest_wait_timeout(unsigned long long limit_ns, int *timed_out);
+
 /* ------------------------------------------------------------- TinyViT */
 
 /*

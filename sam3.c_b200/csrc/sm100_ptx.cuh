@@ -34,6 +34,7 @@ enum DevErr : unsigned int {
   kErrAccFull = 3,     // accumulator never committed
   kErrAccFree = 4,     // accumulator never drained by the epilogue
   kErrTmemAlloc = 5,
+  kErrSelfTest = 6,    // the deliberate timeout of sam3cu_selftest_wait_timeout
 };
 
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -84,23 +85,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait on the phase with the given parity.  Returns false (and
-// records `err`) if the phase does not complete within kWaitLimitNs or if
+// records `err`) if the phase does not complete within limit_ns or if
 // another role of the CTA already aborted (*abort_flag != 0).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned err,
-                                          volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, unsigned err,
+                                             volatile int* abort_flag, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   unsigned long long t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 63u) {
       if (abort_flag && *abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         atomicCAS(&g_dev_error, 0u, err);
         if (abort_flag) *abort_flag = 1;
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned err,
+                                          volatile int* abort_flag) {
+  return mbar_wait_ns(bar, parity, err, abort_flag, kWaitLimitNs);
 }
 
 // True in exactly one lane of the (converged, full) warp.

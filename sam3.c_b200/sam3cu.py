@@ -31,6 +31,7 @@ EXPORTS = (
     "sam3cu_tvit_expand_bias", "sam3cu_tvit_window_attention",
     "sam3cu_tvit_block_create", "sam3cu_tvit_block_forward", "sam3cu_tvit_block_destroy",
     "sam3cu_tvit_mbconv_create", "sam3cu_tvit_mbconv_forward", "sam3cu_tvit_mbconv_destroy",
+    "sam3cu_selftest_wait_timeout",
 )
 
 # sizeof(struct sam3_cuda_backend): {enum type; ops*} + int device + void *impl
@@ -85,6 +86,7 @@ def lib():
         L.sam3cu_tvit_mbconv_create.argtypes = [i32, i32, i32, vp, C.POINTER(C.c_int)]
         L.sam3cu_tvit_mbconv_forward.argtypes = [vp, vp, i32, i32, i32, vp]
         L.sam3cu_tvit_mbconv_destroy.argtypes = [vp]
+        L.sam3cu_selftest_wait_timeout.argtypes = [C.c_ulonglong, C.POINTER(C.c_int)]
         _lib = L
     return _lib
 
@@ -446,3 +448,11 @@ class TvitMBConv:
             self._h = None
 
     __del__ = close
+
+
+def selftest_wait_timeout(limit_ns: int = 20_000_000) -> bool:
+    """Run the bounded-wait failure path once; True when the wait gave up,
+    recorded its error and returned (see sam3cu_selftest_wait_timeout)."""
+    out = C.c_int(0)
+    check(lib().sam3cu_selftest_wait_timeout(limit_ns, C.byref(out)), "sam3cu_selftest_wait_timeout")
+    return out.value == 1
