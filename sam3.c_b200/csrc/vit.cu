@@ -74,13 +74,22 @@ struct sam3cu_vit {
   s3::DevBuf rope_win, rope_glo;  // float2 (cos, sin), pair-major: [32][positions]
   s3::DevBuf win_to_raster;                      // int [np]
   s3::DevBuf raster_to_win;                      // int [np]
-  std::vector<int> graph_nodes;                  // kernel nodes per captured graph
   // activations
-  s3::DevBuf x, xn, qkv, ao, h, img, out;
-  // CUDA graph per batch size
-  std::vector<cudaGraphExec_t> graphs;
-  std::vector<const float*> graph_in;
-  std::vector<float*> graph_out;
+  s3::DevBuf x, xn, qkv, ao, h;
+  // image / feature staging for host-buffer encodes: two sets, so that one
+  // chunk's copies overlap the next chunk's compute (img2/out2 on demand)
+  s3::DevBuf img, out, img2, out2;
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  cudaEvent_t ev_in[2] = {}, ev_done[2] = {}, ev_out[2] = {};
+  // CUDA graphs, one per (batch size, input, output) in use
+  struct Graph {
+    int n;
+    const float* in;
+    float* out;
+    cudaGraphExec_t exec;
+    int nodes;
+  };
+  std::vector<Graph> graphs;
   int launches_per_block = 7;
   // optional per-launch profiling (sam3cu_vit_profile): kind of each launch
   std::vector<int>* prof_kinds = nullptr;
@@ -421,12 +430,17 @@ sam3cu_vit* sam3cu_vit_create(const sam3cu_vit_config* cfg, const sam3cu_vit_wei
 
 void sam3cu_vit_destroy(sam3cu_vit* v) {
   if (!v) return;
-  for (auto g : v->graphs)
-    if (g) cudaGraphExecDestroy(g);
-  if (v->stream) {
-    cudaStreamSynchronize(v->stream);
-    cudaStreamDestroy(v->stream);
-  }
+  if (v->stream) cudaStreamSynchronize(v->stream);
+  for (cudaStream_t s : {v->copy_in, v->copy_out})
+    if (s) {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
+  for (int b = 0; b < 2; ++b)
+    for (cudaEvent_t e : {v->ev_in[b], v->ev_done[b], v->ev_out[b]})
+      if (e) cudaEventDestroy(e);
+  for (auto& g : v->graphs) cudaGraphExecDestroy(g.exec);
+  if (v->stream) cudaStreamDestroy(v->stream);
   delete v;
 }
 
@@ -464,20 +478,18 @@ int sam3cu_vit_launches_per_encode(sam3cu_vit* v, int n) {
 }
 
 // Enqueue through a CUDA graph captured once per (batch size, in, out)
-// triple; falls back to direct launches if capture fails.
+// triple (a few are kept); falls back to direct launches if capture fails.
 int sam3cu_vit_encode_async(sam3cu_vit* v, const float* images, int n, float* out) {
   if (!v || n <= 0 || n > v->max_batch || !images || !out) return SAM3CU_EINVAL;
-  if (static_cast<int>(v->graphs.size()) < n + 1) {
-    v->graphs.resize(n + 1, nullptr);
-    v->graph_in.resize(n + 1, nullptr);
-    v->graph_out.resize(n + 1, nullptr);
-    v->graph_nodes.resize(n + 1, 0);
-  }
-  if (v->graphs[n] && (v->graph_in[n] != images || v->graph_out[n] != out)) {
-    cudaGraphExecDestroy(v->graphs[n]);
-    v->graphs[n] = nullptr;
-  }
-  if (!v->graphs[n]) {
+  sam3cu_vit::Graph* hit = nullptr;
+  for (auto& g : v->graphs)
+    if (g.n == n && g.in == images && g.out == out) hit = &g;
+  if (!hit) {
+    constexpr size_t kMaxGraphs = 8;
+    if (v->graphs.size() >= kMaxGraphs) {  // drop the oldest
+      cudaGraphExecDestroy(v->graphs.front().exec);
+      v->graphs.erase(v->graphs.begin());
+    }
     cudaGraph_t g = nullptr;
     if (cudaStreamBeginCapture(v->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
       cudaGetLastError();
@@ -494,34 +506,89 @@ int sam3cu_vit_encode_async(sam3cu_vit* v, const float* images, int n, float* ou
     }
     size_t nodes = 0;
     cudaGraphGetNodes(g, nullptr, &nodes);
-    v->graph_nodes[n] = static_cast<int>(nodes);
     cudaGraphExec_t ge = nullptr;
     ce = cudaGraphInstantiate(&ge, g, 0);
     cudaGraphDestroy(g);
     if (ce != cudaSuccess) return kErrCuda;
-    v->graphs[n] = ge;
-    v->graph_in[n] = images;
-    v->graph_out[n] = out;
+    v->graphs.push_back({n, images, out, ge, static_cast<int>(nodes)});
+    hit = &v->graphs.back();
   }
-  count_launches(v->graph_nodes[n]);
-  return cudaGraphLaunch(v->graphs[n], v->stream) == cudaSuccess ? kOk : kErrLaunch;
+  count_launches(hit->nodes);
+  return cudaGraphLaunch(hit->exec, v->stream) == cudaSuccess ? kOk : kErrLaunch;
 }
 
+namespace {
+
+// Copy streams, events and the second staging set for pipelined
+// host-buffer encodes (created on first use).
+int ensure_pipeline(sam3cu_vit* v) {
+  if (v->copy_in) return kOk;
+  const size_t in_bytes = static_cast<size_t>(v->max_batch) * 3 * v->c.img_size * v->c.img_size * 4;
+  const size_t out_bytes = static_cast<size_t>(v->max_batch) * v->np * v->c.embed_dim * 4;
+  if (!v->img2.alloc(in_bytes) || !v->out2.alloc(out_bytes)) return kErrNoMem;
+  for (int b = 0; b < 2; ++b)
+    for (cudaEvent_t* e : {&v->ev_in[b], &v->ev_done[b], &v->ev_out[b]})
+      if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return kErrCuda;
+  if (cudaStreamCreateWithFlags(&v->copy_in, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&v->copy_out, cudaStreamNonBlocking) != cudaSuccess)
+    return kErrCuda;
+  return kOk;
+}
+
+}  // namespace
+
+// Host buffers: n may exceed max_batch.  The images are encoded in chunks of
+// max_batch; chunk i uses staging set i % 2, its H2D copy runs on copy_in
+// and its D2H copy on copy_out, so with pinned host memory the copies of
+// one chunk overlap the compute of the next.  Events order each staging
+// set: H2D(i) after compute(i-2) read it, compute(i) after H2D(i) and after
+// D2H(i-2) drained its output buffer, D2H(i) after compute(i).
 int sam3cu_vit_encode(sam3cu_vit* v, const float* images, int n, float* out, int on_device) {
-  if (!v || n <= 0 || n > v->max_batch || !images || !out) return SAM3CU_EINVAL;
-  const size_t in_bytes = static_cast<size_t>(n) * 3 * v->c.img_size * v->c.img_size * 4;
-  const size_t out_bytes = static_cast<size_t>(n) * v->np * v->c.embed_dim * 4;
-  int rc;
+  if (!v || n <= 0 || !images || !out) return SAM3CU_EINVAL;
   if (on_device) {
-    rc = sam3cu_vit_encode_async(v, images, n, out);
-  } else {
-    if (cudaMemcpyAsync(v->img.p, images, in_bytes, cudaMemcpyHostToDevice, v->stream) != cudaSuccess)
+    if (n > v->max_batch) return SAM3CU_EINVAL;
+    const int rc = sam3cu_vit_encode_async(v, images, n, out);
+    if (cudaStreamSynchronize(v->stream) != cudaSuccess) return kErrCuda;
+    return rc;
+  }
+  const size_t img_elems = static_cast<size_t>(3) * v->c.img_size * v->c.img_size;
+  const size_t out_elems = static_cast<size_t>(v->np) * v->c.embed_dim;
+  const int chunks = (n + v->max_batch - 1) / v->max_batch;
+  int rc = kOk;
+  if (chunks == 1) {  // a single chunk has nothing to overlap with
+    if (cudaMemcpyAsync(v->img.p, images, n * img_elems * 4, cudaMemcpyHostToDevice, v->stream) != cudaSuccess)
       return kErrCuda;
     rc = sam3cu_vit_encode_async(v, v->img.as<float>(), n, v->out.as<float>());
-    if (!rc && cudaMemcpyAsync(out, v->out.p, out_bytes, cudaMemcpyDeviceToHost, v->stream) != cudaSuccess)
+    if (!rc && cudaMemcpyAsync(out, v->out.p, n * out_elems * 4, cudaMemcpyDeviceToHost, v->stream) != cudaSuccess)
       rc = kErrCuda;
+    if (cudaStreamSynchronize(v->stream) != cudaSuccess) return kErrCuda;
+    return rc;
   }
-  if (cudaStreamSynchronize(v->stream) != cudaSuccess) return kErrCuda;
+  if ((rc = ensure_pipeline(v))) return rc;
+  for (int i = 0; i < chunks && !rc; ++i) {
+    const int b = i & 1, first = i * v->max_batch;
+    const int cn = std::min(v->max_batch, n - first);
+    float* img = (b ? v->img2 : v->img).as<float>();
+    float* feat = (b ? v->out2 : v->out).as<float>();
+    if (i >= 2 && cudaStreamWaitEvent(v->copy_in, v->ev_done[b], 0) != cudaSuccess) rc = kErrCuda;
+    if (!rc && cudaMemcpyAsync(img, images + first * img_elems, cn * img_elems * 4, cudaMemcpyHostToDevice,
+                               v->copy_in) != cudaSuccess)
+      rc = kErrCuda;
+    if (!rc && cudaEventRecord(v->ev_in[b], v->copy_in) != cudaSuccess) rc = kErrCuda;
+    if (!rc && cudaStreamWaitEvent(v->stream, v->ev_in[b], 0) != cudaSuccess) rc = kErrCuda;
+    if (!rc && i >= 2 && cudaStreamWaitEvent(v->stream, v->ev_out[b], 0) != cudaSuccess) rc = kErrCuda;
+    if (!rc) rc = sam3cu_vit_encode_async(v, img, cn, feat);
+    if (!rc && cudaEventRecord(v->ev_done[b], v->stream) != cudaSuccess) rc = kErrCuda;
+    if (!rc && cudaStreamWaitEvent(v->copy_out, v->ev_done[b], 0) != cudaSuccess) rc = kErrCuda;
+    if (!rc && cudaMemcpyAsync(out + first * out_elems, feat, cn * out_elems * 4, cudaMemcpyDeviceToHost,
+                               v->copy_out) != cudaSuccess)
+      rc = kErrCuda;
+    if (!rc && cudaEventRecord(v->ev_out[b], v->copy_out) != cudaSuccess) rc = kErrCuda;
+  }
+  const bool sync_ok = cudaStreamSynchronize(v->stream) == cudaSuccess &&
+                       cudaStreamSynchronize(v->copy_in) == cudaSuccess &&
+                       cudaStreamSynchronize(v->copy_out) == cudaSuccess;
+  if (!sync_ok) return kErrCuda;
   return rc;
 }
 

@@ -43,3 +43,28 @@ def test_tiny_vit(cuda, wd):
     out2 = enc.encode_host(imgs)
     assert np.array_equal(out, out2)
     enc.close()
+
+
+def test_host_encode_pipelined_chunks(cuda):
+    """Host buffers with more images than max_batch: chunks of max_batch on
+    two staging sets with overlapped copies.  Every image's features must be
+    those of an on-device encode of the same chunk, and the order kept."""
+    import torch
+    import sam3cu
+    cfg = synth.tiny_cfg(depth=4)
+    w = synth.vit_weights(cfg, seed=3)
+    n, mb = 7, 2
+    imgs = synth.images(cfg, n, seed=4)
+    enc = sam3cu.VitEncoder(cfg, w, sam3cu.BF16, max_batch=mb)
+    hin = torch.from_numpy(np.ascontiguousarray(imgs)).pin_memory()
+    hout = torch.empty((n, enc.np, cfg["embed_dim"]), dtype=torch.float32).pin_memory()
+    enc.encode_ptr(hin.data_ptr(), n, hout.data_ptr(), on_device=False)
+    assert sam3cu.device_error() == 0
+    got = hout.numpy()
+    for first in range(0, n, mb):
+        cn = min(mb, n - first)
+        din = torch.from_numpy(np.ascontiguousarray(imgs[first:first + cn])).cuda()
+        dout = torch.empty((cn, enc.np, cfg["embed_dim"]), dtype=torch.float32, device="cuda")
+        enc.encode_ptr(din.data_ptr(), cn, dout.data_ptr(), on_device=True)
+        assert np.array_equal(got[first:first + cn], dout.cpu().numpy()), first
+    enc.close()
