@@ -17,16 +17,17 @@
 // V) instead of 80 KiB plus the 32 KiB P store, and shared-memory bandwidth
 // is what limits a head_dim-64 tile.
 //
-// CTA = 10 warps, two CTAs per SM (112 KiB smem, 256 TMEM columns and
-// 320 threads x 96 registers each):
+// CTA = 6 warps, two CTAs per SM (112 KiB smem, 256 TMEM columns and
+// 192 threads x 168 registers each):
 //   warp 0     TMA (Q tile once, K_j / V_j through a 3-stage ring);
 //              allocates TMEM
-//   warp 1     MMA issue (one thread)
-//   warps 2-9  softmax and the output epilogue; warp w owns TMEM lane
-//              quarter w % 4, i.e. query rows 32*(w%4) .. +31, and key
-//              half (w-2)/4 of every tile: it reads the whole S row for the
-//              row maximum, exponentiates its 64 keys and writes their P;
-//              the two warps of a quarter add their row sums at the end
+//   warp 1     MMA issue (the whole warp; one elected lane issues)
+//   warps 2-5  softmax and the output epilogue; warp w owns TMEM lane
+//              quarter w % 4, i.e. query rows 32*(w%4) .. +31: a thread
+//              holds its whole 128-key S row, so the row maximum and sum
+//              need no exchange.  (S3_ATTN_SPLIT=2 builds the variant with
+//              two warps per quarter, each exponentiating one 64-key half;
+//              it measured slower on the 5184-token case.)
 // A softmax thread copies its S row to registers and releases S at once,
 // so S_{j+1} = Q K_{j+1}^T runs on the tensor cores during the softmax of
 // tile j; the two CTAs of an SM interleave on the exponential units.
@@ -67,8 +68,19 @@ struct HeadCfg {
   static constexpr int kSmem = kTile * (1 + 2 * kStages);  // Q | K0 V0 | K1 V1 | ...
   static_assert(kD == 32 || kD == 64, "head_dim 32 or 64");
 };
-constexpr int kThreads = 320;          // 2 control + 8 softmax warps
-constexpr int kHalf = kKV / 2;           // columns per softmax warp
+#ifndef S3_ATTN_SPLIT
+#define S3_ATTN_SPLIT 1
+#endif
+// Softmax warps per lane quarter: 2 = each row split into two 64-key halves
+// (8 softmax warps), 1 = a whole 128-key row per thread (4 softmax warps).
+constexpr int kSplit = S3_ATTN_SPLIT;
+constexpr int kSoftWarps = 4 * kSplit;
+constexpr int kThreads = 64 + 32 * kSoftWarps;  // 2 control warps + softmax
+constexpr int kHalf = kKV / kSplit;             // keys per softmax warp
+#ifndef S3_ATTN_PSTORE
+#define S3_ATTN_PSTORE 8
+#endif
+constexpr int kPStore = S3_ATTN_PSTORE;         // P columns per tcgen05.st
 constexpr float kRescaleLog2 = 8.0f;     // lazy rescale threshold (x256)
 
 
@@ -170,12 +182,12 @@ struct AttnParams {
 // f32 bias [head, query, key] joins the scaled scores before the softmax
 // (TinyViT's relative position bias, image_encoder_tinyvit.c:842-846).
 template <bool kBf16, int kD, bool kBias>
-__global__ void __launch_bounds__(320, 2)
+__global__ void __launch_bounds__(kThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const AttnParams prm) {
   using HC = HeadCfg<kD>;
   constexpr int kTile = HC::kTile;
-  constexpr int kOHalf = kD / 2;  // O columns per softmax warp
+  constexpr int kOHalf = kD / kSplit;  // O columns per softmax warp
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ uint64_t bars[8 + 2 * kStages];
   __shared__ uint32_t tmem_slot;
@@ -214,8 +226,8 @@ __global__ void __launch_bounds__(320, 2)
       mbar_init(&kv_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_empty, 8);
-    mbar_init(p_full, 8);
+    mbar_init(s_empty, kSoftWarps);
+    mbar_init(p_full, kSoftWarps);
     mbar_init(p_empty, 1);
     mbar_init(o_full, 1);
     abort_flag_s = 0;
@@ -338,6 +350,7 @@ __global__ void __launch_bounds__(320, 2)
           if (kfirst + c >= seq) sv[c] = -INFINITY;
       }
     };
+    auto max_row = [](const float* v) { return kHalf == 64 ? max64(v) : fmaxf(max64(v), max64(v + 64)); };
     float m_used = -INFINITY, l = 0.f;
     // A warp whose 32 query rows all lie past the group end (the last query
     // tile of a 576-token window) only keeps the barrier protocol going.
@@ -353,19 +366,19 @@ __global__ void __launch_bounds__(320, 2)
       uint32_t su[kHalf];  // S bits, loaded in place
       float* sv = reinterpret_cast<float*>(su);
       float mt = -INFINITY;
-      if (rows_live) {
+      if (kSplit == 2 && rows_live) {
         // maximum of the other key half first (its values are discarded)
         const int kbo = j * kKV + (scol ^ kHalf);
         if (kbo < seq) {
           load_s(sv, su, scol ^ kHalf, kbo);
-          mt = max64(sv);
+          mt = max_row(sv);
         }
       }
       if (live) load_s(sv, su, scol, kb);  // this warp's 64 S columns
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_empty);  // S may be overwritten
-      if (live) mt = fmaxf(mt, max64(sv));
+      if (live) mt = fmaxf(mt, max_row(sv));
       const bool need = (mt - m_used) * sl2 > kRescaleLog2;
       // P buffer and O are free once the previous P.V finished
       if (j > 0 && !warp_wait(p_empty, (j - 1) & 1, kErrAccFree, abort_flag, lane)) { ok = false; break; }
@@ -395,17 +408,23 @@ __global__ void __launch_bounds__(320, 2)
         const uint64_t sc2 = f2pack(sl2, sl2), nmb2 = f2pack(-mb, -mb);
         uint64_t l2[2] = {f2pack(0.f, 0.f), f2pack(0.f, 0.f)};
 #pragma unroll
-        for (int c0 = 0; c0 < kHalf; c0 += 16) {  // 16 keys -> 8 columns at a time: few live registers
-          uint32_t pk[8];
+        for (int c0 = 0; c0 < kHalf; c0 += 2 * kPStore) {  // 2*kPStore keys -> kPStore P columns
+          uint32_t pk[kPStore];
 #pragma unroll
-          for (int c = c0; c < c0 + 16; c += 2) {
+          for (int c = c0; c < c0 + 2 * kPStore; c += 2) {
             float e0, e1;
             f2unpack(ffma2(f2pack(sv[c], sv[c + 1]), sc2, nmb2), e0, e1);
             const float p0 = ex2(e0), p1 = ex2(e1);
             l2[(c >> 1) & 1] = fadd2(l2[(c >> 1) & 1], f2pack(p0, p1));
             pk[(c - c0) / 2] = pack2(p0, p1, kBf16);
           }
-          tmem_st_32x32b_x8(tP + lane_off + half * (kHalf / 2) + c0 / 2, pk);
+          const uint32_t ta = tP + lane_off + half * (kHalf / 2) + c0 / 2;
+          if constexpr (kPStore == 8)
+            tmem_st_32x32b_x8(ta, *reinterpret_cast<const uint32_t(*)[8]>(pk));
+          else if constexpr (kPStore == 16)
+            tmem_st_32x32b_x16(ta, *reinterpret_cast<const uint32_t(*)[16]>(pk));
+          else
+            tmem_st_32x32b_x32(ta, *reinterpret_cast<const uint32_t(*)[32]>(pk));
         }
         float a0, a1;
         f2unpack(fadd2(l2[0], l2[1]), a0, a1);
@@ -420,26 +439,26 @@ __global__ void __launch_bounds__(320, 2)
     // (both warps of a quarter reach the exchange, also after an abort)
     const bool o_ok = ok && warp_wait(o_full, 0, kErrAccFull, abort_flag, lane);
     tc_fence_after();
-    if (rows_live) l += pair_exchange(tS, lane_off, half, l, quarter);
+    if (kSplit == 2 && rows_live) l += pair_exchange(tS, lane_off, half, l, quarter);
     if (o_ok) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int qrow = qt * kQ + r;
       uint16_t* orow = prm.o + static_cast<int64_t>(row0 + qrow) * prm.ldo + head * prm.o_hstride + half * kOHalf;
-      uint32_t u[kOHalf];
-      if constexpr (kD == 64)
-        tmem_ld_32x32b_x32(tO + lane_off + half * kOHalf, u);
-      else
-        tmem_ld_32x32b_x16(tO + lane_off + half * kOHalf, u);
-      tmem_ld_wait();
-      if (qrow < seq) {
 #pragma unroll
-        for (int q4 = 0; q4 < kOHalf / 8; ++q4) {
-          uint4 w;
-          w.x = pack2(__uint_as_float(u[q4 * 8 + 0]) * inv, __uint_as_float(u[q4 * 8 + 1]) * inv, kBf16);
-          w.y = pack2(__uint_as_float(u[q4 * 8 + 2]) * inv, __uint_as_float(u[q4 * 8 + 3]) * inv, kBf16);
-          w.z = pack2(__uint_as_float(u[q4 * 8 + 4]) * inv, __uint_as_float(u[q4 * 8 + 5]) * inv, kBf16);
-          w.w = pack2(__uint_as_float(u[q4 * 8 + 6]) * inv, __uint_as_float(u[q4 * 8 + 7]) * inv, kBf16);
-          *reinterpret_cast<uint4*>(orow + q4 * 8) = w;
+      for (int c0 = 0; c0 < kOHalf; c0 += 16) {  // 16 output columns at a time
+        uint32_t u[16];
+        tmem_ld_32x32b_x16(tO + lane_off + half * kOHalf + c0, u);
+        tmem_ld_wait();
+        if (qrow < seq) {
+#pragma unroll
+          for (int q4 = 0; q4 < 2; ++q4) {
+            uint4 w;
+            w.x = pack2(__uint_as_float(u[q4 * 8 + 0]) * inv, __uint_as_float(u[q4 * 8 + 1]) * inv, kBf16);
+            w.y = pack2(__uint_as_float(u[q4 * 8 + 2]) * inv, __uint_as_float(u[q4 * 8 + 3]) * inv, kBf16);
+            w.z = pack2(__uint_as_float(u[q4 * 8 + 4]) * inv, __uint_as_float(u[q4 * 8 + 5]) * inv, kBf16);
+            w.w = pack2(__uint_as_float(u[q4 * 8 + 6]) * inv, __uint_as_float(u[q4 * 8 + 7]) * inv, kBf16);
+            *reinterpret_cast<uint4*>(orow + c0 + q4 * 8) = w;
+          }
         }
       }
     }
