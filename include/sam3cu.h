@@ -229,6 +229,50 @@ SAM3CU_API int sam3cu_tvit_mbconv_forward(sam3cu_tvit_mbconv *mb, float *x, int 
 		int H, int W, void *stream);
 SAM3CU_API void sam3cu_tvit_mbconv_destroy(sam3cu_tvit_mbconv *mb);
 
+/*
+ * Whole TinyViT backbone (sam3_tinyvit_build, image_encoder_tinyvit.c:1058-1290)
+ * on device.
+ *   image [3, S, S] F32 -> patch embed (3x3/2 conv + BN + GELU, 3x3/2 conv
+ *   + BN) -> layer 0: MBConv blocks -> PatchMerging -> layers 1..: TinyViT
+ *   blocks, PatchMerging after every layer but the last -> head (1x1 conv,
+ *   BN, GELU, 3x3 conv + bias) -> features [grid*grid, embed_dim] F32.
+ * Conv weights are OHWI [OC, k, k, IC/groups] with optional bias and BN,
+ * as struct sam3_tvit_conv_weights (image_encoder_tinyvit.h:37-44).
+ */
+struct sam3cu_tvit_conv_weights {
+	const float *w, *b, *bn_w, *bn_b, *bn_mean, *bn_var;
+};
+#define SAM3CU_TVIT_MAX_LAYERS 4
+struct sam3cu_tinyvit_config {
+	int img_size;          /* 1008 */
+	int n_layers;          /* 4 */
+	int embed_dims[SAM3CU_TVIT_MAX_LAYERS];    /* 96, 192, 384, 576 */
+	int depths[SAM3CU_TVIT_MAX_LAYERS];        /* 2, 2, 6, 2 */
+	int num_heads[SAM3CU_TVIT_MAX_LAYERS];     /* 3, 6, 12, 18 */
+	int window_sizes[SAM3CU_TVIT_MAX_LAYERS];  /* 7, 7, 14, 7 */
+	int embed_dim;         /* head output, 1024 */
+	int mlp_ratio;         /* 4 */
+};
+struct sam3cu_tinyvit_layer_weights {
+	const struct sam3cu_tvit_mbconv_weights *conv_blocks;  /* layer 0: depths[0] entries */
+	const struct sam3cu_tvit_block_weights *blocks;        /* layers >= 1: depths[l] entries */
+	struct sam3cu_tvit_conv_weights pm_conv1, pm_conv2, pm_conv3;  /* PatchMerging */
+};
+struct sam3cu_tinyvit_weights {
+	struct sam3cu_tvit_conv_weights patch_embed_0, patch_embed_1;
+	struct sam3cu_tinyvit_layer_weights layers[SAM3CU_TVIT_MAX_LAYERS];
+	struct sam3cu_tvit_conv_weights proj_conv1, proj_bn, proj_conv2;
+};
+typedef struct sam3cu_tinyvit sam3cu_tinyvit;
+SAM3CU_API sam3cu_tinyvit *sam3cu_tinyvit_create(const struct sam3cu_tinyvit_config *cfg,
+		const struct sam3cu_tinyvit_weights *w, int dtype, int max_batch, int *status);
+/* images [n, 3, S, S] F32 -> out [n, grid*grid, embed_dim] F32; device
+ * pointers when on_device, else host pointers; n <= max_batch. */
+SAM3CU_API int sam3cu_tinyvit_encode(sam3cu_tinyvit *tv, const float *images, int n_images,
+		float *out, int on_device);
+SAM3CU_API int sam3cu_tinyvit_grid(const sam3cu_tinyvit *tv);
+SAM3CU_API void sam3cu_tinyvit_destroy(sam3cu_tinyvit *tv);
+
 /* ------------------------------------------- per-node ops (backend vtable)
  * Device helpers and the remaining encoder-graph ops, used by the
  * sam3_backend_ops lowering in cuda_backend.c.  dtype arguments take

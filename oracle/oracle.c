@@ -640,23 +640,26 @@ void orc_tvit_window_attention(const float *qkv, int nw, int N, int heads,
 }
 
 /* tvit_conv_bn (:655-674) for the depthwise 3x3 convs: conv2d NHWC with
- * OHWI weight [C,3,3,1], stride 1, pad 1, groups C (cpu_conv2d.c:320-420),
- * optional conv bias, then eval BatchNorm (cpu_batchnorm.c: (x - mean) *
- * 1/sqrtf(var + 1e-5) * gamma + beta), then tanh-GELU if gelu. */
-void orc_dwconv3x3_bn(const float *x, int B, int H, int W, int C,
-		      const float *w, const float *cb, const float *bn_w,
-		      const float *bn_b, const float *bn_mean,
-		      const float *bn_var, int gelu, float *y)
+ * OHWI weight [C,3,3,1], pad 1, groups C, stride 1 or 2 (cpu_conv2d.c:320-420;
+ * output (H-1)/s+1), optional conv bias, then eval BatchNorm
+ * (cpu_batchnorm.c: (x - mean) * 1/sqrtf(var + 1e-5) * gamma + beta), then
+ * tanh-GELU if gelu. */
+void orc_dwconv3x3_bn_s(const float *x, int B, int H, int W, int C, int stride,
+			const float *w, const float *cb, const float *bn_w,
+			const float *bn_b, const float *bn_mean,
+			const float *bn_var, int gelu, float *y)
 {
+	const int OH = (H - 1) / stride + 1, OW = (W - 1) / stride + 1;
 #pragma omp parallel for schedule(static)
-	for (int64_t p = 0; p < (int64_t)B * H * W; p++) {
-		int b = (int)(p / ((int64_t)H * W)), yy = (int)(p / W % H),
-		    xx = (int)(p % W);
+	for (int64_t p = 0; p < (int64_t)B * OH * OW; p++) {
+		int b = (int)(p / ((int64_t)OH * OW)), oy = (int)(p / OW % OH),
+		    ox = (int)(p % OW);
 		for (int c = 0; c < C; c++) {
 			float acc = 0.0f;
 			for (int ky = 0; ky < 3; ky++)
 				for (int kx = 0; kx < 3; kx++) {
-					int iy = yy + ky - 1, ix = xx + kx - 1;
+					int iy = oy * stride + ky - 1,
+					    ix = ox * stride + kx - 1;
 					if (iy < 0 || iy >= H || ix < 0 || ix >= W)
 						continue;
 					acc += x[(((int64_t)b * H + iy) * W + ix) * C + c] *
@@ -673,6 +676,60 @@ void orc_dwconv3x3_bn(const float *x, int B, int H, int W, int C,
 					acc += bn_b[c];
 			}
 			y[p * C + c] = gelu ? gelu_tanh(acc) : acc;
+		}
+	}
+}
+
+void orc_dwconv3x3_bn(const float *x, int B, int H, int W, int C,
+		      const float *w, const float *cb, const float *bn_w,
+		      const float *bn_b, const float *bn_mean,
+		      const float *bn_var, int gelu, float *y)
+{
+	orc_dwconv3x3_bn_s(x, B, H, W, C, 1, w, cb, bn_w, bn_b, bn_mean, bn_var,
+			   gelu, y);
+}
+
+/* Dense conv2d (cpu_conv2d.c:320-420, groups 1): OHWI weight [OC,k,k,IC],
+ * zero padding, NHWC input (or planar CHW when chw), f32 accumulation over
+ * (ky, kx, c); then optional bias, eval BatchNorm and tanh-GELU, as
+ * tvit_conv_bn / gh_conv2d chain them.  y [B, OH, OW, OC]. */
+void orc_conv2d_bn(const float *x, int chw, int B, int H, int W, int IC, int OC,
+		   int k, int stride, int pad, const float *w, const float *cb,
+		   const float *bn_w, const float *bn_b, const float *bn_mean,
+		   const float *bn_var, int gelu, float *y)
+{
+	const int OH = (H + 2 * pad - k) / stride + 1,
+		  OW = (W + 2 * pad - k) / stride + 1;
+#pragma omp parallel for schedule(static)
+	for (int64_t p = 0; p < (int64_t)B * OH * OW; p++) {
+		int b = (int)(p / ((int64_t)OH * OW)), oy = (int)(p / OW % OH),
+		    ox = (int)(p % OW);
+		for (int o = 0; o < OC; o++) {
+			float acc = 0.0f;
+			for (int ky = 0; ky < k; ky++)
+				for (int kx = 0; kx < k; kx++) {
+					int iy = oy * stride - pad + ky,
+					    ix = ox * stride - pad + kx;
+					if (iy < 0 || iy >= H || ix < 0 || ix >= W)
+						continue;
+					const float *wr = w + (((int64_t)o * k + ky) * k + kx) * IC;
+					for (int c = 0; c < IC; c++) {
+						float v = chw ? x[(((int64_t)b * IC + c) * H + iy) * W + ix]
+							      : x[(((int64_t)b * H + iy) * W + ix) * IC + c];
+						acc += v * wr[c];
+					}
+				}
+			if (cb)
+				acc += cb[o];
+			if (bn_mean) {
+				float inv = 1.0f / sqrtf(bn_var[o] + 1e-5f);
+				acc = (acc - bn_mean[o]) * inv;
+				if (bn_w)
+					acc *= bn_w[o];
+				if (bn_b)
+					acc += bn_b[o];
+			}
+			y[p * OC + o] = gelu ? gelu_tanh(acc) : acc;
 		}
 	}
 }
@@ -799,4 +856,114 @@ void orc_tvit_mbconv_forward(const struct orc_tvit_mbconv *m, float *x, int B,
 	free(h);
 	free(h2);
 	free(o);
+}
+
+
+/* ---- whole TinyViT backbone (sam3_tinyvit_build, :1058-1290) ---------- */
+
+/* These structs have the layouts of the CUDA library's
+ * sam3cu_tvit_conv_weights / _block_weights / _mbconv_weights /
+ * sam3cu_tinyvit_* (include/sam3cu.h), so one weight tree feeds both. */
+struct orc_conv { const float *w, *b, *bn_w, *bn_b, *bn_mean, *bn_var; };
+struct orc_tvit_block_c {
+	const float *attn_norm_w, *attn_norm_b, *qkv_w, *qkv_b, *proj_w,
+		*proj_b, *attn_bias;
+	int attn_bias_offsets;
+	const float *lc_w, *lc_b, *lc_bn_w, *lc_bn_b, *lc_bn_mean, *lc_bn_var;
+	const float *mlp_norm_w, *mlp_norm_b, *fc1_w, *fc1_b, *fc2_w, *fc2_b;
+};
+struct orc_tinyvit_cfg {
+	int img_size, n_layers, embed_dims[4], depths[4], num_heads[4],
+	    window_sizes[4], embed_dim, mlp_ratio;
+};
+struct orc_tinyvit_layer {
+	const struct orc_tvit_mbconv *conv_blocks;
+	const struct orc_tvit_block_c *blocks;
+	struct orc_conv pm_conv1, pm_conv2, pm_conv3;
+};
+struct orc_tinyvit_weights {
+	struct orc_conv patch_embed_0, patch_embed_1;
+	struct orc_tinyvit_layer layers[4];
+	struct orc_conv proj_conv1, proj_bn, proj_conv2;
+};
+
+/* One image [3, S, S] -> out [grid*grid, embed_dim].  Returns the grid. */
+int orc_tinyvit_forward(const struct orc_tinyvit_cfg *c,
+			const struct orc_tinyvit_weights *w, const float *img,
+			float *out)
+{
+	const int S = c->img_size, H1 = (S - 1) / 2 + 1, H2 = (H1 - 1) / 2 + 1;
+	const int C0 = c->embed_dims[0];
+	float *a = malloc(sizeof(float) * (size_t)H1 * H1 * (C0 / 2));
+	float *x = malloc(sizeof(float) * (size_t)H2 * H2 * C0);
+	const struct orc_conv *p0 = &w->patch_embed_0, *p1 = &w->patch_embed_1;
+	orc_conv2d_bn(img, 1, 1, S, S, 3, C0 / 2, 3, 2, 1, p0->w, p0->b, p0->bn_w,
+		      p0->bn_b, p0->bn_mean, p0->bn_var, 1, a);
+	orc_conv2d_bn(a, 0, 1, H1, H1, C0 / 2, C0, 3, 2, 1, p1->w, p1->b,
+		      p1->bn_w, p1->bn_b, p1->bn_mean, p1->bn_var, 0, x);
+	free(a);
+	int H = H2, C = C0;
+	for (int l = 0; l < c->n_layers; l++) {
+		for (int b = 0; b < c->depths[l]; b++) {
+			if (l == 0) {
+				orc_tvit_mbconv_forward(&w->layers[0].conv_blocks[b], x,
+							1, H, H, C, C * c->mlp_ratio);
+			} else {
+				const struct orc_tvit_block_c *bc = &w->layers[l].blocks[b];
+				const int ws = c->window_sizes[l], N = ws * ws;
+				const int heads = c->num_heads[l];
+				float *bias = NULL;
+				if (bc->attn_bias) {
+					bias = malloc(sizeof(float) * (size_t)heads * N * N);
+					orc_tvit_expand_bias(bc->attn_bias, heads,
+							     bc->attn_bias_offsets, ws, bias);
+				}
+				struct orc_tvit_block ob = {
+					bc->attn_norm_w, bc->attn_norm_b, bc->qkv_w,
+					bc->qkv_b, bc->proj_w, bc->proj_b, bias,
+					bc->lc_w, bc->lc_b, bc->lc_bn_w, bc->lc_bn_b,
+					bc->lc_bn_mean, bc->lc_bn_var, bc->mlp_norm_w,
+					bc->mlp_norm_b, bc->fc1_w, bc->fc1_b, bc->fc2_w,
+					bc->fc2_b};
+				orc_tvit_block_forward(&ob, x, H, H, C, heads, ws,
+						       C * c->mlp_ratio);
+				free(bias);
+			}
+		}
+		if (l == c->n_layers - 1)
+			break;
+		/* PatchMerging (tvit_patch_merging, :726-750) */
+		const struct orc_tinyvit_layer *lw = &w->layers[l];
+		const int Cn = c->embed_dims[l + 1], Hn = (H - 1) / 2 + 1;
+		float *h = malloc(sizeof(float) * (size_t)H * H * Cn);
+		float *h2 = malloc(sizeof(float) * (size_t)Hn * Hn * Cn);
+		float *xn = malloc(sizeof(float) * (size_t)Hn * Hn * Cn);
+		orc_conv2d_bn(x, 0, 1, H, H, C, Cn, 1, 1, 0, lw->pm_conv1.w,
+			      lw->pm_conv1.b, lw->pm_conv1.bn_w, lw->pm_conv1.bn_b,
+			      lw->pm_conv1.bn_mean, lw->pm_conv1.bn_var, 1, h);
+		orc_dwconv3x3_bn_s(h, 1, H, H, Cn, 2, lw->pm_conv2.w,
+				   lw->pm_conv2.b, lw->pm_conv2.bn_w,
+				   lw->pm_conv2.bn_b, lw->pm_conv2.bn_mean,
+				   lw->pm_conv2.bn_var, 1, h2);
+		orc_conv2d_bn(h2, 0, 1, Hn, Hn, Cn, Cn, 1, 1, 0, lw->pm_conv3.w,
+			      lw->pm_conv3.b, lw->pm_conv3.bn_w, lw->pm_conv3.bn_b,
+			      lw->pm_conv3.bn_mean, lw->pm_conv3.bn_var, 0, xn);
+		free(x);
+		free(h);
+		free(h2);
+		x = xn;
+		H = Hn;
+		C = Cn;
+	}
+	/* head: 1x1 conv (no bias) -> BN -> GELU -> 3x3 conv + bias (:1230-1262) */
+	const int E = c->embed_dim;
+	float *h = malloc(sizeof(float) * (size_t)H * H * E);
+	orc_conv2d_bn(x, 0, 1, H, H, C, E, 1, 1, 0, w->proj_conv1.w, NULL,
+		      w->proj_bn.bn_w, w->proj_bn.bn_b, w->proj_bn.bn_mean,
+		      w->proj_bn.bn_var, 1, h);
+	orc_conv2d_bn(h, 0, 1, H, H, E, E, 3, 1, 1, w->proj_conv2.w,
+		      w->proj_conv2.b, NULL, NULL, NULL, NULL, 0, out);
+	free(h);
+	free(x);
+	return H;
 }

@@ -545,3 +545,19 @@ def tvit_mbconv_forward(w: dict, x: np.ndarray) -> np.ndarray:
     orc().orc_tvit_mbconv_forward(C.byref(s), _p(x), B, H, W, Cc, mid)
     del keep
     return x
+
+
+def tinyvit_forward(cfg_struct, weights_struct, image: np.ndarray) -> np.ndarray:
+    """Restatement of sam3_tinyvit_build for one image [3, S, S]; the
+    ctypes structs have the CUDA library's layouts (the test builds them
+    with sam3cu.tinyvit_structs).  Returns [grid*grid, embed_dim]."""
+    image = np.ascontiguousarray(image, np.float32)
+    S = cfg_struct.img_size
+    g = (S - 1) // 2 + 1
+    g = (g - 1) // 2 + 1
+    for _ in range(cfg_struct.n_layers - 1):
+        g = (g - 1) // 2 + 1
+    out = np.empty((g * g, cfg_struct.embed_dim), np.float32)
+    got = orc().orc_tinyvit_forward(C.byref(cfg_struct), C.byref(weights_struct), _p(image), _p(out))
+    assert got == g
+    return out

@@ -33,7 +33,9 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
+#include <memory>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -123,7 +125,10 @@ int ln_tvit_dispatch(const float* x, void* y, const float* g, const float* b, in
                      const WinMap& m, int use_map, cudaStream_t st) {
   const int grid = grid_1d(rows * 32, 256);
   switch (C / 32) {
-#define S3_CASE(NE)                                                                             case NE:                                                                                        ln_rows_tvit<TO, NE><<<grid, 256, 0, st>>>(x, y, g, b, rows, C, m, use_map);               break;
+#define S3_CASE(NE)                                                                 \
+  case NE:                                                                          \
+    ln_rows_tvit<TO, NE><<<grid, 256, 0, st>>>(x, y, g, b, rows, C, m, use_map);    \
+    break;
     S3_CASE(2) S3_CASE(3) S3_CASE(4) S3_CASE(6) S3_CASE(8) S3_CASE(9) S3_CASE(12) S3_CASE(16)
     S3_CASE(18) S3_CASE(24) S3_CASE(32)
 #undef S3_CASE
@@ -174,15 +179,16 @@ __device__ __forceinline__ float gelu_f(float v) {
 // thread; w9 [9][C] (tap-major, BatchNorm folded), bias [C]; optional GELU.
 template <int TI, int TO, bool kGelu>
 __global__ void dwconv3x3(const void* __restrict__ x, void* __restrict__ y, const float* __restrict__ w9,
-                          const float* __restrict__ bias, int B, int H, int W, int C) {
+                          const float* __restrict__ bias, int B, int H, int W, int C, int stride, int OH, int OW) {
   const int c4 = C / 4;
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = static_cast<int64_t>(B) * H * W * c4;
+  const int64_t total = static_cast<int64_t>(B) * OH * OW * c4;
   if (i >= total) return;
   const int c = static_cast<int>(i % c4) * 4;
-  const int64_t p = i / c4;
-  const int xx = static_cast<int>(p % W), yy = static_cast<int>((p / W) % H);
-  const int64_t img = p / (static_cast<int64_t>(H) * W);
+  const int64_t p = i / c4;  // output pixel
+  const int ox = static_cast<int>(p % OW), oy = static_cast<int>((p / OW) % OH);
+  const int64_t img = p / (static_cast<int64_t>(OH) * OW);
+  const int yy = oy * stride, xx = ox * stride;  // input centre
   float4 acc = __ldg(reinterpret_cast<const float4*>(bias + c));
 #pragma unroll
   for (int ky = 0; ky < 3; ++ky) {
@@ -209,13 +215,22 @@ __global__ void dwconv3x3(const void* __restrict__ x, void* __restrict__ y, cons
   IO<TO>::st4(y, p * C + c, acc);
 }
 
+// 3x3 depthwise conv, zero padding 1, stride 1 or 2 (output (H-1)/s+1).
 int launch_dwconv3x3(const void* x, int tin, void* y, int tout, const float* w9, const float* bias, int B,
-                     int H, int W, int C, bool gelu, cudaStream_t st) {
-  if (C % 4) return kErrShape;
+                     int H, int W, int C, bool gelu, cudaStream_t st, int stride = 1) {
+  if (C % 4 || stride < 1) return kErrShape;
   count_launches(1);
-  const int64_t total = static_cast<int64_t>(B) * H * W * (C / 4);
+  const int OH = (H - 1) / stride + 1, OW = (W - 1) / stride + 1;
+  const int64_t total = static_cast<int64_t>(B) * OH * OW * (C / 4);
   const int grid = grid_1d(total, 256);
-#define S3_DW(TI, TO)                                                                            if (tin == TI && tout == TO) {                                                                   if (gelu)                                                                                        dwconv3x3<TI, TO, true><<<grid, 256, 0, st>>>(x, y, w9, bias, B, H, W, C);                   else                                                                                             dwconv3x3<TI, TO, false><<<grid, 256, 0, st>>>(x, y, w9, bias, B, H, W, C);                  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;                                 }
+#define S3_DW(TI, TO)                                                                            \
+  if (tin == TI && tout == TO) {                                                                 \
+    if (gelu)                                                                                    \
+      dwconv3x3<TI, TO, true><<<grid, 256, 0, st>>>(x, y, w9, bias, B, H, W, C, stride, OH, OW);  \
+    else                                                                                         \
+      dwconv3x3<TI, TO, false><<<grid, 256, 0, st>>>(x, y, w9, bias, B, H, W, C, stride, OH, OW); \
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;                                 \
+  }
   S3_DW(kF32, kF32) S3_DW(kBF16, kBF16) S3_DW(kF16, kF16) S3_DW(kF32, kBF16) S3_DW(kF32, kF16)
 #undef S3_DW
   return kErrDtype;
@@ -303,6 +318,89 @@ int ensure(DevBuf& d, size_t bytes) {
   return d.alloc(bytes) ? kOk : kErrNoMem;
 }
 
+// im2col for a dense KxK conv (zero padding) -> 16-bit columns: row
+// (img, oy, ox), column (ky, kx, c) to match OHWI weights, zero-filled to
+// kpad.  kChw: the input is planar CHW per image (the raw image), else NHWC.
+template <int TI, int TO, bool kChw>
+__global__ void conv_im2col(const void* __restrict__ x, void* __restrict__ a, int64_t total, int H, int W, int C,
+                            int k, int stride, int pad, int OH, int OW, int kpad) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int col = static_cast<int>(i % kpad);
+  const int64_t row = i / kpad;
+  const int ox = static_cast<int>(row % OW), oy = static_cast<int>((row / OW) % OH);
+  const int64_t b = row / (static_cast<int64_t>(OW) * OH);
+  float v = 0.f;
+  if (col < k * k * C) {
+    const int c = col % C, kx = (col / C) % k, ky = col / (C * k);
+    const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+    if (iy >= 0 && iy < H && ix >= 0 && ix < W) {
+      const int64_t src = kChw ? ((b * C + c) * H + iy) * W + ix : ((b * H + iy) * W + ix) * C + c;
+      if (TI == kF32)
+        v = static_cast<const float*>(x)[src];
+      else if (TI == kBF16)
+        v = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[src]);
+      else
+        v = __half2float(static_cast<const __half*>(x)[src]);
+    }
+  }
+  if (TO == kBF16)
+    static_cast<__nv_bfloat16*>(a)[i] = __float2bfloat16_rn(v);
+  else
+    static_cast<__half*>(a)[i] = __float2half_rn(v);
+}
+
+int launch_conv_im2col(const void* x, int tin, bool chw, void* a, int tout, int B, int H, int W, int C, int k,
+                       int stride, int pad, int kpad, cudaStream_t st) {
+  const int OH = (H + 2 * pad - k) / stride + 1, OW = (W + 2 * pad - k) / stride + 1;
+  const int64_t total = static_cast<int64_t>(B) * OH * OW * kpad;
+  const int grid = grid_1d(total, 256);
+  count_launches(1);
+#define S3_IC(TI, TO, CHW)                                                                               \
+  if (tin == TI && tout == TO && chw == CHW) {                                                           \
+    conv_im2col<TI, TO, CHW><<<grid, 256, 0, st>>>(x, a, total, H, W, C, k, stride, pad, OH, OW, kpad); \
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;                                         \
+  }
+  S3_IC(kF32, kBF16, true) S3_IC(kF32, kF16, true) S3_IC(kF32, kBF16, false) S3_IC(kF32, kF16, false)
+  S3_IC(kBF16, kBF16, false) S3_IC(kF16, kF16, false)
+#undef S3_IC
+  return kErrDtype;
+}
+
+// A dense conv (OHWI weights [OC, k, k, IC]) with its BatchNorm folded, run
+// as (im2col +) GEMM: W 16-bit [OC, kpad], bias f32 [OC].
+struct DenseConv {
+  int oc = 0, ic = 0, k = 1, stride = 1, pad = 0, kpad = 0;
+  DevBuf w, b;
+};
+
+int make_dense_conv(DenseConv& cv, const sam3cu_tvit_conv_weights& cw, int oc, int ic, int k, int stride, int pad,
+                    int act, cudaStream_t st) {
+  if (!cw.w) return kErrShape;
+  cv.oc = oc;
+  cv.ic = ic;
+  cv.k = k;
+  cv.stride = stride;
+  cv.pad = pad;
+  const int kk = k * k * ic;
+  cv.kpad = (kk + 7) / 8 * 8;  // 16-byte GEMM rows
+  std::vector<float> wf(cw.w, cw.w + static_cast<size_t>(oc) * kk), bf;
+  fold_bn(wf, bf, oc, kk, cw.b, cw.bn_w, cw.bn_b, cw.bn_mean, cw.bn_var);
+  std::vector<float> wp(static_cast<size_t>(oc) * cv.kpad, 0.f);
+  for (int o = 0; o < oc; ++o)
+    std::copy(wf.begin() + static_cast<size_t>(o) * kk, wf.begin() + static_cast<size_t>(o + 1) * kk,
+              wp.begin() + static_cast<size_t>(o) * cv.kpad);
+  int rc = upload_w16(cv.w, wp.data(), oc, cv.kpad, act, st);
+  if (!rc) rc = upload(cv.b, bf.data(), bf.size() * 4, st);
+  return rc;
+}
+
+// Depthwise 3x3 weights + folded BN from the conv-weights struct.
+int make_dw_conv(DevBuf& w9, DevBuf& bias, int C, const sam3cu_tvit_conv_weights& cw, cudaStream_t st) {
+  if (!cw.w) return kErrShape;
+  return upload_dw(w9, bias, C, cw.w, cw.b, cw.bn_w, cw.bn_b, cw.bn_mean, cw.bn_var, st);
+}
+
 }  // namespace
 
 struct sam3cu_tvit_block {
@@ -317,6 +415,30 @@ struct sam3cu_tvit_mbconv {
   int C = 0, mid = 0, act = kBF16;
   DevBuf w1, b1, dw_w9, dw_b, w3, b3;
   DevBuf xa, h, h2;  // scratch
+};
+
+struct sam3cu_tinyvit {
+  sam3cu_tinyvit_config c{};
+  int act = kBF16, max_batch = 0, grid = 0;
+  cudaStream_t stream = nullptr;
+  DenseConv pe0, pe1;
+  std::vector<sam3cu_tvit_mbconv*> mb;                 // layer 0
+  std::vector<std::vector<sam3cu_tvit_block*>> blocks;  // layers >= 1
+  struct Merge {
+    DenseConv c1, c3;
+    DevBuf dw_w9, dw_b;
+  } pm[SAM3CU_TVIT_MAX_LAYERS];
+  DenseConv head1, head2;
+  DevBuf img, out, a, x, xa, col, h, h2;  // staging and scratch
+  ~sam3cu_tinyvit() {
+    for (auto* m : mb) sam3cu_tvit_mbconv_destroy(m);
+    for (auto& l : blocks)
+      for (auto* b : l) sam3cu_tvit_block_destroy(b);
+    if (stream) {
+      cudaStreamSynchronize(stream);
+      cudaStreamDestroy(stream);
+    }
+  }
 };
 
 extern "C" {
@@ -558,6 +680,170 @@ int sam3cu_tvit_mbconv_forward(sam3cu_tvit_mbconv* m, float* x, int n_images, in
   else
     gelu_cast<kBF16><<<grid_1d(n4, 256), 256, 0, st>>>(x, m->xa.p, n4);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+namespace {
+
+// y[M, oc] = im2col(x) . W^T + b (optionally GELU), as one GEMM; a 1x1,
+// stride-1 conv reads the 16-bit NHWC input directly.
+int run_conv(sam3cu_tinyvit* t, const DenseConv& cv, const void* x, int tin, bool chw, int n, int H, int W,
+             void* y, int out_type, int act_gelu) {
+  const int OH = (H + 2 * cv.pad - cv.k) / cv.stride + 1, OW = (W + 2 * cv.pad - cv.k) / cv.stride + 1;
+  const int64_t M = static_cast<int64_t>(n) * OH * OW;
+  if (M > 0x7fffffffLL) return kErrShape;
+  const void* a = x;
+  int rc;
+  if (cv.k != 1 || cv.stride != 1 || chw || tin == kF32 || cv.kpad != cv.ic) {
+    if ((rc = ensure(t->col, static_cast<size_t>(M) * cv.kpad * 2))) return rc;
+    if ((rc = launch_conv_im2col(x, tin, chw, t->col.p, t->act, n, H, W, cv.ic, cv.k, cv.stride, cv.pad, cv.kpad,
+                                 t->stream)))
+      return rc;
+    a = t->col.p;
+  }
+  EpiParams e = epi(y, out_type, cv.oc, cv.b.as<float>());
+  e.act = act_gelu;
+  return launch_gemm(a, cv.kpad, cv.w.p, cv.kpad, nullptr, nullptr, t->act, GemmShape{static_cast<int>(M), cv.oc, cv.kpad},
+                     e, t->stream, 0);
+}
+
+int tinyvit_forward(sam3cu_tinyvit* t, const float* images, int n, float* out) {
+  const auto& c = t->c;
+  const int S = c.img_size, H1 = (S - 1) / 2 + 1, H2 = (H1 - 1) / 2 + 1;
+  const int C0 = c.embed_dims[0];
+  int rc;
+  // patch embed: 3x3/2 conv + BN + GELU (CHW image read in place), 3x3/2 conv + BN
+  if ((rc = ensure(t->a, static_cast<size_t>(n) * H1 * H1 * t->pe0.oc * 2))) return rc;
+  if ((rc = run_conv(t, t->pe0, images, kF32, true, n, S, S, t->a.p, t->act, 1))) return rc;
+  size_t xmax = static_cast<size_t>(n) * H2 * H2 * C0;
+  if ((rc = ensure(t->x, xmax * 4))) return rc;
+  if ((rc = run_conv(t, t->pe1, t->a.p, t->act, false, n, H1, H1, t->x.p, kOutF32, 0))) return rc;
+  int H = H2, C = C0;
+  for (int l = 0; l < c.n_layers; ++l) {
+    if (l == 0) {
+      for (auto* m : t->mb)
+        if ((rc = sam3cu_tvit_mbconv_forward(m, t->x.as<float>(), n, H, H, t->stream))) return rc;
+    } else {
+      for (auto* b : t->blocks[l])
+        if ((rc = sam3cu_tvit_block_forward(b, t->x.as<float>(), n, H, H, t->stream))) return rc;
+    }
+    if (l == c.n_layers - 1) break;
+    // PatchMerging (tvit_patch_merging, :726-750): 1x1 + BN, GELU;
+    // 3x3 depthwise stride 2 + BN, GELU; 1x1 + BN
+    const auto& pm = t->pm[l];
+    const int Cn = c.embed_dims[l + 1], Hn = (H - 1) / 2 + 1;
+    const int64_t P = static_cast<int64_t>(n) * H * H, Pn = static_cast<int64_t>(n) * Hn * Hn;
+    if ((rc = ensure(t->xa, static_cast<size_t>(P) * C * 2)) || (rc = ensure(t->h, static_cast<size_t>(P) * Cn * 2)) ||
+        (rc = ensure(t->h2, static_cast<size_t>(Pn) * Cn * 2)))
+      return rc;
+    if ((rc = launch_cast(t->x.p, kF32, t->xa.p, t->act, P * C, t->stream))) return rc;
+    if ((rc = run_conv(t, pm.c1, t->xa.p, t->act, false, n, H, H, t->h.p, t->act, 1))) return rc;
+    if ((rc = launch_dwconv3x3(t->h.p, t->act, t->h2.p, t->act, pm.dw_w9.as<float>(), pm.dw_b.as<float>(), n, H, H,
+                               Cn, true, t->stream, 2)))
+      return rc;
+    if ((rc = ensure(t->x, static_cast<size_t>(Pn) * Cn * 4))) return rc;
+    if ((rc = run_conv(t, pm.c3, t->h2.p, t->act, false, n, Hn, Hn, t->x.p, kOutF32, 0))) return rc;
+    H = Hn;
+    C = Cn;
+  }
+  // head: 1x1 conv + BN, GELU; 3x3 conv + bias (:1230-1262)
+  const int64_t P = static_cast<int64_t>(n) * H * H;
+  if ((rc = ensure(t->xa, static_cast<size_t>(P) * C * 2)) ||
+      (rc = ensure(t->h, static_cast<size_t>(P) * c.embed_dim * 2)))
+    return rc;
+  if ((rc = launch_cast(t->x.p, kF32, t->xa.p, t->act, P * C, t->stream))) return rc;
+  if ((rc = run_conv(t, t->head1, t->xa.p, t->act, false, n, H, H, t->h.p, t->act, 1))) return rc;
+  return run_conv(t, t->head2, t->h.p, t->act, false, n, H, H, out, kOutF32, 0);
+}
+
+}  // namespace
+
+sam3cu_tinyvit* sam3cu_tinyvit_create(const struct sam3cu_tinyvit_config* cfg, const struct sam3cu_tinyvit_weights* w,
+                                      int dtype, int max_batch, int* status) {
+  int dummy;
+  int* st_p = status ? status : &dummy;
+  auto fail = [&](int r) -> sam3cu_tinyvit* {
+    *st_p = r;
+    return nullptr;
+  };
+  if (!cfg || !w || max_batch <= 0 || cfg->n_layers < 2 || cfg->n_layers > SAM3CU_TVIT_MAX_LAYERS ||
+      cfg->img_size < 8 || cfg->embed_dim <= 0 || cfg->embed_dim % 8 || cfg->mlp_ratio <= 0)
+    return fail(SAM3CU_EINVAL);
+  if (dtype != SAM3CU_BF16 && dtype != SAM3CU_F16) return fail(SAM3CU_EDTYPE);
+  for (int l = 0; l < cfg->n_layers; ++l)
+    if (cfg->embed_dims[l] <= 0 || cfg->embed_dims[l] % 32 || cfg->depths[l] < 0 ||
+        (l == 0 ? !w->layers[0].conv_blocks && cfg->depths[0] > 0 : !w->layers[l].blocks && cfg->depths[l] > 0))
+      return fail(SAM3CU_EINVAL);
+  std::unique_ptr<sam3cu_tinyvit> t(new sam3cu_tinyvit());
+  t->c = *cfg;
+  t->act = dtype == SAM3CU_F16 ? kF16 : kBF16;
+  t->max_batch = max_batch;
+  int h = cfg->img_size;
+  h = (h - 1) / 2 + 1;
+  h = (h - 1) / 2 + 1;
+  for (int l = 0; l + 1 < cfg->n_layers; ++l) h = (h - 1) / 2 + 1;
+  t->grid = h;
+  if (cudaStreamCreateWithFlags(&t->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(SAM3CU_ECUDA);
+  cudaStream_t st = t->stream;
+  const int C0 = cfg->embed_dims[0], Ch = C0 / 2;  // patch embed: 3 -> C0/2 -> C0
+  int rc = make_dense_conv(t->pe0, w->patch_embed_0, Ch, 3, 3, 2, 1, t->act, st);
+  if (!rc) rc = make_dense_conv(t->pe1, w->patch_embed_1, C0, Ch, 3, 2, 1, t->act, st);
+  for (int b = 0; !rc && b < cfg->depths[0]; ++b) {
+    sam3cu_tvit_mbconv* m = sam3cu_tvit_mbconv_create(C0, C0 * cfg->mlp_ratio, dtype, &w->layers[0].conv_blocks[b], &rc);
+    if (m) t->mb.push_back(m);
+  }
+  t->blocks.resize(cfg->n_layers);
+  for (int l = 1; !rc && l < cfg->n_layers; ++l)
+    for (int b = 0; !rc && b < cfg->depths[l]; ++b) {
+      const int C = cfg->embed_dims[l];
+      sam3cu_tvit_block* blk = sam3cu_tvit_block_create(C, cfg->num_heads[l], cfg->window_sizes[l],
+                                                        C * cfg->mlp_ratio, dtype, &w->layers[l].blocks[b], &rc);
+      if (blk) t->blocks[l].push_back(blk);
+    }
+  for (int l = 0; !rc && l + 1 < cfg->n_layers; ++l) {
+    const int C = cfg->embed_dims[l], Cn = cfg->embed_dims[l + 1];
+    const auto& lw = w->layers[l];
+    rc = make_dense_conv(t->pm[l].c1, lw.pm_conv1, Cn, C, 1, 1, 0, t->act, st);
+    if (!rc) rc = make_dw_conv(t->pm[l].dw_w9, t->pm[l].dw_b, Cn, lw.pm_conv2, st);
+    if (!rc) rc = make_dense_conv(t->pm[l].c3, lw.pm_conv3, Cn, Cn, 1, 1, 0, t->act, st);
+  }
+  if (!rc) {
+    const int CL = cfg->embed_dims[cfg->n_layers - 1];
+    sam3cu_tvit_conv_weights h1 = w->proj_conv1;  // the head's BN is its own struct
+    h1.b = nullptr;                               // and its 1x1 conv has no bias (:1239-1241)
+    h1.bn_w = w->proj_bn.bn_w;
+    h1.bn_b = w->proj_bn.bn_b;
+    h1.bn_mean = w->proj_bn.bn_mean;
+    h1.bn_var = w->proj_bn.bn_var;
+    rc = make_dense_conv(t->head1, h1, cfg->embed_dim, CL, 1, 1, 0, t->act, st);
+    if (!rc) rc = make_dense_conv(t->head2, w->proj_conv2, cfg->embed_dim, cfg->embed_dim, 3, 1, 1, t->act, st);
+  }
+  if (!rc) rc = ck(cudaStreamSynchronize(st));
+  if (rc) return fail(rc);
+  *st_p = SAM3CU_OK;
+  return t.release();
+}
+
+int sam3cu_tinyvit_grid(const sam3cu_tinyvit* t) { return t ? t->grid : 0; }
+
+void sam3cu_tinyvit_destroy(sam3cu_tinyvit* t) { delete t; }
+
+int sam3cu_tinyvit_encode(sam3cu_tinyvit* t, const float* images, int n, float* out, int on_device) {
+  if (!t || !images || !out || n <= 0 || n > t->max_batch) return SAM3CU_EINVAL;
+  const size_t in_bytes = static_cast<size_t>(n) * 3 * t->c.img_size * t->c.img_size * 4;
+  const size_t out_bytes = static_cast<size_t>(n) * t->grid * t->grid * t->c.embed_dim * 4;
+  int rc;
+  if (on_device) {
+    rc = tinyvit_forward(t, images, n, out);
+  } else {
+    if ((rc = ensure(t->img, in_bytes)) || (rc = ensure(t->out, out_bytes))) return rc;
+    if (cudaMemcpyAsync(t->img.p, images, in_bytes, cudaMemcpyHostToDevice, t->stream) != cudaSuccess)
+      return SAM3CU_ECUDA;
+    rc = tinyvit_forward(t, t->img.as<float>(), n, t->out.as<float>());
+    if (!rc && cudaMemcpyAsync(out, t->out.p, out_bytes, cudaMemcpyDeviceToHost, t->stream) != cudaSuccess)
+      rc = SAM3CU_ECUDA;
+  }
+  if (cudaStreamSynchronize(t->stream) != cudaSuccess) return SAM3CU_ECUDA;
+  return rc;
 }
 
 }  // extern "C"

@@ -32,6 +32,7 @@ EXPORTS = (
     "sam3cu_tvit_block_create", "sam3cu_tvit_block_forward", "sam3cu_tvit_block_destroy",
     "sam3cu_tvit_mbconv_create", "sam3cu_tvit_mbconv_forward", "sam3cu_tvit_mbconv_destroy",
     "sam3cu_selftest_wait_timeout",
+    "sam3cu_tinyvit_create", "sam3cu_tinyvit_encode", "sam3cu_tinyvit_grid", "sam3cu_tinyvit_destroy",
 )
 
 # sizeof(struct sam3_cuda_backend): {enum type; ops*} + int device + void *impl
@@ -87,6 +88,11 @@ def lib():
         L.sam3cu_tvit_mbconv_forward.argtypes = [vp, vp, i32, i32, i32, vp]
         L.sam3cu_tvit_mbconv_destroy.argtypes = [vp]
         L.sam3cu_selftest_wait_timeout.argtypes = [C.c_ulonglong, C.POINTER(C.c_int)]
+        L.sam3cu_tinyvit_create.restype = vp
+        L.sam3cu_tinyvit_create.argtypes = [vp, vp, i32, i32, C.POINTER(C.c_int)]
+        L.sam3cu_tinyvit_encode.argtypes = [vp, vp, i32, vp, i32]
+        L.sam3cu_tinyvit_grid.argtypes = [vp]
+        L.sam3cu_tinyvit_destroy.argtypes = [vp]
         _lib = L
     return _lib
 
@@ -456,3 +462,94 @@ def selftest_wait_timeout(limit_ns: int = 20_000_000) -> bool:
     out = C.c_int(0)
     check(lib().sam3cu_selftest_wait_timeout(limit_ns, C.byref(out)), "sam3cu_selftest_wait_timeout")
     return out.value == 1
+
+
+class TvitConvW(C.Structure):
+    """struct sam3cu_tvit_conv_weights."""
+    _fields_ = [(n, C.c_void_p) for n in ("w", "b", "bn_w", "bn_b", "bn_mean", "bn_var")]
+
+
+class TinyvitCfg(C.Structure):
+    """struct sam3cu_tinyvit_config."""
+    _fields_ = [("img_size", C.c_int), ("n_layers", C.c_int), ("embed_dims", C.c_int * 4),
+                ("depths", C.c_int * 4), ("num_heads", C.c_int * 4), ("window_sizes", C.c_int * 4),
+                ("embed_dim", C.c_int), ("mlp_ratio", C.c_int)]
+
+
+class TinyvitLayerW(C.Structure):
+    """struct sam3cu_tinyvit_layer_weights."""
+    _fields_ = [("conv_blocks", C.c_void_p), ("blocks", C.c_void_p), ("pm_conv1", TvitConvW),
+                ("pm_conv2", TvitConvW), ("pm_conv3", TvitConvW)]
+
+
+class TinyvitW(C.Structure):
+    """struct sam3cu_tinyvit_weights."""
+    _fields_ = [("patch_embed_0", TvitConvW), ("patch_embed_1", TvitConvW), ("layers", TinyvitLayerW * 4),
+                ("proj_conv1", TvitConvW), ("proj_bn", TvitConvW), ("proj_conv2", TvitConvW)]
+
+
+def tinyvit_structs(cfg: dict, w: dict):
+    """ctypes config and weight tree for a TinyViT weight dict (see
+    synth.tinyvit_weights); returns (cfg_struct, weights_struct, keepalive)."""
+    keep = []
+    cs = TinyvitCfg()
+    cs.img_size, cs.n_layers = cfg["img_size"], cfg["n_layers"]
+    for k in ("embed_dims", "depths", "num_heads", "window_sizes"):
+        getattr(cs, k)[:] = list(cfg[k]) + [0] * (4 - len(cfg[k]))
+    cs.embed_dim, cs.mlp_ratio = cfg["embed_dim"], cfg["mlp_ratio"]
+    ws = TinyvitW()
+    for name in ("patch_embed_0", "patch_embed_1", "proj_conv1", "proj_bn", "proj_conv2"):
+        _fill(getattr(ws, name), w[name], keep)
+    for l, lw in enumerate(w["layers"]):
+        L = ws.layers[l]
+        if lw.get("conv_blocks"):
+            arr = (_TvitMbW * len(lw["conv_blocks"]))()
+            for i, d in enumerate(lw["conv_blocks"]):
+                _fill(arr[i], d, keep)
+            keep.append(arr)
+            L.conv_blocks = C.addressof(arr)
+        if lw.get("blocks"):
+            arr = (_TvitBlockW * len(lw["blocks"]))()
+            for i, d in enumerate(lw["blocks"]):
+                _fill(arr[i], d, keep)
+                arr[i].attn_bias_offsets = int(d["attn_bias"].shape[-1])
+            keep.append(arr)
+            L.blocks = C.addressof(arr)
+        for name in ("pm_conv1", "pm_conv2", "pm_conv3"):
+            if name in lw:
+                _fill(getattr(L, name), lw[name], keep)
+    return cs, ws, keep
+
+
+class TinyViT:
+    """The TinyViT backbone on device (sam3cu_tinyvit_*)."""
+
+    def __init__(self, cfg: dict, w: dict, dtype=F16, max_batch=1):
+        self.cfg = cfg
+        cs, ws, keep = tinyvit_structs(cfg, w)
+        st = C.c_int(0)
+        self.h = lib().sam3cu_tinyvit_create(C.byref(cs), C.byref(ws), dtype, max_batch, C.byref(st))
+        del keep
+        if not self.h:
+            check(st.value or -1, "sam3cu_tinyvit_create")
+        self.grid = lib().sam3cu_tinyvit_grid(self.h)
+
+    def encode_host(self, images):
+        import numpy as np
+        images = np.ascontiguousarray(images, np.float32)
+        n = images.shape[0]
+        out = np.empty((n, self.grid * self.grid, self.cfg["embed_dim"]), np.float32)
+        check(lib().sam3cu_tinyvit_encode(self.h, images.ctypes.data, n, out.ctypes.data, 0),
+              "sam3cu_tinyvit_encode")
+        return out
+
+    def encode_ptr(self, images_ptr: int, n: int, out_ptr: int, on_device: bool) -> None:
+        check(lib().sam3cu_tinyvit_encode(self.h, images_ptr, n, out_ptr, 1 if on_device else 0),
+              "sam3cu_tinyvit_encode")
+
+    def close(self):
+        if self.h:
+            lib().sam3cu_tinyvit_destroy(self.h)
+            self.h = None
+
+    __del__ = close

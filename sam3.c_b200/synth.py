@@ -64,3 +64,82 @@ def round_weights(w: dict, fn) -> dict:
             nb[k] = fn(b[k])
         out["blocks"].append(nb)
     return out
+
+
+# ---------------------------------------------------------------- TinyViT
+TINYVIT_21M = dict(img_size=1008, n_layers=4, embed_dims=(96, 192, 384, 576), depths=(2, 2, 6, 2),
+                   num_heads=(3, 6, 12, 18), window_sizes=(7, 7, 14, 7), embed_dim=1024, mlp_ratio=4)
+
+
+def tiny_tinyvit_cfg(img_size=112):
+    """A small TinyViT for parity runs (head_dim 32 everywhere)."""
+    return dict(img_size=img_size, n_layers=4, embed_dims=(32, 64, 96, 128), depths=(1, 1, 2, 1),
+                num_heads=(1, 2, 3, 4), window_sizes=(7, 7, 14, 7), embed_dim=64, mlp_ratio=4)
+
+
+def tinyvit_weights(cfg, seed=0, std=0.02):
+    """Random-init TinyViT weights in the reference's layouts (OHWI convs,
+    [out, in] linears); BN running stats mean 0 / var 1, gamma 1, beta 0
+    perturbed slightly; weights ~N(0, std)."""
+    rng = np.random.default_rng(seed)
+    n = lambda *s, sc=std: (rng.standard_normal(s) * sc).astype(np.float32)
+
+    def bn(c):
+        return dict(bn_w=1 + n(c, sc=0.05), bn_b=n(c, sc=0.05), bn_mean=n(c, sc=0.05),
+                    bn_var=(1 + 0.1 * rng.random(c)).astype(np.float32))
+
+    def conv(oc, ic, k, bias=False, with_bn=True):
+        d = dict(w=n(oc, k, k, ic))
+        if bias:
+            d["b"] = n(oc)
+        if with_bn:
+            d.update(bn(oc))
+        return d
+
+    E = cfg["embed_dims"]
+    r = cfg["mlp_ratio"]
+    w = {"patch_embed_0": conv(E[0] // 2, 3, 3), "patch_embed_1": conv(E[0], E[0] // 2, 3), "layers": []}
+    for l in range(cfg["n_layers"]):
+        C = E[l]
+        layer = {}
+        if l == 0:
+            mid = C * r
+            layer["conv_blocks"] = []
+            for _ in range(cfg["depths"][0]):
+                c1, c2, c3 = conv(mid, C, 1), conv(mid, 1, 3), conv(C, mid, 1)
+                mb = {}
+                for i, cc in ((1, c1), (2, c2), (3, c3)):
+                    mb[f"conv{i}_w"] = cc["w"]
+                    for k in ("w", "b", "mean", "var"):
+                        mb[f"bn{i}_{k}"] = cc[f"bn_{k}"]
+                layer["conv_blocks"].append(mb)
+        else:
+            heads, ws = cfg["num_heads"][l], cfg["window_sizes"][l]
+            layer["blocks"] = []
+            for _ in range(cfg["depths"][l]):
+                lc = conv(C, 1, 3)
+                layer["blocks"].append({
+                    "attn_norm_w": 1 + n(C), "attn_norm_b": n(C), "qkv_w": n(3 * C, C), "qkv_b": n(3 * C),
+                    "proj_w": n(C, C), "proj_b": n(C), "attn_bias": n(heads, ws * ws, sc=0.5),
+                    "lc_w": lc["w"], "lc_bn_w": lc["bn_w"], "lc_bn_b": lc["bn_b"],
+                    "lc_bn_mean": lc["bn_mean"], "lc_bn_var": lc["bn_var"],
+                    "mlp_norm_w": 1 + n(C), "mlp_norm_b": n(C), "fc1_w": n(r * C, C), "fc1_b": n(r * C),
+                    "fc2_w": n(C, r * C), "fc2_b": n(C)})
+        if l + 1 < cfg["n_layers"]:
+            Cn = E[l + 1]
+            layer["pm_conv1"] = conv(Cn, C, 1)
+            layer["pm_conv2"] = conv(Cn, 1, 3)
+            layer["pm_conv3"] = conv(Cn, Cn, 1)
+        w["layers"].append(layer)
+    emb, CL = cfg["embed_dim"], E[cfg["n_layers"] - 1]
+    w["proj_conv1"] = dict(w=n(emb, 1, 1, CL))
+    w["proj_bn"] = bn(emb)
+    w["proj_conv2"] = dict(w=n(emb, 3, 3, emb), b=n(emb))
+    return w
+
+
+def tinyvit_images(cfg, n, seed=0):
+    """Images normalised like the repo's preprocessing: U[0,1) -> 2p - 1."""
+    rng = np.random.default_rng(seed)
+    s = cfg["img_size"]
+    return (rng.random((n, 3, s, s), dtype=np.float32) * 2 - 1).astype(np.float32)
