@@ -64,13 +64,15 @@ int grid_1d(int64_t n, int block) {
 // image, or -1 for a padding token.
 struct WinMap {
   int H, W, ws, nwx, n_tok, per_img;  // per_img = windows * ws * ws
-  __device__ __forceinline__ int64_t src_row(int64_t t) const {
-    const int64_t b = t / per_img;
+  // t < 2^31 (the block forward checks its row count): 32-bit division
+  __device__ __forceinline__ int64_t src_row(int64_t t64) const {
+    const unsigned t = static_cast<unsigned>(t64);
+    const unsigned b = t / per_img;
     const int r = static_cast<int>(t - b * per_img);
     const int w = r / n_tok, k = r - w * n_tok;
     const int py = (w / nwx) * ws + k / ws, px = (w % nwx) * ws + k % ws;
     if (py >= H || px >= W) return -1;
-    return (b * H + py) * W + px;
+    return (static_cast<int64_t>(b) * H + py) * W + px;
   }
 };
 
@@ -153,14 +155,14 @@ int launch_ln_tvit(const float* x, void* y, int tout, const float* g, const floa
 // x[map.src_row(t)] += p[t] for the tokens inside the image (f32, C % 4 == 0).
 __global__ void unpartition_add(float* __restrict__ x, const float* __restrict__ p, int64_t rows, int C,
                                 WinMap map) {
-  const int c4 = C / 4;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const unsigned c4 = C / 4;
+  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;  // rows * C/4 < 2^31 (caller)
   if (i >= rows * c4) return;
-  const int64_t t = i / c4;
+  const unsigned t = i / c4;
   const int c = static_cast<int>(i - t * c4) * 4;
   const int64_t dst = map.src_row(t);
   if (dst < 0) return;
-  const float4 a = *reinterpret_cast<const float4*>(p + t * C + c);
+  const float4 a = *reinterpret_cast<const float4*>(p + static_cast<int64_t>(t) * C + c);
   float4* o = reinterpret_cast<float4*>(x + dst * C + c);
   float4 v = *o;
   v.x += a.x;
@@ -180,14 +182,16 @@ __device__ __forceinline__ float gelu_f(float v) {
 template <int TI, int TO, bool kGelu>
 __global__ void dwconv3x3(const void* __restrict__ x, void* __restrict__ y, const float* __restrict__ w9,
                           const float* __restrict__ bias, int B, int H, int W, int C, int stride, int OH, int OW) {
-  const int c4 = C / 4;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = static_cast<int64_t>(B) * OH * OW * c4;
+  // 32-bit index math (the launcher checks B*OH*OW*C/4 < 2^31): 64-bit
+  // division would dominate this memory-bound kernel
+  const unsigned c4 = C / 4;
+  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+  const unsigned total = static_cast<unsigned>(B) * OH * OW * c4;
   if (i >= total) return;
   const int c = static_cast<int>(i % c4) * 4;
-  const int64_t p = i / c4;  // output pixel
+  const unsigned p = i / c4;  // output pixel
   const int ox = static_cast<int>(p % OW), oy = static_cast<int>((p / OW) % OH);
-  const int64_t img = p / (static_cast<int64_t>(OH) * OW);
+  const int64_t img = p / (static_cast<unsigned>(OH) * OW);
   const int yy = oy * stride, xx = ox * stride;  // input centre
   float4 acc = __ldg(reinterpret_cast<const float4*>(bias + c));
 #pragma unroll
@@ -212,16 +216,17 @@ __global__ void dwconv3x3(const void* __restrict__ x, void* __restrict__ y, cons
     acc.z = gelu_f(acc.z);
     acc.w = gelu_f(acc.w);
   }
-  IO<TO>::st4(y, p * C + c, acc);
+  IO<TO>::st4(y, static_cast<int64_t>(p) * C + c, acc);
 }
 
 // 3x3 depthwise conv, zero padding 1, stride 1 or 2 (output (H-1)/s+1).
 int launch_dwconv3x3(const void* x, int tin, void* y, int tout, const float* w9, const float* bias, int B,
                      int H, int W, int C, bool gelu, cudaStream_t st, int stride = 1) {
   if (C % 4 || stride < 1) return kErrShape;
-  count_launches(1);
   const int OH = (H - 1) / stride + 1, OW = (W - 1) / stride + 1;
   const int64_t total = static_cast<int64_t>(B) * OH * OW * (C / 4);
+  if (total >= (1LL << 31)) return kErrShape;
+  count_launches(1);
   const int grid = grid_1d(total, 256);
 #define S3_DW(TI, TO)                                                                            \
   if (tin == TI && tout == TO) {                                                                 \
@@ -324,12 +329,12 @@ int ensure(DevBuf& d, size_t bytes) {
 template <int TI, int TO, bool kChw>
 __global__ void conv_im2col(const void* __restrict__ x, void* __restrict__ a, int64_t total, int H, int W, int C,
                             int k, int stride, int pad, int OH, int OW, int kpad) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;  // total < 2^31 (launcher)
   if (i >= total) return;
   const int col = static_cast<int>(i % kpad);
-  const int64_t row = i / kpad;
+  const unsigned row = i / kpad;
   const int ox = static_cast<int>(row % OW), oy = static_cast<int>((row / OW) % OH);
-  const int64_t b = row / (static_cast<int64_t>(OW) * OH);
+  const int64_t b = row / (static_cast<unsigned>(OW) * OH);
   float v = 0.f;
   if (col < k * k * C) {
     const int c = col % C, kx = (col / C) % k, ky = col / (C * k);
@@ -350,10 +355,41 @@ __global__ void conv_im2col(const void* __restrict__ x, void* __restrict__ a, in
     static_cast<__half*>(a)[i] = __float2half_rn(v);
 }
 
+// 16-bit NHWC input with C % 8 == 0: one thread copies 8 channels (16
+// bytes) of one tap; 32-bit index math (the launcher checks the count).
+__global__ void conv_im2col_v8(const uint4* __restrict__ x, uint4* __restrict__ a, unsigned total, int H, int W,
+                               int C8, int k, int stride, int pad, int OH, int OW, int kpad8, int kk8) {
+  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const unsigned col = i % kpad8;
+  const unsigned row = i / kpad8;
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (col < static_cast<unsigned>(kk8)) {
+    const int c8 = col % C8, tap = col / C8;
+    const int kx = tap % k, ky = tap / k;
+    const int ox = row % OW, oy = (row / OW) % OH;
+    const unsigned b = row / (static_cast<unsigned>(OW) * OH);
+    const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+    if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+      v = __ldg(x + ((static_cast<int64_t>(b) * H + iy) * W + ix) * C8 + c8);
+  }
+  a[i] = v;
+}
+
 int launch_conv_im2col(const void* x, int tin, bool chw, void* a, int tout, int B, int H, int W, int C, int k,
                        int stride, int pad, int kpad, cudaStream_t st) {
   const int OH = (H + 2 * pad - k) / stride + 1, OW = (W + 2 * pad - k) / stride + 1;
   const int64_t total = static_cast<int64_t>(B) * OH * OW * kpad;
+  if (!chw && tin == tout && tin != kF32 && C % 8 == 0 && kpad % 8 == 0) {
+    const int64_t t8 = total / 8;
+    if (t8 >= (1LL << 31)) return kErrShape;
+    count_launches(1);
+    conv_im2col_v8<<<grid_1d(t8, 256), 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<uint4*>(a),
+                                                     static_cast<unsigned>(t8), H, W, C / 8, k, stride, pad, OH,
+                                                     OW, kpad / 8, k * k * C / 8);
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+  }
+  if (total >= (1LL << 31)) return kErrShape;
   const int grid = grid_1d(total, 256);
   count_launches(1);
 #define S3_IC(TI, TO, CHW)                                                                               \
@@ -584,6 +620,7 @@ int sam3cu_tvit_block_forward(sam3cu_tvit_block* b, float* x, int n_images, int 
   if ((rc = launch_gemm(b->ao.p, C, b->proj_w.p, C, nullptr, nullptr, b->act, GemmShape{static_cast<int>(Tw), C, C},
                         e, st, 0)))
     return rc;
+  if (Tw * (C / 4) >= (1LL << 31)) return SAM3CU_EINVAL;
   count_launches(1);
   unpartition_add<<<grid_1d(Tw * (C / 4), 256), 256, 0, st>>>(x, b->pr.as<float>(), Tw, C, m);
   if ((rc = ck(cudaGetLastError()))) return kErrLaunch;
