@@ -170,9 +170,13 @@ struct AttnParams {
   int in_hstride;      // column distance between heads in the Q/K/V maps
   int seq;             // rows (tokens) per group
   int q_tiles;         // ceil(seq / 128)
+  int pack;            // > 1: this many whole groups share one 128-row tile
+                       // (block-diagonal attention, seq <= 64); q_tiles = 1
+  int n_groups;
   float scale;         // softmax scale (1/sqrt(head_dim))
   float scale_log2;    // scale * log2(e)
-  const float* bias;   // optional additive bias [heads, seq, bias_ld] f32
+  const float* bias;   // optional additive bias [heads, seq, bias_ld] f32, or with
+                       // pack > 1 the per-tile table [heads, pack*seq, bias_ld]
   int bias_ld;         // multiple of 4
 };
 
@@ -204,9 +208,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int seq = prm.seq;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int group = blockIdx.x / prm.q_tiles, qt = blockIdx.x % prm.q_tiles, head = blockIdx.y;
-  const int row0 = group * seq;  // first row of the group in the [rows, ld] matrices
-  const int n_kv = (seq + kKV - 1) / kKV;
+  const int head = blockIdx.y;
+  const bool packed = prm.pack > 1;
+  const int group = packed ? blockIdx.x * prm.pack : blockIdx.x / prm.q_tiles;
+  const int qt = packed ? 0 : blockIdx.x % prm.q_tiles;
+  const int row0 = group * seq;  // first row of the (first) group in the [rows, ld] matrices
+  // rows / keys of this CTA: one group, or up to `pack` consecutive groups
+  const int span = packed ? min(prm.pack, prm.n_groups - group) * seq : seq;
+  const int n_kv = (span + kKV - 1) / kKV;
   const int hx = head * prm.in_hstride;  // column of this head in the Q/K/V maps
 
   if ((smem_u32(smem) & 1023u) != 0) {  // the swizzled layouts need 1 KiB alignment
@@ -271,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     bool ok = mbar_wait_warp(q_full, 0, kErrTmaWait, abort_flag);
     const uint64_t qdesc = sdesc_k(smem_u32(sQ));
     auto keys_in = [&](int j) {  // keys of tile j, rounded up to a multiple of 16
-      const int left = seq - j * kKV;
+      const int left = span - j * kKV;
       return left >= kKV ? kKV : ((left + 15) & ~15);
     };
     // S_j = Q K_j^T into TMEM once K_j landed and the softmax read S_{j-1}
@@ -320,11 +329,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     // With a bias the scores are scaled (and biased) on load; the softmax
     // then works on them with the plain log2(e) factor.
     const float sl2 = kBias ? 1.4426950408889634f : prm.scale_log2;
+    // packed tiles: this row's group occupies keys [klo, klo + seq) of the
+    // tile; with a bias the table is per tile row (block-diagonal, -inf
+    // between groups), so it carries the mask itself
+    const int qrow_t = min(qt * kQ + r, span - 1);
+    const int klo = packed ? (qrow_t / seq) * seq : 0;
+    const int brows = packed ? prm.pack * seq : seq;  // rows of the bias table per head
+    const int kend = packed ? span : seq;             // keys that exist in this tile
     const float* brow = nullptr;
-    if constexpr (kBias) {
-      const int q = min(qt * kQ + r, seq - 1);
-      brow = prm.bias + (static_cast<int64_t>(head) * seq + q) * prm.bias_ld;
-    }
+    if constexpr (kBias) brow = prm.bias + (static_cast<int64_t>(head) * brows + qrow_t) * prm.bias_ld;
     // S columns [c0, c0+64) of key tile j -> sv (scaled and biased if kBias,
     // keys >= seq set to -inf)
     auto load_s = [&](float* sv, uint32_t* su, uint32_t c0, int kfirst) {
@@ -335,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if constexpr (kBias) {
 #pragma unroll
         for (int c = 0; c < kHalf; c += 4) {
-          if (kfirst + c < seq) {  // bias rows are padded to a multiple of 4
+          if (kfirst + c < kend) {  // bias rows are padded to a multiple of 4
             const float4 b = __ldg(reinterpret_cast<const float4*>(brow + kfirst + c));
             sv[c] = fmaf(sv[c], prm.scale, b.x);
             sv[c + 1] = fmaf(sv[c + 1], prm.scale, b.y);
@@ -343,18 +356,24 @@ __global__ void __launch_bounds__(kThreads, 2)
             sv[c + 3] = fmaf(sv[c + 3], prm.scale, b.w);
           }
         }
+      } else if (packed) {  // block-diagonal: keys of the row's own group only
+#pragma unroll
+        for (int c = 0; c < kHalf; ++c) {
+          const int k = kfirst + c - klo;
+          if (k < 0 || k >= seq) sv[c] = -INFINITY;
+        }
       }
-      if (kfirst + kHalf > seq) {  // ragged last tile: keys >= seq do not exist
+      if (kfirst + kHalf > kend) {  // ragged last tile: keys >= kend do not exist
 #pragma unroll
         for (int c = 0; c < kHalf; ++c)
-          if (kfirst + c >= seq) sv[c] = -INFINITY;
+          if (kfirst + c >= kend) sv[c] = -INFINITY;
       }
     };
     auto max_row = [](const float* v) { return kHalf == 64 ? max64(v) : fmaxf(max64(v), max64(v + 64)); };
     float m_used = -INFINITY, l = 0.f;
     // A warp whose 32 query rows all lie past the group end (the last query
     // tile of a 576-token window) only keeps the barrier protocol going.
-    const bool rows_live = qt * kQ + quarter * 32 < seq;
+    const bool rows_live = qt * kQ + quarter * 32 < span;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       if (!warp_wait(s_full, j & 1, kErrAccFull, abort_flag, lane)) { ok = false; break; }
@@ -362,14 +381,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int kb = j * kKV + scol;
       // keys of this half exist (the ragged last tile of a window has none
       // in its upper half; P.V then reads only the lower half of P)
-      const bool live = rows_live && kb < seq;
+      const bool live = rows_live && kb < span;
       uint32_t su[kHalf];  // S bits, loaded in place
       float* sv = reinterpret_cast<float*>(su);
       float mt = -INFINITY;
       if (kSplit == 2 && rows_live) {
         // maximum of the other key half first (its values are discarded)
         const int kbo = j * kKV + (scol ^ kHalf);
-        if (kbo < seq) {
+        if (kbo < span) {
           load_s(sv, su, scol ^ kHalf, kbo);
           mt = max_row(sv);
         }
@@ -449,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t u[16];
         tmem_ld_32x32b_x16(tO + lane_off + half * kOHalf + c0, u);
         tmem_ld_wait();
-        if (qrow < seq) {
+        if (qrow < span) {
 #pragma unroll
           for (int q4 = 0; q4 < 2; ++q4) {
             uint4 w;
@@ -523,11 +542,21 @@ int launch_attention_tc_ex(const AttnArgs& a, cudaStream_t st) {
   prm.in_hstride = in_hs;
   prm.seq = a.seq;
   prm.q_tiles = (a.seq + kQ - 1) / kQ;
+  prm.n_groups = a.n_groups;
   prm.scale = a.scale > 0.f ? a.scale : 1.0f / sqrtf(static_cast<float>(a.head_dim));
   prm.scale_log2 = prm.scale * 1.4426950408889634f;
   prm.bias = a.bias;
   prm.bias_ld = a.bias_ld;
-  dim3 grid(a.n_groups * prm.q_tiles, a.heads);
+  // short groups (TinyViT's 7x7 windows): several per 128-row tile, when
+  // there is no bias or the caller supplies the per-tile bias table
+  prm.pack = (a.seq <= kQ / 2 && (!a.bias || a.bias_tile)) ? kQ / a.seq : 1;
+  if (prm.pack > 1 && a.bias_tile) {
+    if (a.bias_tile_ld % 4 || a.bias_tile_ld < prm.pack * a.seq || (reinterpret_cast<uintptr_t>(a.bias_tile) & 15))
+      return kErrShape;
+    prm.bias = a.bias_tile;
+    prm.bias_ld = a.bias_tile_ld;
+  }
+  dim3 grid(prm.pack > 1 ? (a.n_groups + prm.pack - 1) / prm.pack : a.n_groups * prm.q_tiles, a.heads);
   count_launches(1);
   const bool bf = a.dtype == kBF16, b = a.bias != nullptr;
   if (a.head_dim == 64) {

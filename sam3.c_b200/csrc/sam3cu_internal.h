@@ -48,6 +48,11 @@ struct AttnArgs {
   const float* bias;
   int bias_ld;
   float scale;
+  // optional: for seq <= 64, the bias laid out per 128-row tile of
+  // floor(128/seq) groups, [heads, (128/seq)*seq, bias_tile_ld], -inf
+  // between different groups; lets short groups share a tile
+  const float* bias_tile;
+  int bias_tile_ld;
 };
 int launch_attention_tc_ex(const AttnArgs& a, cudaStream_t st);
 unsigned int dev_error_attn_tc();

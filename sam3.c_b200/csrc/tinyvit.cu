@@ -443,6 +443,8 @@ struct sam3cu_tvit_block {
   int C = 0, heads = 0, ws = 0, mlp = 0, act = kBF16;
   DevBuf ln1_w, ln1_b, qkv_w, qkv_b, proj_w, proj_b, bias;  // bias [heads, N, bias_ld]
   int bias_ld = 0;
+  DevBuf bias_tile;  // N <= 64: per 128-row tile of 128/N windows, block-diagonal
+  int bias_tile_ld = 0;
   DevBuf dw_w9, dw_b, ln2_w, ln2_b, fc1_w, fc1_b, fc2_w, fc2_b;
   DevBuf xn, qkv, ao, pr, lc, h;  // scratch
 };
@@ -576,6 +578,18 @@ sam3cu_tvit_block* sam3cu_tvit_block_create(int dim, int heads, int ws, int mlp_
     std::vector<float> dense(static_cast<size_t>(heads) * N * b->bias_ld);
     rc = sam3cu_tvit_expand_bias(w->attn_bias, heads, w->attn_bias_offsets, ws, dense.data(), b->bias_ld);
     if (!rc) rc = upload(b->bias, dense.data(), dense.size() * 4, st);
+    if (!rc && N <= 64) {  // several windows share one attention tile
+      const int G = 128 / N, R = G * N;
+      b->bias_tile_ld = (R + 3) / 4 * 4;
+      std::vector<float> tile(static_cast<size_t>(heads) * R * b->bias_tile_ld, -INFINITY);
+      for (int h = 0; h < heads; ++h)
+        for (int i = 0; i < R; ++i)
+          for (int j = 0; j < R; ++j)
+            if (i / N == j / N)
+              tile[(static_cast<size_t>(h) * R + i) * b->bias_tile_ld + j] =
+                  dense[(static_cast<size_t>(h) * N + i % N) * b->bias_ld + j % N];
+      rc = upload(b->bias_tile, tile.data(), tile.size() * 4, st);
+    }
   }
   if (!rc) rc = ck(cudaDeviceSynchronize());
   if (rc) {
@@ -612,10 +626,28 @@ int sam3cu_tvit_block_forward(sam3cu_tvit_block* b, float* x, int n_images, int 
   if ((rc = launch_gemm(b->xn.p, C, b->qkv_w.p, C, nullptr, nullptr, b->act, GemmShape{static_cast<int>(Tw), 3 * C, C},
                         e, st, 0)))
     return rc;
-  if ((rc = sam3cu_tvit_window_attention(b->qkv.p, 3 * C, b->ao.p, C, b->act == kF16 ? SAM3CU_F16 : SAM3CU_BF16,
-                                         static_cast<int>(Tw / N), N, b->heads, hd, b->bias.as<float>(),
-                                         b->bias_ld, stream)))
-    return rc;
+  {
+    AttnArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = b->qkv.p;
+    a.k = b->qkv.as<uint8_t>() + hd * es;
+    a.v = b->qkv.as<uint8_t>() + 2 * hd * es;
+    a.ldq = 3 * C;
+    a.in_hstride = 3 * hd;
+    a.o = b->ao.p;
+    a.ldo = C;
+    a.o_hstride = hd;
+    a.dtype = b->act;
+    a.n_groups = static_cast<int>(Tw / N);
+    a.seq = N;
+    a.heads = b->heads;
+    a.head_dim = hd;
+    a.bias = b->bias.as<float>();
+    a.bias_ld = b->bias_ld;
+    a.bias_tile = b->bias_tile.as<float>();
+    a.bias_tile_ld = b->bias_tile_ld;
+    if ((rc = launch_attention_tc_ex(a, st))) return rc;
+  }
   e = epi(b->pr.p, kOutF32, C, b->proj_b.as<float>());
   if ((rc = launch_gemm(b->ao.p, C, b->proj_w.p, C, nullptr, nullptr, b->act, GemmShape{static_cast<int>(Tw), C, C},
                         e, st, 0)))
