@@ -307,12 +307,42 @@ def run_ours(args):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if world == 1 and not args.no_tinyvit:
+            enc.close()
+            line["tinyvit_config5"] = tinyvit_leg(args, dev, sam3cu)
         print(json.dumps(line))
     enc.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def tinyvit_leg(args, dev, sam3cu):
+    """BASELINE config 5 (a parity case, reported beside the headline): the
+    TinyViT-21M backbone at 1008 px, batch 32, F16, random-init weights,
+    device-resident images, CUDA-event time of 5 encodes after 3 warm-ups."""
+    import torch
+    cfg = dict(synth.TINYVIT_21M)
+    B = 32
+    tv = sam3cu.TinyViT(cfg, synth.tinyvit_weights(cfg, seed=0), sam3cu.F16, max_batch=B)
+    imgs = torch.from_numpy(synth.tinyvit_images(cfg, B, seed=1)).to(dev)
+    out = torch.empty((B, tv.grid * tv.grid, cfg["embed_dim"]), dtype=torch.float32, device=dev)
+    for _ in range(3):
+        tv.encode_ptr(imgs.data_ptr(), B, out.data_ptr(), on_device=True)
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(5):
+        tv.encode_ptr(imgs.data_ptr(), B, out.data_ptr(), on_device=True)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / 5
+    tv.close()
+    assert sam3cu.device_error() == 0
+    return {"workload": "config5_tinyvit21m_1008px_batch32", "dtype": "f16", "value": B / (ms / 1000.0),
+            "unit": "images/s", "ms_per_batch": ms, "data": "synthetic (seeded images, random-init weights)"}
 
 
 def main():
@@ -326,6 +356,7 @@ def main():
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16", "q8"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-threads", type=int, default=0)
+    ap.add_argument("--no-tinyvit", action="store_true", help="skip the config-5 TinyViT leg")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
