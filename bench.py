@@ -282,7 +282,7 @@ def run_ours(args):
             "metric": "images_per_sec_1008px_hiera_l", "value": value, "unit": "images/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": {"bf16": "bf16", "f16": "f16", "q8": "q8_0w+bf16"}[args.dtype],
+            "dtype": {"bf16": "bf16", "f16": "f16", "q8": "q8_0w+f16"}[args.dtype],
             "data": "synthetic (seeded images and random-init weights of the Hiera-L ViT)",
             "config": {"workload": "config4_batched_encode_64x1008px_hiera_l",
                        "global_batch": n_total, "images_per_encode_call": B, "seq_len": 5184,

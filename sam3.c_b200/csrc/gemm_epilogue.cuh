@@ -39,6 +39,23 @@ __device__ __forceinline__ uint32_t pack_f16(float a, float b) {
 __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32], int row, int col0,
                                               int N) {
   const bool full = col0 + 32 <= N;
+  if (ep.col_scale) {
+    if (full) {
+      const float4* s4 = reinterpret_cast<const float4*>(ep.col_scale + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 c = __ldg(s4 + j);
+        v[4 * j] *= c.x;
+        v[4 * j + 1] *= c.y;
+        v[4 * j + 2] *= c.z;
+        v[4 * j + 3] *= c.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] *= __ldg(ep.col_scale + col0 + j);
+    }
+  }
   if (ep.bias) {
     if (full) {
       const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);

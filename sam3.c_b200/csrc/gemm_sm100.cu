@@ -89,6 +89,33 @@ __device__ __forceinline__ void q8_dequant_tile(const int8_t* q, const float* sc
   }
 }
 
+// Fast path for f16 operands: every value is made in half2 arithmetic.  Byte
+// u = q + 128 is permuted under the f16 exponent of 1024 (bits 0x64uu =
+// 1024 + u, exact), 1152 is subtracted (exact: q as f16), and the product
+// with the block scale is rounded once to f16.  The scales carry a
+// per-row power-of-two shift that keeps them in f16's normal range; the
+// GEMM epilogue divides it out (EpiParams::col_scale).
+template <int kT>
+__device__ __forceinline__ void q8_dequant_tile_h2(const int8_t* q, const float* sc, uint8_t* dst, int t) {
+  const int c = t & 7;
+  const __half2 k1152 = __float2half2_rn(1152.0f);
+#pragma unroll 4
+  for (int i = 0; i < kBN / (kT / 8); ++i) {
+    const int n = (t >> 3) + (kT / 8) * i;
+    const uint2 raw = *reinterpret_cast<const uint2*>(q + n * kBK + c * 8);
+    const __half2 s = __float2half2_rn(sc[(c >> 2) * kBN + n]);
+    const uint32_t u0 = raw.x ^ 0x80808080u, u1 = raw.y ^ 0x80808080u;
+    uint32_t h[4] = {__byte_perm(u0, 0x64646464u, 0x4140), __byte_perm(u0, 0x64646464u, 0x4342),
+                     __byte_perm(u1, 0x64646464u, 0x4140), __byte_perm(u1, 0x64646464u, 0x4342)};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __half2 v = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&h[k]), k1152), s);
+      h[k] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    *reinterpret_cast<uint4*>(dst + n * 128 + ((c ^ (n & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+  }
+}
+
 template <int kBMode>
 __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -311,6 +338,8 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
           const float* sc = reinterpret_cast<const float*>(stage_sc(s));
           if (b_is_bf16)
             q8_dequant_tile<true, Cfg::kConvThreads>(q, sc, ring_b(it), t);
+          else if (ep.col_scale)  // shifted scales: half2 arithmetic
+            q8_dequant_tile_h2<Cfg::kConvThreads>(q, sc, ring_b(it), t);
           else
             q8_dequant_tile<false, Cfg::kConvThreads>(q, sc, ring_b(it), t);
           fence_proxy_async_smem();  // make generic-proxy writes visible to tcgen05

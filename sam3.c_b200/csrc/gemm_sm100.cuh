@@ -56,6 +56,8 @@ struct EpiParams {
   void* out;             // [M, ldo] (row index possibly remapped)
   int out_type;          // OutType
   int ldo;
+  const float* col_scale;  // [N] or null: multiplies the accumulator first
+                           // (undoes the per-row scale shift of fast Q8 W)
   const float* bias;     // [N] or null
   int act;               // 0 none, 1 tanh-GELU (cpu_gelu.c:23-36)
   const float* residual; // [M, ldr] fp32 added last, may alias out

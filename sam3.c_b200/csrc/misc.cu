@@ -278,6 +278,35 @@ int launch_gather_rows(const void* src, void* dst, int rows, int row_bytes, cons
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
+namespace {
+
+// Per output row n: the largest block scale m_n; scales of the row are
+// multiplied by 2^e_n (exact) with e_n chosen so m_n * 2^e_n lies in
+// [0.5, 1), and col_scale[n] = 2^-e_n undoes it after the GEMM.
+__global__ void q8_row_shift_kernel(float* __restrict__ sc, float* __restrict__ col_scale, int N, int kb) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float m = 0.f;
+  for (int j = 0; j < kb; ++j) m = fmaxf(m, fabsf(sc[static_cast<int64_t>(j) * N + n]));
+  int e = 0;
+  if (m > 0.f) {
+    frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1)
+    e = -e;
+  }
+  const float up = ldexpf(1.0f, e);
+  for (int j = 0; j < kb; ++j) sc[static_cast<int64_t>(j) * N + n] *= up;
+  col_scale[n] = ldexpf(1.0f, -e);
+}
+
+}  // namespace
+
+int launch_q8_row_shift(float* sc, float* col_scale, int N, int K, cudaStream_t st) {
+  if (N <= 0 || K % 32) return kErrShape;
+  count_launches(1);
+  q8_row_shift_kernel<<<(N + 255) / 256, 256, 0, st>>>(sc, col_scale, N, K / 32);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
 int launch_q8_repack(const void* blocks, int8_t* q, float* sc, int N, int K, cudaStream_t st) {
   count_launches(1);
   if (K % 32) return kErrShape;

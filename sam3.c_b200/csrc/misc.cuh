@@ -14,6 +14,7 @@ int launch_patch_im2col(const float* img, void* a, int tout, int n_img, int img_
 int launch_gather_rows(const void* src, void* dst, int rows, int row_bytes, const int* map, int period,
                        cudaStream_t st);
 int launch_q8_repack(const void* blocks, int8_t* q, float* sc, int N, int K, cudaStream_t st);
+int launch_q8_row_shift(float* sc, float* col_scale, int N, int K, cudaStream_t st);
 int launch_cast(const void* x, int tin, void* y, int tout, int64_t n, cudaStream_t st);
 
 }  // namespace s3

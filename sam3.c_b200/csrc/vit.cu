@@ -48,7 +48,8 @@ bool is_global_block(int i) { return i == 7 || i == 15 || i == 23 || i == 31; }
 struct Linear {
   DevBuf w;      // 16-bit [N, K] (or unused for Q8)
   DevBuf q;      // int8 [N, K]
-  DevBuf sc;     // f32 [K/32, N]
+  DevBuf sc;     // f32 [K/32, N] (row-shifted for f16 activations, see cs)
+  DevBuf cs;     // f32 [N]: 2^-shift of each output row, applied in the epilogue
   DevBuf bias;   // f32 [N]
   int N = 0, K = 0;
 };
@@ -140,6 +141,10 @@ int upload_linear(Linear& L, const float* w, const float* b, int N, int K, int w
     if ((rc = launch_q8_quantize(tmp.as<float>(), blocks.p, n, st))) return rc;
     if (!L.q.alloc(n) || !L.sc.alloc((n / 32) * 4)) return kErrNoMem;
     if ((rc = launch_q8_repack(blocks.p, L.q.as<int8_t>(), L.sc.as<float>(), N, K, st))) return rc;
+    // f16 activations: scales shifted per row into f16's normal range for the
+    // half2 dequantiser, the shift undone in the GEMM epilogue
+    if (!L.cs.alloc(static_cast<size_t>(N) * 4)) return kErrNoMem;
+    if ((rc = launch_q8_row_shift(L.sc.as<float>(), L.cs.as<float>(), N, K, st))) return rc;
     return ck(cudaStreamSynchronize(st));
   }
   return upload_w16(L.w, w, N, K, K, wdtype == SAM3CU_F16 ? kF16 : kBF16, st);
@@ -151,10 +156,14 @@ EpiParams epi_default() {
   return e;
 }
 
-int run_linear(sam3cu_vit* v, const Linear& L, const void* a, int lda, int M, const EpiParams& ep) {
+int run_linear(sam3cu_vit* v, const Linear& L, const void* a, int lda, int M, const EpiParams& ep_in) {
   GemmShape shp{M, L.N, L.K};
-  if (L.q.p)
+  if (L.q.p) {
+    EpiParams ep = ep_in;
+    ep.col_scale = L.cs.as<float>();  // null unless the scales were row-shifted
     return launch_gemm(a, lda, nullptr, 0, L.q.as<int8_t>(), L.sc.as<float>(), v->act, shp, ep, v->stream, 0);
+  }
+  const EpiParams& ep = ep_in;
   return launch_gemm(a, lda, L.w.p, L.K, nullptr, nullptr, v->act, shp, ep, v->stream, 0);
 }
 
@@ -414,7 +423,9 @@ sam3cu_vit* sam3cu_vit_create(const sam3cu_vit_config* cfg, const sam3cu_vit_wei
   std::unique_ptr<sam3cu_vit> v(new sam3cu_vit());
   v->c = *cfg;
   v->wdtype = weight_dtype;
-  v->act = weight_dtype == SAM3CU_F16 ? kF16 : kBF16;
+  // Q8_0 weights pair with f16 activations: the int8 tiles are dequantised in
+  // half2 arithmetic (gemm_sm100.cu), and f16 keeps 3 more mantissa bits
+  v->act = (weight_dtype == SAM3CU_F16 || weight_dtype == SAM3CU_Q8_0) ? kF16 : kBF16;
   v->max_batch = max_batch;
   if (cudaStreamCreateWithFlags(&v->stream, cudaStreamNonBlocking) != cudaSuccess) {
     *status_p = kErrCuda;
