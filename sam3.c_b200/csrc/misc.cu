@@ -300,6 +300,62 @@ __global__ void q8_row_shift_kernel(float* __restrict__ sc, float* __restrict__ 
 
 }  // namespace
 
+namespace {
+
+// W16 [N, K] = int8 q [N, K] x scale of its 32-block (sc [K/32, N]); one
+// thread per 16 values (one 16-byte load, two 16-byte stores).  f16: half2
+// arithmetic ((1024 + u) as f16 bits 0x64uu, minus 1152 exactly, times the
+// scale rounded once); bf16: f32 arithmetic, one rounding.
+__global__ void q8_dequant_w16_kernel(const uint4* __restrict__ q, const float* __restrict__ sc,
+                                      uint4* __restrict__ w, int N, int K16, int64_t total, int f16) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int n = static_cast<int>(i / K16), k16 = static_cast<int>(i - static_cast<int64_t>(n) * K16);
+  const float s = __ldg(sc + static_cast<int64_t>(k16 >> 1) * N + n);
+  const uint4 raw = __ldg(q + i);
+  const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t out[8];
+  if (f16) {
+    const __half2 k1152 = __float2half2_rn(1152.0f), s2 = __float2half2_rn(s);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t u = words[j] ^ 0x80808080u;
+      uint32_t h[2] = {__byte_perm(u, 0x64646464u, 0x4140), __byte_perm(u, 0x64646464u, 0x4342)};
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        __half2 v = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&h[k]), k1152), s2);
+        out[2 * j + k] = *reinterpret_cast<uint32_t*>(&v);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t u = words[j] ^ 0x80808080u;
+      float f[4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        f[b] = (__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650 + b)) - 8388736.0f) * s;
+      __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]), c = __floats2bfloat162_rn(f[2], f[3]);
+      out[2 * j] = *reinterpret_cast<uint32_t*>(&a);
+      out[2 * j + 1] = *reinterpret_cast<uint32_t*>(&c);
+    }
+  }
+  w[2 * i] = make_uint4(out[0], out[1], out[2], out[3]);
+  w[2 * i + 1] = make_uint4(out[4], out[5], out[6], out[7]);
+}
+
+}  // namespace
+
+int launch_q8_dequant_w16(const int8_t* q, const float* sc, void* w, int N, int K, int f16, cudaStream_t st) {
+  if (N <= 0 || K % 32 || (reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(w) & 15))
+    return kErrShape;
+  const int64_t total = static_cast<int64_t>(N) * (K / 16);
+  count_launches(1);
+  q8_dequant_w16_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<const uint4*>(q), sc, static_cast<uint4*>(w), N, K / 16, total, f16);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
 int launch_q8_row_shift(float* sc, float* col_scale, int N, int K, cudaStream_t st) {
   if (N <= 0 || K % 32) return kErrShape;
   count_launches(1);

@@ -26,6 +26,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -77,6 +78,7 @@ struct sam3cu_vit {
   s3::DevBuf raster_to_win;                      // int [np]
   // activations
   s3::DevBuf x, xn, qkv, ao, h;
+  s3::DevBuf wq;  // Q8_0 weights: 16-bit dequantised W of the current linear
   // image / feature staging for host-buffer encodes: two sets, so that one
   // chunk's copies overlap the next chunk's compute (img2/out2 on demand)
   s3::DevBuf img, out, img2, out2;
@@ -156,12 +158,19 @@ EpiParams epi_default() {
   return e;
 }
 
+// Q8_0 weights are dequantised once per call into v->wq (16-bit [N, K],
+// at most 9.7 MB, so it stays in L2) and the 16-bit GEMM runs on that: a
+// dequantiser inside the GEMM would redo the conversion for every one of
+// the M/256 row tiles.  The HBM copy of W stays int8.
 int run_linear(sam3cu_vit* v, const Linear& L, const void* a, int lda, int M, const EpiParams& ep_in) {
   GemmShape shp{M, L.N, L.K};
   if (L.q.p) {
+    int rc = launch_q8_dequant_w16(L.q.as<int8_t>(), L.sc.as<float>(), v->wq.p, L.N, L.K, v->act == kF16 ? 1 : 0,
+                                   v->stream);
+    if (rc) return rc;
     EpiParams ep = ep_in;
-    ep.col_scale = L.cs.as<float>();  // null unless the scales were row-shifted
-    return launch_gemm(a, lda, nullptr, 0, L.q.as<int8_t>(), L.sc.as<float>(), v->act, shp, ep, v->stream, 0);
+    ep.col_scale = L.cs.as<float>();  // undoes the per-row scale shift
+    return launch_gemm(a, lda, v->wq.p, L.K, nullptr, nullptr, v->act, shp, ep, v->stream, 0);
   }
   const EpiParams& ep = ep_in;
   return launch_gemm(a, lda, L.w.p, L.K, nullptr, nullptr, v->act, shp, ep, v->stream, 0);
@@ -395,6 +404,10 @@ int vit_setup(sam3cu_vit* v, const sam3cu_vit_weights* w) {
       !v->img.alloc(static_cast<size_t>(v->max_batch) * 3 * c.img_size * c.img_size * 4) ||
       !v->out.alloc(M * e * 4))
     return kErrNoMem;
+  if (v->wdtype == SAM3CU_Q8_0) {  // largest linear: fc1 / fc2 (or QKV)
+    const size_t wmax = std::max(static_cast<size_t>(c.mlp_dim), static_cast<size_t>(3 * e)) * e * 2;
+    if (!v->wq.alloc(wmax)) return kErrNoMem;
+  }
   return ck(cudaStreamSynchronize(st));
 }
 
@@ -485,7 +498,8 @@ int sam3cu_vit_profile(sam3cu_vit* v, const float* images, int n, float* out, do
 int sam3cu_vit_launches_per_encode(sam3cu_vit* v, int n) {
   (void)n;
   if (!v) return 0;
-  return 3 + 7 * v->c.depth + (v->c.depth == 0 ? 1 : 0);
+  // Q8_0: one dequantisation launch before each of the 4 linears of a block
+  return 3 + (v->wdtype == SAM3CU_Q8_0 ? 11 : 7) * v->c.depth + (v->c.depth == 0 ? 1 : 0);
 }
 
 // Enqueue through a CUDA graph captured once per (batch size, in, out)
