@@ -310,12 +310,68 @@ def run_ours(args):
         if world == 1 and not args.no_tinyvit:
             enc.close()
             line["tinyvit_config5"] = tinyvit_leg(args, dev, sam3cu)
+            line.update(q8_legs(args, dev, sam3cu))
         print(json.dumps(line))
     enc.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def _event_ms(fn, iters, stream=None):
+    """Mean ms per call of fn, CUDA events on `stream` (the stream fn's
+    kernels run on; torch's current stream by default)."""
+    import torch
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(stream)
+    for _ in range(iters):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def q8_legs(args, dev, sam3cu):
+    """BASELINE configs 0 and 2 (parity cases, reported beside the headline):
+    the single Q8_0 linear [5184 x 1024] . [4736 x 1024]^T + bias through
+    sam3cu_linear_q8 (bf16 activations, f32 out), and the full 1008px ViT
+    encode of one image with Q8_0 weights (F16 activations).  Device-
+    resident inputs; CUDA-event times after warm-up."""
+    import torch
+    rng = np.random.default_rng(1)
+    M, K, N = 5184, 1024, 4736
+    x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).to(dev).bfloat16()
+    w = torch.from_numpy((rng.standard_normal((N, K)) * 0.02).astype(np.float32)).to(dev)
+    b = torch.from_numpy((rng.standard_normal(N) * 0.01).astype(np.float32)).to(dev)
+    q, sc = sam3cu.q8_repack(sam3cu.q8_quantize(w), N, K)
+    y = torch.empty((M, N), dtype=torch.float32, device=dev)
+    f = lambda: sam3cu.linear_q8(x, q, sc, bias=b, out=y)
+    for _ in range(3):
+        f()
+    torch.cuda.synchronize()
+    ms_lin = _event_ms(f, 20)
+    enc = sam3cu.VitEncoder(CFG, synth.vit_weights(CFG, seed=0), sam3cu.Q8_0, max_batch=1)
+    img = torch.from_numpy(synth.images(CFG, 1, seed=100)).to(dev)
+    out = torch.empty((1, enc.np, CFG["embed_dim"]), dtype=torch.float32, device=dev)
+    g = lambda: enc.encode_async(img, out)
+    for _ in range(3):
+        g()
+    torch.cuda.synchronize()
+    ms_enc = _event_ms(g, 10, torch.cuda.ExternalStream(enc.stream, device=dev))
+    prof = enc.profile(img, out)
+    enc.close()
+    assert sam3cu.device_error() == 0
+    return {
+        "q8_linear_config0": {"tflops": 2 * M * K * N / ms_lin / 1e9, "ms": ms_lin,
+                              "dtype": "q8_0w+bf16a, f32 out",
+                              "note": "dequantise-once path (M >= 2048) of sam3cu_linear_q8"},
+        "q8_encode_config2": {"value": 1000.0 / ms_enc, "unit": "images/s", "ms_per_image": ms_enc,
+                              "gemm_tflops": gemm_gflop_per_image() / prof["gemm"][0],
+                              "dtype": "q8_0w+f16a", "batch": 1},
+    }
 
 
 def tinyvit_leg(args, dev, sam3cu):

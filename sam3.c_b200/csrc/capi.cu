@@ -32,7 +32,21 @@ int linear_common(const void* x, int x_dtype, const void* w, const int8_t* q, co
   ep.residual = residual;
   ep.ldr = N;
   GemmShape shp{M, N, K};
-  return launch_gemm(x, K, w, K, q, sc, x_dtype, shp, ep, as_stream(stream), 0);
+  cudaStream_t st = as_stream(stream);
+  // Large M with Q8 weights: dequantise W once into a stream-ordered 16-bit
+  // buffer and run the 16-bit GEMM on it (an in-GEMM dequantiser converts W
+  // again for every row tile); small M keeps the in-GEMM path.
+  if (q && M >= 2048 && K % 32 == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {
+    void* w16 = nullptr;
+    if (cudaMallocAsync(&w16, static_cast<size_t>(N) * K * 2, st) == cudaSuccess) {
+      int rc = launch_q8_dequant_w16(q, sc, w16, N, K, x_dtype == SAM3CU_F16 ? 2 : 0, st);
+      if (!rc) rc = launch_gemm(x, K, w16, K, nullptr, nullptr, x_dtype, shp, ep, st, 0);
+      cudaFreeAsync(w16, st);
+      return rc;
+    }
+    cudaGetLastError();  // no pool memory: fall through to the in-GEMM dequantiser
+  }
+  return launch_gemm(x, K, w, K, q, sc, x_dtype, shp, ep, st, 0);
 }
 
 }  // namespace

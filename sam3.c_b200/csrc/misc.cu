@@ -303,9 +303,11 @@ __global__ void q8_row_shift_kernel(float* __restrict__ sc, float* __restrict__ 
 namespace {
 
 // W16 [N, K] = int8 q [N, K] x scale of its 32-block (sc [K/32, N]); one
-// thread per 16 values (one 16-byte load, two 16-byte stores).  f16: half2
-// arithmetic ((1024 + u) as f16 bits 0x64uu, minus 1152 exactly, times the
-// scale rounded once); bf16: f32 arithmetic, one rounding.
+// thread per 16 values (one 16-byte load, two 16-byte stores).  mode 1
+// (f16, scales row-shifted into f16's normal range): half2 arithmetic
+// ((1024 + u) as f16 bits 0x64uu, minus 1152 exactly, times the scale
+// rounded once); mode 0 (bf16) and 2 (f16, any scales): f32 arithmetic and
+// one rounding.
 __global__ void q8_dequant_w16_kernel(const uint4* __restrict__ q, const float* __restrict__ sc,
                                       uint4* __restrict__ w, int N, int K16, int64_t total, int f16) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -315,7 +317,7 @@ __global__ void q8_dequant_w16_kernel(const uint4* __restrict__ q, const float* 
   const uint4 raw = __ldg(q + i);
   const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
   uint32_t out[8];
-  if (f16) {
+  if (f16 == 1) {
     const __half2 k1152 = __float2half2_rn(1152.0f), s2 = __float2half2_rn(s);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -335,9 +337,15 @@ __global__ void q8_dequant_w16_kernel(const uint4* __restrict__ q, const float* 
 #pragma unroll
       for (int b = 0; b < 4; ++b)
         f[b] = (__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650 + b)) - 8388736.0f) * s;
-      __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]), c = __floats2bfloat162_rn(f[2], f[3]);
-      out[2 * j] = *reinterpret_cast<uint32_t*>(&a);
-      out[2 * j + 1] = *reinterpret_cast<uint32_t*>(&c);
+      if (f16) {
+        __half2 a = __floats2half2_rn(f[0], f[1]), c = __floats2half2_rn(f[2], f[3]);
+        out[2 * j] = *reinterpret_cast<uint32_t*>(&a);
+        out[2 * j + 1] = *reinterpret_cast<uint32_t*>(&c);
+      } else {
+        __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]), c = __floats2bfloat162_rn(f[2], f[3]);
+        out[2 * j] = *reinterpret_cast<uint32_t*>(&a);
+        out[2 * j + 1] = *reinterpret_cast<uint32_t*>(&c);
+      }
     }
   }
   w[2 * i] = make_uint4(out[0], out[1], out[2], out[3]);

@@ -15,8 +15,9 @@ int launch_gather_rows(const void* src, void* dst, int rows, int row_bytes, cons
                        cudaStream_t st);
 int launch_q8_repack(const void* blocks, int8_t* q, float* sc, int N, int K, cudaStream_t st);
 int launch_q8_row_shift(float* sc, float* col_scale, int N, int K, cudaStream_t st);
-// 16-bit W [N, K] from int8 q [N, K] and scales [K/32, N] (f16 or bf16)
-int launch_q8_dequant_w16(const int8_t* q, const float* sc, void* w, int N, int K, int f16, cudaStream_t st);
+// 16-bit W [N, K] from int8 q [N, K] and scales [K/32, N].  mode: 0 bf16,
+// 1 f16 from row-shifted scales (half2 arithmetic), 2 f16 from any scales
+int launch_q8_dequant_w16(const int8_t* q, const float* sc, void* w, int N, int K, int mode, cudaStream_t st);
 int launch_cast(const void* x, int tin, void* y, int tout, int64_t n, cudaStream_t st);
 
 }  // namespace s3
