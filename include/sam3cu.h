@@ -320,6 +320,31 @@ SAM3CU_API int sam3cu_sdpa_f32(const float *q, const float *k, const float *v,
 			       const float *mask, float *o, int bh, int sq, int sk, int hd,
 			       void *stream);
 
+/* Elementwise a * b with b broadcast over a trailing suffix of a's dims
+ * (n % nb == 0): SAM3_OP_MUL (cpu_elementwise.c). */
+SAM3CU_API int sam3cu_mul(const void *a, const void *b, void *out, int dtype, int64_t n,
+			  int64_t nb, void *stream);
+/* Softmax over the last dim: SAM3_OP_SOFTMAX (cpu_softmax.c:29-47). */
+SAM3CU_API int sam3cu_softmax(const void *x, void *y, int dtype, int64_t rows, int cols,
+			      void *stream);
+/* Batched C[b] = A[b][M,K] . B[b][K,N], f32 accumulation: the N-D MATMUL
+ * TinyViT's window attention emits (image_encoder_tinyvit.c:836-854). */
+SAM3CU_API int sam3cu_bmm(const void *a, const void *b, void *c, int dtype, int batch, int M,
+			  int K, int N, void *stream);
+/* Eval BatchNorm over the last dim: SAM3_OP_BATCHNORM (cpu_batchnorm.c);
+ * gamma / beta may be NULL. */
+SAM3CU_API int sam3cu_batchnorm(const void *x, void *y, int dtype, int64_t n, int C,
+				const float *gamma, const float *beta, const float *mean,
+				const float *var, void *stream);
+/* Grouped NHWC conv with OHWI weights [OC,KH,KW,C/groups] (cpu_conv2d.c,
+ * groups > 1: the depthwise convs of TinyViT). */
+SAM3CU_API int sam3cu_conv2d_grouped_nhwc(const void *x, const void *w, void *y, int dtype,
+		int n, int H, int W, int C, int OC, int KH, int KW, int stride, int pad,
+		int groups, void *stream);
+/* Device-to-device 2-D copy (rows of width bytes), for CONCAT. */
+SAM3CU_API int sam3cu_memcpy2d_d2d(void *dst, size_t dpitch, const void *src, size_t spitch,
+				   size_t width, size_t rows, void *stream);
+
 /* NHWC im2col for CONV2D with OHWI weights (cpu_conv2d.c): rows (n,oy,ox),
  * columns (ky,kx,c) zero-padded to kpad. */
 SAM3CU_API int sam3cu_im2col_nhwc(const void *x, void *a, int dtype, int n, int H, int W,

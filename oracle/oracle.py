@@ -561,3 +561,23 @@ def tinyvit_forward(cfg_struct, weights_struct, image: np.ndarray) -> np.ndarray
     got = orc().orc_tinyvit_forward(C.byref(cfg_struct), C.byref(weights_struct), _p(image), _p(out))
     assert got == g
     return out
+
+
+def ref_tinyvit_encode(cfg_struct, weights_struct, image: np.ndarray, ops=None, be_size=0, be_type=2):
+    """The reference's own sam3_tinyvit_build (image_encoder_tinyvit.c,
+    compiled from source into oracle/_ref) evaluated by a backend: `ops`
+    None is the reference CPU backend (which lacks the batched MATMUL the
+    graph needs), else a struct sam3_backend_ops address such as the CUDA
+    backend's.  Weight structs as for tinyvit_forward."""
+    image = np.ascontiguousarray(image, np.float32)
+    S = cfg_struct.img_size
+    g = (S - 1) // 2 + 1
+    g = (g - 1) // 2 + 1
+    for _ in range(cfg_struct.n_layers - 1):
+        g = (g - 1) // 2 + 1
+    out = np.empty((g * g, cfg_struct.embed_dim), np.float32)
+    rc = ref().ref_tinyvit_encode(C.byref(cfg_struct), C.byref(weights_struct), _p(image), _p(out),
+                                  C.c_void_p(ops), C.c_size_t(be_size), C.c_int(be_type))
+    if rc != 0:
+        raise RuntimeError(f"ref_tinyvit_encode failed rc={rc}")
+    return out

@@ -231,7 +231,7 @@ static void put(struct sam3_tensor *t, const float *src)
 /* Full sam3_vit_build (image_encoder.c:513-963) on the reference CPU
  * backend.  image: planar CHW [3,img,img] F32, already normalised.
  * out: [np, e] F32.  Returns 0 on success. */
-static struct sam3_backend *make_backend(const struct sam3_backend_ops *ops,
+struct sam3_backend *ref_make_backend(const struct sam3_backend_ops *ops,
 					 size_t be_size, int be_type)
 {
 	if (!ops)
@@ -298,7 +298,7 @@ static int vit_encode_impl(int img_size, int patch_size, int embed_dim,
 	    sam3_arena_init(&scratch, sbytes) ||
 	    sam3_arena_init(&persist, 8ul * np * embed_dim + (16ul << 20)))
 		return -2;
-	struct sam3_backend *be = make_backend(ops, be_size, be_type);
+	struct sam3_backend *be = ref_make_backend(ops, be_size, be_type);
 	if (!be)
 		goto done;
 	sam3_vit_init(vit, img_size, patch_size, embed_dim, depth, n_heads,
@@ -371,7 +371,7 @@ int ref_linear_graph(int dt, const void *x, const void *wt, const void *b,
 	if (sam3_arena_init(&a, 64ul << 20))
 		return -2;
 	struct sam3_graph *g = calloc(1, sizeof(*g));
-	struct sam3_backend *be = make_backend(ops, be_size, be_type);
+	struct sam3_backend *be = ref_make_backend(ops, be_size, be_type);
 	int rc = -1;
 	if (!g || !be)
 		goto out;
@@ -423,7 +423,7 @@ int ref_node_graph(int op, int n_in, const struct ref_tdesc *ins,
 	if (sam3_arena_init(&a, 512ul << 20))
 		return -2;
 	struct sam3_graph *g = calloc(1, sizeof(*g));
-	struct sam3_backend *be = make_backend(ops, be_size, be_type);
+	struct sam3_backend *be = ref_make_backend(ops, be_size, be_type);
 	int rc = -1;
 	if (!g || !be)
 		goto out;

@@ -399,6 +399,27 @@ static enum sam3_error f32_view(struct impl *m, const struct sam3_tensor *t,
 
 /* ------------------------------------------------------------------ ops */
 
+/* y broadcasts over x as the reference's check_broadcast allows for these
+ * kernels (cpu_elementwise.c:28-62): same size, a scalar, or y's dims equal
+ * x's trailing dims (leading size-1 dims of y ignored). */
+static int suffix_broadcast(const struct sam3_tensor *x, const struct sam3_tensor *y)
+{
+	int64_t n = nelems(x), nb = nelems(y);
+	if (nb == n || nb == 1)
+		return 1;
+	if (nb == 0 || n % nb)
+		return 0;
+	int yd = y->n_dims;
+	while (yd > 0 && y->dims[y->n_dims - yd] == 1)
+		yd--;  /* skip leading 1s */
+	if (yd > x->n_dims)
+		return 0;
+	for (int d = 0; d < yd; d++)
+		if (y->dims[y->n_dims - 1 - d] != x->dims[x->n_dims - 1 - d])
+			return 0;
+	return 1;
+}
+
 static int produced_in(struct sam3_graph *g, int upto, const struct sam3_tensor *t)
 {
 	for (int i = 0; i < upto; i++)
@@ -421,6 +442,26 @@ static enum sam3_error op_matmul(struct impl *m, struct sam3_graph *g, int ni)
 			w = g->nodes[j].inputs[0];
 			lazy = 1;
 		}
+	if (!lazy && a->n_dims >= 3 && b->n_dims == a->n_dims) {
+		/* batched N-D MATMUL (TinyViT window attention, :836-854): the
+		 * leading dims of A and B must agree */
+		int nd_ = a->n_dims;
+		int64_t batch = 1;
+		for (int d = 0; d < nd_ - 2; d++) {
+			if (a->dims[d] != b->dims[d])
+				return SAM3_EINVAL;
+			batch *= a->dims[d];
+		}
+		int M = a->dims[nd_ - 2], K = a->dims[nd_ - 1], N = b->dims[nd_ - 1];
+		if (b->dims[nd_ - 2] != K || a->dtype != b->dtype || batch > 65535)
+			return SAM3_EINVAL;
+		void *pa, *pb, *py;
+		TRY(dev_of(m, a, produced_in(g, ni, a), &pa));
+		TRY(dev_of(m, b, produced_in(g, ni, b), &pb));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_bmm(pa, pb, py, a->dtype, (int)batch, M, K, N, m->stream));
+		return SAM3_OK;
+	}
 	if (!lazy && b->n_dims != 2)
 		return SAM3_EINVAL;
 	int K = a->dims[a->n_dims - 1];
@@ -572,6 +613,8 @@ static enum sam3_error op_node(struct impl *m, struct sam3_graph *g, int ni)
 		return SAM3_OK;
 	}
 
+	case SAM3_OP_BIAS_ADD:  /* NHWC x + bias[C] (cpu_bias_add.c) */
+	case SAM3_OP_MUL:
 	case SAM3_OP_ADD: {
 		struct sam3_tensor *y = nd->inputs[1];
 		void *pyy;
@@ -579,13 +622,67 @@ static enum sam3_error op_node(struct impl *m, struct sam3_graph *g, int ni)
 		    (x->dtype != SAM3_DTYPE_F32 && !is_16(x->dtype)))
 			return SAM3_EDTYPE;
 		int64_t n = nelems(x), nb = nelems(y);
-		if (!(nb == n || nb == 1 || nb == x->dims[x->n_dims - 1]))
+		if (!suffix_broadcast(x, y))
 			return SAM3_EINVAL;
 		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
 		TRY(dev_of(m, y, produced_in(g, ni, y), &pyy));
 		TRY(out_buf(m, out, &py));
-		TRY(sam3cu_add(px, pyy, py, x->dtype, n, nb, m->stream));
+		if (nd->op == SAM3_OP_MUL)
+			TRY(sam3cu_mul(px, pyy, py, x->dtype, n, nb, m->stream));
+		else
+			TRY(sam3cu_add(px, pyy, py, x->dtype, n, nb, m->stream));
 		return SAM3_OK;
+	}
+
+	case SAM3_OP_SOFTMAX: {  /* last dim (cpu_softmax.c:29-47) */
+		if (x->dtype != SAM3_DTYPE_F32 && !is_16(x->dtype))
+			return SAM3_EDTYPE;
+		int cols = x->dims[x->n_dims - 1];
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_softmax(px, py, x->dtype, nelems(x) / cols, cols, m->stream));
+		return SAM3_OK;
+	}
+
+	case SAM3_OP_BATCHNORM: {  /* NHWC, inputs x, gamma, beta, mean, var */
+		const float *gm = NULL, *bt = NULL, *mu = NULL, *vr = NULL;
+		int C = x->dims[x->n_dims - 1];
+		if (nd->n_inputs < 5 || !nd->inputs[3] || !nd->inputs[4])
+			return SAM3_EINVAL;
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		if (nd->inputs[1])
+			TRY(f32_view(m, nd->inputs[1], produced_in(g, ni, nd->inputs[1]), &gm));
+		if (nd->inputs[2])
+			TRY(f32_view(m, nd->inputs[2], produced_in(g, ni, nd->inputs[2]), &bt));
+		TRY(f32_view(m, nd->inputs[3], produced_in(g, ni, nd->inputs[3]), &mu));
+		TRY(f32_view(m, nd->inputs[4], produced_in(g, ni, nd->inputs[4]), &vr));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_batchnorm(px, py, x->dtype, nelems(x), C, gm, bt, mu, vr, m->stream));
+		return SAM3_OK;
+	}
+
+	case SAM3_OP_CONCAT: {  /* along params[0] (cpu_concat.c) */
+		int axis = nd->params[0];
+		size_t es = dsize(x->dtype);
+		if (!es || axis < 0 || axis >= out->n_dims)
+			return SAM3_EINVAL;
+		int64_t outer = 1;
+		for (int d = 0; d < axis; d++)
+			outer *= out->dims[d];
+		size_t row_out = (size_t)(nelems(out) / outer) * es, off = 0;
+		TRY(out_buf(m, out, &py));
+		for (int k = 0; k < nd->n_inputs; k++) {
+			struct sam3_tensor *in = nd->inputs[k];
+			void *pin;
+			if (!in || in->dtype != out->dtype)
+				return SAM3_EINVAL;
+			size_t row_in = (size_t)(nelems(in) / outer) * es;
+			TRY(dev_of(m, in, produced_in(g, ni, in), &pin));
+			TRY(sam3cu_memcpy2d_d2d((char *)py + off, row_out, pin, row_in, row_in,
+						(size_t)outer, m->stream));
+			off += row_in;
+		}
+		return off == row_out ? SAM3_OK : SAM3_EINVAL;
 	}
 
 	case SAM3_OP_GELU:
@@ -659,6 +756,18 @@ static enum sam3_error op_node(struct impl *m, struct sam3_graph *g, int ni)
 		struct sam3_tensor *w = nd->inputs[1];
 		int stride = nd->params[0] > 0 ? nd->params[0] : 1, pad = nd->params[1];
 		int groups = nd->params[2] > 0 ? nd->params[2] : 1;
+		if (groups > 1 && w && x->n_dims == 4 && w->n_dims == 4 && w->dtype == x->dtype &&
+		    w->dims[3] * groups == x->dims[3] && !(nd->params[3] && nd->params[3] != pad)) {
+			/* grouped / depthwise: direct kernel */
+			void *pw;
+			TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+			TRY(dev_of(m, w, produced_in(g, ni, w), &pw));
+			TRY(out_buf(m, out, &py));
+			TRY(sam3cu_conv2d_grouped_nhwc(px, pw, py, x->dtype, x->dims[0], x->dims[1],
+						       x->dims[2], x->dims[3], w->dims[0], w->dims[1],
+						       w->dims[2], stride, pad, groups, m->stream));
+			return SAM3_OK;
+		}
 		if (!w || x->n_dims != 4 || w->n_dims != 4 || groups != 1 ||
 		    (nd->params[3] && nd->params[3] != pad) || w->dims[3] != x->dims[3] ||
 		    w->dtype != x->dtype)
@@ -726,7 +835,8 @@ static void plan(struct impl *m, struct sam3_graph *g)
 			if (ok && any)
 				m->flags[i] |= F_LAZY_T | F_SKIP;
 		}
-		if (nd->op == SAM3_OP_MATMUL && count_uses(g, i + 1, nd->output) == 1) {
+		if (nd->op == SAM3_OP_MATMUL && nd->inputs[1] && nd->inputs[1]->n_dims <= 2 &&
+		    count_uses(g, i + 1, nd->output) == 1) {
 			for (int j = i + 1; j < g->n_nodes; j++) {
 				struct sam3_node *ad = &g->nodes[j];
 				if (ad->op != SAM3_OP_ADD || ad->inputs[0] != nd->output)

@@ -197,6 +197,98 @@ __global__ void q8_dequant_kernel(const uint8_t* __restrict__ blocks, float* __r
   }
 }
 
+// elementwise product with trailing-suffix broadcast (cpu_elementwise.c)
+template <int T>
+__global__ void mul_kernel(const void* a, const void* b, void* out, int64_t n, int64_t nb) {
+  GRID_LOOP(i, n) st<T>(out, i, ld<T>(a, i) * ld<T>(b, i % nb));
+}
+
+// Row softmax, one warp per row (cpu_softmax.c:29-47: max, expf(x - max),
+// sum, times 1/sum), f32 arithmetic.
+template <int T>
+__global__ void softmax_rows(const void* x, void* y, int64_t rows, int cols) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t base = row * cols;
+  float mx = -FLT_MAX;
+  for (int c = lane; c < cols; c += 32) mx = fmaxf(mx, ld<T>(x, base + c));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+  for (int c = lane; c < cols; c += 32) sum += expf(ld<T>(x, base + c) - mx);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = 1.0f / sum;
+  for (int c = lane; c < cols; c += 32) st<T>(y, base + c, expf(ld<T>(x, base + c) - mx) * inv);
+}
+
+// Batched C[b] = A[b] [M,K] . B[b] [K,N], f32 accumulation in k order,
+// 16x16 tiles through shared memory (the 4-D MATMUL of TinyViT's window
+// attention; the encoder's large GEMMs use the tcgen05 kernels instead).
+template <int T>
+__global__ void bmm_kernel(const void* a, const void* b, void* c, int M, int K, int N) {
+  __shared__ float as[16][17], bs[16][17];
+  const int bz = blockIdx.z;
+  const int row = blockIdx.y * 16 + threadIdx.y, col = blockIdx.x * 16 + threadIdx.x;
+  const int64_t ao = static_cast<int64_t>(bz) * M * K, bo = static_cast<int64_t>(bz) * K * N;
+  float acc = 0.f;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    const int ka = k0 + threadIdx.x, kb = k0 + threadIdx.y;
+    as[threadIdx.y][threadIdx.x] = (row < M && ka < K) ? ld<T>(a, ao + static_cast<int64_t>(row) * K + ka) : 0.f;
+    bs[threadIdx.y][threadIdx.x] = (kb < K && col < N) ? ld<T>(b, bo + static_cast<int64_t>(kb) * N + col) : 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc += as[threadIdx.y][k] * bs[k][threadIdx.x];
+    __syncthreads();
+  }
+  if (row < M && col < N) st<T>(c, static_cast<int64_t>(bz) * M * N + static_cast<int64_t>(row) * N + col, acc);
+}
+
+// Eval BatchNorm over the last dim (cpu_batchnorm.c: inv_std = 1/sqrtf(var
+// + 1e-5), (x - mean) * inv_std * gamma + beta; gamma / beta optional).
+template <int T>
+__global__ void batchnorm_kernel(const void* x, void* y, int64_t n, int C, const float* __restrict__ g,
+                                 const float* __restrict__ b, const float* __restrict__ mean,
+                                 const float* __restrict__ var) {
+  GRID_LOOP(i, n) {
+    const int c = static_cast<int>(i % C);
+    float v = (ld<T>(x, i) - mean[c]) * (1.0f / sqrtf(var[c] + 1e-5f));
+    if (g) v *= g[c];
+    if (b) v += b[c];
+    st<T>(y, i, v);
+  }
+}
+
+// Grouped NHWC conv with OHWI weights [OC, KH, KW, C/groups], direct
+// (cpu_conv2d.c:320-420 with groups > 1: depthwise convs), f32 accumulation
+// over (ky, kx, c).
+template <int T>
+__global__ void conv2d_grouped(const void* x, const void* w, void* y, int64_t n, int H, int W, int C, int OC, int KH,
+                               int KW, int stride, int pad, int OH, int OW, int groups) {
+  const int cpg_in = C / groups, cpg_out = OC / groups;
+  GRID_LOOP(i, n) {
+    const int oc = static_cast<int>(i % OC);
+    int64_t p = i / OC;
+    const int ox = static_cast<int>(p % OW), oy = static_cast<int>((p / OW) % OH);
+    const int64_t b = p / (static_cast<int64_t>(OW) * OH);
+    const int g = oc / cpg_out;
+    float acc = 0.f;
+    for (int ky = 0; ky < KH; ++ky) {
+      const int iy = oy * stride - pad + ky;
+      if (iy < 0 || iy >= H) continue;
+      for (int kx = 0; kx < KW; ++kx) {
+        const int ix = ox * stride - pad + kx;
+        if (ix < 0 || ix >= W) continue;
+        const int64_t xo = ((b * H + iy) * W + ix) * C + g * cpg_in;
+        const int64_t wo = ((static_cast<int64_t>(oc) * KH + ky) * KW + kx) * cpg_in;
+        for (int c = 0; c < cpg_in; ++c) acc += ld<T>(x, xo + c) * ld<T>(w, wo + c);
+      }
+    }
+    st<T>(y, i, acc);
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -348,6 +440,81 @@ int sam3cu_q8_dequantize(const void* blocks, float* out, int64_t n, void* stream
   count_launches(1);
   q8_dequant_kernel<<<grid_for(n, 256), 256, 0, S(stream)>>>(static_cast<const uint8_t*>(blocks), out, n);
   return rc_launch();
+}
+
+int sam3cu_mul(const void* a, const void* b, void* out, int dtype, int64_t n, int64_t nb, void* stream) {
+  if (!a || !b || !out || n < 0 || nb <= 0 || n % nb) return SAM3CU_EINVAL;
+  count_launches(1);
+  const int g = grid_for(n, 256);
+  if (dtype == kF32) mul_kernel<kF32><<<g, 256, 0, S(stream)>>>(a, b, out, n, nb);
+  else if (dtype == kBF16) mul_kernel<kBF16><<<g, 256, 0, S(stream)>>>(a, b, out, n, nb);
+  else if (dtype == kF16) mul_kernel<kF16><<<g, 256, 0, S(stream)>>>(a, b, out, n, nb);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_softmax(const void* x, void* y, int dtype, int64_t rows, int cols, void* stream) {
+  if (!x || !y || rows < 0 || cols <= 0) return SAM3CU_EINVAL;
+  if (!rows) return SAM3CU_OK;
+  count_launches(1);
+  const unsigned g = static_cast<unsigned>((rows * 32 + 255) / 256);
+  if (dtype == kF32) softmax_rows<kF32><<<g, 256, 0, S(stream)>>>(x, y, rows, cols);
+  else if (dtype == kBF16) softmax_rows<kBF16><<<g, 256, 0, S(stream)>>>(x, y, rows, cols);
+  else if (dtype == kF16) softmax_rows<kF16><<<g, 256, 0, S(stream)>>>(x, y, rows, cols);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_bmm(const void* a, const void* b, void* c, int dtype, int batch, int M, int K, int N, void* stream) {
+  if (!a || !b || !c || batch <= 0 || M <= 0 || K <= 0 || N <= 0 || batch > 65535) return SAM3CU_EINVAL;
+  count_launches(1);
+  const dim3 grid((N + 15) / 16, (M + 15) / 16, batch), block(16, 16);
+  if (dtype == kF32) bmm_kernel<kF32><<<grid, block, 0, S(stream)>>>(a, b, c, M, K, N);
+  else if (dtype == kBF16) bmm_kernel<kBF16><<<grid, block, 0, S(stream)>>>(a, b, c, M, K, N);
+  else if (dtype == kF16) bmm_kernel<kF16><<<grid, block, 0, S(stream)>>>(a, b, c, M, K, N);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_batchnorm(const void* x, void* y, int dtype, int64_t n, int C, const float* gamma, const float* beta,
+                     const float* mean, const float* var, void* stream) {
+  if (!x || !y || !mean || !var || C <= 0 || n % C) return SAM3CU_EINVAL;
+  count_launches(1);
+  const int g = grid_for(n, 256);
+  if (dtype == kF32) batchnorm_kernel<kF32><<<g, 256, 0, S(stream)>>>(x, y, n, C, gamma, beta, mean, var);
+  else if (dtype == kBF16) batchnorm_kernel<kBF16><<<g, 256, 0, S(stream)>>>(x, y, n, C, gamma, beta, mean, var);
+  else if (dtype == kF16) batchnorm_kernel<kF16><<<g, 256, 0, S(stream)>>>(x, y, n, C, gamma, beta, mean, var);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_conv2d_grouped_nhwc(const void* x, const void* w, void* y, int dtype, int n, int H, int W, int C, int OC,
+                               int KH, int KW, int stride, int pad, int groups, void* stream) {
+  if (!x || !w || !y || groups <= 0 || C % groups || OC % groups || stride <= 0) return SAM3CU_EINVAL;
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0) return SAM3CU_EINVAL;
+  const int64_t total = static_cast<int64_t>(n) * OH * OW * OC;
+  count_launches(1);
+  const int g = grid_for(total, 256);
+  if (dtype == kF32)
+    conv2d_grouped<kF32><<<g, 256, 0, S(stream)>>>(x, w, y, total, H, W, C, OC, KH, KW, stride, pad, OH, OW, groups);
+  else if (dtype == kBF16)
+    conv2d_grouped<kBF16><<<g, 256, 0, S(stream)>>>(x, w, y, total, H, W, C, OC, KH, KW, stride, pad, OH, OW, groups);
+  else if (dtype == kF16)
+    conv2d_grouped<kF16><<<g, 256, 0, S(stream)>>>(x, w, y, total, H, W, C, OC, KH, KW, stride, pad, OH, OW, groups);
+  else
+    return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
+int sam3cu_memcpy2d_d2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t rows,
+                        void* stream) {
+  if (!dst || !src) return SAM3CU_EINVAL;
+  if (!rows || !width) return SAM3CU_OK;
+  return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, cudaMemcpyDeviceToDevice, S(stream)) ==
+                 cudaSuccess
+             ? SAM3CU_OK
+             : SAM3CU_ECUDA;
 }
 
 }  // extern "C"
