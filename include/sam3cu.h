@@ -341,6 +341,18 @@ SAM3CU_API int sam3cu_batchnorm(const void *x, void *y, int dtype, int64_t n, in
 SAM3CU_API int sam3cu_conv2d_grouped_nhwc(const void *x, const void *w, void *y, int dtype,
 		int n, int H, int W, int C, int OC, int KH, int KW, int stride, int pad,
 		int groups, void *stream);
+/* Transposed conv NHWC x OHWI [OC,KH,KW,C] (cpu_conv_transpose2d.c): direct
+ * kernel, any stride / padding; output (H-1)*stride - 2*pad + KH. */
+SAM3CU_API int sam3cu_conv_transpose2d_nhwc(const void *x, const void *w, void *y, int dtype,
+		int n, int H, int W, int C, int OC, int KH, int KW, int stride, int pad,
+		void *stream);
+/* Pixel shuffle after a kernel-k, stride-k transposed conv run as a GEMM:
+ * g [n*H*W, k*k*OC] (columns (ky, kx, oc)) -> y [n, H*k, W*k, OC]. */
+SAM3CU_API int sam3cu_convt_shuffle(const void *g, void *y, int elem_size, int n, int H, int W,
+				    int k, int OC, void *stream);
+/* NHWC max pool, kernel k, stride s, no padding (cpu_maxpool2d.c). */
+SAM3CU_API int sam3cu_maxpool2d_nhwc(const void *x, void *y, int dtype, int n, int H, int W,
+				     int C, int k, int s, void *stream);
 /* Device-to-device 2-D copy (rows of width bytes), for CONCAT. */
 SAM3CU_API int sam3cu_memcpy2d_d2d(void *dst, size_t dpitch, const void *src, size_t spitch,
 				   size_t width, size_t rows, void *stream);

@@ -967,3 +967,90 @@ int orc_tinyvit_forward(const struct orc_tinyvit_cfg *c,
 	free(x);
 	return H;
 }
+
+/* ---- FPN neck (src/model/necks.c) --------------------------------------- */
+
+/* One stage of sam3_neck_build (build_stage, necks.c:327-369), stage plan
+ * per scale factor as init_stage_4x / _2x / _1x / _half (:37-148):
+ *   >= 3.5: ConvT(dim->dim/2, k2 s2), GELU, ConvT(dim/2->dim/4, k2 s2),
+ *           Conv1x1(->d), Conv3x3(d->d, pad 1)
+ *   >= 1.5: ConvT(dim->dim/2), Conv1x1(->d), Conv3x3
+ *   >= 0.75: Conv1x1(dim->d), Conv3x3
+ *   else: MaxPool(2, 2), Conv1x1(dim->d), Conv3x3
+ * every conv with bias (a BIAS_ADD node).  x [H, W, dim] NHWC; returns the
+ * output size through *oh; out must hold it. */
+static void convt_k2s2(const float *x, int H, int W, int C, int OC,
+		       const float *w, const float *b, int gelu, float *y)
+{
+	/* cpu_conv_transpose2d.c with stride 2, pad 0, kernel 2: output
+	 * (2h+ky, 2w+kx) = sum_c x[h, w, c] * w[oc, ky, kx, c] */
+#pragma omp parallel for schedule(static)
+	for (int64_t p = 0; p < (int64_t)H * W; p++) {
+		int h = (int)(p / W), ww = (int)(p % W);
+		const float *xr = x + p * C;
+		for (int ky = 0; ky < 2; ky++)
+			for (int kx = 0; kx < 2; kx++) {
+				float *yo = y + (((int64_t)(2 * h + ky) * 2 * W) + 2 * ww + kx) * OC;
+				for (int o = 0; o < OC; o++) {
+					const float *wr = w + (((int64_t)o * 2 + ky) * 2 + kx) * C;
+					float acc = 0.0f;
+					for (int c = 0; c < C; c++)
+						acc += xr[c] * wr[c];
+					acc += b ? b[o] : 0.0f;
+					yo[o] = gelu ? gelu_tanh(acc) : acc;
+				}
+			}
+	}
+}
+
+void orc_neck_forward(int d_model, int dim, int grid, int n_scales,
+		      const float *scales, const float *const *w,
+		      const float *const *b, const float *feat,
+		      float *const *outs)
+{
+	for (int i = 0; i < n_scales; i++) {
+		const float sf = scales[i];
+		const float *const *ws = w + i * 4, *const *bs = b + i * 4;
+		int H = grid, C = dim;
+		float *cur = malloc(sizeof(float) * (size_t)grid * grid * dim);
+		memcpy(cur, feat, sizeof(float) * (size_t)grid * grid * dim);
+		int j = 0;
+		if (sf < 0.75f) {  /* MaxPool(2, 2) (cpu_maxpool2d.c) */
+			int Hn = (H - 2) / 2 + 1;
+			float *nx = malloc(sizeof(float) * (size_t)Hn * Hn * C);
+			for (int y = 0; y < Hn; y++)
+				for (int xx = 0; xx < Hn; xx++)
+					for (int c = 0; c < C; c++) {
+						float m = -FLT_MAX;
+						for (int ky = 0; ky < 2; ky++)
+							for (int kx = 0; kx < 2; kx++) {
+								float v = cur[((int64_t)(2 * y + ky) * H + 2 * xx + kx) * C + c];
+								if (v > m)
+									m = v;
+							}
+						nx[((int64_t)y * Hn + xx) * C + c] = m;
+					}
+			free(cur);
+			cur = nx;
+			H = Hn;
+		}
+		int n_t = sf >= 3.5f ? 2 : (sf >= 1.5f ? 1 : 0);
+		for (int t = 0; t < n_t; t++, j++) {
+			int OC = C / 2;
+			float *nx = malloc(sizeof(float) * (size_t)4 * H * H * OC);
+			convt_k2s2(cur, H, H, C, OC, ws[j], bs[j], sf >= 3.5f && t == 0, nx);
+			free(cur);
+			cur = nx;
+			H *= 2;
+			C = OC;
+		}
+		float *p1 = malloc(sizeof(float) * (size_t)H * H * d_model);
+		orc_conv2d_bn(cur, 0, 1, H, H, C, d_model, 1, 1, 0, ws[j], bs[j], NULL,
+			      NULL, NULL, NULL, 0, p1);
+		j++;
+		orc_conv2d_bn(p1, 0, 1, H, H, d_model, d_model, 3, 1, 1, ws[j], bs[j],
+			      NULL, NULL, NULL, NULL, 0, outs[i]);
+		free(p1);
+		free(cur);
+	}
+}

@@ -581,3 +581,64 @@ def ref_tinyvit_encode(cfg_struct, weights_struct, image: np.ndarray, ops=None, 
     if rc != 0:
         raise RuntimeError(f"ref_tinyvit_encode failed rc={rc}")
     return out
+
+
+# ---------------------------------------------------------------- FPN neck
+def _neck_ptrs(w: dict):
+    """(w, b) -> two [4*4] pointer arrays (stage-major, layer-minor)."""
+    W = (VP * 16)()
+    B = (VP * 16)()
+    keep = []
+    for i, layers in enumerate(w["w"]):
+        for j, a in enumerate(layers):
+            a = np.ascontiguousarray(a, np.float32)
+            keep.append(a)
+            W[i * 4 + j] = a.ctypes.data
+            bb = np.ascontiguousarray(w["b"][i][j], np.float32)
+            keep.append(bb)
+            B[i * 4 + j] = bb.ctypes.data
+    return W, B, keep
+
+
+def neck_out_sizes(grid, scales):
+    out = []
+    for sf in scales:
+        if sf >= 3.5:
+            out.append(grid * 4)
+        elif sf >= 1.5:
+            out.append(grid * 2)
+        elif sf >= 0.75:
+            out.append(grid)
+        else:
+            out.append((grid - 2) // 2 + 1)
+    return out
+
+
+def neck_forward(d_model, dim, grid, scales, w: dict, feat: np.ndarray):
+    """Restatement of sam3_neck_build: feat [grid*grid, dim] -> list of
+    [H_i, H_i, d_model] arrays."""
+    feat = np.ascontiguousarray(feat, np.float32)
+    W, B, keep = _neck_ptrs(w)
+    sizes = neck_out_sizes(grid, scales)
+    outs = [np.empty((h, h, d_model), np.float32) for h in sizes]
+    optr = (VP * 4)(*[o.ctypes.data for o in outs])
+    sc = np.ascontiguousarray(scales, np.float32)
+    orc().orc_neck_forward(d_model, dim, grid, len(scales), _p(sc), W, B, _p(feat), optr)
+    return outs
+
+
+def ref_neck(d_model, dim, grid, scales, w: dict, feat: np.ndarray, ops=None, be_size=0, be_type=2):
+    """The reference's own sam3_neck_build (necks.c, compiled from source)
+    evaluated by a backend (ops None: the reference CPU backend)."""
+    feat = np.ascontiguousarray(feat, np.float32)
+    W, B, keep = _neck_ptrs(w)
+    sizes = neck_out_sizes(grid, scales)
+    outs = [np.empty((h, h, d_model), np.float32) for h in sizes]
+    optr = (VP * 4)(*[o.ctypes.data for o in outs])
+    sc = np.ascontiguousarray(scales, np.float32)
+    WB = (VP * 32)(*(list(W) + list(B)))  # struct rn_weights {w[4][4]; b[4][4];}
+    rc = ref().ref_neck_run(d_model, dim, grid, len(scales), _p(sc), C.byref(WB), _p(feat), optr,
+                            C.c_void_p(ops), C.c_size_t(be_size), C.c_int(be_type))
+    if rc != 0:
+        raise RuntimeError(f"ref_neck_run failed rc={rc}")
+    return outs

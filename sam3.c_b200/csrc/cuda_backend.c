@@ -797,6 +797,58 @@ static enum sam3_error op_node(struct impl *m, struct sam3_graph *g, int ni)
 		return SAM3_OK;
 	}
 
+	case SAM3_OP_CONV_TRANSPOSE2D: {  /* NHWC x OHWI (cpu_conv_transpose2d.c) */
+		struct sam3_tensor *w = nd->inputs[1];
+		int stride = nd->params[0] > 0 ? nd->params[0] : 1, pad = nd->params[1];
+		if (!w || x->n_dims != 4 || w->n_dims != 4 || w->dims[3] != x->dims[3] ||
+		    w->dtype != x->dtype || (x->dtype != SAM3_DTYPE_F32 && !is_16(x->dtype)))
+			return SAM3_EDTYPE;
+		int N = x->dims[0], H = x->dims[1], W = x->dims[2], C = x->dims[3];
+		int OC = w->dims[0], KH = w->dims[1], KW = w->dims[2];
+		size_t es = dsize(x->dtype);
+		void *pw;
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(dev_of(m, w, produced_in(g, ni, w), &pw));
+		TRY(out_buf(m, out, &py));
+		if (KH == stride && KW == stride && pad == 0 && C % (es == 4 ? 4 : 8) == 0) {
+			/* non-overlapping (the FPN neck's k2 s2): one GEMM
+			 * [N*H*W, C] x [(ky,kx,oc), C]^T, then a pixel shuffle;
+			 * the weight re-layout is cached per weight */
+			struct devent *e = map_find(m, w);
+			void *wg = e ? (void *)e->aux : NULL;
+			if (!wg) {
+				int dims[4] = {OC, KH, KW, C}, perm[4] = {1, 2, 0, 3};
+				TRY(sam3cu_dev_alloc(&wg, (size_t)OC * KH * KW * C * es));
+				TRY(sam3cu_permute(pw, wg, (int)es, 4, dims, perm, m->stream));
+				if (e)
+					e->aux = wg;
+			}
+			void *tmp;
+			int64_t M = (int64_t)N * H * W;
+			TRY(tmp_alloc(m, (size_t)M * KH * KW * OC * es, &tmp));
+			TRY(sam3cu_linear(px, x->dtype, wg, NULL, NULL, tmp, x->dtype, (int)M, C,
+					  KH * KW * OC, 0, m->stream));
+			TRY(sam3cu_convt_shuffle(tmp, py, (int)es, N, H, W, KH, OC, m->stream));
+			if (!e)
+				sam3cu_dev_free(wg);
+			return SAM3_OK;
+		}
+		TRY(sam3cu_conv_transpose2d_nhwc(px, pw, py, x->dtype, N, H, W, C, OC, KH, KW, stride,
+						 pad, m->stream));
+		return SAM3_OK;
+	}
+
+	case SAM3_OP_MAXPOOL2D: {  /* NHWC, params kernel, stride (cpu_maxpool2d.c) */
+		int k = nd->params[0], kst = nd->params[1] > 0 ? nd->params[1] : k;
+		if (x->n_dims != 4 || k <= 0 || (x->dtype != SAM3_DTYPE_F32 && !is_16(x->dtype)))
+			return SAM3_EDTYPE;
+		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(out_buf(m, out, &py));
+		TRY(sam3cu_maxpool2d_nhwc(px, py, x->dtype, x->dims[0], x->dims[1], x->dims[2],
+					  x->dims[3], k, kst, m->stream));
+		return SAM3_OK;
+	}
+
 	default:
 		fprintf(stderr, "[sam3cu] op %d (dtype %d) is not supported on CUDA\n",
 			(int)nd->op, (int)x->dtype);

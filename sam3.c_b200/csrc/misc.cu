@@ -241,6 +241,90 @@ int grid_for(int64_t n, int threads) {
 
 }  // namespace
 
+namespace {
+
+// im2col for a dense KxK conv (zero padding) -> 16-bit columns: row
+// (img, oy, ox), column (ky, kx, c) to match OHWI weights, zero-filled to
+// kpad.  kChw: the input is planar CHW per image (the raw image), else NHWC.
+template <int TI, int TO, bool kChw>
+__global__ void conv_im2col(const void* __restrict__ x, void* __restrict__ a, int64_t total, int H, int W, int C,
+                            int k, int stride, int pad, int OH, int OW, int kpad) {
+  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;  // total < 2^31 (launcher)
+  if (i >= total) return;
+  const int col = static_cast<int>(i % kpad);
+  const unsigned row = i / kpad;
+  const int ox = static_cast<int>(row % OW), oy = static_cast<int>((row / OW) % OH);
+  const int64_t b = row / (static_cast<unsigned>(OW) * OH);
+  float v = 0.f;
+  if (col < k * k * C) {
+    const int c = col % C, kx = (col / C) % k, ky = col / (C * k);
+    const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+    if (iy >= 0 && iy < H && ix >= 0 && ix < W) {
+      const int64_t src = kChw ? ((b * C + c) * H + iy) * W + ix : ((b * H + iy) * W + ix) * C + c;
+      if (TI == kF32)
+        v = static_cast<const float*>(x)[src];
+      else if (TI == kBF16)
+        v = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[src]);
+      else
+        v = __half2float(static_cast<const __half*>(x)[src]);
+    }
+  }
+  if (TO == kBF16)
+    static_cast<__nv_bfloat16*>(a)[i] = __float2bfloat16_rn(v);
+  else
+    static_cast<__half*>(a)[i] = __float2half_rn(v);
+}
+
+// 16-bit NHWC input with C % 8 == 0: one thread copies 8 channels (16
+// bytes) of one tap; 32-bit index math (the launcher checks the count).
+__global__ void conv_im2col_v8(const uint4* __restrict__ x, uint4* __restrict__ a, unsigned total, int H, int W,
+                               int C8, int k, int stride, int pad, int OH, int OW, int kpad8, int kk8) {
+  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const unsigned col = i % kpad8;
+  const unsigned row = i / kpad8;
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (col < static_cast<unsigned>(kk8)) {
+    const int c8 = col % C8, tap = col / C8;
+    const int kx = tap % k, ky = tap / k;
+    const int ox = row % OW, oy = (row / OW) % OH;
+    const unsigned b = row / (static_cast<unsigned>(OW) * OH);
+    const int iy = oy * stride - pad + ky, ix = ox * stride - pad + kx;
+    if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+      v = __ldg(x + ((static_cast<int64_t>(b) * H + iy) * W + ix) * C8 + c8);
+  }
+  a[i] = v;
+}
+
+}  // namespace
+
+int launch_conv_im2col(const void* x, int tin, bool chw, void* a, int tout, int B, int H, int W, int C, int k,
+                       int stride, int pad, int kpad, cudaStream_t st) {
+  const int OH = (H + 2 * pad - k) / stride + 1, OW = (W + 2 * pad - k) / stride + 1;
+  const int64_t total = static_cast<int64_t>(B) * OH * OW * kpad;
+  if (!chw && tin == tout && tin != kF32 && C % 8 == 0 && kpad % 8 == 0) {
+    const int64_t t8 = total / 8;
+    if (t8 >= (1LL << 31)) return kErrShape;
+    count_launches(1);
+    conv_im2col_v8<<<grid_for(t8, 256), 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<uint4*>(a),
+                                                     static_cast<unsigned>(t8), H, W, C / 8, k, stride, pad, OH,
+                                                     OW, kpad / 8, k * k * C / 8);
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+  }
+  if (total >= (1LL << 31)) return kErrShape;
+  const int grid = grid_for(total, 256);
+  count_launches(1);
+#define S3_IC(TI, TO, CHW)                                                                               \
+  if (tin == TI && tout == TO && chw == CHW) {                                                           \
+    conv_im2col<TI, TO, CHW><<<grid, 256, 0, st>>>(x, a, total, H, W, C, k, stride, pad, OH, OW, kpad); \
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;                                         \
+  }
+  S3_IC(kF32, kBF16, true) S3_IC(kF32, kF16, true) S3_IC(kF32, kBF16, false) S3_IC(kF32, kF16, false)
+  S3_IC(kBF16, kBF16, false) S3_IC(kF16, kF16, false)
+#undef S3_IC
+  return kErrDtype;
+}
+
 int launch_layernorm(const void* x, int tin, void* y, int tout, const float* g, const float* b, int rows,
                      int cols, const int* out_row_map, int out_row_period, cudaStream_t st) {
   if (rows <= 0) return kOk;

@@ -19,5 +19,10 @@ int launch_q8_row_shift(float* sc, float* col_scale, int N, int K, cudaStream_t 
 // 1 f16 from row-shifted scales (half2 arithmetic), 2 f16 from any scales
 int launch_q8_dequant_w16(const int8_t* q, const float* sc, void* w, int N, int K, int mode, cudaStream_t st);
 int launch_cast(const void* x, int tin, void* y, int tout, int64_t n, cudaStream_t st);
+// im2col of a dense KxK conv (zero padding) into 16-bit columns (row
+// (img, oy, ox), column (ky, kx, c), zero-filled to kpad); chw: planar CHW
+// input per image, else NHWC; a 16-byte path for 16-bit NHWC, C % 8 == 0
+int launch_conv_im2col(const void* x, int tin, bool chw, void* a, int tout, int B, int H, int W, int C, int k,
+                       int stride, int pad, int kpad, cudaStream_t st);
 
 }  // namespace s3

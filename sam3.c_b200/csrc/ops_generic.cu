@@ -289,6 +289,70 @@ __global__ void conv2d_grouped(const void* x, const void* w, void* y, int64_t n,
   }
 }
 
+// Direct transposed conv, NHWC x OHWI [OC, KH, KW, C] (cpu_conv_transpose2d.c:
+// output (oh, ow) gathers input (ih, iw) with oh + pad - kh = ih * stride),
+// f32 accumulation.
+template <int T>
+__global__ void conv_transpose2d_direct(const void* x, const void* w, void* y, int64_t n, int H, int W, int C,
+                                        int OC, int KH, int KW, int stride, int pad, int OH, int OW) {
+  GRID_LOOP(i, n) {
+    const int oc = static_cast<int>(i % OC);
+    int64_t p = i / OC;
+    const int ow = static_cast<int>(p % OW), oh = static_cast<int>((p / OW) % OH);
+    const int64_t b = p / (static_cast<int64_t>(OW) * OH);
+    float acc = 0.f;
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ho = oh + pad - kh;
+      if (ho < 0 || ho % stride) continue;
+      const int ih = ho / stride;
+      if (ih >= H) continue;
+      for (int kw = 0; kw < KW; ++kw) {
+        const int wo = ow + pad - kw;
+        if (wo < 0 || wo % stride) continue;
+        const int iw = wo / stride;
+        if (iw >= W) continue;
+        const int64_t xo = ((b * H + ih) * W + iw) * C;
+        const int64_t wofs = ((static_cast<int64_t>(oc) * KH + kh) * KW + kw) * C;
+        for (int c = 0; c < C; ++c) acc += ld<T>(x, xo + c) * ld<T>(w, wofs + c);
+      }
+    }
+    st<T>(y, i, acc);
+  }
+}
+
+// y[b, h*k + ky, w*k + kx, oc] = g[(b, h, w), (ky*k + kx)*OC + oc]: the
+// pixel shuffle after a stride-k, kernel-k transposed conv run as one GEMM.
+template <typename E>
+__global__ void convt_shuffle(const E* __restrict__ g, E* __restrict__ y, int64_t n, int H, int W, int k, int OC) {
+  GRID_LOOP(i, n) {
+    const int oc = static_cast<int>(i % OC);
+    int64_t p = i / OC;
+    const int OW = W * k, OH = H * k;
+    const int ox = static_cast<int>(p % OW), oy = static_cast<int>((p / OW) % OH);
+    const int64_t b = p / (static_cast<int64_t>(OW) * OH);
+    const int hh = oy / k, ky = oy % k, ww = ox / k, kx = ox % k;
+    y[i] = g[((b * H + hh) * W + ww) * static_cast<int64_t>(k * k * OC) + (ky * k + kx) * OC + oc];
+  }
+}
+
+// NHWC max pool, kernel k, stride s, no padding (cpu_maxpool2d.c).
+template <int T>
+__global__ void maxpool_nhwc(const void* x, void* y, int64_t n, int H, int W, int C, int k, int s, int OH, int OW) {
+  GRID_LOOP(i, n) {
+    const int c = static_cast<int>(i % C);
+    int64_t p = i / C;
+    const int ox = static_cast<int>(p % OW), oy = static_cast<int>((p / OW) % OH);
+    const int64_t b = p / (static_cast<int64_t>(OW) * OH);
+    float m = -FLT_MAX;
+    for (int ky = 0; ky < k; ++ky)
+      for (int kx = 0; kx < k; ++kx) {
+        const int iy = oy * s + ky, ix = ox * s + kx;
+        if (iy < H && ix < W) m = fmaxf(m, ld<T>(x, ((b * H + iy) * W + ix) * C + c));
+      }
+    st<T>(y, i, m);
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -515,6 +579,54 @@ int sam3cu_memcpy2d_d2d(void* dst, size_t dpitch, const void* src, size_t spitch
                  cudaSuccess
              ? SAM3CU_OK
              : SAM3CU_ECUDA;
+}
+
+int sam3cu_conv_transpose2d_nhwc(const void* x, const void* w, void* y, int dtype, int n, int H, int W, int C,
+                                  int OC, int KH, int KW, int stride, int pad, void* stream) {
+  if (!x || !w || !y || stride <= 0 || pad < 0) return SAM3CU_EINVAL;
+  const int OH = (H - 1) * stride - 2 * pad + KH, OW = (W - 1) * stride - 2 * pad + KW;
+  if (OH <= 0 || OW <= 0) return SAM3CU_EINVAL;
+  const int64_t total = static_cast<int64_t>(n) * OH * OW * OC;
+  count_launches(1);
+  const int g = grid_for(total, 256);
+#define S3_CT(TT)                                                                                        \
+  conv_transpose2d_direct<TT><<<g, 256, 0, S(stream)>>>(x, w, y, total, H, W, C, OC, KH, KW, stride, pad, OH, OW)
+  if (dtype == kF32) S3_CT(kF32);
+  else if (dtype == kBF16) S3_CT(kBF16);
+  else if (dtype == kF16) S3_CT(kF16);
+  else return SAM3CU_EDTYPE;
+#undef S3_CT
+  return rc_launch();
+}
+
+int sam3cu_convt_shuffle(const void* g, void* y, int elem_size, int n, int H, int W, int k, int OC, void* stream) {
+  if (!g || !y || k <= 0 || OC <= 0) return SAM3CU_EINVAL;
+  const int64_t total = static_cast<int64_t>(n) * H * k * W * k * OC;
+  count_launches(1);
+  const int gr = grid_for(total, 256);
+  if (elem_size == 4)
+    convt_shuffle<float><<<gr, 256, 0, S(stream)>>>(static_cast<const float*>(g), static_cast<float*>(y), total, H, W,
+                                                    k, OC);
+  else if (elem_size == 2)
+    convt_shuffle<uint16_t><<<gr, 256, 0, S(stream)>>>(static_cast<const uint16_t*>(g), static_cast<uint16_t*>(y),
+                                                       total, H, W, k, OC);
+  else
+    return SAM3CU_EINVAL;
+  return rc_launch();
+}
+
+int sam3cu_maxpool2d_nhwc(const void* x, void* y, int dtype, int n, int H, int W, int C, int k, int s, void* stream) {
+  if (!x || !y || k <= 0 || s <= 0) return SAM3CU_EINVAL;
+  const int OH = (H - k) / s + 1, OW = (W - k) / s + 1;
+  if (OH <= 0 || OW <= 0) return SAM3CU_EINVAL;
+  const int64_t total = static_cast<int64_t>(n) * OH * OW * C;
+  count_launches(1);
+  const int g = grid_for(total, 256);
+  if (dtype == kF32) maxpool_nhwc<kF32><<<g, 256, 0, S(stream)>>>(x, y, total, H, W, C, k, s, OH, OW);
+  else if (dtype == kBF16) maxpool_nhwc<kBF16><<<g, 256, 0, S(stream)>>>(x, y, total, H, W, C, k, s, OH, OW);
+  else if (dtype == kF16) maxpool_nhwc<kF16><<<g, 256, 0, S(stream)>>>(x, y, total, H, W, C, k, s, OH, OW);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
 }
 
 }  // extern "C"

@@ -143,3 +143,32 @@ def tinyvit_images(cfg, n, seed=0):
     rng = np.random.default_rng(seed)
     s = cfg["img_size"]
     return (rng.random((n, 3, s, s), dtype=np.float32) * 2 - 1).astype(np.float32)
+
+
+# ---------------------------------------------------------------- FPN neck
+SAM3_NECK = dict(d_model=256, dim=1024, grid=72, scales=(4.0, 2.0, 1.0, 0.5))
+
+
+def neck_layer_dims(d_model, dim, sf):
+    """(kind, c_in, c_out, k) per layer of one stage (necks.c:188-236)."""
+    if sf >= 3.5:
+        return [("t", dim, dim // 2, 2), ("t", dim // 2, dim // 4, 2), ("c", dim // 4, d_model, 1),
+                ("c", d_model, d_model, 3)]
+    if sf >= 1.5:
+        return [("t", dim, dim // 2, 2), ("c", dim // 2, d_model, 1), ("c", d_model, d_model, 3)]
+    return [("c", dim, d_model, 1), ("c", d_model, d_model, 3)]
+
+
+def neck_weights(d_model, dim, scales, seed=0):
+    """Random-init neck weights: OHWI convs ~N(0, 1/fan_in), biases ~N(0, 0.01)."""
+    rng = np.random.default_rng(seed)
+    w = {"w": [], "b": []}
+    for sf in scales:
+        ws, bs = [], []
+        for kind, ci, co, k in neck_layer_dims(d_model, dim, sf):
+            fan = ci * k * k
+            ws.append((rng.standard_normal((co, k, k, ci)) / np.sqrt(fan)).astype(np.float32))
+            bs.append((rng.standard_normal(co) * 0.01).astype(np.float32))
+        w["w"].append(ws)
+        w["b"].append(bs)
+    return w
