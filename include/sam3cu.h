@@ -65,7 +65,9 @@ enum sam3cu_status {
 	SAM3CU_OK        = 0,
 	SAM3CU_EINVAL    = -1,   /* = SAM3_EINVAL */
 	SAM3CU_ENOMEM    = -2,   /* = SAM3_ENOMEM */
+	SAM3CU_EIO       = -3,   /* = SAM3_EIO */
 	SAM3CU_EBACKEND  = -4,   /* = SAM3_EBACKEND */
+	SAM3CU_EMODEL    = -5,   /* = SAM3_EMODEL: malformed weight file */
 	SAM3CU_EDTYPE    = -6,   /* = SAM3_EDTYPE */
 	SAM3CU_ESHAPE    = -101, /* shape/alignment the kernels do not take */
 	SAM3CU_ETMA      = -102, /* TMA descriptor creation failed */
@@ -75,6 +77,7 @@ enum sam3cu_status {
 	SAM3CU_EDTYPE2   = -106, /* unsupported dtype combination */
 	SAM3CU_ENOMEM2   = -107, /* device allocation failed */
 	SAM3CU_ESCRATCH  = -108, /* request exceeds a fixed static scratch buffer */
+	SAM3CU_ENOENT    = -109, /* tensor name not in a .sam3 file */
 };
 
 /* Activation fused into a linear's epilogue. */
@@ -463,6 +466,54 @@ SAM3CU_API int sam3cu_vit_profile(sam3cu_vit *vit, const float *images,
 
 /* Kernel launches one encode of n_images enqueues. */
 SAM3CU_API int sam3cu_vit_launches_per_encode(sam3cu_vit *vit, int n_images);
+
+/* ------------------------------------------------------ .sam3 weight files */
+
+/*
+ * Validate a .sam3 file image (the bytes sam3_weight_open maps,
+ * src/core/weight.c:303-470; format src/core/weight.h:26-72): magic, version
+ * 3 or 4, tensor table and every tensor's data range inside the image.
+ * Returns SAM3CU_EMODEL for a malformed image.  Host only, no device work.
+ */
+SAM3CU_API int sam3cu_sam3_check(const void *image, size_t bytes, uint32_t *n_tensors,
+				 uint32_t *version);
+
+/*
+ * sam3_weight_find + sam3_weight_to_tensor (weight.c:505-558) on a file
+ * image: dtype (enum sam3_dtype), n_dims, dims[4], the tensor's byte offset
+ * from the start of the IMAGE and its byte size.  SAM3CU_ENOENT if absent.
+ */
+SAM3CU_API int sam3cu_sam3_find(const void *image, size_t bytes, const char *name, int *dtype,
+				int *n_dims, int *dims, uint64_t *data_offset, uint64_t *nbytes);
+
+/*
+ * sam3_vit_load (src/model/image_encoder.c:223-456) + sam3cu_vit_create from
+ * a .sam3 file image: the detector_model.vision_encoder.backbone.* tensors
+ * are found by the reference's names and uploaded AS STORED (F32, F16, BF16
+ * or Q8_0, the dtypes sam3_convert writes), then converted on the device.
+ * Q8_0 linear weights going to a SAM3CU_Q8_0 encoder are only repacked,
+ * never requantised, so the int8 payload of the file is what the GEMMs
+ * read; a Q8_0 tensor anywhere else (the converter quantises every float
+ * tensor of >= 1024 elements, tools/cli_convert.c:340-352, LayerNorm gains
+ * and biases included) is dequantised to F32.  q/k/v are concatenated into
+ * the fused QKV as fuse_3 does.
+ * cfg NULL: the shape is taken from the file (embed_dim and patch_size from
+ * the patch weight, mlp_dim from layer 0's fc1, depth from the layers
+ * present, img_size from the header; 64-wide heads, window 24).
+ * A missing or mis-sized tensor returns SAM3CU_EMODEL (the reference warns
+ * and continues with an uninitialised tensor, graph_helpers.c:143), except
+ * the patch bias, which is optional and zero when absent, as in the
+ * reference (image_encoder.c:271-297).  The image may be freed after the
+ * call returns.
+ */
+SAM3CU_API sam3cu_vit *sam3cu_vit_create_from_sam3(const void *image, size_t bytes,
+						   const struct sam3cu_vit_config *cfg,
+						   int weight_dtype, int max_batch, int *status);
+
+/* The shape an encoder was created with (after sam3cu_vit_create_from_sam3
+ * with cfg NULL: the one read from the file).  No counterpart in the
+ * reference, whose struct sam3_vit is caller-visible. */
+SAM3CU_API int sam3cu_vit_get_config(const sam3cu_vit *vit, struct sam3cu_vit_config *cfg);
 
 #ifdef __cplusplus
 }

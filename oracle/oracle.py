@@ -642,3 +642,69 @@ def ref_neck(d_model, dim, grid, scales, w: dict, feat: np.ndarray, ops=None, be
     if rc != 0:
         raise RuntimeError(f"ref_neck_run failed rc={rc}")
     return outs
+
+
+# ---------------------------------------------------------------- .sam3 files
+class _RwTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_int), ("n_dims", C.c_int),
+                ("dims", C.c_int * 4), ("data", VP)]
+
+
+def ref_write_sam3(path: str, tensors, quantize: bool = False, image_size: int = 0,
+                   encoder_dim: int = 0, n_layers: int = 0) -> None:
+    """Write a .sam3 file with the reference's own sam3_weight_write
+    (weight.c:64-236).  tensors: (name, array[, dtype]) with float32 arrays
+    (dtype F32) or uint16 bit patterns (dtype 1 F16 / 2 BF16).  quantize:
+    the converter's Q8_0 rule (cli_convert.c:340-425)."""
+    keep = []
+    arr = (_RwTensor * len(tensors))()
+    for i, item in enumerate(tensors):
+        name, a = item[0], item[1]
+        dt = item[2] if len(item) > 2 else 0
+        a = np.ascontiguousarray(a, np.float32 if dt == 0 else np.uint16)
+        nm = name.encode()
+        keep += [a, nm]
+        arr[i].name, arr[i].dtype, arr[i].n_dims = nm, dt, a.ndim
+        for d in range(a.ndim):
+            arr[i].dims[d] = a.shape[d]
+        arr[i].data = a.ctypes.data
+    rc = ref().ref_write_sam3(path.encode(), arr, len(tensors), int(quantize), image_size,
+                              encoder_dim, n_layers)
+    if rc != 0:
+        raise RuntimeError(f"sam3_weight_write failed rc={rc}")
+
+
+def ref_find_sam3(path: str, name: str):
+    """sam3_weight_open + sam3_weight_find: dict like sam3cu.sam3_find, None
+    if absent; raises with the sam3_error of a file the reference rejects."""
+    dt, nd = C.c_int(0), C.c_int(0)
+    dims = (C.c_int * 4)()
+    off, nb = C.c_ulonglong(0), C.c_ulonglong(0)
+    rc = ref().ref_find_sam3(path.encode(), name.encode(), C.byref(dt), C.byref(nd), dims,
+                             C.byref(off), C.byref(nb))
+    if rc == 1:
+        return None
+    if rc != 0:
+        raise RuntimeError(f"sam3_weight_open failed rc={rc}")
+    return dict(dtype=dt.value, dims=tuple(dims[i] for i in range(nd.value)), offset=off.value,
+                nbytes=nb.value)
+
+
+def ref_open_sam3(path: str) -> int:
+    """sam3_weight_open's status (enum sam3_error) for a file."""
+    return ref().ref_open_sam3(path.encode())
+
+
+def ref_vit_encode_file(path: str, cfg: dict, image: np.ndarray) -> np.ndarray:
+    """The reference encoder loaded from a .sam3 file the way an application
+    loads it (sam3_weight_open, sam3_vit_load with the file, sam3_vit_build on
+    the CPU backend)."""
+    image = np.ascontiguousarray(image, np.float32)
+    gs = cfg["img_size"] // cfg["patch_size"]
+    out = np.empty((gs * gs, cfg["embed_dim"]), np.float32)
+    rc = ref().ref_vit_encode_file(path.encode(), cfg["img_size"], cfg["patch_size"], cfg["embed_dim"],
+                                   cfg["depth"], cfg["n_heads"], cfg["window_size"], cfg["mlp_dim"],
+                                   _p(image), _p(out))
+    if rc != 0:
+        raise RuntimeError(f"ref_vit_encode_file failed rc={rc}")
+    return out

@@ -77,6 +77,9 @@ const char* sam3cu_strerror(int s) {
     case SAM3CU_EDTYPE2: return "unsupported dtype combination";
     case SAM3CU_ENOMEM2: return "device allocation failed";
     case SAM3CU_ESCRATCH: return "request exceeds the fixed static scratch buffer";
+    case SAM3CU_EIO: return "I/O error";
+    case SAM3CU_EMODEL: return "malformed .sam3 weight file or missing / mis-shaped tensor";
+    case SAM3CU_ENOENT: return "tensor not in the weight file";
     default: return "unknown status";
   }
 }

@@ -36,6 +36,7 @@
 #include "devbuf.cuh"
 #include "gemm_sm100.cuh"
 #include "misc.cuh"
+#include "sam3_file.h"
 #include "sam3cu_internal.h"
 
 namespace s3 {
@@ -58,6 +59,25 @@ struct Linear {
 struct Block {
   DevBuf ln1_w, ln1_b, ln2_w, ln2_b;
   Linear qkv, proj, fc1, fc2;
+};
+
+// One weight as the host holds it: up to three parts of n elements each
+// (the q, k, v tensors fuse_3 concatenates, image_encoder.c:223-265), each
+// in one reference dtype (F32, F16, BF16 or Q8_0).  p == nullptr: zeros.
+struct WPart {
+  const void* p = nullptr;
+  int dt = kF32;
+};
+struct WSrc {
+  WPart part[3];
+  int nparts = 1;
+  int64_t n = 0;
+};
+struct VitSrc {
+  WSrc patch_w, patch_b, pos_raw, ln_pre_w, ln_pre_b;
+  struct BlockSrc {
+    WSrc ln1_w, ln1_b, qkv_w, qkv_b, proj_w, proj_b, ln2_w, ln2_b, fc1_w, fc1_b, fc2_w, fc2_b;
+  } blocks[kMaxLayers];
 };
 
 }  // namespace
@@ -104,43 +124,108 @@ namespace {
 
 int ck(cudaError_t e) { return e == cudaSuccess ? kOk : kErrCuda; }
 
-// Upload host f32 [n] to a new device buffer as f32.
-int upload_f32(DevBuf& d, const float* h, size_t n, cudaStream_t st) {
-  if (!d.alloc(n * 4)) return kErrNoMem;
-  if (!h) return ck(cudaMemsetAsync(d.p, 0, n * 4, st));
-  return ck(cudaMemcpyAsync(d.p, h, n * 4, cudaMemcpyHostToDevice, st));
+size_t dt_bytes(int dt, int64_t n) {
+  switch (dt) {
+    case kF32: return static_cast<size_t>(n) * 4;
+    case kF16:
+    case kBF16: return static_cast<size_t>(n) * 2;
+    case kQ8: return static_cast<size_t>((n + 31) / 32) * 36;
+    default: return 0;
+  }
 }
 
-// Upload host f32 [N,K] (row pitch K) to a device [N, ldk] 16-bit matrix
+// Stage a weight as F32 on the device.  The host bytes go up as stored and
+// are converted there: F16/BF16 are widened, Q8_0 blocks dequantised
+// (sam3_q8_dequantize, quant.c:134-151).  Parts land back to back, which is
+// fuse_3's concatenation (image_encoder.c:223-265).
+int stage_f32(DevBuf& d, const WSrc& s, cudaStream_t st) {
+  const int64_t total = s.n * s.nparts;
+  if (!d.alloc(static_cast<size_t>(total) * 4)) return kErrNoMem;
+  for (int i = 0; i < s.nparts; ++i) {
+    const WPart& p = s.part[i];
+    float* dst = d.as<float>() + i * s.n;
+    if (!p.p) {
+      if (cudaMemsetAsync(dst, 0, static_cast<size_t>(s.n) * 4, st) != cudaSuccess) return kErrCuda;
+      continue;
+    }
+    if (p.dt == kF32) {
+      if (cudaMemcpyAsync(dst, p.p, static_cast<size_t>(s.n) * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return kErrCuda;
+      continue;
+    }
+    const size_t nb = dt_bytes(p.dt, s.n);
+    if (!nb) return kErrDtype;
+    DevBuf raw;
+    if (!raw.alloc(nb)) return kErrNoMem;
+    if (cudaMemcpyAsync(raw.p, p.p, nb, cudaMemcpyHostToDevice, st) != cudaSuccess) return kErrCuda;
+    const int rc = p.dt == kQ8 ? sam3cu_q8_dequantize(raw.p, dst, s.n, st)
+                               : launch_cast(raw.p, p.dt, dst, kF32, s.n, st);
+    if (rc) return rc;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return kErrCuda;  // raw is freed on scope exit
+  }
+  return kOk;
+}
+
+// Upload a weight to a new device buffer as f32.
+int upload_f32(DevBuf& d, const WSrc& s, cudaStream_t st) {
+  const int rc = stage_f32(d, s, st);
+  return rc ? rc : ck(cudaStreamSynchronize(st));
+}
+
+// Upload a host f32 table [n].
+int upload_f32(DevBuf& d, const float* h, size_t n, cudaStream_t st) {
+  WSrc s;
+  s.part[0].p = h;
+  s.n = static_cast<int64_t>(n);
+  return upload_f32(d, s, st);
+}
+
+// Upload a weight [N,K] (row pitch K) to a device [N, ldk] 16-bit matrix
 // (zero-padded columns K..ldk).
-int upload_w16(DevBuf& d, const float* h, int N, int K, int ldk, int dt, cudaStream_t st) {
-  DevBuf tmp;
-  if (!tmp.alloc(static_cast<size_t>(N) * ldk * 4)) return kErrNoMem;
+int upload_w16(DevBuf& d, const WSrc& s, int N, int K, int ldk, int dt, cudaStream_t st) {
+  DevBuf tmp, pad;
+  int rc = stage_f32(tmp, s, st);
+  if (rc) return rc;
+  const DevBuf* src = &tmp;
   if (ldk != K) {
-    if (cudaMemsetAsync(tmp.p, 0, tmp.bytes, st) != cudaSuccess) return kErrCuda;
-    if (cudaMemcpy2DAsync(tmp.p, static_cast<size_t>(ldk) * 4, h, static_cast<size_t>(K) * 4,
-                          static_cast<size_t>(K) * 4, N, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    if (!pad.alloc(static_cast<size_t>(N) * ldk * 4)) return kErrNoMem;
+    if (cudaMemsetAsync(pad.p, 0, pad.bytes, st) != cudaSuccess) return kErrCuda;
+    if (cudaMemcpy2DAsync(pad.p, static_cast<size_t>(ldk) * 4, tmp.p, static_cast<size_t>(K) * 4,
+                          static_cast<size_t>(K) * 4, N, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return kErrCuda;
-  } else if (cudaMemcpyAsync(tmp.p, h, tmp.bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
-    return kErrCuda;
+    src = &pad;
   }
   if (!d.alloc(static_cast<size_t>(N) * ldk * 2)) return kErrNoMem;
-  int rc = launch_cast(tmp.p, kF32, d.p, dt, static_cast<int64_t>(N) * ldk, st);
+  rc = launch_cast(src->p, kF32, d.p, dt, static_cast<int64_t>(N) * ldk, st);
   if (rc) return rc;
-  return ck(cudaStreamSynchronize(st));  // tmp is freed on return
+  return ck(cudaStreamSynchronize(st));  // tmp / pad are freed on return
 }
 
-int upload_linear(Linear& L, const float* w, const float* b, int N, int K, int wdtype, cudaStream_t st) {
+int upload_linear(Linear& L, const WSrc& w, const WSrc& b, int N, int K, int wdtype, cudaStream_t st) {
   L.N = N;
   L.K = K;
-  int rc = upload_f32(L.bias, b, N, st);
+  int rc = upload_f32(L.bias, b, st);
   if (rc) return rc;
   if (wdtype == SAM3CU_Q8_0) {
-    DevBuf tmp, blocks;
+    DevBuf blocks;
     const int64_t n = static_cast<int64_t>(N) * K;
-    if (!tmp.alloc(n * 4) || !blocks.alloc((n / 32) * 36)) return kErrNoMem;
-    if (cudaMemcpyAsync(tmp.p, w, n * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) return kErrCuda;
-    if ((rc = launch_q8_quantize(tmp.as<float>(), blocks.p, n, st))) return rc;
+    if (!blocks.alloc((n / 32) * 36)) return kErrNoMem;
+    bool all_q8 = w.n % 32 == 0;
+    for (int i = 0; i < w.nparts; ++i) all_q8 = all_q8 && w.part[i].p && w.part[i].dt == kQ8;
+    if (all_q8) {
+      // already Q8_0 (a quantised .sam3 file): the blocks go up as stored and
+      // are only repacked; nothing is requantised
+      const size_t pb = dt_bytes(kQ8, w.n);
+      for (int i = 0; i < w.nparts; ++i)
+        if (cudaMemcpyAsync(static_cast<uint8_t*>(blocks.p) + i * pb, w.part[i].p, pb, cudaMemcpyHostToDevice,
+                            st) != cudaSuccess)
+          return kErrCuda;
+    } else {
+      DevBuf tmp;
+      if ((rc = stage_f32(tmp, w, st))) return rc;
+      if ((rc = launch_q8_quantize(tmp.as<float>(), blocks.p, n, st))) return rc;
+      if ((rc = ck(cudaStreamSynchronize(st)))) return rc;
+    }
     if (!L.q.alloc(n) || !L.sc.alloc((n / 32) * 4)) return kErrNoMem;
     if ((rc = launch_q8_repack(blocks.p, L.q.as<int8_t>(), L.sc.as<float>(), N, K, st))) return rc;
     // f16 activations: scales shifted per row into f16's normal range for the
@@ -320,7 +405,7 @@ void host_rope_table(int n_pos, int grid_w, int hd, float scale, std::vector<flo
     }
 }
 
-int vit_setup(sam3cu_vit* v, const sam3cu_vit_weights* w) {
+int vit_setup(sam3cu_vit* v, const VitSrc& w) {
   const sam3cu_vit_config& c = v->c;
   const int e = c.embed_dim, ps = c.patch_size, ws = c.window_size;
   cudaStream_t st = v->stream;
@@ -365,31 +450,36 @@ int vit_setup(sam3cu_vit* v, const sam3cu_vit_weights* w) {
   pair_major(np, w2r.data());
   if ((rc = upload_f32(v->rope_glo, tab.data(), tab.size(), st))) return rc;
   if ((rc = cudaStreamSynchronize(st) == cudaSuccess ? kOk : kErrCuda)) return rc;
-  // tiled pos-embed in window order (tile_pos_embed, image_encoder.c:167-218)
+  // tiled pos-embed in window order (tile_pos_embed, image_encoder.c:167-218):
+  // row r takes raw row 1 + (py % 24) * 24 + (px % 24), gathered on device
   {
-    std::vector<float> pos(static_cast<size_t>(np) * e);
+    std::vector<int> src_row(np);
     for (int r = 0; r < np; ++r) {
       const int rp = w2r[r], py = rp / gs, px = rp % gs;
-      const float* src = w->pos_raw + static_cast<size_t>(1 + (py % 24) * 24 + (px % 24)) * e;
-      memcpy(&pos[static_cast<size_t>(r) * e], src, e * 4);
+      src_row[r] = 1 + (py % 24) * 24 + (px % 24);
     }
-    if ((rc = upload_f32(v->pos_win, pos.data(), pos.size(), st))) return rc;
+    DevBuf raw, map;
+    if ((rc = stage_f32(raw, w.pos_raw, st))) return rc;
+    if (!map.alloc(np * 4) || !v->pos_win.alloc(static_cast<size_t>(np) * e * 4)) return kErrNoMem;
+    if ((rc = ck(cudaMemcpyAsync(map.p, src_row.data(), np * 4, cudaMemcpyHostToDevice, st)))) return rc;
+    if ((rc = launch_gather_rows(raw.p, v->pos_win.p, np, e * 4, map.as<int>(), np, st))) return rc;
     if ((rc = ck(cudaStreamSynchronize(st)))) return rc;
   }
-  if ((rc = upload_f32(v->ln_pre_w, w->ln_pre_w, e, st))) return rc;
-  if ((rc = upload_f32(v->ln_pre_b, w->ln_pre_b, e, st))) return rc;
-  // patch embedding as a GEMM: W [e, ps*ps*3] OHWI, K padded to kpad.
-  // It always runs with 16-bit weights (the reference's conv weight stays
-  // F32 in a Q8 file: the converter quantises only 2-D linears).
+  if ((rc = upload_f32(v->ln_pre_w, w.ln_pre_w, st))) return rc;
+  if ((rc = upload_f32(v->ln_pre_b, w.ln_pre_b, st))) return rc;
+  // patch embedding as a GEMM: W [e, ps*ps*3] OHWI, K padded to kpad.  It
+  // always runs with 16-bit weights; a Q8_0 patch weight (the converter
+  // quantises every float tensor of >= 1024 elements, cli_convert.c:340-352)
+  // is dequantised on upload.
   v->patch.N = e;
   v->patch.K = v->kpad;
-  if ((rc = upload_f32(v->patch.bias, w->patch_b, e, st))) return rc;
-  if ((rc = upload_w16(v->patch.w, w->patch_w, e, ps * ps * 3, v->kpad, v->act, st))) return rc;
+  if ((rc = upload_f32(v->patch.bias, w.patch_b, st))) return rc;
+  if ((rc = upload_w16(v->patch.w, w.patch_w, e, ps * ps * 3, v->kpad, v->act, st))) return rc;
   for (int i = 0; i < c.depth; ++i) {
-    const sam3cu_vit_block_weights& bw = w->blocks[i];
+    const VitSrc::BlockSrc& bw = w.blocks[i];
     Block& B = v->blocks[i];
-    if ((rc = upload_f32(B.ln1_w, bw.ln1_w, e, st)) || (rc = upload_f32(B.ln1_b, bw.ln1_b, e, st)) ||
-        (rc = upload_f32(B.ln2_w, bw.ln2_w, e, st)) || (rc = upload_f32(B.ln2_b, bw.ln2_b, e, st)))
+    if ((rc = upload_f32(B.ln1_w, bw.ln1_w, st)) || (rc = upload_f32(B.ln1_b, bw.ln1_b, st)) ||
+        (rc = upload_f32(B.ln2_w, bw.ln2_w, st)) || (rc = upload_f32(B.ln2_b, bw.ln2_b, st)))
       return rc;
     if ((rc = upload_linear(B.qkv, bw.qkv_w, bw.qkv_b, 3 * e, e, v->wdtype, st))) return rc;
     if ((rc = upload_linear(B.proj, bw.proj_w, bw.proj_b, e, e, v->wdtype, st))) return rc;
@@ -411,21 +501,14 @@ int vit_setup(sam3cu_vit* v, const sam3cu_vit_weights* w) {
   return ck(cudaStreamSynchronize(st));
 }
 
-}  // namespace
-}  // namespace s3
 
-using namespace s3;
-
-extern "C" {
-
-sam3cu_vit* sam3cu_vit_create(const sam3cu_vit_config* cfg, const sam3cu_vit_weights* w, int weight_dtype,
-                              int max_batch, int* status) {
-  int st_dummy;
-  int* status_p = status ? status : &st_dummy;
+sam3cu_vit* vit_create(const sam3cu_vit_config* cfg, const VitSrc& w, int weight_dtype, int max_batch,
+                       int* status_p) {
   *status_p = kOk;
-  if (!cfg || !w || max_batch <= 0 || cfg->depth < 0 || cfg->depth > kMaxLayers || cfg->n_heads <= 0 ||
-      cfg->embed_dim / cfg->n_heads != 64 || cfg->embed_dim % 64 || cfg->mlp_dim % 64 ||
-      cfg->img_size % cfg->patch_size || (cfg->img_size / cfg->patch_size) % cfg->window_size) {
+  if (!cfg || max_batch <= 0 || cfg->depth < 0 || cfg->depth > kMaxLayers || cfg->n_heads <= 0 ||
+      cfg->embed_dim / cfg->n_heads != 64 || cfg->embed_dim % 64 || cfg->mlp_dim % 64 || cfg->patch_size <= 0 ||
+      cfg->window_size <= 0 || cfg->img_size % cfg->patch_size ||
+      (cfg->img_size / cfg->patch_size) % cfg->window_size) {
     *status_p = SAM3CU_EINVAL;
     return nullptr;
   }
@@ -450,6 +533,168 @@ sam3cu_vit* sam3cu_vit_create(const sam3cu_vit_config* cfg, const sam3cu_vit_wei
     return nullptr;
   }
   return v.release();
+}
+
+// Tensor names of the reference's ViT weights (image_encoder.c:155, 346-452).
+#define VIT_P "detector_model.vision_encoder.backbone."
+
+// A file tensor as a weight part, checked to hold n elements (the reference
+// sam3_vit_load does not check shapes; a mis-sized tensor here is an error).
+int file_part(const Sam3File& f, const char* name, int64_t n, bool optional, WPart& out) {
+  const Sam3FileDesc* d = f.find(name);
+  if (!d) return optional ? kOk : SAM3CU_EMODEL;
+  if (Sam3File::numel(d) != n) return SAM3CU_EMODEL;
+  const int dt = static_cast<int>(d->dtype);
+  if (dt != kF32 && dt != kF16 && dt != kBF16 && dt != kQ8) return SAM3CU_EDTYPE;
+  if (d->data_size < dt_bytes(dt, n)) return SAM3CU_EMODEL;
+  out.p = f.tensor_data(d);
+  out.dt = dt;
+  return kOk;
+}
+
+int file_src(const Sam3File& f, const char* name, int64_t n, WSrc& s, bool optional = false) {
+  s = WSrc();
+  s.n = n;
+  return file_part(f, name, n, optional, s.part[0]);
+}
+
+// fuse_3 (image_encoder.c:223-265): q, k, v concatenated in that order
+int file_src3(const Sam3File& f, int layer, const char* what, int64_t n, WSrc& s) {
+  static const char* qkv[3] = {"q_proj", "k_proj", "v_proj"};
+  s = WSrc();
+  s.n = n;
+  s.nparts = 3;
+  char name[160];
+  for (int j = 0; j < 3; ++j) {
+    snprintf(name, sizeof(name), VIT_P "layers.%d.attention.%s.%s", layer, qkv[j], what);
+    const int rc = file_part(f, name, n, false, s.part[j]);
+    if (rc) return rc;
+  }
+  return kOk;
+}
+
+// The encoder shape a file holds, for callers that pass no config.
+int config_from_file(const Sam3File& f, sam3cu_vit_config& c) {
+  const Sam3FileDesc* pw = f.find(VIT_P "embeddings.patch_embeddings.projection.weight");
+  const Sam3FileDesc* fc1 = f.find(VIT_P "layers.0.mlp.fc1.weight");
+  if (!pw || !fc1 || pw->n_dims != 4 || fc1->n_dims != 2) return SAM3CU_EMODEL;
+  c.embed_dim = pw->dims[0];
+  c.patch_size = pw->dims[1];
+  c.mlp_dim = fc1->dims[0];
+  c.img_size = f.hdr->image_size;
+  c.n_heads = c.embed_dim / 64;
+  c.window_size = 24;
+  c.depth = 0;
+  char name[160];
+  for (int i = 0; i < kMaxLayers; ++i) {
+    snprintf(name, sizeof(name), VIT_P "layers.%d.layer_norm1.weight", i);
+    if (!f.find(name)) break;
+    c.depth = i + 1;
+  }
+  return kOk;
+}
+
+int vit_src_from_file(const Sam3File& f, const sam3cu_vit_config& c, VitSrc& src) {
+  const int64_t e = c.embed_dim, m = c.mlp_dim, ps = c.patch_size;
+  int rc;
+  if ((rc = file_src(f, VIT_P "embeddings.patch_embeddings.projection.weight", e * ps * ps * 3, src.patch_w)) ||
+      (rc = file_src(f, VIT_P "embeddings.patch_embeddings.projection.bias", e, src.patch_b, true)) ||
+      (rc = file_src(f, VIT_P "embeddings.position_embedding.weight", 577 * e, src.pos_raw)) ||
+      (rc = file_src(f, VIT_P "layer_norm.weight", e, src.ln_pre_w)) ||
+      (rc = file_src(f, VIT_P "layer_norm.bias", e, src.ln_pre_b)))
+    return rc;
+  char name[160];
+  auto one = [&](int i, const char* what, int64_t n, WSrc& s) {
+    snprintf(name, sizeof(name), VIT_P "layers.%d.%s", i, what);
+    return file_src(f, name, n, s);
+  };
+  for (int i = 0; i < c.depth; ++i) {
+    VitSrc::BlockSrc& b = src.blocks[i];
+    if ((rc = one(i, "layer_norm1.weight", e, b.ln1_w)) || (rc = one(i, "layer_norm1.bias", e, b.ln1_b)) ||
+        (rc = file_src3(f, i, "weight", e * e, b.qkv_w)) || (rc = file_src3(f, i, "bias", e, b.qkv_b)) ||
+        (rc = one(i, "attention.o_proj.weight", e * e, b.proj_w)) ||
+        (rc = one(i, "attention.o_proj.bias", e, b.proj_b)) ||
+        (rc = one(i, "layer_norm2.weight", e, b.ln2_w)) || (rc = one(i, "layer_norm2.bias", e, b.ln2_b)) ||
+        (rc = one(i, "mlp.fc1.weight", m * e, b.fc1_w)) || (rc = one(i, "mlp.fc1.bias", m, b.fc1_b)) ||
+        (rc = one(i, "mlp.fc2.weight", e * m, b.fc2_w)) || (rc = one(i, "mlp.fc2.bias", e, b.fc2_b)))
+      return rc;
+  }
+  return kOk;
+}
+
+WSrc f32src(const float* p, int64_t n) {
+  WSrc s;
+  s.part[0].p = p;
+  s.n = n;
+  return s;
+}
+
+}  // namespace
+}  // namespace s3
+
+using namespace s3;
+
+extern "C" {
+
+sam3cu_vit* sam3cu_vit_create(const sam3cu_vit_config* cfg, const sam3cu_vit_weights* w, int weight_dtype,
+                              int max_batch, int* status) {
+  int st_dummy;
+  int* status_p = status ? status : &st_dummy;
+  if (!cfg || !w || cfg->depth < 0 || cfg->depth > kMaxLayers) {
+    *status_p = SAM3CU_EINVAL;
+    return nullptr;
+  }
+  const int64_t e = cfg->embed_dim, m = cfg->mlp_dim, ps = cfg->patch_size;
+  VitSrc src;
+  src.patch_w = f32src(w->patch_w, e * ps * ps * 3);
+  src.patch_b = f32src(w->patch_b, e);
+  src.pos_raw = f32src(w->pos_raw, 577 * e);
+  src.ln_pre_w = f32src(w->ln_pre_w, e);
+  src.ln_pre_b = f32src(w->ln_pre_b, e);
+  for (int i = 0; i < cfg->depth; ++i) {
+    const sam3cu_vit_block_weights& b = w->blocks[i];
+    VitSrc::BlockSrc& d = src.blocks[i];
+    d.ln1_w = f32src(b.ln1_w, e);
+    d.ln1_b = f32src(b.ln1_b, e);
+    d.ln2_w = f32src(b.ln2_w, e);
+    d.ln2_b = f32src(b.ln2_b, e);
+    d.qkv_w = f32src(b.qkv_w, 3 * e * e);
+    d.qkv_b = f32src(b.qkv_b, 3 * e);
+    d.proj_w = f32src(b.proj_w, e * e);
+    d.proj_b = f32src(b.proj_b, e);
+    d.fc1_w = f32src(b.fc1_w, m * e);
+    d.fc1_b = f32src(b.fc1_b, m);
+    d.fc2_w = f32src(b.fc2_w, e * m);
+    d.fc2_b = f32src(b.fc2_b, e);
+  }
+  return vit_create(cfg, src, weight_dtype, max_batch, status_p);
+}
+
+sam3cu_vit* sam3cu_vit_create_from_sam3(const void* image, size_t bytes, const sam3cu_vit_config* cfg,
+                                        int weight_dtype, int max_batch, int* status) {
+  int st_dummy;
+  int* status_p = status ? status : &st_dummy;
+  Sam3File f;
+  int rc = f.open(image, bytes);
+  sam3cu_vit_config c{};
+  if (!rc) {
+    if (cfg) c = *cfg;
+    else rc = config_from_file(f, c);
+  }
+  if (!rc && (c.depth < 0 || c.depth > kMaxLayers || c.embed_dim <= 0 || c.patch_size <= 0)) rc = SAM3CU_EINVAL;
+  VitSrc src;
+  if (!rc) rc = vit_src_from_file(f, c, src);
+  if (rc) {
+    *status_p = rc;
+    return nullptr;
+  }
+  return vit_create(&c, src, weight_dtype, max_batch, status_p);
+}
+
+int sam3cu_vit_get_config(const sam3cu_vit* v, sam3cu_vit_config* cfg) {
+  if (!v || !cfg) return SAM3CU_EINVAL;
+  *cfg = v->c;
+  return kOk;
 }
 
 void sam3cu_vit_destroy(sam3cu_vit* v) {

@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libsam3cu.so")
 
 F32, F16, BF16, Q8_0 = 0, 1, 2, 5
 ACT_NONE, ACT_GELU_TANH = 0, 1
+EMODEL, ENOENT = -5, -109
 
 EXPORTS = (
     "sam3cu_init", "sam3cu_strerror", "sam3cu_last_device_error",
@@ -33,6 +34,7 @@ EXPORTS = (
     "sam3cu_tvit_mbconv_create", "sam3cu_tvit_mbconv_forward", "sam3cu_tvit_mbconv_destroy",
     "sam3cu_selftest_wait_timeout",
     "sam3cu_tinyvit_create", "sam3cu_tinyvit_encode", "sam3cu_tinyvit_grid", "sam3cu_tinyvit_destroy",
+    "sam3cu_sam3_check", "sam3cu_sam3_find", "sam3cu_vit_create_from_sam3", "sam3cu_vit_get_config",
 )
 
 # sizeof(struct sam3_cuda_backend): {enum type; ops*} + int device + void *impl
@@ -69,6 +71,12 @@ def lib():
         L.sam3cu_vit_create.restype = vp
         L.sam3cu_vit_create.argtypes = [vp, vp, i32, i32, C.POINTER(C.c_int)]
         L.sam3cu_vit_destroy.argtypes = [vp]
+        L.sam3cu_vit_create_from_sam3.restype = vp
+        L.sam3cu_vit_create_from_sam3.argtypes = [vp, C.c_size_t, vp, i32, i32, C.POINTER(C.c_int)]
+        L.sam3cu_vit_get_config.argtypes = [vp, vp]
+        L.sam3cu_sam3_check.argtypes = [vp, C.c_size_t, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]
+        L.sam3cu_sam3_find.argtypes = [vp, C.c_size_t, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                       C.POINTER(C.c_int), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
         L.sam3cu_vit_encode.argtypes = [vp, vp, i32, vp, i32]
         L.sam3cu_vit_encode_async.argtypes = [vp, vp, i32, vp]
         L.sam3cu_vit_stream.restype = vp
@@ -230,6 +238,37 @@ def conv2d_nhwc_noalloc(x, w, bias=None, stride=1, pad=0, out=None):
 
 
 # ------------------------------------------------------------------ ViT
+def _map_file(path) -> np.ndarray:
+    """A read-only uint8 view of a file (np.memmap), or of a bytes-like."""
+    if isinstance(path, (bytes, bytearray, memoryview, np.ndarray)):
+        return np.frombuffer(path, np.uint8) if not isinstance(path, np.ndarray) else path.view(np.uint8)
+    return np.memmap(path, np.uint8, mode="r")
+
+
+def sam3_check(path) -> tuple:
+    """sam3_weight_open's validation of a .sam3 image: (n_tensors, version)."""
+    image = _map_file(path)
+    n, v = C.c_uint32(0), C.c_uint32(0)
+    check(lib().sam3cu_sam3_check(image.ctypes.data, image.nbytes, C.byref(n), C.byref(v)),
+          "sam3cu_sam3_check")
+    return n.value, v.value
+
+
+def sam3_find(path, name: str) -> Optional[dict]:
+    """sam3_weight_find on a .sam3 image: dtype, dims, byte offset from the
+    start of the file and byte size; None if the tensor is absent."""
+    image = _map_file(path)
+    dt, nd, off, nb = C.c_int(0), C.c_int(0), C.c_uint64(0), C.c_uint64(0)
+    dims = (C.c_int * 4)()
+    rc = lib().sam3cu_sam3_find(image.ctypes.data, image.nbytes, name.encode(), C.byref(dt), C.byref(nd),
+                                dims, C.byref(off), C.byref(nb))
+    if rc == ENOENT:
+        return None
+    check(rc, "sam3cu_sam3_find")
+    return dict(dtype=dt.value, dims=tuple(dims[i] for i in range(nd.value)), offset=off.value,
+                nbytes=nb.value)
+
+
 class _Cfg(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("img_size", "patch_size", "embed_dim", "depth",
                                        "n_heads", "window_size", "mlp_dim")]
@@ -283,6 +322,31 @@ class VitEncoder:
         self.max_batch = max_batch
         gs = cfg["img_size"] // cfg["patch_size"]
         self.np = gs * gs
+
+    @classmethod
+    def from_sam3(cls, path, cfg: Optional[dict] = None, weight_dtype: int = BF16,
+                  max_batch: int = 1) -> "VitEncoder":
+        """sam3_weight_open + sam3_vit_load from a .sam3 file: the file is
+        memory-mapped and its tensors go to the device as stored (Q8_0
+        blocks repacked there, never requantised).  cfg None: the encoder
+        shape is read from the file."""
+        image = _map_file(path)
+        st = C.c_int(0)
+        c = C.byref(_Cfg(*(cfg[k] for k in CFG_KEYS))) if cfg is not None else None
+        h = lib().sam3cu_vit_create_from_sam3(image.ctypes.data, image.nbytes, c, weight_dtype,
+                                              max_batch, C.byref(st))
+        del image
+        if not h:
+            check(st.value or -1, "sam3cu_vit_create_from_sam3")
+        self = cls.__new__(cls)
+        self.h = h
+        got = _Cfg()
+        check(lib().sam3cu_vit_get_config(h, C.byref(got)), "sam3cu_vit_get_config")
+        self.cfg = {k: getattr(got, k) for k in CFG_KEYS}
+        self.max_batch = max_batch
+        gs = self.cfg["img_size"] // self.cfg["patch_size"]
+        self.np = gs * gs
+        return self
 
     def close(self):
         if self.h:

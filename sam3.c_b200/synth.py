@@ -66,6 +66,33 @@ def round_weights(w: dict, fn) -> dict:
     return out
 
 
+VIT_PREFIX = "detector_model.vision_encoder.backbone."
+
+
+def vit_sam3_tensors(cfg: dict, w: dict, patch_bias: bool = True) -> list:
+    """The encoder weights as the tensors of a .sam3 file: (name, array)
+    under the reference's names (image_encoder.c:155, 346-452), with the
+    fused QKV split back into q_proj / k_proj / v_proj."""
+    e = cfg["embed_dim"]
+    P = VIT_PREFIX
+    t = [(P + "embeddings.patch_embeddings.projection.weight", w["patch_w"])]
+    if patch_bias:
+        t.append((P + "embeddings.patch_embeddings.projection.bias", w["patch_b"]))
+    t += [(P + "embeddings.position_embedding.weight", w["pos_raw"]),
+          (P + "layer_norm.weight", w["ln_pre_w"]), (P + "layer_norm.bias", w["ln_pre_b"])]
+    for i, b in enumerate(w["blocks"]):
+        L = f"{P}layers.{i}."
+        t += [(L + "layer_norm1.weight", b["ln1_w"]), (L + "layer_norm1.bias", b["ln1_b"])]
+        for j, q in enumerate(("q_proj", "k_proj", "v_proj")):
+            t += [(L + f"attention.{q}.weight", b["qkv_w"][j * e:(j + 1) * e]),
+                  (L + f"attention.{q}.bias", b["qkv_b"][j * e:(j + 1) * e])]
+        t += [(L + "attention.o_proj.weight", b["proj_w"]), (L + "attention.o_proj.bias", b["proj_b"]),
+              (L + "layer_norm2.weight", b["ln2_w"]), (L + "layer_norm2.bias", b["ln2_b"]),
+              (L + "mlp.fc1.weight", b["fc1_w"]), (L + "mlp.fc1.bias", b["fc1_b"]),
+              (L + "mlp.fc2.weight", b["fc2_w"]), (L + "mlp.fc2.bias", b["fc2_b"])]
+    return t
+
+
 # ---------------------------------------------------------------- TinyViT
 TINYVIT_21M = dict(img_size=1008, n_layers=4, embed_dims=(96, 192, 384, 576), depths=(2, 2, 6, 2),
                    num_heads=(3, 6, 12, 18), window_sizes=(7, 7, 14, 7), embed_dim=1024, mlp_ratio=4)
