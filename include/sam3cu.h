@@ -464,6 +464,28 @@ SAM3CU_API int sam3cu_vit_profile(sam3cu_vit *vit, const float *images,
 				  int n_images, float *out, double *ms,
 				  int *counts);
 
+/* Launch kinds of sam3cu_vit_profile_detail. */
+enum sam3cu_prof_kind {
+	SAM3CU_PROF_PATCH = 0,        /* patch-embedding GEMM */
+	SAM3CU_PROF_QKV = 1,
+	SAM3CU_PROF_PROJ = 2,
+	SAM3CU_PROF_FC1 = 3,
+	SAM3CU_PROF_FC2 = 4,
+	SAM3CU_PROF_DEQUANT = 5,      /* Q8_0: a block's weights to 16-bit */
+	SAM3CU_PROF_ATTN_WINDOW = 6,
+	SAM3CU_PROF_ATTN_GLOBAL = 7,
+	SAM3CU_PROF_LAYERNORM = 8,
+	SAM3CU_PROF_OTHER = 9,
+	SAM3CU_PROF_KINDS = 10
+};
+
+/* As sam3cu_vit_profile with ms / counts of SAM3CU_PROF_KINDS entries, one
+ * per enum sam3cu_prof_kind (sam3cu_vit_profile sums kinds 0-5 as GEMM,
+ * 6-7 as attention).  No counterpart in the reference. */
+SAM3CU_API int sam3cu_vit_profile_detail(sam3cu_vit *vit, const float *images,
+					 int n_images, float *out, double *ms,
+					 int *counts);
+
 /* Kernel launches one encode of n_images enqueues. */
 SAM3CU_API int sam3cu_vit_launches_per_encode(sam3cu_vit *vit, int n_images);
 

@@ -44,7 +44,7 @@ constexpr int kPTmemCols = 2 * kPN;
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  const __grid_constant__ CUtensorMap tmap_o, GemmShape shp, EpiParams ep, uint32_t idesc,
-                 int epi_mode) {
+                 int epi_mode, int splits) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_out = smem + kPStages * kPStage;
@@ -60,8 +60,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int m_tiles = (shp.M + 2 * kPM - 1) / (2 * kPM);
   const int n_tiles = (shp.N + kPN - 1) / kPN;
-  const int num_tiles = m_tiles * n_tiles;
+  // split-K (splits > 1, reduce-add epilogue only): work item t covers
+  // output tile t / splits and K slice t % splits; slice 0 adds the bias
+  const int num_tiles = m_tiles * n_tiles * splits;
   const int k_iters = (shp.K + kPK - 1) / kPK;
+  auto k_begin = [&](int tile) { return (tile % splits) * k_iters / splits; };
+  auto k_end = [&](int tile) { return (tile % splits + 1) * k_iters / splits; };
   auto stage_a = [&](int s) { return smem + s * kPStage; };
   auto stage_b = [&](int s) { return smem + s * kPStage + kPTile; };
 
@@ -98,9 +102,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        const int m0 = (tile / n_tiles) * 2 * kPM + rank * kPM;
-        const int n0 = (tile % n_tiles) * kPN + rank * (kPN / 2);
-        for (int kt = 0; kt < k_iters; ++kt, ++it) {
+        const int mn = tile / splits;
+        const int m0 = (mn / n_tiles) * 2 * kPM + rank * kPM;
+        const int n0 = (mn % n_tiles) * kPN + rank * (kPN / 2);
+        for (int kt = k_begin(tile); kt < k_end(tile); ++kt, ++it) {
           const int s = it % kPStages;
           const uint32_t ph = (it / kPStages) & 1;
           if (!mbar_wait_warp(&empty_bar[s], ph ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
@@ -127,7 +132,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         if (!mbar_wait_warp(&acce_bar[acc], aph ^ 1, kErrAccFree, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kPN;
-        for (int kt = 0; kt < k_iters; ++kt, ++it) {
+        const int kt0 = k_begin(tile);
+        for (int kt = kt0; kt < k_end(tile); ++kt, ++it) {
           const int s = it % kPStages;
           const uint32_t ph = (it / kPStages) & 1;
           if (!mbar_wait_warp(&full_bar[s], ph, kErrTmaWait, abort_flag)) { ok = false; break; }
@@ -136,7 +142,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           const uint64_t bdesc = make_sdesc_sw128(smem_u32(stage_b(s)));
 #pragma unroll
           for (int k = 0; k < kPK / kUmmaK; ++k)
-            umma_ss_pair_warp(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+            umma_ss_pair_warp(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt != kt0 || k) ? 1u : 0u);
           // free the stage in both CTAs once these MMAs have read it
           umma_commit_pair_warp(mapa_shared(smem_u32(&empty_bar[s]), 0));
           umma_commit_pair_warp(mapa_shared(smem_u32(&empty_bar[s]), 1));
@@ -157,8 +163,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const uint32_t lead_acce1 = mapa_shared(smem_u32(&acce_bar[1]), 0);
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
-      const int m0 = (tile / n_tiles) * 2 * kPM + rank * kPM;
-      const int n0 = (tile % n_tiles) * kPN;
+      const int mn = tile / splits;
+      const int m0 = (mn / n_tiles) * 2 * kPM + rank * kPM;
+      const int n0 = (mn % n_tiles) * kPN;
+      const bool first_slice = tile % splits == 0;
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       int got = 0;
@@ -181,11 +189,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
         if (epi_mode == kEpiDirect) {
           if (row < shp.M) {
-            epilogue_math(ep, v, row, col0, shp.N);
+            epilogue_math(ep, v, row, col0, shp.N, first_slice);
             epilogue_store_direct(ep, v, row, col0, shp.N);
           }
         } else {
-          epilogue_math(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N);
+          epilogue_math(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N, first_slice);
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
           stage_chunk(my_stage, v, lane, epi_mode == kEpiTmaAdd ? kOutF32 : ep.out_type);
@@ -223,6 +231,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 
 }  // namespace
 
+// K slices per output tile for the pair kernel.  Only an epilogue that adds
+// into an F32 destination (TMA reduce-add) with nothing non-linear after the
+// bias can take partial sums; then the count (at most 4, each slice at
+// least 16 K-iterations: shorter slices measured slower) that best fills the
+// last wave of `pairs` CTA pairs is used, the smaller on a tie.  Example,
+// M = 5184 (one image), N = 1024: 84 tiles fill 57% of two waves of 74
+// pairs; fc2 (K = 4736) takes 4 slices (91%): 896 -> 1025 TFLOP/s.  The
+// partial sums reach the destination in no fixed order, so such results are
+// reproducible to F32 rounding, not bit for bit.
+int pair_splits(const GemmShape& shp, bool additive, int pairs) {
+  if (!additive || pairs <= 0) return 1;
+  static const int max_splits = [] {  // S3CU_GEMM_MAX_SPLITS caps it (measurements)
+    const char* e = getenv("S3CU_GEMM_MAX_SPLITS");
+    return e ? atoi(e) : 4;
+  }();
+  const long tiles = static_cast<long>((shp.M + 2 * kPM - 1) / (2 * kPM)) * ((shp.N + kPN - 1) / kPN);
+  const int k_iters = (shp.K + kPK - 1) / kPK;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= max_splits; ++s) {
+    if (s > 1 && k_iters / s < 16) break;
+    const long work = tiles * s;
+    const double eff = static_cast<double>(work) / (static_cast<double>((work + pairs - 1) / pairs) * pairs);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
 // Pair launch of the 16-bit linear; the caller has validated shapes and
 // alignment (launch_gemm).  Returns kOk, kErrTma or kErrLaunch.
 int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, GemmShape shp, const EpiParams& ep,
@@ -232,8 +271,9 @@ int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, Ge
   if (!make_tmap_2d(&ta, A, dt, 2, shp.M, shp.K, lda, kPM, kPK, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
   if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, kPN / 2, kPK, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
   const int m_tiles = (shp.M + 2 * kPM - 1) / (2 * kPM), n_tiles = (shp.N + kPN - 1) / kPN;
-  int pairs = m_tiles * n_tiles;
   const int cap = (max_ctas > 0 ? max_ctas : num_sms()) / 2;
+  const int splits = pair_splits(shp, mode == kEpiTmaAdd && ep.act == 0 && ep.rope_cols == 0, cap);
+  int pairs = m_tiles * n_tiles * splits;
   if (pairs > cap) pairs = cap;
   const uint32_t idesc = make_idesc(bf ? 1u : 0u, 2 * kPM, kPN);
   static bool attr = false;
@@ -241,7 +281,7 @@ int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, Ge
     cudaFuncSetAttribute(gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
     attr = true;
   }
-  gemm2_kernel<<<2 * pairs, kPThreads, kPSmem, stream>>>(ta, tb, to, shp, ep, idesc, mode);
+  gemm2_kernel<<<2 * pairs, kPThreads, kPSmem, stream>>>(ta, tb, to, shp, ep, idesc, mode, splits);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 

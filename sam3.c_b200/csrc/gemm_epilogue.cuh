@@ -37,7 +37,7 @@ __device__ __forceinline__ uint32_t pack_f16(float a, float b) {
 // Bias, activation and RoPE on 32 consecutive columns [col0, col0+32) of
 // one output row, in registers.
 __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32], int row, int col0,
-                                              int N) {
+                                              int N, bool add_bias = true) {
   const bool full = col0 + 32 <= N;
   if (ep.col_scale) {
     if (full) {
@@ -56,7 +56,7 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32
         if (col0 + j < N) v[j] *= __ldg(ep.col_scale + col0 + j);
     }
   }
-  if (ep.bias) {
+  if (ep.bias && add_bias) {
     if (full) {
       const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col0);
 #pragma unroll

@@ -361,14 +361,15 @@ int g_num_sms = 0;
 
 // 2-SM pair tiles (gemm2_sm100.cu) for the 16-bit path unless SAM3CU_GEMM=1sm
 // or the problem is too small to keep the SMs busy with 256x256 tiles.
-bool use_pair_gemm(const GemmShape& shp) {
+bool use_pair_gemm(const GemmShape& shp, bool additive) {
   static const int mode = [] {
     const char* e = getenv("SAM3CU_GEMM");
     return e && strcmp(e, "1sm") == 0 ? 0 : 1;
   }();
   if (!mode) return false;
-  const long pairs = static_cast<long>((shp.M + 255) / 256) * ((shp.N + 255) / 256);
-  return pairs >= num_sms();  // at least two waves of pairs
+  const long pairs = static_cast<long>((shp.M + 255) / 256) * ((shp.N + 255) / 256) *
+                     pair_splits(shp, additive, num_sms() / 2);
+  return pairs >= num_sms();  // at least two waves of pairs (K slices included)
 }
 std::atomic<uint64_t> g_launches{0};
 
@@ -438,7 +439,7 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       mode = kEpiDirect;  // e.g. an output base that is not 16-byte aligned
   }
   count_launches(1);
-  if (!q8 && !f32in && use_pair_gemm(shp)) {
+  if (!q8 && !f32in && use_pair_gemm(shp, mode == kEpiTmaAdd && ep.act == 0 && ep.rope_cols == 0)) {
     if (ldw % 8 != 0) return kErrShape;
     return launch_gemm_pair(A, lda, W, ldw, bf, shp, ep, to, mode, stream, max_ctas);
   }

@@ -115,6 +115,10 @@ struct GemmCfg {
                                     1024 /*align*/ + 256 /*barriers*/;
 };
 
+// K slices per output tile the pair kernel uses (1 unless `additive`: an
+// in-place F32 reduce-add epilogue without activation or RoPE).
+int pair_splits(const GemmShape& shp, bool additive, int pairs);
+
 // 2-SM pair launch (gemm2_sm100.cu); shapes validated by launch_gemm.
 int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, GemmShape shp, const EpiParams& ep,
                      const CUtensorMap& to, int mode, cudaStream_t stream, int max_ctas);

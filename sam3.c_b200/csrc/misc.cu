@@ -392,10 +392,8 @@ namespace {
 // ((1024 + u) as f16 bits 0x64uu, minus 1152 exactly, times the scale
 // rounded once); mode 0 (bf16) and 2 (f16, any scales): f32 arithmetic and
 // one rounding.
-__global__ void q8_dequant_w16_kernel(const uint4* __restrict__ q, const float* __restrict__ sc,
-                                      uint4* __restrict__ w, int N, int K16, int64_t total, int f16) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= total) return;
+__device__ __forceinline__ void q8_dequant_w16_one(const uint4* __restrict__ q, const float* __restrict__ sc,
+                                                   uint4* __restrict__ w, int N, int K16, int64_t i, int f16) {
   const int n = static_cast<int>(i / K16), k16 = static_cast<int>(i - static_cast<int64_t>(n) * K16);
   const float s = __ldg(sc + static_cast<int64_t>(k16 >> 1) * N + n);
   const uint4 raw = __ldg(q + i);
@@ -436,6 +434,28 @@ __global__ void q8_dequant_w16_kernel(const uint4* __restrict__ q, const float* 
   w[2 * i + 1] = make_uint4(out[4], out[5], out[6], out[7]);
 }
 
+__global__ void q8_dequant_w16_kernel(const uint4* __restrict__ q, const float* __restrict__ sc,
+                                      uint4* __restrict__ w, int N, int K16, int64_t total, int f16) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < total) q8_dequant_w16_one(q, sc, w, N, K16, i, f16);
+}
+
+// Several weights in one launch: thread i works on the job whose range of
+// 16-element groups holds it.
+__global__ void q8_dequant_w16_multi_kernel(Q8DequantJobs jobs, int f16) {
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+#pragma unroll 1
+  for (int j = 0; j < jobs.n; ++j) {
+    const int64_t total = static_cast<int64_t>(jobs.job[j].N) * (jobs.job[j].K / 16);
+    if (i < total) {
+      q8_dequant_w16_one(reinterpret_cast<const uint4*>(jobs.job[j].q), jobs.job[j].sc,
+                         static_cast<uint4*>(jobs.job[j].w), jobs.job[j].N, jobs.job[j].K / 16, i, f16);
+      return;
+    }
+    i -= total;
+  }
+}
+
 }  // namespace
 
 int launch_q8_dequant_w16(const int8_t* q, const float* sc, void* w, int N, int K, int f16, cudaStream_t st) {
@@ -445,6 +465,20 @@ int launch_q8_dequant_w16(const int8_t* q, const float* sc, void* w, int N, int 
   count_launches(1);
   q8_dequant_w16_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const uint4*>(q), sc, static_cast<uint4*>(w), N, K / 16, total, f16);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int launch_q8_dequant_w16_multi(const Q8DequantJobs& jobs, int f16, cudaStream_t st) {
+  if (jobs.n <= 0 || jobs.n > Q8DequantJobs::kMax) return kErrShape;
+  int64_t total = 0;
+  for (int j = 0; j < jobs.n; ++j) {
+    const Q8DequantJob& d = jobs.job[j];
+    if (d.N <= 0 || d.K % 32 || (reinterpret_cast<uintptr_t>(d.q) & 15) || (reinterpret_cast<uintptr_t>(d.w) & 15))
+      return kErrShape;
+    total += static_cast<int64_t>(d.N) * (d.K / 16);
+  }
+  count_launches(1);
+  q8_dequant_w16_multi_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(jobs, f16);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
@@ -477,6 +511,26 @@ int launch_cast(const void* x, int tin, void* y, int tout, int64_t n, cudaStream
   S3_CAST(kF32, kBF16) S3_CAST(kF32, kF16) S3_CAST(kBF16, kF32) S3_CAST(kF16, kF32) S3_CAST(kF32, kF32)
 #undef S3_CAST
   return kErrDtype;
+}
+
+namespace {
+// One thread waits until %globaltimer has advanced by `ns` (bounded by
+// construction): parks a stream while the host enqueues work behind it.
+__global__ void gpu_sleep_kernel(unsigned long long ns) {
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 >= ns) break;
+    __nanosleep(10000);
+  }
+}
+}  // namespace
+
+int launch_gpu_sleep(unsigned long long ns, cudaStream_t st) {
+  gpu_sleep_kernel<<<1, 1, 0, st>>>(ns);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 }  // namespace s3

@@ -18,11 +18,28 @@ int launch_q8_row_shift(float* sc, float* col_scale, int N, int K, cudaStream_t 
 // 16-bit W [N, K] from int8 q [N, K] and scales [K/32, N].  mode: 0 bf16,
 // 1 f16 from row-shifted scales (half2 arithmetic), 2 f16 from any scales
 int launch_q8_dequant_w16(const int8_t* q, const float* sc, void* w, int N, int K, int mode, cudaStream_t st);
+// The same for up to four weights in one launch (one pass over all of them).
+struct Q8DequantJob {
+  const int8_t* q;
+  const float* sc;
+  void* w;
+  int N, K;
+};
+struct Q8DequantJobs {
+  static constexpr int kMax = 4;
+  Q8DequantJob job[kMax];
+  int n;
+};
+int launch_q8_dequant_w16_multi(const Q8DequantJobs& jobs, int mode, cudaStream_t st);
 int launch_cast(const void* x, int tin, void* y, int tout, int64_t n, cudaStream_t st);
 // im2col of a dense KxK conv (zero padding) into 16-bit columns (row
 // (img, oy, ox), column (ky, kx, c), zero-filled to kpad); chw: planar CHW
 // input per image, else NHWC; a 16-byte path for 16-bit NHWC, C % 8 == 0
 int launch_conv_im2col(const void* x, int tin, bool chw, void* a, int tout, int B, int H, int W, int C, int k,
                        int stride, int pad, int kpad, cudaStream_t st);
+
+// Park the stream for `ns` nanoseconds of device time (measurement runs: the
+// host enqueues the launches being timed meanwhile, so no host gap is timed).
+int launch_gpu_sleep(unsigned long long ns, cudaStream_t st);
 
 }  // namespace s3

@@ -98,7 +98,7 @@ struct sam3cu_vit {
   s3::DevBuf raster_to_win;                      // int [np]
   // activations
   s3::DevBuf x, xn, qkv, ao, h;
-  s3::DevBuf wq;  // Q8_0 weights: 16-bit dequantised W of the current linear
+  s3::DevBuf wq;  // Q8_0 weights: 16-bit dequantised W of the current block's four linears
   // image / feature staging for host-buffer encodes: two sets, so that one
   // chunk's copies overlap the next chunk's compute (img2/out2 on demand)
   s3::DevBuf img, out, img2, out2;
@@ -247,21 +247,58 @@ EpiParams epi_default() {
 // at most 9.7 MB, so it stays in L2) and the 16-bit GEMM runs on that: a
 // dequantiser inside the GEMM would redo the conversion for every one of
 // the M/256 row tiles.  The HBM copy of W stays int8.
-int run_linear(sam3cu_vit* v, const Linear& L, const void* a, int lda, int M, const EpiParams& ep_in) {
+// w16: for a Q8_0 linear, its dequantised 16-bit W (dequant_block).
+int run_linear(sam3cu_vit* v, const Linear& L, const void* a, int lda, int M, const EpiParams& ep_in,
+               const void* w16 = nullptr) {
   GemmShape shp{M, L.N, L.K};
   if (L.q.p) {
-    int rc = launch_q8_dequant_w16(L.q.as<int8_t>(), L.sc.as<float>(), v->wq.p, L.N, L.K, v->act == kF16 ? 1 : 0,
-                                   v->stream);
-    if (rc) return rc;
+    if (!w16) return kErrShape;
     EpiParams ep = ep_in;
     ep.col_scale = L.cs.as<float>();  // undoes the per-row scale shift
-    return launch_gemm(a, lda, v->wq.p, L.K, nullptr, nullptr, v->act, shp, ep, v->stream, 0);
+    return launch_gemm(a, lda, w16, L.K, nullptr, nullptr, v->act, shp, ep, v->stream, 0);
   }
   const EpiParams& ep = ep_in;
   return launch_gemm(a, lda, L.w.p, L.K, nullptr, nullptr, v->act, shp, ep, v->stream, 0);
 }
 
-enum ProfKind { kProfGemm = 0, kProfAttn = 1, kProfLn = 2, kProfOther = 3, kProfKinds = 4 };
+// Q8_0 weights: the four linears of a block are dequantised in one launch at
+// the start of the block into consecutive 16-bit slots of v->wq (27.8 MB at
+// the ViT-L sizes, so the GEMMs read them from L2); slot[k] = qkv, proj,
+// fc1, fc2.
+int dequant_block(sam3cu_vit* v, const Block& B, const void* (&slot)[4]) {
+  const Linear* L[4] = {&B.qkv, &B.proj, &B.fc1, &B.fc2};
+  Q8DequantJobs jobs;
+  jobs.n = 4;
+  uint8_t* p = static_cast<uint8_t*>(v->wq.p);
+  for (int k = 0; k < 4; ++k) {
+    jobs.job[k] = Q8DequantJob{L[k]->q.as<int8_t>(), L[k]->sc.as<float>(), p, L[k]->N, L[k]->K};
+    slot[k] = p;
+    p += static_cast<size_t>(L[k]->N) * L[k]->K * 2;
+  }
+  return launch_q8_dequant_w16_multi(jobs, v->act == kF16 ? 1 : 0, v->stream);
+}
+
+// Launch kinds of the profiling runs: the detailed kinds of
+// sam3cu_vit_profile_detail (enum sam3cu_prof_kind), summed into GEMM /
+// attention / LayerNorm / other for sam3cu_vit_profile.
+enum ProfKind {
+  kProfPatch = SAM3CU_PROF_PATCH,
+  kProfQkv = SAM3CU_PROF_QKV,
+  kProfProj = SAM3CU_PROF_PROJ,
+  kProfFc1 = SAM3CU_PROF_FC1,
+  kProfFc2 = SAM3CU_PROF_FC2,
+  kProfDequant = SAM3CU_PROF_DEQUANT,
+  kProfAttnWin = SAM3CU_PROF_ATTN_WINDOW,
+  kProfAttnGlob = SAM3CU_PROF_ATTN_GLOBAL,
+  kProfLn = SAM3CU_PROF_LAYERNORM,
+  kProfOther = SAM3CU_PROF_OTHER,
+  kProfKinds = SAM3CU_PROF_KINDS
+};
+int coarse_kind(int k) {
+  if (k <= kProfDequant) return 0;  // GEMM (the Q8_0 dequantisation included)
+  if (k <= kProfAttnGlob) return 1;
+  return k == kProfLn ? 2 : 3;
+}
 
 // Record an event after a launch of the given kind (profiling runs only).
 void tick(sam3cu_vit* v, int kind) {
@@ -297,7 +334,7 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
     ep.ldr = e;
     ep.res_row_period = np;
     if ((rc = run_linear(v, v->patch, acol, v->kpad, M, ep))) return rc;
-    tick(v, kProfGemm);
+    tick(v, kProfPatch);
   }
   if ((rc = launch_layernorm(v->x.p, kF32, v->x.p, kF32, v->ln_pre_w.as<float>(), v->ln_pre_b.as<float>(), M, e,
                              nullptr, 0, v->stream)))
@@ -309,6 +346,11 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
     const Block& B = v->blocks[i];
     const bool glob = is_global_block(i);
     const bool last = i == c.depth - 1;
+    const void* w16[4] = {nullptr, nullptr, nullptr, nullptr};
+    if (v->wdtype == SAM3CU_Q8_0) {
+      if ((rc = dequant_block(v, B, w16))) return rc;
+      tick(v, kProfDequant);
+    }
     if ((rc = launch_layernorm(v->x.p, kF32, v->xn.p, v->act, B.ln1_w.as<float>(), B.ln1_b.as<float>(), M, e,
                                nullptr, 0, v->stream)))
       return rc;
@@ -327,8 +369,8 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
         ep.rope_cs = v->rope_win.as<float2>();
         ep.rope_period = ws * ws;
       }
-      if ((rc = run_linear(v, B.qkv, v->xn.p, e, M, ep))) return rc;
-      tick(v, kProfGemm);
+      if ((rc = run_linear(v, B.qkv, v->xn.p, e, M, ep, w16[0]))) return rc;
+      tick(v, kProfQkv);
     }
     {
       const uint16_t* qkv = v->qkv.as<uint16_t>();
@@ -337,7 +379,7 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
       if ((rc = launch_attention(qkv, qkv + e, qkv + 2 * e, 3 * e, v->ao.p, e, v->act, groups, seq, c.n_heads, hd,
                                  v->stream)))
         return rc;
-      tick(v, kProfAttn);
+      tick(v, glob ? kProfAttnGlob : kProfAttnWin);
     }
     {
       EpiParams ep = epi_default();
@@ -347,8 +389,8 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
       ep.bias = B.proj.bias.as<float>();
       ep.residual = v->x.as<float>();
       ep.ldr = e;
-      if ((rc = run_linear(v, B.proj, v->ao.p, e, M, ep))) return rc;
-      tick(v, kProfGemm);
+      if ((rc = run_linear(v, B.proj, v->ao.p, e, M, ep, w16[1]))) return rc;
+      tick(v, kProfProj);
     }
     if ((rc = launch_layernorm(v->x.p, kF32, v->xn.p, v->act, B.ln2_w.as<float>(), B.ln2_b.as<float>(), M, e,
                                nullptr, 0, v->stream)))
@@ -361,8 +403,8 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
       ep.ldo = c.mlp_dim;
       ep.bias = B.fc1.bias.as<float>();
       ep.act = 1;
-      if ((rc = run_linear(v, B.fc1, v->xn.p, e, M, ep))) return rc;
-      tick(v, kProfGemm);
+      if ((rc = run_linear(v, B.fc1, v->xn.p, e, M, ep, w16[2]))) return rc;
+      tick(v, kProfFc1);
     }
     {
       EpiParams ep = epi_default();
@@ -376,8 +418,8 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
         ep.out_row_map = w2r;
         ep.out_row_period = np;
       }
-      if ((rc = run_linear(v, B.fc2, v->h.p, c.mlp_dim, M, ep))) return rc;
-      tick(v, kProfGemm);
+      if ((rc = run_linear(v, B.fc2, v->h.p, c.mlp_dim, M, ep, w16[3]))) return rc;
+      tick(v, kProfFc2);
     }
   }
   return kOk;
@@ -494,9 +536,9 @@ int vit_setup(sam3cu_vit* v, const VitSrc& w) {
       !v->img.alloc(static_cast<size_t>(v->max_batch) * 3 * c.img_size * c.img_size * 4) ||
       !v->out.alloc(M * e * 4))
     return kErrNoMem;
-  if (v->wdtype == SAM3CU_Q8_0) {  // largest linear: fc1 / fc2 (or QKV)
-    const size_t wmax = std::max(static_cast<size_t>(c.mlp_dim), static_cast<size_t>(3 * e)) * e * 2;
-    if (!v->wq.alloc(wmax)) return kErrNoMem;
+  if (v->wdtype == SAM3CU_Q8_0) {  // one block's four dequantised linears
+    const size_t wsum = (static_cast<size_t>(4) * e + 2 * static_cast<size_t>(c.mlp_dim)) * e * 2;
+    if (!v->wq.alloc(wsum)) return kErrNoMem;
   }
   return ck(cudaStreamSynchronize(st));
 }
@@ -715,13 +757,17 @@ void sam3cu_vit_destroy(sam3cu_vit* v) {
 
 void* sam3cu_vit_stream(sam3cu_vit* v) { return v ? v->stream : nullptr; }
 
-int sam3cu_vit_profile(sam3cu_vit* v, const float* images, int n, float* out, double* ms, int* counts) {
+int sam3cu_vit_profile_detail(sam3cu_vit* v, const float* images, int n, float* out, double* ms, int* counts) {
   if (!v || n <= 0 || n > v->max_batch || !images || !out || !ms || !counts) return SAM3CU_EINVAL;
   std::vector<int> kinds;
   std::vector<cudaEvent_t> evs;
   v->prof_kinds = &kinds;
   v->prof_events = &evs;
-  int rc = forward(v, images, n, out);
+  // The GPU waits 30 ms while every launch and event is enqueued, so the
+  // per-launch intervals hold device time only (with one image the kernels
+  // are shorter than the host's per-launch work).
+  int rc = launch_gpu_sleep(30000000ull, v->stream);
+  if (!rc) rc = forward(v, images, n, out);
   v->prof_kinds = nullptr;
   v->prof_events = nullptr;
   cudaError_t ce = cudaStreamSynchronize(v->stream);
@@ -740,11 +786,28 @@ int sam3cu_vit_profile(sam3cu_vit* v, const float* images, int n, float* out, do
   return ce == cudaSuccess ? kOk : kErrCuda;
 }
 
+int sam3cu_vit_profile(sam3cu_vit* v, const float* images, int n, float* out, double* ms, int* counts) {
+  if (!ms || !counts) return SAM3CU_EINVAL;
+  double fms[kProfKinds];
+  int fc[kProfKinds];
+  const int rc = sam3cu_vit_profile_detail(v, images, n, out, fms, fc);
+  for (int k = 0; k < 4; ++k) {
+    ms[k] = 0.0;
+    counts[k] = 0;
+  }
+  if (rc) return rc;
+  for (int k = 0; k < kProfKinds; ++k) {
+    ms[coarse_kind(k)] += fms[k];
+    counts[coarse_kind(k)] += fc[k];
+  }
+  return kOk;
+}
+
 int sam3cu_vit_launches_per_encode(sam3cu_vit* v, int n) {
   (void)n;
   if (!v) return 0;
-  // Q8_0: one dequantisation launch before each of the 4 linears of a block
-  return 3 + (v->wdtype == SAM3CU_Q8_0 ? 11 : 7) * v->c.depth + (v->c.depth == 0 ? 1 : 0);
+  // Q8_0: one dequantisation launch for the 4 linears of a block
+  return 3 + (v->wdtype == SAM3CU_Q8_0 ? 8 : 7) * v->c.depth + (v->c.depth == 0 ? 1 : 0);
 }
 
 // Enqueue through a CUDA graph captured once per (batch size, in, out)

@@ -27,7 +27,7 @@ EXPORTS = (
     "sam3cu_q8_repack", "sam3cu_q8_quantize", "sam3cu_layernorm",
     "sam3cu_sdpa", "sam3cu_vit_create", "sam3cu_vit_destroy",
     "sam3cu_vit_encode", "sam3cu_vit_encode_async", "sam3cu_vit_stream",
-    "sam3cu_vit_launches_per_encode", "sam3cu_vit_profile",
+    "sam3cu_vit_launches_per_encode", "sam3cu_vit_profile", "sam3cu_vit_profile_detail",
     "sam3_cuda_backend_ops", "sam3cu_conv2d_nhwc_noalloc",
     "sam3cu_tvit_expand_bias", "sam3cu_tvit_window_attention",
     "sam3cu_tvit_block_create", "sam3cu_tvit_block_forward", "sam3cu_tvit_block_destroy",
@@ -42,6 +42,8 @@ CUDA_BACKEND_SIZE = 32
 CUDA_BACKEND_TYPE = 2
 
 PROFILE_KINDS = ("gemm", "attention", "layernorm", "other")
+PROFILE_DETAIL_KINDS = ("patch", "qkv", "proj", "fc1", "fc2", "dequant", "attn_window", "attn_global",
+                        "layernorm", "other")
 
 _lib = None
 
@@ -84,6 +86,7 @@ def lib():
         L.sam3cu_vit_launches_per_encode.argtypes = [vp, i32]
         L.sam3cu_conv2d_nhwc_noalloc.argtypes = [vp, vp, vp, vp] + [i32] * 10 + [vp]
         L.sam3cu_vit_profile.argtypes = [vp, vp, i32, vp, C.POINTER(C.c_double), C.POINTER(C.c_int)]
+        L.sam3cu_vit_profile_detail.argtypes = [vp, vp, i32, vp, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         L.sam3cu_tvit_expand_bias.argtypes = [vp, i32, i32, i32, vp, i32]
         L.sam3cu_tvit_window_attention.argtypes = [vp, i64, vp, i64, i32, i32, i32, i32, i32, vp, i32,
                                                    vp]
@@ -388,6 +391,15 @@ class VitEncoder:
         check(lib().sam3cu_vit_profile(self.h, images.data_ptr(), images.shape[0], out.data_ptr(),
                                        ms, cnt), "sam3cu_vit_profile")
         return {k: (ms[i], cnt[i]) for i, k in enumerate(PROFILE_KINDS)}
+
+    def profile_detail(self, images, out) -> dict:
+        """As profile(), per PROFILE_DETAIL_KINDS (each linear, the Q8_0
+        dequantisation, window / global attention, LayerNorm, other)."""
+        ms = (C.c_double * len(PROFILE_DETAIL_KINDS))()
+        cnt = (C.c_int * len(PROFILE_DETAIL_KINDS))()
+        check(lib().sam3cu_vit_profile_detail(self.h, images.data_ptr(), images.shape[0], out.data_ptr(),
+                                              ms, cnt), "sam3cu_vit_profile_detail")
+        return {k: (ms[i], cnt[i]) for i, k in enumerate(PROFILE_DETAIL_KINDS)}
 
     def encode_async(self, images, out) -> None:
         """Device tensors; enqueue on the encoder's stream, no wait."""

@@ -68,3 +68,28 @@ def test_host_encode_pipelined_chunks(cuda):
         enc.encode_ptr(din.data_ptr(), cn, dout.data_ptr(), on_device=True)
         assert np.array_equal(got[first:first + cn], dout.cpu().numpy()), first
     enc.close()
+
+
+def test_profile_detail_kinds(cuda):
+    """sam3cu_vit_profile_detail: one launch per linear and block in its
+    own kind, window / global attention apart, one Q8_0 dequantisation
+    launch per block; the coarse sam3cu_vit_profile counts are their sums."""
+    import torch
+    import sam3cu
+    cfg = synth.tiny_cfg(depth=8)
+    w = synth.vit_weights(cfg, seed=5)
+    img = torch.from_numpy(synth.images(cfg, 1, seed=6)).cuda()
+    for code in (sam3cu.BF16, sam3cu.Q8_0):
+        enc = sam3cu.VitEncoder(cfg, w, code, max_batch=1)
+        out = torch.empty((1, enc.np, cfg["embed_dim"]), dtype=torch.float32, device="cuda")
+        d = enc.profile_detail(img, out)
+        c = enc.profile(img, out)
+        enc.close()
+        n = {k: v[1] for k, v in d.items()}
+        assert n["qkv"] == n["proj"] == n["fc1"] == n["fc2"] == 8 and n["patch"] == 1
+        assert n["attn_global"] == 1 and n["attn_window"] == 7  # block 7 is global
+        assert n["dequant"] == (8 if code == sam3cu.Q8_0 else 0)
+        assert n["layernorm"] == 17
+        gemm = sum(n[k] for k in ("patch", "qkv", "proj", "fc1", "fc2", "dequant"))
+        assert c["gemm"][1] == gemm and c["attention"][1] == 8 and c["layernorm"][1] == 17
+        assert all(v[0] >= 0.0 for v in d.values())
