@@ -194,6 +194,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           }
         } else {
           epilogue_math(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N, first_slice);
+          // a residual other than the destination (e.g. the periodic pos-embed)
+          if (epi_mode == kEpiTmaStore && ep.residual)
+            epilogue_residual(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N);
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
           stage_chunk(my_stage, v, lane, epi_mode == kEpiTmaAdd ? kOutF32 : ep.out_type);

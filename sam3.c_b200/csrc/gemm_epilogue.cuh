@@ -95,11 +95,10 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& ep, float (&v)[32
   }
 }
 
-// Residual add and per-thread store of the same 32 columns (kEpiDirect).
-__device__ __forceinline__ void epilogue_store_direct(const EpiParams& ep, float (&v)[32], int row,
-                                                      int col0, int N) {
+// v += residual row (row % res_row_period when periodic), in registers.
+__device__ __forceinline__ void epilogue_residual(const EpiParams& ep, float (&v)[32], int row, int col0, int N) {
   const bool full = col0 + 32 <= N;
-  if (ep.residual) {
+  {
     int rr = ep.res_row_period > 0 ? row % ep.res_row_period : row;
     const float* r = ep.residual + static_cast<int64_t>(rr) * ep.ldr + col0;
     if (full) {
@@ -117,6 +116,13 @@ __device__ __forceinline__ void epilogue_store_direct(const EpiParams& ep, float
         if (col0 + j < N) v[j] += r[j];
     }
   }
+}
+
+// Residual add and per-thread store of the same 32 columns (kEpiDirect).
+__device__ __forceinline__ void epilogue_store_direct(const EpiParams& ep, float (&v)[32], int row,
+                                                      int col0, int N) {
+  const bool full = col0 + 32 <= N;
+  if (ep.residual) epilogue_residual(ep, v, row, col0, N);
   int orow = row;
   if (ep.out_row_map) {
     int per = ep.out_row_period;

@@ -298,6 +298,9 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
         } else {
           // rows >= M and columns >= N are clipped by the TMA store
           epilogue_math(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N);
+          // a residual other than the destination (e.g. the periodic pos-embed)
+          if (epi_mode == kEpiTmaStore && ep.residual)
+            epilogue_residual(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N);
           if (lane == 0) bulk_wait_read<0>();  // previous chunk's smem read done
           __syncwarp();
           stage_chunk(my_stage, v, lane, epi_mode == kEpiTmaAdd ? kOutF32 : ep.out_type);
@@ -423,10 +426,10 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
   CUtensorMap to;
   memset(&to, 0, sizeof(to));
   int mode = kEpiDirect;
-  if (!ep.out_row_map && ep.res_row_period == 0) {
-    if (!ep.residual)
-      mode = kEpiTmaStore;
-    else if (ep.residual == ep.out && ep.out_type == kOutF32 && ep.ldr == ep.ldo)
+  if (!ep.out_row_map) {
+    if (!ep.residual || ep.residual != ep.out)
+      mode = kEpiTmaStore;  // a separate residual is added in registers
+    else if (ep.out_type == kOutF32 && ep.ldr == ep.ldo && ep.res_row_period == 0)
       mode = kEpiTmaAdd;
   }
   if (mode != kEpiDirect) {

@@ -46,7 +46,8 @@ enum BMode : int { kBTma16 = 0, kBQ8 = 1, kBF32 = 2 };
 
 // How the epilogue writes a chunk:
 //   kEpiDirect    per-thread vector stores (every fused op, any layout)
-//   kEpiTmaStore  swizzled smem staging + TMA bulk store (no residual / remap)
+//   kEpiTmaStore  swizzled smem staging + TMA bulk store (no row remap; a
+//                 residual other than the output is added in registers)
 //   kEpiTmaAdd    staging + TMA bulk reduce-add into the f32 output, which
 //                 is the residual (in-place x += linear(...))
 enum EpiMode : int { kEpiDirect = 0, kEpiTmaStore = 1, kEpiTmaAdd = 2 };

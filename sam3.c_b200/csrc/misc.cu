@@ -158,6 +158,52 @@ __global__ void patch_im2col(const float* __restrict__ img, void* __restrict__ a
   }
 }
 
+// The same for 16-bit output, one thread per (row, ky): it reads the three
+// 14-float runs of image line py*ps + ky (one per channel) and writes the 42
+// consecutive columns (ky*ps + kx)*3 + c as 21 packed pairs; thread ky == ps
+// of a row zero-fills columns ps*ps*3 .. kpad.  32-bit index math; ps even.
+template <int TO>
+__global__ void patch_im2col16(const float* __restrict__ img, uint32_t* __restrict__ a, int rows, int img_sz,
+                               int ps, int gs, int kpad, const int* __restrict__ src_of_row) {
+  const int np = gs * gs;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = ps + 1;
+  if (t >= rows * per_row) return;
+  const int row = t / per_row, ky = t - row * per_row;
+  uint32_t* arow = a + static_cast<int64_t>(row) * (kpad / 2);
+  if (ky == ps) {  // zero padding of K
+    for (int k2 = ps * ps * 3 / 2; k2 < kpad / 2; ++k2) arow[k2] = 0u;
+    return;
+  }
+  const int im = row / np;
+  int p = row - im * np;
+  if (src_of_row) p = src_of_row[p];
+  const int py = p / gs, px = p - py * gs;
+  const int64_t plane = static_cast<int64_t>(img_sz) * img_sz;
+  const float* src = img + static_cast<int64_t>(im) * 3 * plane + static_cast<int64_t>(py * ps + ky) * img_sz + px * ps;
+  uint32_t* dst = arow + ky * ps * 3 / 2;
+  float buf[2];
+  int nb = 0, k2 = 0;
+  for (int kx = 0; kx < ps; ++kx) {
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      buf[nb++] = __ldg(src + c * plane + kx);
+      if (nb == 2) {
+        uint32_t w;
+        if (TO == kBF16) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(buf[0], buf[1]);
+          w = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(buf[0], buf[1]);
+          w = *reinterpret_cast<uint32_t*>(&h);
+        }
+        dst[k2++] = w;
+        nb = 0;
+      }
+    }
+  }
+}
+
 // Row gather: dst[(r/period)*period + r%period] = src[(r/period)*period +
 // map[r%period]] for 16-byte vectors of `row_bytes`.
 __global__ void gather_rows(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int rows,
@@ -343,7 +389,20 @@ int launch_patch_im2col(const float* img, void* a, int tout, int n_img, int img_
                         const int* src_of_row, cudaStream_t st) {
   count_launches(1);
   const int gs = img_sz / ps;
-  const int64_t total = static_cast<int64_t>(n_img) * gs * gs * kpad;
+  const int64_t rows = static_cast<int64_t>(n_img) * gs * gs;
+  if ((tout == kBF16 || tout == kF16) && ps % 2 == 0 && kpad % 2 == 0 && rows * (ps + 1) < (1LL << 31)) {
+    const int threads = static_cast<int>(rows * (ps + 1));
+    if (tout == kBF16)
+      patch_im2col16<kBF16><<<(threads + 255) / 256, 256, 0, st>>>(img, static_cast<uint32_t*>(a),
+                                                                  static_cast<int>(rows), img_sz, ps, gs, kpad,
+                                                                  src_of_row);
+    else
+      patch_im2col16<kF16><<<(threads + 255) / 256, 256, 0, st>>>(img, static_cast<uint32_t*>(a),
+                                                                 static_cast<int>(rows), img_sz, ps, gs, kpad,
+                                                                 src_of_row);
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+  }
+  const int64_t total = rows * kpad;
   const int grid = grid_for(total, 256);
   if (tout == kBF16) patch_im2col<kBF16><<<grid, 256, 0, st>>>(img, a, n_img, img_sz, ps, gs, kpad, src_of_row);
   else if (tout == kF16) patch_im2col<kF16><<<grid, 256, 0, st>>>(img, a, n_img, img_sz, ps, gs, kpad, src_of_row);

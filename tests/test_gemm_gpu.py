@@ -124,3 +124,22 @@ def test_linear_f32_3xtf32(cuda, M, K, N):
     sam3cu.linear(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), residual=tres, out=tres,
                   act=sam3cu.ACT_GELU_TANH)
     assert rel_err(to_np(tres), O.linear(x, w, None, res=res, act=1)) < 1e-4
+
+
+@pytest.mark.parametrize("out_dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("M,K,N", [(300, 256, 160), (5184, 1024, 1024)])
+def test_linear_separate_residual(cuda, out_dtype, M, K, N):
+    """y = x . W^T + b + r with r a different buffer from y: the TMA-store
+    epilogue adds r in registers."""
+    import torch
+    import sam3cu
+    x, w, b, tx, tw, tb = _inputs(M, K, N, 5, "bf16")
+    res = np.random.default_rng(6).standard_normal((M, N), dtype=np.float32)
+    tres = torch.from_numpy(res).cuda()
+    odt = torch.float32 if out_dtype == "f32" else torch.bfloat16
+    y = torch.empty((M, N), dtype=odt, device="cuda")
+    sam3cu.linear(tx, tw, bias=tb, residual=tres, out=y)
+    ref = O.linear(x, w, b, res=res)
+    assert np.array_equal(to_np(tres), res)  # the residual is only read
+    tol = 2e-4 * max(1.0, K / 1024) if out_dtype == "f32" else 1e-2
+    assert rel_err(to_np(y), ref) < tol
