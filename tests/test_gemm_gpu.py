@@ -61,7 +61,8 @@ def test_linear_gelu_bf16out(cuda, M, K, N):
 
 # the fc2-sized shapes run split-K on the pair kernel (4 K slices
 # reduce-added into the residual; the bias is added by the first slice only)
-@pytest.mark.parametrize("M,K,N", [(300, 256, 128), (5184, 4736, 1024), (5184, 1024, 1024), (10368, 4736, 1024)])
+@pytest.mark.parametrize("M,K,N", [(300, 256, 128), (5184, 4736, 1024), (5184, 1024, 1024), (10368, 4736, 1024),
+                                   (5000, 4736, 1000)])  # ragged M and N tiles under split-K
 def test_linear_residual_inplace(cuda, M, K, N):
     import torch
     import sam3cu

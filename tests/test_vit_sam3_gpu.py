@@ -149,3 +149,36 @@ def test_missing_patch_bias_is_zero_and_bad_tensors_rejected(cuda, tmp_path):
         with pytest.raises(sam3cu.Sam3cuError) as ei:
             sam3cu.VitEncoder.from_sam3(bad, cfg, sam3cu.BF16)
         assert f"({sam3cu.EMODEL})" in str(ei.value)
+
+
+@needs_ref
+@pytest.mark.parametrize("half", [1, 2])
+def test_half_precision_file(cuda, tmp_path, half):
+    """An F16 (1) or BF16 (2) .sam3 file, as sam3_convert writes without
+    quantisation: tensors are widened on the device, and both a 16-bit and a
+    Q8_0 encoder built from the file match sam3cu_vit_create on the widened
+    values exactly."""
+    import torch
+    cfg = synth.tiny_cfg(depth=2)
+    w = synth.vit_weights(cfg, seed=51)
+    img = synth.images(cfg, 1, seed=52)
+    tdt = torch.float16 if half == 1 else torch.bfloat16
+    bits = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(tdt).view(torch.int16).numpy().view(np.uint16)
+    wide = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(tdt).float().numpy().reshape(np.shape(a))
+    t = [(n, bits(a), half) for n, a in synth.vit_sam3_tensors(cfg, w)]
+    path = str(tmp_path / "vit_half.sam3")
+    O.ref_write_sam3(path, t, quantize=False, image_size=cfg["img_size"], encoder_dim=cfg["embed_dim"],
+                     n_layers=cfg["depth"])
+    assert sam3cu.sam3_find(path, synth.VIT_PREFIX + "layer_norm.weight")["dtype"] == half
+    ww = dict(w)
+    for k in ("patch_w", "patch_b", "pos_raw", "ln_pre_w", "ln_pre_b"):
+        ww[k] = wide(w[k])
+    ww["blocks"] = [{k: wide(a) for k, a in b.items()} for b in w["blocks"]]
+    for code in (sam3cu.BF16, sam3cu.Q8_0):
+        enc = sam3cu.VitEncoder.from_sam3(path, cfg, code)
+        got = enc.encode_host(img)[0]
+        enc.close()
+        enc = sam3cu.VitEncoder(cfg, ww, code)
+        want = enc.encode_host(img)[0]
+        enc.close()
+        assert np.array_equal(got, want), code
