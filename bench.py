@@ -310,6 +310,7 @@ def run_ours(args):
         if world == 1 and not args.no_tinyvit:
             enc.close()
             line["tinyvit_config5"] = tinyvit_leg(args, dev, sam3cu)
+            line["fpn_neck"] = neck_leg(args, dev, sam3cu)
             line.update(q8_legs(args, dev, sam3cu))
         print(json.dumps(line))
     enc.close()
@@ -372,6 +373,63 @@ def q8_legs(args, dev, sam3cu):
                               "gemm_tflops": gemm_gflop_per_image() / prof["gemm"][0],
                               "dtype": "q8_0w+f16a", "batch": 1},
     }
+
+
+NECK_SCALES = (4.0, 2.0, 1.0, 0.5)
+
+
+def neck_gflop_per_image(d_model=256, dim=1024, grid=72):
+    """Algorithmic GFLOP of the FPN neck (2 per multiply-add), per image."""
+    fl = 0.0
+    for sf in NECK_SCALES:
+        H = (grid - 2) // 2 + 1 if sf < 0.75 else grid
+        for kind, ci, co, k in synth.neck_layer_dims(d_model, dim, sf):
+            if kind == "t":  # k2 s2 transposed conv: every input pixel feeds 4 outputs
+                fl += 2.0 * H * H * ci * 4 * co
+                H *= 2
+            else:
+                fl += 2.0 * H * H * ci * k * k * co
+    return fl / 1e9
+
+
+def neck_leg(args, dev, sam3cu):
+    """The FPN neck after the encoder (sam3_neck_build,
+    necks.c): ViT features [8, 5184, 1024] f32 -> 4 scales of d_model 256,
+    BF16 compute.  Device-resident input; CUDA events on the neck's stream.
+    With the CPU baseline on, the reference's own sam3_neck_build on its CPU
+    backend (oracle/_ref) is timed on one image beside it."""
+    import torch
+    B = 8
+    w = synth.neck_weights(256, 1024, NECK_SCALES, seed=0)
+    neck = sam3cu.FpnNeck(256, 1024, 72, NECK_SCALES, w, sam3cu.BF16, max_batch=B)
+    feat = torch.randn(B, 5184, 1024, device=dev)
+    outs = neck.outputs(B, dev)
+    f = lambda: neck.forward(feat, outs, sync=False)
+    for _ in range(3):
+        f()
+    torch.cuda.synchronize()
+    ms = _event_ms(f, 10, torch.cuda.ExternalStream(neck.stream, device=dev))
+    neck.close()
+    assert sam3cu.device_error() == 0
+    gf = neck_gflop_per_image()
+    res = {"workload": "sam3 FPN neck 72x72x1024 -> 288/144/72/36 x 256, 8 images per call",
+           "dtype": "bf16", "value": B / (ms / 1000.0), "unit": "images/s", "ms_per_image": ms / B,
+           "tflops": gf * B / ms, "gflop_per_image": gf}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        if O.ref_available():
+            O.ref_set_threads(args.cpu_threads)
+            x = np.random.default_rng(0).standard_normal((5184, 1024)).astype(np.float32)
+            t = time.perf_counter()
+            try:
+                O.ref_neck(256, 1024, 72, NECK_SCALES, w, x)
+                res["cpu_reference_s_per_image"] = time.perf_counter() - t
+                res["cpu_reference"] = ("reference sam3_neck_build on its CPU backend (oracle/_ref), 1 image, "
+                                        f"the backend's own thread pool over {os.cpu_count()} host threads")
+            except RuntimeError as e:
+                res["cpu_reference_unavailable"] = str(e)
+    return res
 
 
 def tinyvit_leg(args, dev, sam3cu):

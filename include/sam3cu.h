@@ -489,6 +489,40 @@ SAM3CU_API int sam3cu_vit_profile_detail(sam3cu_vit *vit, const float *images,
 /* Kernel launches one encode of n_images enqueues. */
 SAM3CU_API int sam3cu_vit_launches_per_encode(sam3cu_vit *vit, int n_images);
 
+/* ---------------------------------------------------------------- FPN neck */
+
+/*
+ * The SAM3 FPN neck: sam3_neck_init + sam3_neck_build (src/model/necks.c:
+ * 150-178, 260-360) as fused kernels.  Per scale factor (>= 3.5: two k2s2
+ * ConvTranspose with GELU after the first; >= 1.5: one; >= 0.75: none;
+ * below: a 2x2 max pool first), then Conv1x1 to d_model and Conv3x3 (pad 1),
+ * each with its bias.  Weights are HOST F32 in the reference layouts
+ * (struct sam3_neck, necks.h): conv_w[stage][layer] OHWI in build order,
+ * conv_b[stage][layer] (NULL: zero).  dtype: SAM3CU_BF16 or SAM3CU_F16,
+ * the compute type (F32 accumulation); dim % 32 == 0, d_model % 8 == 0.
+ */
+struct sam3cu_neck_weights {
+	const float *conv_w[4][4];
+	const float *conv_b[4][4];
+};
+typedef struct sam3cu_neck sam3cu_neck;
+SAM3CU_API sam3cu_neck *sam3cu_neck_create(int d_model, int dim, int grid, int n_scales,
+					   const float *scales,
+					   const struct sam3cu_neck_weights *w, int dtype,
+					   int max_batch, int *status);
+/* Output side length of stage i (outputs are [n, H_i, H_i, d_model]). */
+SAM3CU_API int sam3cu_neck_out_size(const sam3cu_neck *nk, int i);
+/* feat: device [n, grid*grid, dim] F32 (the ViT output layout); outs[i]:
+ * device F32 [n, H_i, H_i, d_model].  Blocks until done. */
+SAM3CU_API int sam3cu_neck_forward(sam3cu_neck *nk, const float *feat, int n_images,
+				   float *const *outs);
+/* The same, enqueued on the neck's stream without waiting. */
+SAM3CU_API int sam3cu_neck_forward_async(sam3cu_neck *nk, const float *feat, int n_images,
+					 float *const *outs);
+/* cudaStream_t of the neck, as void *. */
+SAM3CU_API void *sam3cu_neck_stream(sam3cu_neck *nk);
+SAM3CU_API void sam3cu_neck_destroy(sam3cu_neck *nk);
+
 /* ------------------------------------------------------ .sam3 weight files */
 
 /*

@@ -8,6 +8,7 @@
 #include <string.h>
 
 #include "backend/backend.h"
+#include "backend/cpu/cpu_backend.h"
 #include "core/alloc.h"
 #include "core/graph.h"
 #include "model/graph_helpers.h"
@@ -15,6 +16,24 @@
 
 struct sam3_backend *ref_make_backend(const struct sam3_backend_ops *ops,
 				      size_t be_size, int be_type);
+
+/* The reference CPU backend with the scratch capacity its header asks for
+ * on full-size necks (cpu_backend.h:26-31: >= 1 GiB for the 3x3 conv on
+ * 288x288x256); what sam3_backend_init does otherwise (backend.c:30-75). */
+static struct sam3_backend *cpu_backend_big_scratch(void)
+{
+	struct sam3_cpu_backend *cpu = calloc(1, sizeof(*cpu));
+	if (!cpu)
+		return NULL;
+	cpu->base.type = SAM3_BACKEND_CPU;
+	cpu->base.ops = sam3_cpu_backend_ops();
+	cpu->scratch_capacity = 2ul << 30;
+	if (cpu->base.ops->init(&cpu->base) != SAM3_OK) {
+		free(cpu);
+		return NULL;
+	}
+	return &cpu->base;
+}
 
 /* conv (transpose) weights per stage and layer: OHWI [OC, k, k, IC] F32,
  * biases [OC] */
@@ -34,11 +53,12 @@ int ref_neck_run(int d_model, int dim, int grid, int n_scales,
 	struct sam3_arena a;
 	struct sam3_graph *g = calloc(1, sizeof(*g));
 	int rc = -1;
-	if (!g || sam3_arena_init(&a, 1ul << 30)) {
+	if (!g || sam3_arena_init(&a, 3ul << 30)) {
 		free(g);
 		return -2;
 	}
-	struct sam3_backend *be = ref_make_backend(ops, be_size, be_type);
+	struct sam3_backend *be = ops ? ref_make_backend(ops, be_size, be_type)
+				      : cpu_backend_big_scratch();
 	if (!be)
 		goto done;
 	if (sam3_neck_init(&neck, d_model, dim, grid, n_scales, scales) != SAM3_OK ||

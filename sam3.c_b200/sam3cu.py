@@ -35,6 +35,8 @@ EXPORTS = (
     "sam3cu_selftest_wait_timeout",
     "sam3cu_tinyvit_create", "sam3cu_tinyvit_encode", "sam3cu_tinyvit_grid", "sam3cu_tinyvit_destroy",
     "sam3cu_sam3_check", "sam3cu_sam3_find", "sam3cu_vit_create_from_sam3", "sam3cu_vit_get_config",
+    "sam3cu_neck_create", "sam3cu_neck_forward", "sam3cu_neck_forward_async", "sam3cu_neck_out_size",
+    "sam3cu_neck_stream", "sam3cu_neck_destroy",
 )
 
 # sizeof(struct sam3_cuda_backend): {enum type; ops*} + int device + void *impl
@@ -76,6 +78,14 @@ def lib():
         L.sam3cu_vit_create_from_sam3.restype = vp
         L.sam3cu_vit_create_from_sam3.argtypes = [vp, C.c_size_t, vp, i32, i32, C.POINTER(C.c_int)]
         L.sam3cu_vit_get_config.argtypes = [vp, vp]
+        L.sam3cu_neck_create.restype = vp
+        L.sam3cu_neck_create.argtypes = [i32, i32, i32, i32, vp, vp, i32, i32, C.POINTER(C.c_int)]
+        L.sam3cu_neck_out_size.argtypes = [vp, i32]
+        L.sam3cu_neck_forward.argtypes = [vp, vp, i32, vp]
+        L.sam3cu_neck_forward_async.argtypes = [vp, vp, i32, vp]
+        L.sam3cu_neck_stream.restype = vp
+        L.sam3cu_neck_stream.argtypes = [vp]
+        L.sam3cu_neck_destroy.argtypes = [vp]
         L.sam3cu_sam3_check.argtypes = [vp, C.c_size_t, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]
         L.sam3cu_sam3_find.argtypes = [vp, C.c_size_t, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_int),
                                        C.POINTER(C.c_int), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
@@ -629,3 +639,66 @@ class TinyViT:
             self.h = None
 
     __del__ = close
+
+
+# ---------------------------------------------------------------- FPN neck
+class _NeckW(C.Structure):
+    _fields_ = [("conv_w", (C.c_void_p * 4) * 4), ("conv_b", (C.c_void_p * 4) * 4)]
+
+
+class FpnNeck:
+    """sam3_neck_init + sam3_neck_build (necks.c) on one B200.  ``weights``:
+    {"w": [[OHWI f32 per layer] per stage], "b": [[bias f32] per stage]} in
+    the reference's build order; dtype BF16 or F16 (compute type)."""
+
+    def __init__(self, d_model: int, dim: int, grid: int, scales, weights: dict, dtype: int = BF16,
+                 max_batch: int = 1):
+        self.scales = list(scales)
+        sc = np.ascontiguousarray(self.scales, np.float32)
+        nw = _NeckW()
+        keep = [sc]
+        for i, (ws, bs) in enumerate(zip(weights["w"], weights["b"])):
+            for j, (wa, ba) in enumerate(zip(ws, bs)):
+                wa = np.ascontiguousarray(wa, np.float32)
+                ba = np.ascontiguousarray(ba, np.float32)
+                keep += [wa, ba]
+                nw.conv_w[i][j] = wa.ctypes.data
+                nw.conv_b[i][j] = ba.ctypes.data
+        st = C.c_int(0)
+        h = lib().sam3cu_neck_create(d_model, dim, grid, len(self.scales), sc.ctypes.data, C.byref(nw), dtype,
+                                     max_batch, C.byref(st))
+        del keep
+        if not h:
+            check(st.value or -1, "sam3cu_neck_create")
+        self.h = h
+        self.d_model, self.dim, self.grid = d_model, dim, grid
+        self.sizes = [lib().sam3cu_neck_out_size(h, i) for i in range(len(self.scales))]
+
+    @property
+    def stream(self) -> int:
+        return lib().sam3cu_neck_stream(self.h)
+
+    def outputs(self, n: int, device):
+        import torch
+        return [torch.empty((n, s, s, self.d_model), dtype=torch.float32, device=device) for s in self.sizes]
+
+    def forward(self, feat, outs=None, sync: bool = True):
+        """feat: cuda f32 [n, grid*grid, dim] -> list of [n, H_i, H_i, d_model] f32."""
+        n = feat.shape[0]
+        if outs is None:
+            outs = self.outputs(n, feat.device)
+        ptrs = (C.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+        fn = lib().sam3cu_neck_forward if sync else lib().sam3cu_neck_forward_async
+        check(fn(self.h, feat.data_ptr(), n, ptrs), "sam3cu_neck_forward")
+        return outs
+
+    def close(self):
+        if self.h:
+            lib().sam3cu_neck_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
