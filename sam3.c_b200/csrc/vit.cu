@@ -571,6 +571,8 @@ sam3cu_vit* vit_create(const sam3cu_vit_config* cfg, const VitSrc& w, int weight
   }
   int rc = vit_setup(v.get(), w);
   if (rc) {
+    cudaStreamSynchronize(v->stream);
+    cudaStreamDestroy(v->stream);
     *status_p = rc;
     return nullptr;
   }
