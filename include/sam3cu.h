@@ -437,10 +437,10 @@ SAM3CU_API void sam3cu_vit_destroy(sam3cu_vit *vit);
  * features [n, np, e] F32 in raster patch order (the layout sam3_vit_build
  * returns).  images/out: device pointers when on_device != 0 (then
  * n_images <= max_batch), else host pointers.  With host pointers any
- * n_images is accepted: the batch is encoded in chunks of max_batch, and
- * with page-locked host memory each chunk's copies overlap the neighbouring
- * chunks' compute (two staging sets, separate copy streams).  Blocks until
- * done.
+ * n_images is accepted: the batch is encoded in chunks of max_batch (a batch
+ * of 4 .. max_batch images in two halves), and with page-locked host memory
+ * each chunk's copies overlap the neighbouring chunks' compute (two staging
+ * sets, separate copy streams).  Blocks until done.
  */
 SAM3CU_API int sam3cu_vit_encode(sam3cu_vit *vit, const float *images, int n_images,
 		      float *out, int on_device);

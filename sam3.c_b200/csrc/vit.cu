@@ -888,7 +888,11 @@ int sam3cu_vit_encode(sam3cu_vit* v, const float* images, int n, float* out, int
   }
   const size_t img_elems = static_cast<size_t>(3) * v->c.img_size * v->c.img_size;
   const size_t out_elems = static_cast<size_t>(v->np) * v->c.embed_dim;
-  const int chunks = (n + v->max_batch - 1) / v->max_batch;
+  // Chunks of max_batch; a batch of 4 .. max_batch images is split in two, so
+  // the copies of one half overlap the other half's compute (a single chunk
+  // would expose all of its H2D and D2H time).
+  const int cs = (n <= v->max_batch && n >= 4) ? (n + 1) / 2 : v->max_batch;
+  const int chunks = (n + cs - 1) / cs;
   int rc = kOk;
   if (chunks == 1) {  // a single chunk has nothing to overlap with
     if (cudaMemcpyAsync(v->img.p, images, n * img_elems * 4, cudaMemcpyHostToDevice, v->stream) != cudaSuccess)
@@ -901,8 +905,8 @@ int sam3cu_vit_encode(sam3cu_vit* v, const float* images, int n, float* out, int
   }
   if ((rc = ensure_pipeline(v))) return rc;
   for (int i = 0; i < chunks && !rc; ++i) {
-    const int b = i & 1, first = i * v->max_batch;
-    const int cn = std::min(v->max_batch, n - first);
+    const int b = i & 1, first = i * cs;
+    const int cn = std::min(cs, n - first);
     float* img = (b ? v->img2 : v->img).as<float>();
     float* feat = (b ? v->out2 : v->out).as<float>();
     if (i >= 2 && cudaStreamWaitEvent(v->copy_in, v->ev_done[b], 0) != cudaSuccess) rc = kErrCuda;

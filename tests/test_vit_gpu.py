@@ -45,7 +45,8 @@ def test_tiny_vit(cuda, wd):
     enc.close()
 
 
-def test_host_encode_pipelined_chunks(cuda):
+@pytest.mark.parametrize("n,mb,chunk", [(7, 2, 2), (5, 8, 3)])  # (5, 8): one batch split in halves
+def test_host_encode_pipelined_chunks(cuda, n, mb, chunk):
     """Host buffers with more images than max_batch: chunks of max_batch on
     two staging sets with overlapped copies.  Every image's features must be
     those of an on-device encode of the same chunk, and the order kept."""
@@ -53,7 +54,6 @@ def test_host_encode_pipelined_chunks(cuda):
     import sam3cu
     cfg = synth.tiny_cfg(depth=4)
     w = synth.vit_weights(cfg, seed=3)
-    n, mb = 7, 2
     imgs = synth.images(cfg, n, seed=4)
     enc = sam3cu.VitEncoder(cfg, w, sam3cu.BF16, max_batch=mb)
     hin = torch.from_numpy(np.ascontiguousarray(imgs)).pin_memory()
@@ -61,8 +61,8 @@ def test_host_encode_pipelined_chunks(cuda):
     enc.encode_ptr(hin.data_ptr(), n, hout.data_ptr(), on_device=False)
     assert sam3cu.device_error() == 0
     got = hout.numpy()
-    for first in range(0, n, mb):
-        cn = min(mb, n - first)
+    for first in range(0, n, chunk):
+        cn = min(chunk, n - first)
         din = torch.from_numpy(np.ascontiguousarray(imgs[first:first + cn])).cuda()
         dout = torch.empty((cn, enc.np, cfg["embed_dim"]), dtype=torch.float32, device="cuda")
         enc.encode_ptr(din.data_ptr(), cn, dout.data_ptr(), on_device=True)
