@@ -177,6 +177,18 @@ __device__ __forceinline__ float gelu_f(float v) {
   return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
 }
 
+// The same with the SFU's tanh.approx.f32 (relative error about 2^-11), for
+// 16-bit outputs, whose rounding is coarser.
+__device__ __forceinline__ float gelu_f16out(float v) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.7978845608f * (v + 0.044715f * v * v * v)));
+  return 0.5f * v * (1.0f + t);
+}
+template <int TO>
+__device__ __forceinline__ float gelu_out(float v) {
+  return TO == kF32 ? gelu_f(v) : gelu_f16out(v);
+}
+
 // 3x3 depthwise conv, stride 1, zero padding 1, NHWC, four channels per
 // thread; w9 [9][C] (tap-major, BatchNorm folded), bias [C]; optional GELU.
 template <int TI, int TO, bool kGelu>
@@ -211,12 +223,91 @@ __global__ void dwconv3x3(const void* __restrict__ x, void* __restrict__ y, cons
     }
   }
   if (kGelu) {
-    acc.x = gelu_f(acc.x);
-    acc.y = gelu_f(acc.y);
-    acc.z = gelu_f(acc.z);
-    acc.w = gelu_f(acc.w);
+    acc.x = gelu_out<TO>(acc.x);
+    acc.y = gelu_out<TO>(acc.y);
+    acc.z = gelu_out<TO>(acc.z);
+    acc.w = gelu_out<TO>(acc.w);
   }
   IO<TO>::st4(y, static_cast<int64_t>(p) * C + c, acc);
+}
+
+// The same conv, each thread computing kRows consecutive output rows of one
+// column and 4 channels: the three input rows under the 3x3 window stay in
+// registers, so each further output row loads one new input row (stride 1)
+// or two (stride 2) instead of three, and each input value is read about
+// 1.3x (stride 1) rather than 9x.  kS: the stride.
+template <int TI, int TO, bool kGelu, int kS>
+__global__ void dwconv3x3_rows(const void* __restrict__ x, void* __restrict__ y, const float* __restrict__ w9,
+                               const float* __restrict__ bias, int H, int W, int C, int OH, int OW, int row_blocks,
+                               unsigned total) {
+  constexpr int kRows = 8;
+  const unsigned c4 = C / 4;
+  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int c = static_cast<int>(i % c4) * 4;
+  unsigned q = i / c4;
+  const int ox = static_cast<int>(q % OW);
+  q /= OW;
+  const int oy0 = static_cast<int>(q % row_blocks) * kRows;
+  const unsigned img = q / row_blocks;
+  float4 k[9];
+#pragma unroll
+  for (int t = 0; t < 9; ++t) k[t] = __ldg(reinterpret_cast<const float4*>(w9 + t * C + c));
+  const float4 b4 = __ldg(reinterpret_cast<const float4*>(bias + c));
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  // the three horizontal neighbours (zero outside the image) of input row iy
+  auto load_row = [&](int iy, float4 (&r)[3]) {
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx) {
+      const int ix = ox * kS + kx - 1;
+      r[kx] = (iy >= 0 && iy < H && ix >= 0 && ix < W)
+                  ? IO<TI>::ld4(x, ((static_cast<int64_t>(img) * H + iy) * W + ix) * C + c)
+                  : zero;
+    }
+  };
+  auto fma4 = [](float4& a, const float4& v, const float4& w) {
+    a.x = fmaf(v.x, w.x, a.x);
+    a.y = fmaf(v.y, w.y, a.y);
+    a.z = fmaf(v.z, w.z, a.z);
+    a.w = fmaf(v.w, w.w, a.w);
+  };
+  float4 r0[3], r1[3], r2[3];
+  load_row(oy0 * kS - 1, r0);
+  if (kS == 1) load_row(oy0, r1);
+#pragma unroll
+  for (int rr = 0; rr < kRows; ++rr) {
+    const int oy = oy0 + rr;
+    if (oy >= OH) break;
+    if (kS == 1) {
+      load_row(oy + 1, r2);
+    } else {
+      load_row(oy * 2, r1);
+      load_row(oy * 2 + 1, r2);
+    }
+    float4 acc = b4;
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx) {
+      fma4(acc, r0[kx], k[kx]);
+      fma4(acc, r1[kx], k[3 + kx]);
+      fma4(acc, r2[kx], k[6 + kx]);
+    }
+    if (kGelu) {
+      acc.x = gelu_out<TO>(acc.x);
+      acc.y = gelu_out<TO>(acc.y);
+      acc.z = gelu_out<TO>(acc.z);
+      acc.w = gelu_out<TO>(acc.w);
+    }
+    IO<TO>::st4(y, ((static_cast<int64_t>(img) * OH + oy) * OW + ox) * C + c, acc);
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx) {
+      if (kS == 1) {
+        r0[kx] = r1[kx];
+        r1[kx] = r2[kx];
+      } else {
+        r0[kx] = r2[kx];
+      }
+    }
+  }
 }
 
 // 3x3 depthwise conv, zero padding 1, stride 1 or 2 (output (H-1)/s+1).
@@ -224,6 +315,34 @@ int launch_dwconv3x3(const void* x, int tin, void* y, int tout, const float* w9,
                      int H, int W, int C, bool gelu, cudaStream_t st, int stride = 1) {
   if (C % 4 || stride < 1) return kErrShape;
   const int OH = (H - 1) / stride + 1, OW = (W - 1) / stride + 1;
+  // stride 1: the row kernel (F32 blocks 0.369 -> 0.284 ms at 32 images);
+  // stride 2: one output per thread measured faster (0.475 vs 0.904 ms)
+  if (stride == 1) {
+    const int row_blocks = (OH + 7) / 8;
+    const int64_t total = static_cast<int64_t>(B) * row_blocks * OW * (C / 4);
+    if (total >= (1LL << 31)) return kErrShape;
+    count_launches(1);
+    const int grid = grid_1d(total, 256);
+    const unsigned t = static_cast<unsigned>(total);
+#define S3_DWR(TI, TO)                                                                                    \
+  if (tin == TI && tout == TO) {                                                                          \
+    if (stride == 1) {                                                                                    \
+      if (gelu)                                                                                           \
+        dwconv3x3_rows<TI, TO, true, 1><<<grid, 256, 0, st>>>(x, y, w9, bias, H, W, C, OH, OW, row_blocks, t);  \
+      else                                                                                                \
+        dwconv3x3_rows<TI, TO, false, 1><<<grid, 256, 0, st>>>(x, y, w9, bias, H, W, C, OH, OW, row_blocks, t); \
+    } else {                                                                                              \
+      if (gelu)                                                                                           \
+        dwconv3x3_rows<TI, TO, true, 2><<<grid, 256, 0, st>>>(x, y, w9, bias, H, W, C, OH, OW, row_blocks, t);  \
+      else                                                                                                \
+        dwconv3x3_rows<TI, TO, false, 2><<<grid, 256, 0, st>>>(x, y, w9, bias, H, W, C, OH, OW, row_blocks, t); \
+    }                                                                                                     \
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;                                          \
+  }
+    S3_DWR(kF32, kF32) S3_DWR(kBF16, kBF16) S3_DWR(kF16, kF16) S3_DWR(kF32, kBF16) S3_DWR(kF32, kF16)
+#undef S3_DWR
+    return kErrDtype;
+  }
   const int64_t total = static_cast<int64_t>(B) * OH * OW * (C / 4);
   if (total >= (1LL << 31)) return kErrShape;
   count_launches(1);
