@@ -311,6 +311,7 @@ def run_ours(args):
             enc.close()
             line["tinyvit_config5"] = tinyvit_leg(args, dev, sam3cu)
             line["fpn_neck"] = neck_leg(args, dev, sam3cu)
+            line["gemm_sweep_config1"] = gemm_sweep_leg(args, dev, sam3cu)
             line.update(q8_legs(args, dev, sam3cu))
         print(json.dumps(line))
     enc.close()
@@ -373,6 +374,59 @@ def q8_legs(args, dev, sam3cu):
                               "gemm_tflops": gemm_gflop_per_image() / prof["gemm"][0],
                               "dtype": "q8_0w+f16a", "batch": 1},
     }
+
+
+# (name, K, N, epilogue) of the four ViT-block linears
+SWEEP_SHAPES = (("qkv", 1024, 3072, "bias"), ("proj", 1024, 1024, "residual"), ("fc1", 1024, 4736, "gelu"),
+                ("fc2", 4736, 1024, "residual"))
+
+
+def gemm_sweep_leg(args, dev, sam3cu):
+    """the ViT-block linears at M = 5184*B for B in
+    {1, 2, 4, 8}, values ~N(0,1)/sqrt(K), FP32 accumulation, each with the
+    encoder's epilogue (bias; tanh-GELU on fc1; F32 residual added in place
+    on proj / fc2).  BF16 at every B, F16 at B = 8.  Device-resident
+    operands, CUDA events over 20 launches after 3 warm-ups.  With the CPU
+    baseline on, the reference's cpu_kernel_matmul_bf16 (oracle/_ref) is
+    timed on the proj shape at B = 1 beside it."""
+    import torch
+    res = {"unit": "TFLOP/s", "m_per_image": 5184, "shapes": {}}
+    g = torch.Generator(device=dev).manual_seed(0)
+    for dt_name, dt, Bs in (("bf16", torch.bfloat16, (1, 2, 4, 8)), ("f16", torch.float16, (8,))):
+        for name, K, N, epi in SWEEP_SHAPES:
+            w = (torch.randn(N, K, device=dev, generator=g) / K ** 0.5).to(dt)
+            b = torch.randn(N, device=dev, generator=g) / K ** 0.5
+            for B in Bs:
+                M = 5184 * B
+                x = (torch.randn(M, K, device=dev, generator=g) / K ** 0.5).to(dt)
+                if epi == "residual":
+                    y = torch.randn(M, N, device=dev, generator=g)
+                    f = lambda: sam3cu.linear(x, w, bias=b, residual=y, out=y)
+                else:
+                    y = torch.empty(M, N, device=dev, dtype=dt)
+                    act = sam3cu.ACT_GELU_TANH if epi == "gelu" else sam3cu.ACT_NONE
+                    f = lambda: sam3cu.linear(x, w, bias=b, act=act, out=y)
+                for _ in range(3):
+                    f()
+                ms = _event_ms(f, 20)
+                res["shapes"][f"{dt_name}_{name}_B{B}"] = round(2.0 * M * K * N / ms / 1e9, 1)
+                del x, y
+    assert sam3cu.device_error() == 0
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        if O.ref_available():
+            O.ref_set_threads(args.cpu_threads)
+            rng = np.random.default_rng(0)
+            a = rng.standard_normal((5184, 1024)).astype(np.float32)
+            wt = (rng.standard_normal((1024, 1024)) / 32.0).astype(np.float32)
+            bits = lambda v: (np.ascontiguousarray(v).view(np.uint32) >> 16).astype(np.uint16)
+            O.ref_matmul(bits(a[:64]), bits(wt), "bf16")
+            t = time.perf_counter()
+            O.ref_matmul(bits(a), bits(wt), "bf16")
+            s = time.perf_counter() - t
+            res["cpu_reference_bf16_proj_B1_gflops"] = round(2.0 * 5184 * 1024 * 1024 / s / 1e9, 1)
+    return res
 
 
 NECK_SCALES = (4.0, 2.0, 1.0, 0.5)
