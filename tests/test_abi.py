@@ -45,6 +45,8 @@ def test_strerror_codes():
     assert L.sam3cu_strerror(0) == b"ok"
     assert L.sam3cu_strerror(-1) == b"invalid argument"
     assert L.sam3cu_strerror(-105).startswith(b"device")
+    assert L.sam3cu_strerror(-5).startswith(b"malformed")  # SAM3_EMODEL
+    assert L.sam3cu_strerror(-109).startswith(b"tensor not in")
 
 
 def test_bad_arguments_rejected_on_host():
