@@ -276,8 +276,9 @@ __global__ void dwconv3x3_rows(const void* __restrict__ x, void* __restrict__ y,
   if (kS == 1) load_row(oy0, r1);
 #pragma unroll
   for (int rr = 0; rr < kRows; ++rr) {
+    // no early exit: rows past the image load zeros and skip the store, so
+    // the fully unrolled loop can issue later rows' loads early
     const int oy = oy0 + rr;
-    if (oy >= OH) break;
     if (kS == 1) {
       load_row(oy + 1, r2);
     } else {
@@ -297,7 +298,7 @@ __global__ void dwconv3x3_rows(const void* __restrict__ x, void* __restrict__ y,
       acc.z = gelu_out<TO>(acc.z);
       acc.w = gelu_out<TO>(acc.w);
     }
-    IO<TO>::st4(y, ((static_cast<int64_t>(img) * OH + oy) * OW + ox) * C + c, acc);
+    if (oy < OH) IO<TO>::st4(y, ((static_cast<int64_t>(img) * OH + oy) * OW + ox) * C + c, acc);
 #pragma unroll
     for (int kx = 0; kx < 3; ++kx) {
       if (kS == 1) {
