@@ -426,6 +426,9 @@ def gemm_sweep_leg(args, dev, sam3cu):
             O.ref_matmul(bits(a), bits(wt), "bf16")
             s = time.perf_counter() - t
             res["cpu_reference_bf16_proj_B1_gflops"] = round(2.0 * 5184 * 1024 * 1024 / s / 1e9, 1)
+            # release the reference's worker threads: left alive they keep the
+            # host cores busy and starve the launches of the legs that follow
+            O.ref_set_threads(1)
     return res
 
 
