@@ -102,3 +102,40 @@ def test_malformed_files_rejected_like_reference(files, tmp_path, case):
     with pytest.raises(sam3cu.Sam3cuError) as ei:
         sam3cu.sam3_check(p)
     assert f"{sam3cu.EMODEL}" in str(ei.value) or "malformed" in str(ei.value)
+
+
+@needs_ref
+def test_duplicate_and_long_names_like_reference(tmp_path):
+    """Duplicate names: the first descriptor wins in both readers (the
+    reference probes its table in file order).  Names longer than 127 bytes
+    are truncated by the writer and found under the truncated name."""
+    long = "x" * 200
+    t = [("dup", np.full(8, 1.0, np.float32)), ("dup", np.full(8, 2.0, np.float32)),
+         ("y" * 127, np.arange(4, dtype=np.float32)), (long, np.arange(6, dtype=np.float32))]
+    p = str(tmp_path / "names.sam3")
+    O.ref_write_sam3(p, t)
+    raw = np.fromfile(p, np.uint8)
+    for name in ("dup", "y" * 127, "x" * 127):
+        ours, ref = sam3cu.sam3_find(p, name), O.ref_find_sam3(p, name)
+        assert ours == ref, name
+    d = sam3cu.sam3_find(p, "dup")
+    assert raw[d["offset"]:d["offset"] + d["nbytes"]].view(np.float32)[0] == 1.0
+    assert sam3cu.sam3_find(p, long) is None and O.ref_find_sam3(p, "x" * 127)["dims"] == (6,)
+
+
+@needs_ref
+@pytest.mark.parametrize("pad", [False, True])
+def test_empty_table_like_reference(tmp_path, pad):
+    """A v4 header with no tensors: valid only when the file reaches the
+    page-aligned data blob start (4096), as sam3_weight_open rules."""
+    hdr = struct.pack("<4I5i4I", 0x334D4153, 4, 0, 0, 1008, 1024, 256, 32, 0, 0, 0, 0, 0)
+    assert len(hdr) == 52
+    p = str(tmp_path / "empty.sam3")
+    open(p, "wb").write(hdr + (bytes(4096 - 52) if pad else b""))
+    ref = O.ref_open_sam3(p)
+    if pad:
+        assert ref == 0 and sam3cu.sam3_check(p) == (0, 4)
+    else:
+        assert ref == sam3cu.EMODEL
+        with pytest.raises(sam3cu.Sam3cuError):
+            sam3cu.sam3_check(p)
