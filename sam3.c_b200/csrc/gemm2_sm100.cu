@@ -44,7 +44,7 @@ constexpr int kPTmemCols = 2 * kPN;
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  const __grid_constant__ CUtensorMap tmap_o, GemmShape shp, EpiParams ep, uint32_t idesc,
-                 int epi_mode, int splits) {
+                 int epi_mode, int splits, ConvGeom cg) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_out = smem + kPStages * kPStage;
@@ -58,8 +58,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int m_tiles = (shp.M + 2 * kPM - 1) / (2 * kPM);
+  // conv: one M tile = two 128-pixel blocks (this CTA's = 2 * tile + rank)
+  const int m_tiles = cg.on ? (cg.n_img * cg.n_by * cg.n_bx + 1) / 2 : (shp.M + 2 * kPM - 1) / (2 * kPM);
   const int n_tiles = (shp.N + kPN - 1) / kPN;
+  // conv block b -> (image, first output row, first column, flat output row)
+  auto conv_block = [&](int b, int& img, int& y0, int& x0) {
+    const int bx = b % cg.n_bx, t = b / cg.n_bx;
+    x0 = bx * 32;
+    y0 = (t % cg.n_by) * 4;
+    img = t / cg.n_by;
+  };
   // split-K (splits > 1, reduce-add epilogue only): work item t covers
   // output tile t / splits and K slice t % splits; slice 0 adds the bias
   const int num_tiles = m_tiles * n_tiles * splits;
@@ -105,6 +113,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         const int mn = tile / splits;
         const int m0 = (mn / n_tiles) * 2 * kPM + rank * kPM;
         const int n0 = (mn % n_tiles) * kPN + rank * (kPN / 2);
+        int cimg = 0, cy0 = 0, cx0 = 0;
+        if (cg.on) conv_block((mn / n_tiles) * 2 + rank, cimg, cy0, cx0);
+        const int cchunks = cg.C / kPK;
         for (int kt = k_begin(tile); kt < k_end(tile); ++kt, ++it) {
           const int s = it % kPStages;
           const uint32_t ph = (it / kPStages) & 1;
@@ -112,7 +123,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           const uint32_t lead_full = mapa_shared(smem_u32(&full_bar[s]), 0);
           if (elect_one()) {
             if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kPStage);  // both CTAs' bytes
-            tma_load_2d_pair(stage_a(s), &tmap_a, lead_full, kt * kPK, m0);
+            if (cg.on) {  // tap (ky, kx), channels c0..c0+63, shifted by the padding
+              const int tap = kt / cchunks, c0 = (kt - tap * cchunks) * kPK;
+              tma_load_4d_pair(stage_a(s), &tmap_a, lead_full, c0, cx0 + tap % 3 - 1, cy0 + tap / 3 - 1, cimg);
+            } else {
+              tma_load_2d_pair(stage_a(s), &tmap_a, lead_full, kt * kPK, m0);
+            }
             tma_load_2d_pair(stage_b(s), &tmap_b, lead_full, kt * kPK, n0);
           }
           __syncwarp();
@@ -164,9 +180,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
       const int mn = tile / splits;
-      const int m0 = (mn / n_tiles) * 2 * kPM + rank * kPM;
+      int m0 = (mn / n_tiles) * 2 * kPM + rank * kPM;
       const int n0 = (mn % n_tiles) * kPN;
       const bool first_slice = tile % splits == 0;
+      // conv: this warp's 32 rows are output row y0 + quarter, columns x0..x0+31
+      int conv_row = 0;
+      if (cg.on) {
+        int cimg, cy0, cx0;
+        conv_block((mn / n_tiles) * 2 + rank, cimg, cy0, cx0);
+        conv_row = (cimg * cg.H + cy0 + quarter) * cg.W + cx0;
+        m0 = conv_row - quarter * 32;  // so that m0 + quarter * 32 below is conv_row
+      }
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       int got = 0;
@@ -284,7 +308,55 @@ int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, Ge
     cudaFuncSetAttribute(gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
     attr = true;
   }
-  gemm2_kernel<<<2 * pairs, kPThreads, kPSmem, stream>>>(ta, tb, to, shp, ep, idesc, mode, splits);
+  ConvGeom off;
+  memset(&off, 0, sizeof(off));
+  gemm2_kernel<<<2 * pairs, kPThreads, kPSmem, stream>>>(ta, tb, to, shp, ep, idesc, mode, splits, off);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int launch_conv3x3_implicit(const void* x, const void* w, int ab_dtype, int n, int H, int W, int C, int OC,
+                            const EpiParams& ep, cudaStream_t stream) {
+  if ((ab_dtype != kBF16 && ab_dtype != kF16) || n <= 0 || H % 4 || W % 32 || C % kPK || OC % 8 ||
+      ep.residual || ep.out_row_map || ep.rope_cols || ep.ldo != OC)
+    return kErrShape;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(ep.out)) & 15)
+    return kErrShape;
+  const int64_t rows = static_cast<int64_t>(n) * H * W;
+  if (rows >= (1LL << 31) || static_cast<int64_t>(9) * C >= (1LL << 31)) return kErrShape;
+  const bool bf = ab_dtype == kBF16;
+  const CUtensorMapDataType dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap ta, tb, to;
+  // A: 64 channels x 32 columns x 4 rows of one image per 128-row operand tile
+  if (!make_tmap_nhwc(&ta, x, dt, 2, n, H, W, C, kPK, 32, 4, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
+  if (!make_tmap_2d(&tb, w, dt, 2, OC, 9 * C, 9 * C, kPN / 2, kPK, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
+  const bool f32 = ep.out_type == kOutF32;
+  const CUtensorMapDataType odt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                      : (ep.out_type == kOutBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+  if (!make_tmap_2d(&to, ep.out, odt, f32 ? 4 : 2, rows, OC, OC, 32, 32,
+                    f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+    return kErrTma;
+  ConvGeom cg;
+  cg.on = 1;
+  cg.H = H;
+  cg.W = W;
+  cg.C = C;
+  cg.n_img = n;
+  cg.n_bx = W / 32;
+  cg.n_by = H / 4;
+  const GemmShape shp{static_cast<int>(rows), OC, 9 * C};
+  const int m_tiles = (n * cg.n_by * cg.n_bx + 1) / 2, n_tiles = (OC + kPN - 1) / kPN;
+  int pairs = m_tiles * n_tiles;
+  const int cap = num_sms() / 2;
+  if (pairs > cap) pairs = cap;
+  const uint32_t idesc = make_idesc(bf ? 1u : 0u, 2 * kPM, kPN);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
+    attr = true;
+  }
+  count_launches(1);
+  gemm2_kernel<<<2 * pairs, kPThreads, kPSmem, stream>>>(ta, tb, to, shp, ep, idesc, kEpiTmaStore, 1, cg);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 

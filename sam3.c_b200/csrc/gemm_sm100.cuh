@@ -81,6 +81,17 @@ struct GemmShape {
   int M, N, K;
 };
 
+// Implicit-GEMM 3x3 convolution (stride 1, padding 1) on the pair kernel:
+// A is read straight from the NHWC input through a 4-D tensor map, each
+// CTA's 128 rows being a block of 4 image rows x 32 columns; K runs over
+// (ky, kx, 64-channel slice).  Needs H % 4 == 0, W % 32 == 0, C % 64 == 0.
+struct ConvGeom {
+  int on;         // 0: plain GEMM
+  int H, W, C;    // input = output spatial size, channels
+  int n_img;
+  int n_bx, n_by;  // 32-column / 4-row blocks per image
+};
+
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;          // 64 x 16-bit = 128 B rows (SWIZZLE_128B)
@@ -119,6 +130,13 @@ struct GemmCfg {
 // K slices per output tile the pair kernel uses (1 unless `additive`: an
 // in-place F32 reduce-add epilogue without activation or RoPE).
 int pair_splits(const GemmShape& shp, bool additive, int pairs);
+
+// y[n*H*W, OC] = conv3x3(x NHWC [n, H, W, C], w [OC, 3, 3, C] OHWI) + bias
+// as an implicit GEMM on the pair kernel (gemm2_sm100.cu); x / w 16-bit of
+// dtype ab_dtype, y of ep.out_type (TMA store).  Returns kErrShape when the
+// shape does not qualify (see ConvGeom), the caller then takes im2col.
+int launch_conv3x3_implicit(const void* x, const void* w, int ab_dtype, int n, int H, int W, int C, int OC,
+                            const EpiParams& ep, cudaStream_t stream);
 
 // 2-SM pair launch (gemm2_sm100.cu); shapes validated by launch_gemm.
 int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, GemmShape shp, const EpiParams& ep,

@@ -14,8 +14,11 @@
 //                a pixel shuffle to [n, 2H, 2W, oc]; Wt is the OHWI weight
 //                permuted once at creation
 //   Conv1x1      GEMM with the bias in the epilogue
-//   Conv3x3      16-byte NHWC im2col, GEMM + bias, written F32 straight into
-//                the caller's output (the reference's outputs are F32)
+//   Conv3x3      an implicit GEMM reading the NHWC map directly when the map
+//                tiles into 4x32-pixel blocks (the 288x288 stage; no im2col
+//                buffer), else 16-byte NHWC im2col + GEMM; bias fused, written
+//                F32 straight into the caller's output (the reference's
+//                outputs are F32)
 // The input features [n, grid*grid, dim] F32 are cast to T once and shared
 // by all stages.
 #include <cuda_bf16.h>
@@ -23,6 +26,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <vector>
@@ -38,6 +42,12 @@ using namespace s3;
 namespace {
 
 int ck(cudaError_t e) { return e == cudaSuccess ? kOk : kErrCuda; }
+
+// S3CU_NECK_IM2COL=1 keeps every 3x3 conv on im2col + GEMM (measurements).
+const bool g_no_implicit = [] {
+  const char* e = getenv("S3CU_NECK_IM2COL");
+  return e && atoi(e) != 0;
+}();
 
 struct NeckLayer {
   int kind = 0;  // 0 ConvT k2 s2, 1 Conv1x1, 2 Conv3x3
@@ -138,8 +148,11 @@ int neck_setup(sam3cu_neck* nk, const float* scales, const sam3cu_neck_weights* 
       std::vector<float> bt(static_cast<size_t>(L.co), 0.f);
       if (w->conv_b[i][j]) memcpy(bt.data(), w->conv_b[i][j], static_cast<size_t>(L.co) * 4);
       if ((rc = upload16(L.w, wt, nk->act, st)) || (rc = upload32(L.bias, bt, st))) return rc;
+      // the 3x3 conv needs im2col columns unless it runs as an implicit GEMM
+      // (launch_conv3x3_implicit: H % 4 == 0, W % 32 == 0, C % 64 == 0)
+      const bool implicit = !g_no_implicit && H % 4 == 0 && H % 32 == 0 && d % 64 == 0;
       if (c == 0) g_max = std::max(g_max, static_cast<size_t>(H) * H * d);
-      else col_max = std::max(col_max, static_cast<size_t>(H) * H * 9 * d);
+      else if (!implicit) col_max = std::max(col_max, static_cast<size_t>(H) * H * 9 * d);
     }
     S.n_layers = j;
     S.out_hw = H;
@@ -192,6 +205,14 @@ int neck_run(sam3cu_neck* nk, const float* feat, int n, float* const* outs) {
         C = L.co;
       } else {  // Conv3x3, pad 1 -> F32 output
         const int kk = 9 * C;
+        // implicit GEMM straight from the NHWC map when the shape tiles into
+        // 4x32-pixel blocks (the 288x288 stage); im2col + GEMM otherwise
+        if (!g_no_implicit && H % 4 == 0 && H % 32 == 0 && C % 64 == 0) {
+          rc = launch_conv3x3_implicit(cur, L.w.p, T, n, H, H, C, d, epi(outs[i], kOutF32, d, L.bias.as<float>(), 0),
+                                       st);
+          if (rc) return rc;  // the columns for this size were not allocated
+          continue;
+        }
         if ((rc = launch_conv_im2col(cur, T, false, nk->col.p, T, n, H, H, C, 3, 1, 1, kk, st))) return rc;
         GemmShape shp{M, d, kk};
         if ((rc = launch_gemm(nk->col.p, kk, L.w.p, kk, nullptr, nullptr, T, shp,

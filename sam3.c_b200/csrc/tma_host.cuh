@@ -49,4 +49,21 @@ inline bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
   return r == CUDA_SUCCESS;
 }
 
+// NHWC tensor [n, h, w, c] (dense), boxes of (box_c, box_w, box_h, 1).
+inline bool make_tmap_nhwc(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem, uint64_t n,
+                           uint64_t h, uint64_t w, uint64_t c, uint32_t box_c, uint32_t box_w, uint32_t box_h,
+                           CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = get_encode_tiled();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+  if ((c * elem) % 16 != 0 || (box_c * elem) % 16 != 0) return false;
+  cuuint64_t dims[4] = {c, w, h, n};
+  cuuint64_t strides[3] = {c * elem, w * c * elem, h * w * c * elem};
+  cuuint32_t box[4] = {box_c, box_w, box_h, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace s3
