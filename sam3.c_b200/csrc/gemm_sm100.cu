@@ -64,7 +64,7 @@ __device__ __forceinline__ void q8_dequant_tile(const int8_t* q, const float* sc
                                                 int t) {
   const int c = t & 7;
 #pragma unroll 4
-  for (int i = 0; i < kBN / (kT / 8); ++i) {
+  for (int i = 0; i < kBN / (kT >= 8 ? kT / 8 : 1); ++i) {  // kT = 0: not instantiated for use
     const int n = (t >> 3) + (kT / 8) * i;
     const uint2 raw = *reinterpret_cast<const uint2*>(q + n * kBK + c * 8);
     const float s = sc[(c >> 2) * kBN + n];
@@ -100,7 +100,7 @@ __device__ __forceinline__ void q8_dequant_tile_h2(const int8_t* q, const float*
   const int c = t & 7;
   const __half2 k1152 = __float2half2_rn(1152.0f);
 #pragma unroll 4
-  for (int i = 0; i < kBN / (kT / 8); ++i) {
+  for (int i = 0; i < kBN / (kT >= 8 ? kT / 8 : 1); ++i) {  // kT = 0: not instantiated for use
     const int n = (t >> 3) + (kT / 8) * i;
     const uint2 raw = *reinterpret_cast<const uint2*>(q + n * kBK + c * 8);
     const __half2 s = __float2half2_rn(sc[(c >> 2) * kBN + n]);

@@ -586,7 +586,7 @@ sam3cu_vit* vit_create(const sam3cu_vit_config* cfg, const VitSrc& w, int weight
 // sam3_vit_load does not check shapes; a mis-sized tensor here is an error).
 int file_part(const Sam3File& f, const char* name, int64_t n, bool optional, WPart& out) {
   const Sam3FileDesc* d = f.find(name);
-  if (!d) return optional ? kOk : SAM3CU_EMODEL;
+  if (!d) return optional ? static_cast<int>(kOk) : static_cast<int>(SAM3CU_EMODEL);
   if (Sam3File::numel(d) != n) return SAM3CU_EMODEL;
   const int dt = static_cast<int>(d->dtype);
   if (dt != kF32 && dt != kF16 && dt != kBF16 && dt != kQ8) return SAM3CU_EDTYPE;
