@@ -450,7 +450,7 @@ def neck_gflop_per_image(d_model=256, dim=1024, grid=72):
 
 
 def neck_leg(args, dev, sam3cu):
-    """The FPN neck after the encoder (SURVEY 8(f) rank 2: sam3_neck_build,
+    """The FPN neck after the encoder (sam3_neck_build,
     necks.c): ViT features [8, 5184, 1024] f32 -> 4 scales of d_model 256,
     BF16 compute.  Device-resident input; CUDA events on the neck's stream.
     With the CPU baseline on, the reference's own sam3_neck_build on its CPU
