@@ -378,8 +378,10 @@ SAM3CU_API int sam3cu_im2col_nhwc(const void *x, void *a, int dtype, int n, int 
  * device array that every GPU loading the library holds until exit;
  * requests that need more return SAM3CU_ESCRATCH (split the batch).  All
  * calls share that array: calls that can overlap on the GPU race, so order
- * them on one stream.  The first call on a device resolves the array's
- * address (cudaGetSymbolAddress); make it before any stream capture.
+ * them on one stream.  Each call resolves the array's address in the
+ * current context (cudaGetSymbolAddress, host side only); the first call on
+ * a device also loads the module there, so make it before any stream
+ * capture.
  */
 SAM3CU_API int sam3cu_conv2d_nhwc_noalloc(const void *x, const void *w, const float *bias,
 					  void *y, int dtype, int n, int H, int W, int C,

@@ -24,7 +24,7 @@
 #include <cstdlib>
 #include <cstring>
 
-#include "attention.cuh"
+#include "sam3cu_internal.h"
 #include "sam3cu_internal.h"
 #include "sm100_ptx.cuh"
 

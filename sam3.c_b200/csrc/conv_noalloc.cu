@@ -20,14 +20,17 @@
 //   * The array keeps the previous call's contents; nothing in it needs to
 //     start at zero, because im2col writes every element it later reads
 //     (padding columns and out-of-image taps included).
-//   * The first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (with that device current); make that first call
-//     before any stream capture.
+//   * Every call looks up the array's device address with
+//     cudaGetSymbolAddress for the current device and context (a host-side
+//     lookup, no device work), so the address stays right after
+//     cudaDeviceReset or under a context other than the primary one.  The
+//     first call on a device also loads the module there: make that first
+//     call before any stream capture.
 #include <cuda_runtime.h>
 
 #include <cstdint>
 #include <cstdio>
-#include <mutex>
+#include <climits>
 
 #include "../../include/sam3cu.h"
 #include "sam3cu_internal.h"
@@ -35,33 +38,27 @@
 namespace {
 
 constexpr size_t kScratchBytes = 32ull << 20;
-constexpr int kMaxDevices = 64;
 
 // Device-side scratch.  In host code this name is only a stand-in for the
 // symbol: its device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) uint8_t g_conv_scratch[kScratchBytes];
 
-std::mutex g_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
-
-// Device address of g_conv_scratch on the current device (set-up once per
-// device, with that device current).  Returns nullptr on failure.
+// Device address of g_conv_scratch in the current device's current context,
+// or nullptr on failure.  Looked up on every call: the address belongs to the
+// context that loaded the module, and a cached copy would go stale when that
+// context is replaced (cudaDeviceReset, a cuCtxCreate'd context).
 void* scratch_for_current_device() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_conv_scratch);
-    if (e != cudaSuccess) {
-      fprintf(stderr, "[sam3cu] cudaGetSymbolAddress(conv scratch) failed on device %d: %s\n", dev,
-              cudaGetErrorString(e));
-      cudaGetLastError();
-      return nullptr;
-    }
-    g_scratch_ptr[dev] = p;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_conv_scratch);
+  if (e != cudaSuccess) {
+    int dev = -1;
+    cudaGetDevice(&dev);
+    fprintf(stderr, "[sam3cu] cudaGetSymbolAddress(conv scratch) failed on device %d: %s\n", dev,
+            cudaGetErrorString(e));
+    cudaGetLastError();
+    return nullptr;
   }
-  return g_scratch_ptr[dev];
+  return p;
 }
 
 }  // namespace
@@ -74,35 +71,41 @@ int sam3cu_conv2d_nhwc_noalloc(const void* x, const void* w, const float* bias, 
       pad < 0)
     return SAM3CU_EINVAL;
   if (dtype != SAM3CU_F32 && dtype != SAM3CU_BF16 && dtype != SAM3CU_F16) return SAM3CU_EDTYPE;
-  const int OH = (H + 2 * pad - kh) / stride + 1, OW = (W + 2 * pad - kw) / stride + 1;
-  if (OH <= 0 || OW <= 0) return SAM3CU_EINVAL;
+  // Sizes in 64-bit arithmetic, range-checked before any is narrowed to int.
+  const int64_t OH = (static_cast<int64_t>(H) + 2 * static_cast<int64_t>(pad) - kh) / stride + 1;
+  const int64_t OW = (static_cast<int64_t>(W) + 2 * static_cast<int64_t>(pad) - kw) / stride + 1;
+  if (OH <= 0 || OW <= 0 || OH > INT_MAX || OW > INT_MAX) return SAM3CU_EINVAL;
   const size_t es = dtype == SAM3CU_F32 ? 4 : 2;
-  const int kk = kh * kw * C;
-  const int al = dtype == SAM3CU_F32 ? 4 : 8;  // GEMM row pitch: 16 bytes
-  const int kpad = (kk + al - 1) / al * al;
-  const size_t rows = static_cast<size_t>(n) * OH * OW;
-  const size_t col_bytes = (rows * kpad * es + 255) & ~static_cast<size_t>(255);
-  const size_t wpad_bytes = kpad != kk ? static_cast<size_t>(OC) * kpad * es : 0;
-  if (rows > 0x7fffffffull || col_bytes + wpad_bytes > kScratchBytes) {
+  const int64_t kk = static_cast<int64_t>(kh) * kw * C;
+  const int64_t al = dtype == SAM3CU_F32 ? 4 : 8;  // GEMM row pitch: 16 bytes
+  const int64_t kpad = (kk + al - 1) / al * al;
+  if (kpad > INT_MAX) return SAM3CU_EINVAL;
+  const uint64_t rows = static_cast<uint64_t>(n) * static_cast<uint64_t>(OH) * static_cast<uint64_t>(OW);
+  if (rows > 0x7fffffffull) return SAM3CU_EINVAL;
+  const uint64_t col_bytes = (rows * static_cast<uint64_t>(kpad) * es + 255) & ~static_cast<uint64_t>(255);
+  const uint64_t wpad_bytes = kpad != kk ? static_cast<uint64_t>(OC) * static_cast<uint64_t>(kpad) * es : 0;
+  if (col_bytes + wpad_bytes > kScratchBytes) {
     fprintf(stderr,
-            "[sam3cu] conv2d_nhwc_noalloc: needs %zu bytes of scratch, the static buffer holds %zu "
+            "[sam3cu] conv2d_nhwc_noalloc: needs %llu bytes of scratch, the static buffer holds %zu "
             "(split the batch)\n",
-            col_bytes + wpad_bytes, kScratchBytes);
+            static_cast<unsigned long long>(col_bytes + wpad_bytes), kScratchBytes);
     return SAM3CU_ESCRATCH;
   }
   uint8_t* scratch = static_cast<uint8_t*>(scratch_for_current_device());
   if (!scratch) return SAM3CU_ECUDA;
   void* col = scratch;
-  int rc = sam3cu_im2col_nhwc(x, col, dtype, n, H, W, C, kh, kw, stride, pad, kpad, stream);
+  int rc = sam3cu_im2col_nhwc(x, col, dtype, n, H, W, C, kh, kw, stride, pad, static_cast<int>(kpad), stream);
   if (rc) return rc;
   const void* wk = w;
   if (kpad != kk) {  // weight rows [OC, kk] -> [OC, kpad] with zero columns
     void* wpad = scratch + col_bytes;
-    rc = sam3cu_im2col_nhwc(w, wpad, dtype, OC, 1, 1, kk, 1, 1, 1, 0, kpad, stream);
+    rc = sam3cu_im2col_nhwc(w, wpad, dtype, OC, 1, 1, static_cast<int>(kk), 1, 1, 1, 0, static_cast<int>(kpad),
+                           stream);
     if (rc) return rc;
     wk = wpad;
   }
-  return sam3cu_linear(col, dtype, wk, bias, nullptr, y, dtype, static_cast<int>(rows), kpad, OC, SAM3CU_ACT_NONE,
+  return sam3cu_linear(col, dtype, wk, bias, nullptr, y, dtype, static_cast<int>(rows), static_cast<int>(kpad), OC,
+                       SAM3CU_ACT_NONE,
                        stream);
 }
 

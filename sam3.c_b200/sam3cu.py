@@ -238,12 +238,21 @@ def conv2d_nhwc_noalloc(x, w, bias=None, stride=1, pad=0, out=None):
     """CONV2D (NHWC x OHWI, groups 1) through the entry point that allocates
     no device memory (its column buffer is a static device array)."""
     import torch
+    if x.dim() != 4 or w.dim() != 4:
+        raise ValueError("x must be NHWC [n,H,W,C] and w OHWI [OC,kh,kw,C]")
     n, H, W, C = x.shape
     OC, kh, kw, C2 = w.shape
-    assert C == C2
+    if C != C2:
+        raise ValueError(f"channel mismatch: x has {C}, w has {C2}")
+    if w.dtype != x.dtype:
+        raise TypeError(f"w dtype {w.dtype} differs from x dtype {x.dtype}")
+    if not (x.is_contiguous() and w.is_contiguous()):
+        raise ValueError("x and w must be contiguous")
     OH, OW = (H + 2 * pad - kh) // stride + 1, (W + 2 * pad - kw) // stride + 1
     if out is None:
         out = torch.empty((n, OH, OW, OC), dtype=x.dtype, device=x.device)
+    elif tuple(out.shape) != (n, OH, OW, OC) or out.dtype != x.dtype or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {x.dtype} tensor of shape {(n, OH, OW, OC)}")
     check(lib().sam3cu_conv2d_nhwc_noalloc(_ptr(x), _ptr(w), _f32(bias, 'bias'), _ptr(out),
                                            dtype_code(x), n, H, W, C, OC, kh, kw, stride, pad,
                                            _stream()), "sam3cu_conv2d_nhwc_noalloc")

@@ -3,15 +3,20 @@
 Runs the UNMODIFIED reference sam3_vit_build on its own CPU backend
 (oracle/_ref/libsam3_ref.so, built from the sam3.c sources by
 oracle/Makefile) for the Hiera-L geometry at 1008 px with 8 blocks (seven
-windowed, block 7 global), seeded synthetic weights (sam3.c_b200/synth.py,
+windowed, block 7 global) and with all 32 blocks (globals at 7/15/23/31,
+image_encoder.c:35), seeded synthetic weights (sam3.c_b200/synth.py,
 seed 11) and one seeded image (seed 12), in three weight precisions:
   f32  : the weights as generated
   bf16 : linear / patch weights rounded to bf16 (what the BF16 encoder holds)
   q8   : linear weights through sam3_q8_quantize / dequantize, patch bf16
 and stores a fixed random sample of 16384 output positions per variant plus
 whole-output statistics, so the fixture stays small (the full output is
-21 MB).  Usage:  python tests/golden/gen_vit_golden.py   (~5 min, 8 cores)
+21 MB).  Usage:
+    python tests/golden/gen_vit_golden.py            # depth 8  (~5 min, 8 cores)
+    python tests/golden/gen_vit_golden.py --depth 32 # depth 32 (~15 min, 8 cores)
+writes tests/golden/vit_1008_depth<D>.npz.
 """
+import argparse
 import os
 import sys
 import time
@@ -25,7 +30,6 @@ sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "sam3.c_b200")]
 import oracle as O  # noqa: E402
 import synth  # noqa: E402
 
-CFG = dict(synth.HIERA_L, depth=8)
 W_SEED, IMG_SEED, N_SAMPLE = 11, 12, 16384
 
 
@@ -36,6 +40,9 @@ def variants(w):
 
 
 def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--depth", type=int, default=8)
+    CFG = dict(synth.HIERA_L, depth=ap.parse_args().depth)
     w = synth.vit_weights(CFG, seed=W_SEED)
     img = synth.images(CFG, 1, seed=IMG_SEED)[0]
     rng = np.random.default_rng(0)
@@ -50,7 +57,7 @@ def main():
         print(f"{name}: {time.time() - t:.1f}s  max|y|={np.abs(y).max():.4f}", flush=True)
         out[f"{name}_sample"] = y[idx]
         out[f"{name}_stats"] = np.array([y.mean(), y.std(), np.abs(y).max(), float(np.abs(y).sum())])
-    np.savez_compressed(os.path.join(HERE, "vit_1008_depth8.npz"), **out)
+    np.savez_compressed(os.path.join(HERE, f"vit_1008_depth{CFG['depth']}.npz"), **out)
 
 
 if __name__ == "__main__":

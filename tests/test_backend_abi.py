@@ -9,7 +9,20 @@ import tempfile
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = "/root/reference"
+
+def _ref_dir() -> str:
+    """The sam3.c checkout: SAM3C_REF, else BASELINE.json's reference_path."""
+    if os.environ.get("SAM3C_REF"):
+        return os.environ["SAM3C_REF"]
+    try:
+        import json
+        with open(os.path.join(ROOT, "BASELINE.json")) as f:
+            return json.load(f).get("reference_path", "")
+    except (OSError, ValueError):
+        return ""
+
+
+REF = _ref_dir()
 
 PROBE = r"""
 #include <stdio.h>
@@ -44,7 +57,7 @@ def _run(include, flags):
         return subprocess.run([exe], check=True, capture_output=True, text=True).stdout
 
 
-@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "src")), reason="reference sources absent")
+@pytest.mark.skipif(not REF or not os.path.isdir(os.path.join(REF, "src")), reason="reference sources absent")
 def test_struct_layouts_match_reference():
     ours = _run('#include "sam3cu_backend.h"', ["-I" + os.path.join(ROOT, "include")])
     ref = _run('#include "backend/backend.h"',

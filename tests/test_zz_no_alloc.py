@@ -8,8 +8,10 @@ by every call, so the test makes two calls in a row (with different inputs
 and shapes) through the C ABI and checks each against the allocating CONV2D
 path of the CUDA backend (the vtable's graph_eval), or the CPU oracle where
 the reference library is absent, at the tolerances of the other parity
-tests: 1e-4 (F32) and 1e-2 (BF16), normwise.  It sits in a file pytest
-collects last and must pass alone in a fresh process as well.
+tests: 1e-4 (F32) and 1e-2 (BF16, F16), normwise.  It also checks the
+optional bias and that a warm call leaves the device's free memory
+unchanged.  It sits in a file pytest collects last and must pass alone in a
+fresh process as well.
 """
 import numpy as np
 import pytest
@@ -58,9 +60,48 @@ def test_noalloc_conv_matches_allocating_path_twice(cuda):
         torch.cuda.synchronize()
         assert sam3cu.device_error() == 0
         assert rel_err(to_np(y), ref) < 1e-4
-        yb = sam3cu.conv2d_nhwc_noalloc(torch.from_numpy(x).cuda().bfloat16(),
-                                        torch.from_numpy(w).cuda().bfloat16(), stride=stride, pad=pad)
-        assert rel_err(to_np(yb), ref) < 1e-2
+        for dt in (torch.bfloat16, torch.float16):
+            y16 = sam3cu.conv2d_nhwc_noalloc(torch.from_numpy(x).cuda().to(dt),
+                                             torch.from_numpy(w).cuda().to(dt), stride=stride, pad=pad)
+            torch.cuda.synchronize()
+            assert sam3cu.device_error() == 0
+            assert rel_err(to_np(y16), ref) < 1e-2
+
+
+def test_noalloc_conv_bias(cuda):
+    """With an F32 bias [OC]: the allocating path's result plus the bias."""
+    import torch
+    import sam3cu
+    rng = np.random.default_rng(22)
+    x, w = _case(rng, 1, 48, 48, 3, 64, 3, 2, 1)
+    b = rng.standard_normal(64, dtype=np.float32)
+    ref = _conv_existing(x, w, 2, 1) + b
+    for dt, tol in ((torch.float32, 1e-4), (torch.float16, 1e-2)):
+        y = sam3cu.conv2d_nhwc_noalloc(torch.from_numpy(x).cuda().to(dt), torch.from_numpy(w).cuda().to(dt),
+                                       bias=torch.from_numpy(b).cuda(), stride=2, pad=1)
+        torch.cuda.synchronize()
+        assert sam3cu.device_error() == 0
+        assert rel_err(to_np(y), ref) < tol
+
+
+def test_noalloc_conv_allocates_nothing(cuda):
+    """A warm call leaves the device's free memory unchanged: nothing on the
+    path (im2col, weight padding, GEMM) allocated device memory."""
+    import torch
+    import sam3cu
+    rng = np.random.default_rng(23)
+    x, w = _case(rng, 2, 40, 36, 3, 64, 3, 1, 1)
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    out = torch.empty((2, 40, 36, 64), device="cuda")
+    sam3cu.conv2d_nhwc_noalloc(xd, wd, stride=1, pad=1, out=out)   # warm: module loaded
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        sam3cu.conv2d_nhwc_noalloc(xd, wd, stride=1, pad=1, out=out)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert sam3cu.device_error() == 0
 
 
 def test_noalloc_conv_rejects_oversize(cuda):
