@@ -312,6 +312,7 @@ def run_ours(args):
             line["tinyvit_config5"] = tinyvit_leg(args, dev, sam3cu)
             line["fpn_neck"] = neck_leg(args, dev, sam3cu)
             line["gemm_sweep_config1"] = gemm_sweep_leg(args, dev, sam3cu)
+            line["dropin_vtable_f32"] = dropin_leg(args, dev, sam3cu)
             line.update(q8_legs(args, dev, sam3cu))
         print(json.dumps(line))
     enc.close()
@@ -339,13 +340,14 @@ def _event_ms(fn, iters, stream=None):
 def q8_legs(args, dev, sam3cu):
     """BASELINE configs 0 and 2 (parity cases, reported beside the headline):
     the single Q8_0 linear [5184 x 1024] . [4736 x 1024]^T + bias through
-    sam3cu_linear_q8 (bf16 activations, f32 out), and the full 1008px ViT
+    sam3cu_linear_q8 (F32 activations as configured, rounded to BF16 inside
+    the timed call; F32 out), and the full 1008px ViT
     encode of one image with Q8_0 weights (F16 activations).  Device-
     resident inputs; CUDA-event times after warm-up."""
     import torch
     rng = np.random.default_rng(1)
     M, K, N = 5184, 1024, 4736
-    x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).to(dev).bfloat16()
+    x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).to(dev)
     w = torch.from_numpy((rng.standard_normal((N, K)) * 0.02).astype(np.float32)).to(dev)
     b = torch.from_numpy((rng.standard_normal(N) * 0.01).astype(np.float32)).to(dev)
     q, sc = sam3cu.q8_repack(sam3cu.q8_quantize(w), N, K)
@@ -368,8 +370,9 @@ def q8_legs(args, dev, sam3cu):
     assert sam3cu.device_error() == 0
     return {
         "q8_linear_config0": {"tflops": 2 * M * K * N / ms_lin / 1e9, "ms": ms_lin,
-                              "dtype": "q8_0w+bf16a, f32 out",
-                              "note": "dequantise-once path (M >= 2048) of sam3cu_linear_q8"},
+                              "dtype": "q8_0w x f32a (bf16 on chip), f32 out",
+                              "note": "F32 activations cast inside the call + dequantise-once path "
+                                      "(M >= 2048) of sam3cu_linear_q8"},
         "q8_encode_config2": {"value": 1000.0 / ms_enc, "unit": "images/s", "ms_per_image": ms_enc,
                               "gemm_tflops": gemm_gflop_per_image() / prof["gemm"][0],
                               "dtype": "q8_0w+f16a", "batch": 1},
@@ -385,14 +388,17 @@ def gemm_sweep_leg(args, dev, sam3cu):
     """the ViT-block linears at M = 5184*B for B in
     {1, 2, 4, 8}, values ~N(0,1)/sqrt(K), FP32 accumulation, each with the
     encoder's epilogue (bias; tanh-GELU on fc1; F32 residual added in place
-    on proj / fc2).  BF16 at every B, F16 at B = 8.  Device-resident
+    on proj / fc2).  BF16 at every B, F16 at B = 8, F32 (3xTF32: three
+    kind::tf32 MMAs per product, hi*hi + hi*lo + lo*hi) at B = 1 and 8,
+    whose TFLOP/s count the F32 product once.  Device-resident
     operands, CUDA events over 20 launches after 3 warm-ups.  With the CPU
     baseline on, the reference's cpu_kernel_matmul_bf16 (oracle/_ref) is
     timed on the proj shape at B = 1 beside it."""
     import torch
     res = {"unit": "TFLOP/s", "m_per_image": 5184, "shapes": {}}
     g = torch.Generator(device=dev).manual_seed(0)
-    for dt_name, dt, Bs in (("bf16", torch.bfloat16, (1, 2, 4, 8)), ("f16", torch.float16, (8,))):
+    for dt_name, dt, Bs in (("bf16", torch.bfloat16, (1, 2, 4, 8)), ("f16", torch.float16, (8,)),
+                            ("f32", torch.float32, (1, 8))):
         for name, K, N, epi in SWEEP_SHAPES:
             w = (torch.randn(N, K, device=dev, generator=g) / K ** 0.5).to(dt)
             b = torch.randn(N, device=dev, generator=g) / K ** 0.5
@@ -412,6 +418,11 @@ def gemm_sweep_leg(args, dev, sam3cu):
                 res["shapes"][f"{dt_name}_{name}_B{B}"] = round(2.0 * M * K * N / ms / 1e9, 1)
                 del x, y
     assert sam3cu.device_error() == 0
+    pk, pk_src = peaks()
+    tf32 = 0.5 * pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    res["f32_peak"] = {"tf32_tflops": tf32, "f32_via_3xtf32_tflops": tf32 / 3.0,
+                       "source": f"{pk_src} bf16_tflops x 1/2 (B200 datasheet TF32:BF16 dense ratio; "
+                                 "no TF32 peak is measured); 3 MMAs per F32 product"}
     if not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
@@ -489,6 +500,36 @@ def neck_leg(args, dev, sam3cu):
     return res
 
 
+def dropin_leg(args, dev, sam3cu):
+    """The drop-in path: the reference's own sam3_vit_build (compiled from
+    the sam3.c sources, dropin/_ref) evaluating its F32 Hiera-L graph on one
+    1008 px image through sam3_cuda_backend_ops(), host buffers in and out,
+    exactly the call sequence of a sam3.c build with the CUDA backend
+    registered (16 graph_evals, the residual stream read back to the host
+    between them).  One untimed encode uploads the weights (the session
+    keeps them, as a sam3_ctx does); then the host wall time of each
+    sam3_vit_build call is taken (the call returns after its last
+    synchronous read-back)."""
+    sys.path.insert(0, os.path.join(ROOT, "dropin"))
+    import dropin as D
+    if not D.available():
+        return {"unavailable": "dropin/_ref/libsam3_dropin.so not built"}
+    w = synth.vit_weights(CFG, seed=0)
+    img = synth.images(CFG, 1, seed=100)[0]
+    dv = D.DropinVit(CFG, w, dev.index or 0)
+    del w
+    dv.encode(img)
+    secs = [dv.encode(img)[1] for _ in range(args.dropin_iters)]
+    dv.close()
+    assert sam3cu.device_error() == 0
+    t = float(np.median(secs))
+    return {"workload": "reference sam3_vit_build (F32 graph, 32 blocks) on sam3_cuda_backend_ops, "
+                        "1 image 1008px, host image in / host features out",
+            "dtype": "f32 (3xTF32 GEMMs, F32 attention)", "value": 1.0 / t, "unit": "images/s",
+            "ms_per_image": 1000.0 * t, "iters": len(secs),
+            "ms_min": 1000.0 * min(secs), "ms_max": 1000.0 * max(secs)}
+
+
 def tinyvit_leg(args, dev, sam3cu):
     """BASELINE config 5 (a parity case, reported beside the headline): the
     TinyViT-21M backbone at 1008 px, batch 32, F16, random-init weights,
@@ -516,6 +557,18 @@ def tinyvit_leg(args, dev, sam3cu):
             "unit": "images/s", "ms_per_batch": ms, "data": "synthetic (seeded images, random-init weights)"}
 
 
+def run_leg(args):
+    import torch
+    import sam3cu
+    torch.cuda.set_device(0)
+    sam3cu.init(0)
+    dev = torch.device("cuda", 0)
+    fn = {"dropin": dropin_leg, "sweep": gemm_sweep_leg, "q8": q8_legs, "neck": neck_leg,
+          "tinyvit": tinyvit_leg}[args.leg]
+    print(json.dumps({"leg": args.leg, "result": fn(args, dev, sam3cu)}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -528,7 +581,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--no-tinyvit", action="store_true", help="skip the config-5 TinyViT leg")
+    ap.add_argument("--dropin-iters", type=int, default=3)
+    ap.add_argument("--leg", default=None,
+                    choices=["dropin", "sweep", "q8", "neck", "tinyvit"],
+                    help="run one side leg alone on GPU 0 and print its result")
     args = ap.parse_args()
+    if args.leg:
+        return run_leg(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

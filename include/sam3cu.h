@@ -115,7 +115,9 @@ SAM3CU_API int sam3cu_linear(const void *x, int x_dtype, const void *w, const fl
 /*
  * Same as sam3cu_linear with a Q8_0 weight, already repacked on the device
  * by sam3cu_q8_repack: q [N,K] int8 and scales [K/32, N] F32.  K % 64 == 0.
- * x is BF16 or F16 (the weight is dequantised to that type on chip).
+ * x is BF16 or F16 (the weight is dequantised to that type on chip), or
+ * F32 as cpu_kernel_matmul_q8 takes it (cpu_matmul_q8.c:168-235): F32 x is
+ * rounded to BF16 inside the call, in a stream-ordered buffer.
  */
 SAM3CU_API int sam3cu_linear_q8(const void *x, int x_dtype, const int8_t *q,
 		     const float *scales, const float *bias,
@@ -291,6 +293,14 @@ SAM3CU_API int sam3cu_memcpy_h2d(void *dst, const void *host_src, size_t n, void
 SAM3CU_API int sam3cu_memcpy_d2h(void *host_dst, const void *src, size_t n, void *stream);
 SAM3CU_API int sam3cu_memcpy_d2d(void *dst, const void *src, size_t n, void *stream);
 
+/* Strided gather into a contiguous tensor: dst[i0,..,i3] =
+ * src[sum_k i_k * strides[k]] (element strides, up to 4 dims).  The
+ * backend's lowering keeps PERMUTE / SLICE / RESHAPE results as strided
+ * views and calls this only where a consumer needs contiguous data
+ * (cpu_transpose.c:312-387, cpu_slice.c). */
+SAM3CU_API int sam3cu_gather_strided(const void *src, void *dst, int elem_size, int n_dims,
+				     const int *dims, const int64_t *strides, void *stream);
+
 /* TRANSPOSE / PERMUTE of up to 4 dims (cpu_transpose.c:312-387):
  * out dims[i] = dims[perm[i]]; elem_size 1, 2 or 4 bytes. */
 SAM3CU_API int sam3cu_permute(const void *src, void *dst, int elem_size, int n_dims,
@@ -313,6 +323,14 @@ SAM3CU_API int sam3cu_gelu(const void *x, void *y, int dtype, int64_t n, void *s
 SAM3CU_API int sam3cu_rope(const void *x, const float *cos_t, const float *sin_t, void *y,
 			   int dtype, int batch, int seq, int heads, int hd, void *stream);
 
+/* ROPE as above on row-strided data: row (b, s) of heads*hd elements
+ * starts at (b*seq + s)*ldx in x and (b*seq + s)*ldy in y (element
+ * strides).  Lets the backend rotate the Q / K column slices of the fused
+ * QKV output without materialising the SLICE (graph_helpers.c:771-800). */
+SAM3CU_API int sam3cu_rope_rows(const void *x, int64_t ldx, const float *cos_t,
+				const float *sin_t, void *y, int64_t ldy, int dtype, int batch,
+				int seq, int heads, int hd, void *stream);
+
 /* CAST between F32, F16 and BF16 (cpu_cast.c), round to nearest even. */
 SAM3CU_API int sam3cu_cast(const void *x, int x_dtype, void *y, int y_dtype, int64_t n,
 			   void *stream);
@@ -322,6 +340,19 @@ SAM3CU_API int sam3cu_cast(const void *x, int x_dtype, void *y, int y_dtype, int
 SAM3CU_API int sam3cu_sdpa_f32(const float *q, const float *k, const float *v,
 			       const float *mask, float *o, int bh, int sq, int sk, int hd,
 			       void *stream);
+
+/* F32 SDPA (cpu_sdpa.c:216-288) on strided tensors: element (b, h, s, d)
+ * of Q lies at q[b*qs[0] + h*qs[1] + s*qs[2] + d] (K, V, O likewise), so the
+ * [B,S,H,hd] <-> [B,H,S,hd] permutes around gh_multihead_attention_rope's
+ * SDPA (graph_helpers.c:840-880) need no copies.  hd 32 or 64; pointers
+ * 16-byte aligned, strides multiples of 4; optional additive [sq, sk] mask
+ * shared by every (b, h). */
+SAM3CU_API int sam3cu_sdpa_f32_strided(const float *q, const int64_t *q_strides,
+				       const float *k, const int64_t *k_strides,
+				       const float *v, const int64_t *v_strides,
+				       const float *mask, float *o, const int64_t *o_strides,
+				       int batch, int heads, int sq, int sk, int hd,
+				       void *stream);
 
 /* Elementwise a * b with b broadcast over a trailing suffix of a's dims
  * (n % nb == 0): SAM3_OP_MUL (cpu_elementwise.c). */

@@ -18,7 +18,24 @@ int linear_common(const void* x, int x_dtype, const void* w, const int8_t* q, co
                   const float* residual, void* y, int y_dtype, int M, int K, int N, int act, void* stream) {
   if (!x || !y || (!w && !q) || M < 0 || K <= 0 || N <= 0) return SAM3CU_EINVAL;
   if (x_dtype != SAM3CU_BF16 && x_dtype != SAM3CU_F16 && x_dtype != SAM3CU_F32) return SAM3CU_EDTYPE;
-  if (x_dtype == SAM3CU_F32 && q) return SAM3CU_EDTYPE;  // Q8 weights take 16-bit activations
+  if (x_dtype == SAM3CU_F32 && q) {
+    // F32 activations x Q8_0 weights (cpu_matmul_q8.c:168-235 takes F32 A):
+    // A is rounded to BF16 in a stream-ordered buffer inside the call, then
+    // the 16-bit path below runs (Q8's own rounding dominates the error)
+    if (!x || !y || M < 0 || K <= 0 || N <= 0) return SAM3CU_EINVAL;
+    if (M == 0) return SAM3CU_OK;
+    cudaStream_t st = as_stream(stream);
+    void* xb = nullptr;
+    const size_t nb = static_cast<size_t>(M) * K * 2;
+    if (cudaMallocAsync(&xb, nb, st) != cudaSuccess) {
+      cudaGetLastError();
+      return SAM3CU_ENOMEM2;
+    }
+    int rc = sam3cu_cast(x, SAM3CU_F32, xb, SAM3CU_BF16, static_cast<int64_t>(M) * K, stream);
+    if (!rc) rc = linear_common(xb, SAM3CU_BF16, w, q, sc, bias, residual, y, y_dtype, M, K, N, act, stream);
+    cudaFreeAsync(xb, st);
+    return rc;
+  }
   if (y_dtype != SAM3CU_F32 && y_dtype != SAM3CU_BF16 && y_dtype != SAM3CU_F16) return SAM3CU_EDTYPE;
   if (act != SAM3CU_ACT_NONE && act != SAM3CU_ACT_GELU_TANH) return SAM3CU_EINVAL;
   if (residual == y && y_dtype != SAM3CU_F32) return SAM3CU_EINVAL;

@@ -9,14 +9,28 @@
  * GEMM reads W [N,K] K-major), an ADD of a [N] bias to a MATMUL output and
  * a following GELU are fused into the GEMM epilogue.
  *
+ * Views: RESHAPE, TRANSPOSE/PERMUTE and SLICE produce no data.  Their
+ * result is a strided view of the input's device buffer (element strides
+ * per dim); ROPE, SDPA and MATMUL's B operand read views directly, every
+ * other consumer gets a contiguous copy made on first use.  SDPA writes its
+ * output [B,H,S,hd] with head-interleaved strides, so the permute(0,2,1,3)
+ * + reshape that gh_multihead_attention_rope puts after it
+ * (graph_helpers.c:840-880) are free, and the F32 / 16-bit attention
+ * kernels read Q, K and V where the QKV GEMM wrote them.
+ *
  * Memory: graph inputs are copied host->device from t->data (non-ephemeral
- * ones once, then cached by header address); node outputs get device
- * buffers for the duration of graph_eval (RESHAPE aliases its input);
- * outputs no later node consumes are copied back to t->data.
+ * ones once, then cached by header address).  Node outputs come from a
+ * device arena owned by the backend: a bump allocator over one buffer that
+ * is reset at the end of every graph_eval and regrown (once) to the
+ * largest demand seen, so a steady stream of graphs makes no cudaMalloc /
+ * cudaFree calls.  Outputs no later node consumes are copied back to
+ * t->data; under g->no_readback they get their own device buffer instead
+ * and stay cached for the next graph.
  */
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include "../../include/sam3cu_backend.h"
 
@@ -29,6 +43,17 @@ struct devent {                   /* device copy of a host tensor */
 	void                     *dptr;
 	int                       kind;   /* 0 empty, 1 cached input, 2 graph-local */
 	const void               *aux;    /* derived buffer (f32 bias, q8 repack...) */
+	int                       view;   /* dptr + str describe a strided view */
+	int                       own;    /* graph-local dptr owned (not arena) */
+	int64_t                   str[SAM3_MAX_DIMS];  /* element strides (view) */
+};
+
+/* bump allocator for graph-local device buffers */
+struct arena {
+	char   *base;
+	size_t  cap, off, need;
+	void  **extra;                    /* overflow allocations of this graph */
+	size_t  nextra, capextra;
 };
 
 struct hostblk {
@@ -40,8 +65,11 @@ struct impl {
 	struct devent   *map;             /* open addressing on tensor address */
 	size_t           cap, used;
 	struct hostblk  *host;            /* alloc_tensor buffers */
-	void           **tmp;             /* graph-local device allocations */
-	size_t           ntmp, captmp;
+	struct arena     ar;              /* graph-local device buffers */
+	struct sam3_graph *g;             /* graph being evaluated */
+	int              prof;            /* SAM3CU_VTABLE_PROFILE set */
+	double           prof_s[SAM3_OP_COUNT + 2];
+	long             prof_n[SAM3_OP_COUNT + 2];
 	/* per-graph scratch tables, sized to n_nodes */
 	int             *uses;
 	int             *flags;
@@ -101,6 +129,13 @@ static enum sam3_error st(int rc)
 	fprintf(stderr, "[sam3cu] %s:%d: %s failed: %s\n", __FILE__, __LINE__, #x, \
 		sam3cu_strerror(x)); return e_; } } while (0)
 
+static double now_s(void)
+{
+	struct timespec ts;
+	clock_gettime(CLOCK_MONOTONIC, &ts);
+	return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
 /* ------------------------------------------------------------------ map */
 
 static size_t hptr(const void *p, size_t cap)
@@ -127,7 +162,7 @@ static struct devent *map_find(struct impl *m, const struct sam3_tensor *t)
 
 static void devent_free(struct devent *e)
 {
-	if (e->dptr && e->kind == 1)
+	if (e->dptr && (e->kind == 1 || e->own))
 		sam3cu_dev_free(e->dptr);
 	if (e->aux)
 		sam3cu_dev_free((void *)e->aux);
@@ -185,6 +220,11 @@ static void map_drop_local(struct impl *m)
 		if (m->map[i].kind == 2) {
 			if (m->map[i].aux)
 				sam3cu_dev_free((void *)m->map[i].aux);
+			if (m->map[i].own && m->map[i].dptr)
+				sam3cu_dev_free(m->map[i].dptr);
+			m->map[i].dptr = NULL;
+			m->map[i].aux = NULL;
+			m->map[i].own = 0;
 			m->map[i].kind = -1; /* tombstone */
 			any = 1;
 		}
@@ -194,24 +234,62 @@ static void map_drop_local(struct impl *m)
 
 static enum sam3_error tmp_alloc(struct impl *m, size_t bytes, void **p)
 {
-	if (m->ntmp == m->captmp) {
-		size_t nc = m->captmp ? m->captmp * 2 : 256;
-		void **n = realloc(m->tmp, nc * sizeof(void *));
+	struct arena *a = &m->ar;
+	bytes = (bytes + 255) & ~(size_t)255;
+	if (!bytes)
+		bytes = 256;
+	a->need += bytes;
+	if (a->base && a->off + bytes <= a->cap) {
+		*p = a->base + a->off;
+		a->off += bytes;
+		return SAM3_OK;
+	}
+	/* past the arena: a separate buffer for this graph; the arena grows to
+	 * the whole demand when the graph ends */
+	if (a->nextra == a->capextra) {
+		size_t nc = a->capextra ? a->capextra * 2 : 64;
+		void **n = realloc(a->extra, nc * sizeof(void *));
 		if (!n)
 			return SAM3_ENOMEM;
-		m->tmp = n;
-		m->captmp = nc;
+		a->extra = n;
+		a->capextra = nc;
 	}
-	TRY(sam3cu_dev_alloc(p, (bytes + 255) & ~(size_t)255));
-	m->tmp[m->ntmp++] = *p;
+	TRY(sam3cu_dev_alloc(p, bytes));
+	a->extra[a->nextra++] = *p;
 	return SAM3_OK;
 }
 
+/* end of a graph (the stream is idle): release the overflow buffers and
+ * regrow the arena to this graph's total demand */
 static void tmp_free_all(struct impl *m)
 {
-	for (size_t i = 0; i < m->ntmp; i++)
-		sam3cu_dev_free(m->tmp[i]);
-	m->ntmp = 0;
+	struct arena *a = &m->ar;
+	for (size_t i = 0; i < a->nextra; i++)
+		sam3cu_dev_free(a->extra[i]);
+	if (a->nextra && a->need > a->cap) {
+		size_t ncap = (a->need + a->need / 8 + ((size_t)1 << 20) - 1) & ~(((size_t)1 << 20) - 1);
+		void *nb = NULL;
+		if (a->base)
+			sam3cu_dev_free(a->base);
+		a->base = NULL;
+		a->cap = 0;
+		if (sam3cu_dev_alloc(&nb, ncap) == 0) {
+			a->base = nb;
+			a->cap = ncap;
+		}
+	}
+	a->nextra = 0;
+	a->off = 0;
+	a->need = 0;
+}
+
+static void arena_release(struct impl *m)
+{
+	tmp_free_all(m);
+	if (m->ar.base)
+		sam3cu_dev_free(m->ar.base);
+	free(m->ar.extra);
+	memset(&m->ar, 0, sizeof(m->ar));
 }
 
 /* ------------------------------------------------------------------ vtable */
@@ -228,6 +306,8 @@ static enum sam3_error cu_init(struct sam3_backend *be)
 		free(m);
 		return SAM3_EBACKEND;
 	}
+	const char *pv = getenv("SAM3CU_VTABLE_PROFILE");
+	m->prof = pv && *pv && *pv != '0';
 	cb->impl = m;
 	return SAM3_OK;
 }
@@ -247,12 +327,25 @@ static void cu_free(struct sam3_backend *be)
 	if (!m)
 		return;
 	sam3cu_stream_sync(m->stream);
-	tmp_free_all(m);
+	if (m->prof) {
+		static const char *names[SAM3_OP_COUNT + 2] = {
+			[SAM3_OP_MATMUL] = "MATMUL", [SAM3_OP_ADD] = "ADD", [SAM3_OP_MUL] = "MUL",
+			[SAM3_OP_SOFTMAX] = "SOFTMAX", [SAM3_OP_GELU] = "GELU",
+			[SAM3_OP_LAYERNORM] = "LAYERNORM", [SAM3_OP_CONV2D] = "CONV2D",
+			[SAM3_OP_RESHAPE] = "RESHAPE", [SAM3_OP_TRANSPOSE] = "TRANSPOSE",
+			[SAM3_OP_CAST] = "CAST", [SAM3_OP_CONCAT] = "CONCAT", [SAM3_OP_SLICE] = "SLICE",
+			[SAM3_OP_ROPE] = "ROPE", [SAM3_OP_SDPA] = "SDPA",
+			[SAM3_OP_COUNT] = "readback", [SAM3_OP_COUNT + 1] = "graph_eval total"};
+		for (int i = 0; i < SAM3_OP_COUNT + 2; i++)
+			if (m->prof_n[i])
+				fprintf(stderr, "[sam3cu profile] %-18s %6ld calls %10.3f ms\n",
+					names[i] ? names[i] : "other", m->prof_n[i], 1e3 * m->prof_s[i]);
+	}
+	arena_release(m);
 	for (size_t i = 0; i < m->cap; i++)
 		if (m->map[i].kind > 0)
 			devent_free(&m->map[i]);
 	free(m->map);
-	free(m->tmp);
 	free(m->uses);
 	free(m->flags);
 	host_free_all(m);
@@ -314,13 +407,42 @@ static void cu_cache_invalidate(struct sam3_backend *be, const void *start,
 		map_rehash(m, m->cap);
 }
 
-/* device pointer of a tensor that is produced in this graph or is an input */
-static enum sam3_error dev_of(struct impl *m, const struct sam3_tensor *t,
-			      int produced, void **p)
+static void contig_strides(const struct sam3_tensor *t, int64_t *str)
+{
+	int64_t acc = 1;
+	for (int i = t->n_dims - 1; i >= 0; i--) {
+		str[i] = acc;
+		acc *= t->dims[i];
+	}
+}
+
+static int is_contig(const struct sam3_tensor *t, const int64_t *str)
+{
+	int64_t acc = 1;
+	for (int i = t->n_dims - 1; i >= 0; i--) {
+		if (t->dims[i] != 1 && str[i] != acc)
+			return 0;
+		acc *= t->dims[i];
+	}
+	return 1;
+}
+
+static int uses_of(struct sam3_graph *g, const struct sam3_tensor *t);
+
+/* device pointer (and element strides) of a tensor produced in this graph
+ * or a graph input; a view is returned as such */
+static enum sam3_error dev_view(struct impl *m, const struct sam3_tensor *t,
+				int produced, void **p, int64_t *str)
 {
 	struct devent *e = map_find(m, t);
 	if (e && (e->kind == 2 || (e->data == t->data && e->nbytes == tbytes(t)))) {
 		*p = e->dptr;
+		if (str) {
+			if (e->view)
+				memcpy(str, e->str, sizeof(e->str));
+			else
+				contig_strides(t, str);
+		}
 		return SAM3_OK;
 	}
 	if (produced) {
@@ -349,21 +471,99 @@ static enum sam3_error dev_of(struct impl *m, const struct sam3_tensor *t,
 	e->dptr = d;
 	e->kind = t->ephemeral ? 2 : 1;
 	*p = d;
+	if (str)
+		contig_strides(t, str);
+	return SAM3_OK;
+}
+
+/* contiguous device pointer: a view is gathered into an arena buffer on
+ * first use, and the entry then refers to that copy */
+static enum sam3_error dev_of(struct impl *m, const struct sam3_tensor *t,
+			      int produced, void **p)
+{
+	TRY(dev_view(m, t, produced, p, NULL));
+	struct devent *e = map_find(m, t);
+	if (!e || !e->view)
+		return SAM3_OK;
+	size_t es = dsize(t->dtype);
+	void *c;
+	if (!es)
+		return SAM3_EDTYPE;
+	TRY(tmp_alloc(m, tbytes(t), &c));
+	TRY(sam3cu_gather_strided(e->dptr, c, (int)es, t->n_dims, t->dims, e->str, m->stream));
+	e->dptr = c;
+	e->view = 0;
+	*p = c;
+	return SAM3_OK;
+}
+
+/* register `t` as a view of device memory p with element strides str */
+static enum sam3_error set_view(struct impl *m, const struct sam3_tensor *t, void *p,
+				const int64_t *str)
+{
+	struct devent *e = map_insert(m, t);
+	if (!e)
+		return SAM3_ENOMEM;
+	e->data = t->data;
+	e->nbytes = tbytes(t);
+	e->dptr = p;
+	e->kind = 2;
+	e->view = !is_contig(t, str);
+	memcpy(e->str, str, sizeof(int64_t) * (size_t)t->n_dims);
 	return SAM3_OK;
 }
 
 static enum sam3_error out_buf(struct impl *m, const struct sam3_tensor *t,
 			       void **p)
 {
-	TRY(tmp_alloc(m, tbytes(t), p));
+	/* a graph output that stays resident (no_readback) gets its own buffer:
+	 * it outlives this graph's arena */
+	int keep = m->g && m->g->no_readback && uses_of(m->g, t) == 0;
+	if (keep)
+		TRY(sam3cu_dev_alloc(p, tbytes(t)));
+	else
+		TRY(tmp_alloc(m, tbytes(t), p));
 	struct devent *e = map_insert(m, t);
-	if (!e)
+	if (!e) {
+		if (keep)
+			sam3cu_dev_free(*p);
 		return SAM3_ENOMEM;
+	}
 	e->data = t->data;
 	e->nbytes = tbytes(t);
 	e->dptr = *p;
 	e->kind = 2;
+	e->own = keep;
 	return SAM3_OK;
+}
+
+/* strides of the tensor `to` (dims) viewing the same elements as one with
+ * dims `from` and strides fs, without a copy; 0 if no such strides exist
+ * (the grouping of dims into chunks that are contiguous in memory) */
+static int reshape_strides(const struct sam3_tensor *from, const int64_t *fs,
+			   const struct sam3_tensor *to, int64_t *ts)
+{
+	int vd = to->n_dims - 1;
+	int64_t base = fs[from->n_dims - 1], tn = 1, vn = 1;
+	for (int d = from->n_dims - 1; d >= 0; d--) {
+		tn *= from->dims[d];
+		int chunk_end = d == 0 || (from->dims[d - 1] != 1 && fs[d - 1] != tn * base);
+		if (!chunk_end)
+			continue;
+		while (vd >= 0 && (vn < tn || to->dims[vd] == 1)) {
+			ts[vd] = vn * base;
+			vn *= to->dims[vd];
+			vd--;
+		}
+		if (vn != tn)
+			return 0;
+		if (d > 0) {
+			base = fs[d - 1];
+			tn = 1;
+			vn = 1;
+		}
+	}
+	return vd == -1;
 }
 
 static int is_16(enum sam3_dtype d)
@@ -539,12 +739,19 @@ static enum sam3_error op_matmul(struct impl *m, struct sam3_graph *g, int ni)
 	if (lazy) {
 		TRY(dev_of(m, w, produced_in(g, ni, w), &pw));
 	} else {
-		/* B [K,N] -> [N,K] */
+		/* B [K,N]: a transposed view of a contiguous [N,K] is used as it
+		 * lies; otherwise B is transposed into [N,K] */
 		void *pbk;
-		TRY(dev_of(m, b, produced_in(g, ni, b), &pbk));
-		TRY(tmp_alloc(m, (size_t)K * N * dsize(b->dtype), &pw));
-		int dims[2] = {K, N}, perm[2] = {1, 0};
-		TRY(sam3cu_permute(pbk, pw, (int)dsize(b->dtype), 2, dims, perm, m->stream));
+		int64_t bs[SAM3_MAX_DIMS];
+		TRY(dev_view(m, b, produced_in(g, ni, b), &pbk, bs));
+		if (b->n_dims == 2 && bs[0] == 1 && bs[1] == K) {
+			pw = pbk;
+		} else {
+			TRY(dev_of(m, b, produced_in(g, ni, b), &pbk));
+			TRY(tmp_alloc(m, (size_t)K * N * dsize(b->dtype), &pw));
+			int dims[2] = {K, N}, perm[2] = {1, 0};
+			TRY(sam3cu_permute(pbk, pw, (int)dsize(b->dtype), 2, dims, perm, m->stream));
+		}
 	}
 	TRY(sam3cu_linear(pa, a->dtype, pw, pb, NULL, py, dst->dtype, (int)M, K, N, act,
 			  m->stream));
@@ -564,25 +771,23 @@ static enum sam3_error op_node(struct impl *m, struct sam3_graph *g, int ni)
 	case SAM3_OP_MATMUL:
 		return op_matmul(m, g, ni);
 
-	case SAM3_OP_RESHAPE: {  /* alias (cpu_reshape.c:20-38) */
+	case SAM3_OP_RESHAPE: {  /* a view (cpu_reshape.c:20-38) */
+		int64_t xs[SAM3_MAX_DIMS], ys[SAM3_MAX_DIMS];
 		if (tbytes(out) != tbytes(x))
 			return SAM3_EINVAL;
-		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
-		struct devent *e = map_insert(m, out);
-		if (!e)
-			return SAM3_ENOMEM;
-		e->data = out->data;
-		e->nbytes = tbytes(out);
-		e->dptr = px;
-		e->kind = 2;
-		return SAM3_OK;
+		TRY(dev_view(m, x, produced_in(g, ni, x), &px, xs));
+		if (x->dtype == SAM3_DTYPE_Q8_0 || !reshape_strides(x, xs, out, ys)) {
+			TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+			contig_strides(out, ys);
+		}
+		return set_view(m, out, px, ys);
 	}
 
-	case SAM3_OP_TRANSPOSE: {
-		size_t es = dsize(x->dtype);
-		if (!es)
+	case SAM3_OP_TRANSPOSE: {  /* a view with permuted strides (cpu_transpose.c:312-387) */
+		int64_t xs[SAM3_MAX_DIMS], ys[SAM3_MAX_DIMS];
+		if (!dsize(x->dtype))
 			return SAM3_EDTYPE;
-		int axes[4], has = 0, nd_ = x->n_dims;
+		int axes[SAM3_MAX_DIMS], has = 0, nd_ = x->n_dims;
 		for (int i = 0; i < nd_; i++) {
 			axes[i] = nd->params[i];
 			if (axes[i])
@@ -596,21 +801,28 @@ static enum sam3_error op_node(struct impl *m, struct sam3_graph *g, int ni)
 				axes[nd_ - 1] = nd_ - 2;
 			}
 		}
-		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
-		TRY(out_buf(m, out, &py));
-		TRY(sam3cu_permute(px, py, (int)es, nd_, x->dims, axes, m->stream));
-		return SAM3_OK;
+		if (out->n_dims != nd_)
+			return SAM3_EINVAL;
+		TRY(dev_view(m, x, produced_in(g, ni, x), &px, xs));
+		for (int i = 0; i < nd_; i++) {
+			if (axes[i] < 0 || axes[i] >= nd_ || out->dims[i] != x->dims[axes[i]])
+				return SAM3_EINVAL;
+			ys[i] = xs[axes[i]];
+		}
+		return set_view(m, out, px, ys);
 	}
 
-	case SAM3_OP_SLICE: {
+	case SAM3_OP_SLICE: {  /* a view: [start, end) along params[0] (cpu_slice.c) */
+		int64_t xs[SAM3_MAX_DIMS];
 		size_t es = dsize(x->dtype);
+		int axis = nd->params[0], start = nd->params[1];
 		if (!es)
 			return SAM3_EDTYPE;
-		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
-		TRY(out_buf(m, out, &py));
-		TRY(sam3cu_slice(px, py, (int)es, x->n_dims, x->dims, nd->params[0],
-				 nd->params[1], nd->params[2], m->stream));
-		return SAM3_OK;
+		if (axis < 0 || axis >= x->n_dims || start < 0 || out->n_dims != x->n_dims ||
+		    start + out->dims[axis] > x->dims[axis])
+			return SAM3_EINVAL;
+		TRY(dev_view(m, x, produced_in(g, ni, x), &px, xs));
+		return set_view(m, out, (char *)px + (size_t)start * (size_t)xs[axis] * es, xs);
 	}
 
 	case SAM3_OP_BIAS_ADD:  /* NHWC x + bias[C] (cpu_bias_add.c) */
@@ -713,40 +925,102 @@ static enum sam3_error op_node(struct impl *m, struct sam3_graph *g, int ni)
 		return SAM3_OK;
 	}
 
-	case SAM3_OP_ROPE: {
+	case SAM3_OP_ROPE: {  /* [B,S,H,hd]; reads a row-strided view in place */
 		struct sam3_tensor *cs = nd->inputs[1], *sn = nd->inputs[2];
 		void *pc, *ps;
+		int64_t xs[SAM3_MAX_DIMS];
 		if (x->n_dims != 4 || !cs || !sn || cs->dtype != SAM3_DTYPE_F32 ||
 		    sn->dtype != SAM3_DTYPE_F32)
 			return SAM3_EINVAL;
-		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+		TRY(dev_view(m, x, produced_in(g, ni, x), &px, xs));
+		int hd = x->dims[3], H = x->dims[2], S_ = x->dims[1];
+		if (!(xs[3] == 1 && xs[2] == hd && xs[1] >= (int64_t)H * hd &&
+		      xs[0] == (int64_t)S_ * xs[1])) {
+			TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+			xs[1] = (int64_t)H * hd;
+		}
 		TRY(dev_of(m, cs, produced_in(g, ni, cs), &pc));
 		TRY(dev_of(m, sn, produced_in(g, ni, sn), &ps));
 		TRY(out_buf(m, out, &py));
-		TRY(sam3cu_rope(px, pc, ps, py, x->dtype, x->dims[0], x->dims[1], x->dims[2],
-				x->dims[3], m->stream));
+		TRY(sam3cu_rope_rows(px, xs[1], pc, ps, py, (int64_t)H * hd, x->dtype, x->dims[0],
+				     S_, H, hd, m->stream));
 		return SAM3_OK;
 	}
 
-	case SAM3_OP_SDPA: {  /* [S,hd] or [B,H,S,hd], optional mask [Sq,Sk] */
+	case SAM3_OP_SDPA: {  /* [S,hd] or [B,H,S,hd], optional mask [Sq,Sk] (cpu_sdpa.c:216-288) */
 		struct sam3_tensor *k = nd->inputs[1], *v = nd->inputs[2];
 		struct sam3_tensor *mk = nd->n_inputs > 3 ? nd->inputs[3] : NULL;
 		void *pk, *pv, *pm = NULL;
+		int64_t qs[SAM3_MAX_DIMS], ks[SAM3_MAX_DIMS], vs[SAM3_MAX_DIMS];
 		int hd = x->dims[x->n_dims - 1];
 		int sq = x->dims[x->n_dims - 2], sk = k->dims[k->n_dims - 2];
-		int bh = (int)(nelems(x) / ((int64_t)sq * hd));
-		TRY(dev_of(m, x, produced_in(g, ni, x), &px));
-		TRY(dev_of(m, k, produced_in(g, ni, k), &pk));
-		TRY(dev_of(m, v, produced_in(g, ni, v), &pv));
+		int four = x->n_dims == 4 && k->n_dims == 4 && v->n_dims == 4 && out->n_dims == 4;
+		int B = four ? x->dims[0] : 1;
+		int H = four ? x->dims[1] : (int)(nelems(x) / ((int64_t)sq * hd));
+		if (k->dtype != x->dtype || v->dtype != x->dtype || k->dims[k->n_dims - 1] != hd)
+			return SAM3_EINVAL;
+		if (four) {
+			TRY(dev_view(m, x, produced_in(g, ni, x), &px, qs));
+			TRY(dev_view(m, k, produced_in(g, ni, k), &pk, ks));
+			TRY(dev_view(m, v, produced_in(g, ni, v), &pv, vs));
+		} else {  /* leading dims flattened into heads of one batch */
+			TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+			TRY(dev_of(m, k, produced_in(g, ni, k), &pk));
+			TRY(dev_of(m, v, produced_in(g, ni, v), &pv));
+			qs[1] = (int64_t)sq * hd, qs[2] = hd, qs[3] = 1;
+			ks[1] = vs[1] = (int64_t)sk * hd, ks[2] = vs[2] = hd, ks[3] = vs[3] = 1;
+			qs[0] = qs[1] * H, ks[0] = vs[0] = ks[1] * H;
+		}
 		if (mk)
 			TRY(dev_of(m, mk, produced_in(g, ni, mk), &pm));
-		TRY(out_buf(m, out, &py));
+		/* the output in head-interleaved order [B,S,H,hd]: the permute(0,2,1,3)
+		 * that follows in gh_multihead_attention_rope is then contiguous */
+		int64_t ld_o = (int64_t)H * hd;
+		int64_t os[SAM3_MAX_DIMS] = {(int64_t)sq * ld_o, hd, ld_o, 1};
+		void *buf;
+		TRY(tmp_alloc(m, tbytes(out), &buf));
+		if (four) {
+			TRY(set_view(m, out, buf, os));
+		} else {
+			struct devent *e = map_insert(m, out);
+			if (!e)
+				return SAM3_ENOMEM;
+			e->data = out->data;
+			e->nbytes = tbytes(out);
+			e->dptr = buf;
+			e->kind = 2;
+		}
 		if (x->dtype == SAM3_DTYPE_F32) {
-			TRY(sam3cu_sdpa_f32(px, pk, pv, pm, py, bh, sq, sk, hd, m->stream));
+			int64_t q3[3] = {qs[0], qs[1], qs[2]}, k3[3] = {ks[0], ks[1], ks[2]};
+			int64_t v3[3] = {vs[0], vs[1], vs[2]};
+			int64_t o3[3] = {(int64_t)sq * ld_o, hd, ld_o};
+			if (!four)
+				o3[0] = 0, o3[1] = (int64_t)sq * hd, o3[2] = hd;
+			if (qs[3] != 1 || ks[3] != 1 || vs[3] != 1)
+				return SAM3_EINVAL;
+			TRY(sam3cu_sdpa_f32_strided(px, q3, pk, k3, pv, v3, pm, buf, o3, B, H, sq, sk,
+						    hd, m->stream));
 			return SAM3_OK;
 		}
+		/* 16-bit: the tcgen05 kernel reads Q/K/V rows (b*S + s) of one
+		 * shared pitch with head h at column h*hd, and writes O the same way */
 		if (is_16(x->dtype) && !mk && sq == sk && hd == 64) {
-			TRY(sam3cu_sdpa(px, pk, pv, 64, py, 64, x->dtype, bh, sq, 1, 64, m->stream));
+			int64_t ld = qs[2];
+			int ok = qs[3] == 1 && ks[3] == 1 && vs[3] == 1 && qs[1] == hd && ks[1] == hd &&
+				 vs[1] == hd && ks[2] == ld && vs[2] == ld && qs[0] == sq * ld &&
+				 ks[0] == sk * ld && vs[0] == sk * ld;
+			if (!ok) {
+				TRY(dev_of(m, x, produced_in(g, ni, x), &px));
+				TRY(dev_of(m, k, produced_in(g, ni, k), &pk));
+				TRY(dev_of(m, v, produced_in(g, ni, v), &pv));
+				/* contiguous [B,H,S,hd]: one group per (b, h), one head */
+				TRY(sam3cu_sdpa(px, pk, pv, 64, buf, 64, x->dtype, B * H, sq, 1, 64,
+						m->stream));
+				int64_t cs_[SAM3_MAX_DIMS];
+				contig_strides(out, cs_);
+				return set_view(m, out, buf, cs_);
+			}
+			TRY(sam3cu_sdpa(px, pk, pv, ld, buf, ld_o, x->dtype, B, sq, H, 64, m->stream));
 			return SAM3_OK;
 		}
 		return SAM3_EDTYPE;
@@ -866,6 +1140,11 @@ static int count_uses(struct sam3_graph *g, int from, const struct sam3_tensor *
 	return n;
 }
 
+static int uses_of(struct sam3_graph *g, const struct sam3_tensor *t)
+{
+	return count_uses(g, 0, t);
+}
+
 /* mark the peepholes: lazy W transposes, bias / GELU fusion into MATMUL */
 static void plan(struct impl *m, struct sam3_graph *g)
 {
@@ -930,61 +1209,78 @@ static enum sam3_error cu_graph_eval(struct sam3_backend *be,
 		m->nflags = g->n_nodes;
 	}
 	plan(m, g);
+	m->g = g;
+	double t_eval0 = m->prof ? now_s() : 0.0;
 	for (int i = 0; i < g->n_nodes; i++) {
 		if (m->flags[i] & F_SKIP)
 			continue;
+		double t0 = 0.0;
+		if (m->prof) {
+			sam3cu_stream_sync(m->stream);
+			t0 = now_s();
+		}
 		err = op_node(m, g, i);
+		if (m->prof) {
+			int op = g->nodes[i].op;
+			sam3cu_stream_sync(m->stream);
+			if (op >= 0 && op < SAM3_OP_COUNT) {
+				m->prof_s[op] += now_s() - t0;
+				m->prof_n[op]++;
+			}
+		}
 		if (err != SAM3_OK) {
 			fprintf(stderr, "[sam3cu] graph_eval: node %d (op=%d) failed (%d)\n", i,
 				(int)g->nodes[i].op, (int)err);
 			break;
 		}
 	}
-	/* outputs nobody in this graph consumes go back to host (or stay cached) */
+	double t_rb0 = m->prof ? now_s() : 0.0;
+	/* outputs nobody in this graph consumes go back to host (or stay
+	 * resident); a fused MATMUL's result is its ADD / GELU node's output */
 	for (int i = 0; err == SAM3_OK && i < g->n_nodes; i++) {
 		struct sam3_tensor *t = g->nodes[i].output;
-		if (m->flags[i] & F_SKIP)
+		if (m->flags[i] & (F_BIAS_FUSED | F_GELU_FUSED))
+			continue;  /* the fused chain's last node holds the result */
+		if ((m->flags[i] & F_SKIP) && g->nodes[i].op == SAM3_OP_TRANSPOSE)
 			continue;
 		if (count_uses(g, i + 1, t))
 			continue;
-		/* a fused MATMUL writes the final ADD/GELU tensor: find what it wrote */
 		struct devent *e = map_find(m, t);
-		if ((m->flags[i] & F_BIAS_FUSED))
-			continue;  /* its ADD (skipped) output is handled below */
 		if (!e)
 			continue;
+		void *d;
+		if ((err = dev_of(m, t, 1, &d)) != SAM3_OK)  /* views made contiguous */
+			break;
 		if (g->no_readback) {
-			e->kind = 1;  /* keep resident for the next graph */
-			e->data = t->data;
-			void *keep;
-			if (sam3cu_dev_alloc(&keep, e->nbytes) == 0) {
+			if (!e->own) {  /* an alias of arena memory: copy it out */
+				void *keep;
+				if (sam3cu_dev_alloc(&keep, e->nbytes) != 0) {
+					err = SAM3_ENOMEM;
+					break;
+				}
 				sam3cu_memcpy_d2d(keep, e->dptr, e->nbytes, m->stream);
 				e->dptr = keep;
 			}
+			e->kind = 1;  /* keep resident for the next graph */
+			e->own = 0;
+			e->data = t->data;
 		} else if (t->data) {
 			if (sam3cu_memcpy_d2h(t->data, e->dptr, tbytes(t), m->stream) != 0)
 				err = SAM3_EBACKEND;
 		}
 	}
-	/* fused outputs (the ADD / GELU tensors written by a MATMUL) */
-	for (int i = 0; err == SAM3_OK && i < g->n_nodes; i++) {
-		if (!(m->flags[i] & F_SKIP) || g->nodes[i].op == SAM3_OP_TRANSPOSE)
-			continue;
-		struct sam3_tensor *t = g->nodes[i].output;
-		if (count_uses(g, i + 1, t))
-			continue;
-		if ((m->flags[i] & F_GELU_FUSED))
-			continue;  /* the GELU node holds the result */
-		struct devent *e = map_find(m, t);
-		if (!e || !t->data || g->no_readback)
-			continue;
-		if (sam3cu_memcpy_d2h(t->data, e->dptr, tbytes(t), m->stream) != 0)
-			err = SAM3_EBACKEND;
-	}
 	if (sam3cu_stream_sync(m->stream) != 0 && err == SAM3_OK)
 		err = SAM3_EBACKEND;
 	if (err == SAM3_OK && sam3cu_last_device_error() != 0)
 		err = SAM3_EBACKEND;
+	if (m->prof) {
+		double t1 = now_s();
+		m->prof_s[SAM3_OP_COUNT] += t1 - t_rb0;
+		m->prof_n[SAM3_OP_COUNT]++;
+		m->prof_s[SAM3_OP_COUNT + 1] += t1 - t_eval0;
+		m->prof_n[SAM3_OP_COUNT + 1]++;
+	}
+	m->g = NULL;
 	tmp_free_all(m);
 	map_drop_local(m);
 	return err;

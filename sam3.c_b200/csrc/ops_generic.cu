@@ -89,80 +89,29 @@ __global__ void gelu_kernel(const void* x, void* y, int64_t n) {
   }
 }
 
-// RoPE on [batch, seq, heads, hd] with F32 [seq, hd/2] tables (cpu_rope.c)
+// RoPE on [batch, seq, heads, hd] with F32 [seq, hd/2] tables (cpu_rope.c).
+// Row r = (b, s) of heads*hd elements starts at r*ldx in x and r*ldy in y,
+// so a column slice of a wider matrix (the Q or K third of the fused QKV
+// output) is rotated where it lies.
 template <int T>
-__global__ void rope_kernel(const void* x, const float* __restrict__ cs, const float* __restrict__ sn, void* y,
-                            int64_t npairs, int seq, int heads, int half) {
+__global__ void rope_kernel(const void* x, int64_t ldx, const float* __restrict__ cs, const float* __restrict__ sn,
+                            void* y, int64_t ldy, int64_t npairs, int seq, int heads, int half) {
   GRID_LOOP(p, npairs) {
     const int d = static_cast<int>(p % half);
     const int64_t bsh = p / half;
-    const int s = static_cast<int>((bsh / heads) % seq);
+    const int64_t row = bsh / heads;
+    const int s = static_cast<int>(row % seq);
+    const int64_t col = (bsh % heads) * 2 * half + 2 * d;
     const float c = cs[s * half + d], si = sn[s * half + d];
-    const float x0 = ld<T>(x, 2 * p), x1 = ld<T>(x, 2 * p + 1);
-    st<T>(y, 2 * p, x0 * c - x1 * si);
-    st<T>(y, 2 * p + 1, x0 * si + x1 * c);
+    const float x0 = ld<T>(x, row * ldx + col), x1 = ld<T>(x, row * ldx + col + 1);
+    st<T>(y, row * ldy + col, x0 * c - x1 * si);
+    st<T>(y, row * ldy + col + 1, x0 * si + x1 * c);
   }
 }
 
 template <int TI, int TO>
 __global__ void cast_any(const void* x, void* y, int64_t n) {
   GRID_LOOP(i, n) st<TO>(y, i, ld<TI>(x, i));
-}
-
-// F32 attention, one thread per query row (online softmax exactly as
-// cpu_sdpa.c:49-159, in k order, expf), 64 queries per block; K and V tiles
-// of 64 keys staged in shared memory and read as broadcasts.
-template <int HD>
-__global__ void __launch_bounds__(64) sdpa_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
-                                                      const float* __restrict__ v, const float* __restrict__ mask,
-                                                      float* __restrict__ o, int sq, int sk, float scale) {
-  __shared__ float ks[64][HD];
-  __shared__ float vs[64][HD];
-  const int bh = blockIdx.y;
-  const int qi = blockIdx.x * 64 + threadIdx.x;
-  const float* qr = q + (static_cast<int64_t>(bh) * sq + (qi < sq ? qi : 0)) * HD;
-  float qv[HD], acc[HD];
-#pragma unroll
-  for (int d = 0; d < HD; ++d) {
-    qv[d] = qr[d];
-    acc[d] = 0.f;
-  }
-  float mx = -FLT_MAX, sum = 0.f;
-  const float* kb = k + static_cast<int64_t>(bh) * sk * HD;
-  const float* vb = v + static_cast<int64_t>(bh) * sk * HD;
-  for (int t0 = 0; t0 < sk; t0 += 64) {
-    const int nt = sk - t0 < 64 ? sk - t0 : 64;
-    __syncthreads();
-    for (int e = threadIdx.x; e < nt * HD; e += 64) {
-      ks[e / HD][e % HD] = kb[static_cast<int64_t>(t0) * HD + e];
-      vs[e / HD][e % HD] = vb[static_cast<int64_t>(t0) * HD + e];
-    }
-    __syncthreads();
-    for (int j = 0; j < nt; ++j) {
-      float s = 0.f;
-#pragma unroll
-      for (int d = 0; d < HD; ++d) s += qv[d] * ks[j][d];
-      s *= scale;
-      if (mask && qi < sq) s += mask[static_cast<int64_t>(qi) * sk + t0 + j];
-      if (s > mx) {
-        const float corr = expf(mx - s);
-        sum *= corr;
-#pragma unroll
-        for (int d = 0; d < HD; ++d) acc[d] *= corr;
-        mx = s;
-      }
-      const float w = expf(s - mx);
-#pragma unroll
-      for (int d = 0; d < HD; ++d) acc[d] += w * vs[j][d];
-      sum += w;
-    }
-  }
-  if (qi < sq) {
-    const float inv = sum > 0.f ? 1.f / sum : 0.f;
-    float* orow = o + (static_cast<int64_t>(bh) * sq + qi) * HD;
-#pragma unroll
-    for (int d = 0; d < HD; ++d) orow[d] = acc[d] * inv;
-  }
 }
 
 // NHWC im2col for CONV2D with OHWI weights (cpu_conv2d.c): row (n, oy, ox),
@@ -379,6 +328,31 @@ int sam3cu_memcpy_d2d(void* dst, const void* src, size_t n, void* s) {
   return cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToDevice, S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA;
 }
 
+int sam3cu_gather_strided(const void* src, void* dst, int elem_size, int n_dims, const int* dims,
+                          const int64_t* strides, void* stream) {
+  if (!src || !dst || n_dims < 1 || n_dims > 4) return SAM3CU_EINVAL;
+  int d[4] = {1, 1, 1, 1};
+  int64_t st[4] = {0, 0, 0, 0};
+  const int off = 4 - n_dims;
+  for (int i = 0; i < n_dims; ++i) {
+    if (dims[i] <= 0 || strides[i] < 0 || strides[i] >= (1ll << 31)) return SAM3CU_ESHAPE;
+    d[off + i] = dims[i];
+    st[off + i] = strides[i];
+  }
+  const int64_t n = static_cast<int64_t>(d[0]) * d[1] * d[2] * d[3];
+  if (n >= (1ll << 31)) return SAM3CU_ESHAPE;
+  int4 odims = make_int4(d[0], d[1], d[2], d[3]);
+  int4 istr = make_int4(static_cast<int>(st[0]), static_cast<int>(st[1]), static_cast<int>(st[2]),
+                        static_cast<int>(st[3]));
+  count_launches(1);
+  const int g = grid_for(n, 256);
+  if (elem_size == 4) permute_kernel<uint32_t><<<g, 256, 0, S(stream)>>>(static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst), n, odims, istr);
+  else if (elem_size == 2) permute_kernel<uint16_t><<<g, 256, 0, S(stream)>>>(static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), n, odims, istr);
+  else if (elem_size == 1) permute_kernel<uint8_t><<<g, 256, 0, S(stream)>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), n, odims, istr);
+  else return SAM3CU_EDTYPE;
+  return rc_launch();
+}
+
 int sam3cu_permute(const void* src, void* dst, int elem_size, int n_dims, const int* dims, const int* perm,
                    void* stream) {
   if (!src || !dst || n_dims < 1 || n_dims > 4) return SAM3CU_EINVAL;
@@ -447,17 +421,25 @@ int sam3cu_gelu(const void* x, void* y, int dtype, int64_t n, void* stream) {
   return rc_launch();
 }
 
-int sam3cu_rope(const void* x, const float* cos_t, const float* sin_t, void* y, int dtype, int batch, int seq,
-                int heads, int hd, void* stream) {
+int sam3cu_rope_rows(const void* x, int64_t ldx, const float* cos_t, const float* sin_t, void* y, int64_t ldy,
+                     int dtype, int batch, int seq, int heads, int hd, void* stream) {
   if (!x || !y || !cos_t || !sin_t || hd % 2 || batch <= 0 || seq <= 0 || heads <= 0) return SAM3CU_EINVAL;
+  if (ldx < static_cast<int64_t>(heads) * hd || ldy < static_cast<int64_t>(heads) * hd) return SAM3CU_EINVAL;
   const int64_t np = static_cast<int64_t>(batch) * seq * heads * (hd / 2);
   count_launches(1);
   const int g = grid_for(np, 256);
-  if (dtype == kF32) rope_kernel<kF32><<<g, 256, 0, S(stream)>>>(x, cos_t, sin_t, y, np, seq, heads, hd / 2);
-  else if (dtype == kBF16) rope_kernel<kBF16><<<g, 256, 0, S(stream)>>>(x, cos_t, sin_t, y, np, seq, heads, hd / 2);
-  else if (dtype == kF16) rope_kernel<kF16><<<g, 256, 0, S(stream)>>>(x, cos_t, sin_t, y, np, seq, heads, hd / 2);
+  cudaStream_t st = S(stream);
+  if (dtype == kF32) rope_kernel<kF32><<<g, 256, 0, st>>>(x, ldx, cos_t, sin_t, y, ldy, np, seq, heads, hd / 2);
+  else if (dtype == kBF16) rope_kernel<kBF16><<<g, 256, 0, st>>>(x, ldx, cos_t, sin_t, y, ldy, np, seq, heads, hd / 2);
+  else if (dtype == kF16) rope_kernel<kF16><<<g, 256, 0, st>>>(x, ldx, cos_t, sin_t, y, ldy, np, seq, heads, hd / 2);
   else return SAM3CU_EDTYPE;
   return rc_launch();
+}
+
+int sam3cu_rope(const void* x, const float* cos_t, const float* sin_t, void* y, int dtype, int batch, int seq,
+                int heads, int hd, void* stream) {
+  const int64_t ld = static_cast<int64_t>(heads) * hd;
+  return sam3cu_rope_rows(x, ld, cos_t, sin_t, y, ld, dtype, batch, seq, heads, hd, stream);
 }
 
 int sam3cu_cast(const void* x, int xdt, void* y, int ydt, int64_t n, void* stream) {
@@ -472,17 +454,6 @@ int sam3cu_cast(const void* x, int xdt, void* y, int ydt, int64_t n, void* strea
   return SAM3CU_EDTYPE;
 }
 
-int sam3cu_sdpa_f32(const float* q, const float* k, const float* v, const float* mask, float* o, int bh, int sq,
-                    int sk, int hd, void* stream) {
-  if (!q || !k || !v || !o || bh <= 0 || sq <= 0 || sk <= 0) return SAM3CU_EINVAL;
-  dim3 grid((sq + 63) / 64, bh);
-  const float scale = 1.0f / sqrtf(static_cast<float>(hd));
-  count_launches(1);
-  if (hd == 64) sdpa_f32_kernel<64><<<grid, 64, 0, S(stream)>>>(q, k, v, mask, o, sq, sk, scale);
-  else if (hd == 32) sdpa_f32_kernel<32><<<grid, 64, 0, S(stream)>>>(q, k, v, mask, o, sq, sk, scale);
-  else return SAM3CU_ESHAPE;
-  return rc_launch();
-}
 
 int sam3cu_im2col_nhwc(const void* x, void* a, int dtype, int n, int H, int W, int C, int kh, int kw, int stride,
                        int pad, int kpad, void* stream) {

@@ -106,6 +106,29 @@ def test_linear_q8(cuda, M, K, N):
     assert rel_err(to_np(y), O.linear(x, O.round_bf16(wdq), b)) < 1e-4 * max(1.0, K / 256)
 
 
+@pytest.mark.parametrize("M,K,N", [(300, 64, 128), (5184, 1024, 4736)])
+def test_linear_q8_f32_activations(cuda, M, K, N):
+    """BASELINE config 0 as stated: F32 activations ~N(0,1) x Q8_0 weights
+    (the reference's own quantiser, blocks along K) + F32 bias -> F32, the
+    operands of cpu_kernel_matmul_q8 (cpu_matmul_q8.c:168-235), against the
+    exact x . dequant(W)^T + b at the north-star Q8 bound 1e-2."""
+    import torch
+    import sam3cu
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
+    b = rng.standard_normal(N, dtype=np.float32) * np.float32(0.01)
+    blocks = O.q8_quantize(w)
+    wdq = O.q8_dequantize(blocks, N * K).reshape(N, K)
+    tb = torch.from_numpy(np.frombuffer(blocks.tobytes(), np.uint8).copy()).cuda()
+    q, sc = sam3cu.q8_repack(tb, N, K)
+    y = sam3cu.linear_q8(torch.from_numpy(x).cuda(), q, sc, bias=torch.from_numpy(b).cuda(),
+                         out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert sam3cu.device_error() == 0
+    assert rel_err(to_np(y), O.linear(x, wdq, b)) < 1e-2
+
+
 @pytest.mark.parametrize("M,K,N", [(128, 32, 256), (257, 100, 320), (5184, 1024, 1024),
                                    (5184, 4736, 1024)])
 def test_linear_f32_3xtf32(cuda, M, K, N):

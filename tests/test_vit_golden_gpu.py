@@ -1,8 +1,8 @@
 """Full-size encoder parity against committed golden fixtures of the
-reference itself (tests/golden/vit_1008_depth8.npz, made by
+reference itself (tests/golden/vit_1008_depth{8,32}.npz, made by
 tests/golden/gen_vit_golden.py from the reference sam3_vit_build on its CPU
-backend): Hiera-L geometry at 1008 px, 8 blocks (block 7 global), seeded
-weights and image.  Compared on the fixture's 16384 sampled positions,
+backend): Hiera-L geometry at 1008 px, 8 blocks (block 7 global) and the
+full 32 blocks (globals 7/15/23/31), seeded weights and image.  Compared on the fixture's 16384 sampled positions,
 normwise: BF16 / F16 / Q8 encoders within 1e-2, the F32 graph through the
 CUDA backend vtable within 1e-4."""
 import os
@@ -16,12 +16,15 @@ from _util import rel_err
 
 pytestmark = pytest.mark.gpu
 
-GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "vit_1008_depth8.npz")
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "vit_1008_depth{}.npz")
 
 
-@pytest.fixture(scope="module")
-def gold():
-    g = np.load(GOLD)
+@pytest.fixture(scope="module", params=[8, 32], ids=["depth8", "depth32"])
+def gold(request):
+    path = GOLD.format(request.param)
+    if not os.path.exists(path):
+        pytest.skip(f"{path} absent")
+    g = np.load(path)
     cfg = dict(zip(("img_size", "patch_size", "embed_dim", "depth", "n_heads", "window_size", "mlp_dim"),
                    (int(v) for v in g["cfg"])))
     w_seed, img_seed = (int(v) for v in g["seeds"])
