@@ -33,6 +33,7 @@ def lib():
         _lib.dropin_vit_encode.restype = C.c_int
         _lib.dropin_vit_encode.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_double)]
         _lib.dropin_vit_free.argtypes = [C.c_void_p]
+        _lib.dropin_vit_profile_dump.argtypes = [C.c_void_p]
     return _lib
 
 
@@ -65,6 +66,11 @@ class DropinVit:
         if rc != 0:
             raise RuntimeError(f"dropin_vit_encode failed rc={rc}")
         return out, sec.value
+
+    def profile_dump(self):
+        """Print and reset the backend's per-op profile (only when
+        SAM3CU_VTABLE_PROFILE=1 was set before the session was created)."""
+        lib().dropin_vit_profile_dump(self._s)
 
     def close(self):
         if self._s:

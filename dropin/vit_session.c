@@ -160,3 +160,9 @@ int dropin_vit_encode(struct dropin_vit *s, const float *image, float *out, doub
 	memcpy(out, res->data, 4ul * s->np * s->e);
 	return 0;
 }
+
+/* print and reset the backend's SAM3CU_VTABLE_PROFILE counters */
+void dropin_vit_profile_dump(struct dropin_vit *s)
+{
+	sam3cu_backend_profile_dump(s->be);
+}

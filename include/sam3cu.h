@@ -292,6 +292,14 @@ SAM3CU_API int sam3cu_stream_sync(void *stream);
 SAM3CU_API int sam3cu_memcpy_h2d(void *dst, const void *host_src, size_t n, void *stream);
 SAM3CU_API int sam3cu_memcpy_d2h(void *host_dst, const void *src, size_t n, void *stream);
 SAM3CU_API int sam3cu_memcpy_d2d(void *dst, const void *src, size_t n, void *stream);
+/* page-locked host staging buffers and events for the backend's host
+ * transfers (cudaMallocHost / cudaEvent*, no timing) */
+SAM3CU_API int sam3cu_host_alloc_pinned(void **p, size_t bytes);
+SAM3CU_API int sam3cu_host_free_pinned(void *p);
+SAM3CU_API int sam3cu_event_create(void **event);
+SAM3CU_API int sam3cu_event_destroy(void *event);
+SAM3CU_API int sam3cu_event_record(void *event, void *stream);
+SAM3CU_API int sam3cu_event_sync(void *event);
 
 /* Strided gather into a contiguous tensor: dst[i0,..,i3] =
  * src[sum_k i_k * strides[k]] (element strides, up to 4 dims).  The

@@ -143,6 +143,13 @@ struct sam3_cuda_backend {
  */
 SAM3CU_API const struct sam3_backend_ops *sam3_cuda_backend_ops(void);
 
+/* Measurement hook, no counterpart in the reference: with the environment
+ * variable SAM3CU_VTABLE_PROFILE=1 set when the backend was created, every
+ * graph node is timed with a stream sync around it; this prints the
+ * per-op-kind totals (plus uploads and read-backs) to stderr and resets
+ * them.  A no-op otherwise. */
+SAM3CU_API void sam3cu_backend_profile_dump(struct sam3_backend *be);
+
 #ifdef __cplusplus
 }
 #endif

@@ -65,7 +65,7 @@ def build(verbose: bool = False) -> str:
         raise RuntimeError("libsam3cu build failed:\n" + "\n".join(errs))
     objs = [o for o, _ in results]
     if _newer(objs, LIB):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart"]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart", "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")

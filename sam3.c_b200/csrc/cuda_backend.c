@@ -33,6 +33,7 @@
 #include <time.h>
 
 #include "../../include/sam3cu_backend.h"
+#include "host_xfer.h"
 
 /* ------------------------------------------------------------------ state */
 
@@ -66,10 +67,12 @@ struct impl {
 	size_t           cap, used;
 	struct hostblk  *host;            /* alloc_tensor buffers */
 	struct arena     ar;              /* graph-local device buffers */
+	struct hxfer    *hx;              /* staged host transfers (may be NULL) */
 	struct sam3_graph *g;             /* graph being evaluated */
 	int              prof;            /* SAM3CU_VTABLE_PROFILE set */
-	double           prof_s[SAM3_OP_COUNT + 2];
-	long             prof_n[SAM3_OP_COUNT + 2];
+	double           prof_s[SAM3_OP_COUNT + 3];  /* ops, readback, total, uploads */
+	long             prof_n[SAM3_OP_COUNT + 3];
+	double           prof_b[2];                  /* bytes uploaded / read back */
 	/* per-graph scratch tables, sized to n_nodes */
 	int             *uses;
 	int             *flags;
@@ -306,6 +309,7 @@ static enum sam3_error cu_init(struct sam3_backend *be)
 		free(m);
 		return SAM3_EBACKEND;
 	}
+	m->hx = hxfer_create();  /* NULL: plain cudaMemcpyAsync transfers */
 	const char *pv = getenv("SAM3CU_VTABLE_PROFILE");
 	m->prof = pv && *pv && *pv != '0';
 	cb->impl = m;
@@ -321,27 +325,50 @@ static void host_free_all(struct impl *m)
 	}
 }
 
+/* SAM3CU_VTABLE_PROFILE: host time per op kind with a stream sync around
+ * every node (so the sum is device + host time, serialised), uploads and
+ * read-backs separately; printed to stderr and reset */
+static void profile_print(struct impl *m)
+{
+	static const char *names[SAM3_OP_COUNT + 3] = {
+		[SAM3_OP_MATMUL] = "MATMUL", [SAM3_OP_ADD] = "ADD", [SAM3_OP_MUL] = "MUL",
+		[SAM3_OP_SOFTMAX] = "SOFTMAX", [SAM3_OP_GELU] = "GELU",
+		[SAM3_OP_LAYERNORM] = "LAYERNORM", [SAM3_OP_CONV2D] = "CONV2D",
+		[SAM3_OP_RESHAPE] = "RESHAPE", [SAM3_OP_TRANSPOSE] = "TRANSPOSE",
+		[SAM3_OP_CAST] = "CAST", [SAM3_OP_CONCAT] = "CONCAT", [SAM3_OP_SLICE] = "SLICE",
+		[SAM3_OP_ROPE] = "ROPE", [SAM3_OP_SDPA] = "SDPA",
+		[SAM3_OP_COUNT] = "readback", [SAM3_OP_COUNT + 1] = "graph_eval total",
+		[SAM3_OP_COUNT + 2] = "(uploads in ops)"};
+	for (int i = 0; i < SAM3_OP_COUNT + 3; i++)
+		if (m->prof_n[i])
+			fprintf(stderr, "[sam3cu profile] %-18s %6ld calls %10.3f ms\n",
+				names[i] ? names[i] : "other", m->prof_n[i], 1e3 * m->prof_s[i]);
+	fprintf(stderr, "[sam3cu profile] uploaded %.1f MB, read back %.1f MB\n",
+		m->prof_b[0] / 1e6, m->prof_b[1] / 1e6);
+	memset(m->prof_s, 0, sizeof(m->prof_s));
+	memset(m->prof_n, 0, sizeof(m->prof_n));
+	memset(m->prof_b, 0, sizeof(m->prof_b));
+}
+
+/* measurement hook (no counterpart in the reference): print and reset the
+ * SAM3CU_VTABLE_PROFILE counters of a CUDA backend instance */
+void sam3cu_backend_profile_dump(struct sam3_backend *be)
+{
+	struct impl *m = IM(be);
+	if (m && m->prof)
+		profile_print(m);
+}
+
 static void cu_free(struct sam3_backend *be)
 {
 	struct impl *m = IM(be);
 	if (!m)
 		return;
 	sam3cu_stream_sync(m->stream);
-	if (m->prof) {
-		static const char *names[SAM3_OP_COUNT + 2] = {
-			[SAM3_OP_MATMUL] = "MATMUL", [SAM3_OP_ADD] = "ADD", [SAM3_OP_MUL] = "MUL",
-			[SAM3_OP_SOFTMAX] = "SOFTMAX", [SAM3_OP_GELU] = "GELU",
-			[SAM3_OP_LAYERNORM] = "LAYERNORM", [SAM3_OP_CONV2D] = "CONV2D",
-			[SAM3_OP_RESHAPE] = "RESHAPE", [SAM3_OP_TRANSPOSE] = "TRANSPOSE",
-			[SAM3_OP_CAST] = "CAST", [SAM3_OP_CONCAT] = "CONCAT", [SAM3_OP_SLICE] = "SLICE",
-			[SAM3_OP_ROPE] = "ROPE", [SAM3_OP_SDPA] = "SDPA",
-			[SAM3_OP_COUNT] = "readback", [SAM3_OP_COUNT + 1] = "graph_eval total"};
-		for (int i = 0; i < SAM3_OP_COUNT + 2; i++)
-			if (m->prof_n[i])
-				fprintf(stderr, "[sam3cu profile] %-18s %6ld calls %10.3f ms\n",
-					names[i] ? names[i] : "other", m->prof_n[i], 1e3 * m->prof_s[i]);
-	}
+	if (m->prof)
+		profile_print(m);
 	arena_release(m);
+	hxfer_destroy(m->hx);
 	for (size_t i = 0; i < m->cap; i++)
 		if (m->map[i].kind > 0)
 			devent_free(&m->map[i]);
@@ -462,7 +489,21 @@ static enum sam3_error dev_view(struct impl *m, const struct sam3_tensor *t,
 	} else {
 		TRY(sam3cu_dev_alloc(&d, nb));
 	}
-	TRY(sam3cu_memcpy_h2d(d, t->data, nb, m->stream));
+	double tu = 0.0;
+	if (m->prof) {
+		sam3cu_stream_sync(m->stream);
+		tu = now_s();
+	}
+	if (m->hx)
+		TRY(hxfer_h2d(m->hx, d, t->data, nb, m->stream));
+	else
+		TRY(sam3cu_memcpy_h2d(d, t->data, nb, m->stream));
+	if (m->prof) {
+		sam3cu_stream_sync(m->stream);
+		m->prof_s[SAM3_OP_COUNT + 2] += now_s() - tu;
+		m->prof_n[SAM3_OP_COUNT + 2]++;
+		m->prof_b[0] += (double)nb;
+	}
 	e = map_insert(m, t);
 	if (!e)
 		return SAM3_ENOMEM;
@@ -1265,8 +1306,11 @@ static enum sam3_error cu_graph_eval(struct sam3_backend *be,
 			e->own = 0;
 			e->data = t->data;
 		} else if (t->data) {
-			if (sam3cu_memcpy_d2h(t->data, e->dptr, tbytes(t), m->stream) != 0)
+			int rc = m->hx ? hxfer_d2h(m->hx, t->data, e->dptr, tbytes(t), m->stream)
+				       : sam3cu_memcpy_d2h(t->data, e->dptr, tbytes(t), m->stream);
+			if (rc != 0)
 				err = SAM3_EBACKEND;
+			m->prof_b[1] += (double)tbytes(t);
 		}
 	}
 	if (sam3cu_stream_sync(m->stream) != 0 && err == SAM3_OK)

@@ -295,8 +295,9 @@ namespace {
 template <int TI, int TO, bool kChw>
 __global__ void conv_im2col(const void* __restrict__ x, void* __restrict__ a, int64_t total, int H, int W, int C,
                             int k, int stride, int pad, int OH, int OW, int kpad) {
-  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;  // total < 2^31 (launcher)
-  if (i >= total) return;
+  // grid-stride: the launcher caps the grid at 16 CTAs per SM
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total;  // total < 2^31 (launcher)
+       i += gridDim.x * blockDim.x) {
   const int col = static_cast<int>(i % kpad);
   const unsigned row = i / kpad;
   const int ox = static_cast<int>(row % OW), oy = static_cast<int>((row / OW) % OH);
@@ -319,14 +320,15 @@ __global__ void conv_im2col(const void* __restrict__ x, void* __restrict__ a, in
     static_cast<__nv_bfloat16*>(a)[i] = __float2bfloat16_rn(v);
   else
     static_cast<__half*>(a)[i] = __float2half_rn(v);
+  }
 }
 
 // 16-bit NHWC input with C % 8 == 0: one thread copies 8 channels (16
 // bytes) of one tap; 32-bit index math (the launcher checks the count).
 __global__ void conv_im2col_v8(const uint4* __restrict__ x, uint4* __restrict__ a, unsigned total, int H, int W,
                                int C8, int k, int stride, int pad, int OH, int OW, int kpad8, int kk8) {
-  const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= total) return;
+  // grid-stride: the launcher caps the grid at 16 CTAs per SM
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
   const unsigned col = i % kpad8;
   const unsigned row = i / kpad8;
   uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -340,6 +342,7 @@ __global__ void conv_im2col_v8(const uint4* __restrict__ x, uint4* __restrict__ 
       v = __ldg(x + ((static_cast<int64_t>(b) * H + iy) * W + ix) * C8 + c8);
   }
   a[i] = v;
+  }
 }
 
 }  // namespace

@@ -318,6 +318,21 @@ int sam3cu_stream_create(void** s) {
 }
 int sam3cu_stream_destroy(void* s) { return cudaStreamDestroy(S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA; }
 int sam3cu_stream_sync(void* s) { return cudaStreamSynchronize(S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA; }
+int sam3cu_host_alloc_pinned(void** p, size_t bytes) {
+  return cudaMallocHost(p, bytes ? bytes : 16) == cudaSuccess ? SAM3CU_OK : SAM3CU_ENOMEM;
+}
+int sam3cu_host_free_pinned(void* p) { return cudaFreeHost(p) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA; }
+int sam3cu_event_create(void** e) {
+  cudaEvent_t ev;
+  if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return SAM3CU_ECUDA;
+  *e = ev;
+  return SAM3CU_OK;
+}
+int sam3cu_event_destroy(void* e) { return cudaEventDestroy(static_cast<cudaEvent_t>(e)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA; }
+int sam3cu_event_record(void* e, void* s) {
+  return cudaEventRecord(static_cast<cudaEvent_t>(e), S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA;
+}
+int sam3cu_event_sync(void* e) { return cudaEventSynchronize(static_cast<cudaEvent_t>(e)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA; }
 int sam3cu_memcpy_h2d(void* dst, const void* src, size_t n, void* s) {
   return cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, S(s)) == cudaSuccess ? SAM3CU_OK : SAM3CU_ECUDA;
 }
