@@ -379,6 +379,17 @@ def q8_legs(args, dev, sam3cu):
         f()
     torch.cuda.synchronize()
     ms_lin = _event_ms(f, 20)
+    # breakdown: the same call with BF16 activations (no cast), and the bare
+    # 16-bit GEMM on the dequantised weight (no cast, no dequantisation)
+    xb = x.bfloat16()
+    fb = lambda: sam3cu.linear_q8(xb, q, sc, bias=b, out=y)
+    wdq = w.bfloat16()  # same shape and layout as the dequantised weight
+    fg = lambda: sam3cu.linear(xb, wdq, bias=b, out=y)
+    for g_ in (fb, fg):
+        for _ in range(3):
+            g_()
+    ms_bf = _event_ms(fb, 20)
+    ms_gemm = _event_ms(fg, 20)
     enc = sam3cu.VitEncoder(CFG, synth.vit_weights(CFG, seed=0), sam3cu.Q8_0, max_batch=1)
     img = torch.from_numpy(synth.images(CFG, 1, seed=100)).to(dev)
     out = torch.empty((1, enc.np, CFG["embed_dim"]), dtype=torch.float32, device=dev)
@@ -394,7 +405,9 @@ def q8_legs(args, dev, sam3cu):
         "q8_linear_config0": {"tflops": 2 * M * K * N / ms_lin / 1e9, "ms": ms_lin,
                               "dtype": "q8_0w x f32a (bf16 on chip), f32 out",
                               "note": "F32 activations cast inside the call + dequantise-once path "
-                                      "(M >= 2048) of sam3cu_linear_q8"},
+                                      "(M >= 2048) of sam3cu_linear_q8",
+                              "breakdown_ms": {"f32_x_call": ms_lin, "bf16_x_call": ms_bf,
+                                               "bf16_gemm_only_f32_out": ms_gemm}},
         "q8_encode_config2": {"value": 1000.0 / ms_enc, "unit": "images/s", "ms_per_image": ms_enc,
                               "gemm_tflops": gemm_gflop_per_image() / prof["gemm"][0],
                               "dtype": "q8_0w+f16a", "batch": 1},
@@ -522,6 +535,28 @@ def neck_leg(args, dev, sam3cu):
     return res
 
 
+def attention_leg(args, dev, sam3cu):
+    """The tcgen05 attention alone at the encoder's shapes for 8 images:
+    global (8 groups x 5184 tokens) and windowed (72 windows x 576 tokens),
+    16 heads of 64, BF16 Q|K|V packed as the QKV GEMM writes them.  CUDA
+    events over 10 launches after 3 warm-ups; 4*S^2*64 FLOP per (group,
+    head)."""
+    import torch
+    res = {"unit": "TFLOP/s"}
+    g = torch.Generator(device=dev).manual_seed(0)
+    for name, groups, seq in (("global_8img", 8, 5184), ("window_8img", 72, 576)):
+        qkv = torch.randn(groups * seq, 3 * 1024, device=dev, generator=g).bfloat16()
+        out = torch.empty(groups * seq, 1024, device=dev, dtype=torch.bfloat16)
+        f = lambda: sam3cu.sdpa_packed(qkv, groups, seq, 16, 64, out=out)
+        for _ in range(3):
+            f()
+        ms = _event_ms(f, 10)
+        res[name] = 4.0 * seq * seq * 64 * 16 * groups / ms / 1e9
+        del qkv, out
+    assert sam3cu.device_error() == 0
+    return res
+
+
 def dropin_leg(args, dev, sam3cu):
     """The drop-in path: the reference's own sam3_vit_build (compiled from
     the sam3.c sources, dropin/_ref) evaluating its F32 Hiera-L graph on one
@@ -588,7 +623,7 @@ def run_leg(args):
     sam3cu.init(0)
     dev = torch.device("cuda", 0)
     fn = {"dropin": dropin_leg, "sweep": gemm_sweep_leg, "q8": q8_legs, "neck": neck_leg,
-          "tinyvit": tinyvit_leg}[args.leg]
+          "tinyvit": tinyvit_leg, "attn": attention_leg}[args.leg]
     print(json.dumps({"leg": args.leg, "result": fn(args, dev, sam3cu)}))
     return 0
 
@@ -609,7 +644,7 @@ def main():
     ap.add_argument("--no-tinyvit", action="store_true", help="skip the config-5 TinyViT leg")
     ap.add_argument("--dropin-iters", type=int, default=3)
     ap.add_argument("--leg", default=None,
-                    choices=["dropin", "sweep", "q8", "neck", "tinyvit"],
+                    choices=["dropin", "sweep", "q8", "neck", "tinyvit", "attn"],
                     help="run one side leg alone on GPU 0 and print its result")
     args = ap.parse_args()
     if args.leg:

@@ -18,8 +18,13 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
-OBJ = os.path.join(HERE, "_build")
-LIB = os.path.join(HERE, "lib", "libsam3cu.so")
+# SAM3CU_BUILD_OUT=<dir> builds a variant library (<dir>/libsam3cu.so, objects
+# in <dir>/_build) with the extra -D flags of SAM3CU_BUILD_DEFS, for A/B
+# measurements of compile-time kernel switches (loaded via SAM3CU_LIB).
+_VAR = os.environ.get("SAM3CU_BUILD_OUT")
+OBJ = os.path.join(_VAR, "_build") if _VAR else os.path.join(HERE, "_build")
+LIB = os.path.join(_VAR, "libsam3cu.so") if _VAR else os.path.join(HERE, "lib", "libsam3cu.so")
+DEFS = os.environ.get("SAM3CU_BUILD_DEFS", "").split()
 INC = os.path.join(os.path.dirname(HERE), "include")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
@@ -45,9 +50,9 @@ def _compile(src):
     if not _newer([src] + headers + [__file__], obj):
         return obj, None
     if src.endswith(".cu"):
-        cmd = [NVCC] + CUFLAGS + ["-c", src, "-o", obj]
+        cmd = [NVCC] + CUFLAGS + DEFS + ["-c", src, "-o", obj]
     else:
-        cmd = ["gcc"] + CFLAGS + ["-c", src, "-o", obj]
+        cmd = ["gcc"] + CFLAGS + DEFS + ["-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         return obj, f"{' '.join(cmd)}\n{r.stdout}\n{r.stderr}"

@@ -126,6 +126,47 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t fadd2_rm(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+#ifndef S3_ATTN_POLY
+#define S3_ATTN_POLY 0
+#endif
+// Of every 8 key pairs a softmax thread exponentiates, this many take
+// exp2_poly2 (FMA pipe) instead of two MUFU ex2 (16 results per clock per
+// SM).  Measured at 8 images (global / window TFLOP/s): 0 -> 706 / 437,
+// 1 -> 724 / 417, 2 -> 687 / 418, 3 -> 617 / 398: the softmax is bound by
+// its dependency chain more than by the exponential unit, so 0 is kept.
+constexpr int kPolyPairs = S3_ATTN_POLY;
+
+// 2^x for a pair of exponents x <= 8 on the FMA pipe: x = n + f with
+// n = floor(x) (round-down add of 1.5*2^23, which leaves n in the low
+// mantissa bits), 2^f on [0, 1) by a degree-3 polynomial fitted here for
+// relative error (max 7.5e-5, below the 16-bit rounding of P), and n added
+// to the exponent field.  Exponents below -126 (masked keys: -inf) are
+// clamped to -126, whose result is 2^-126 or a denormal: zero once P is
+// rounded to fp16, and negligible in bf16 P and in the row sum.  (At -127
+// the exponent field of a p(f) < 1 would wrap.)
+__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& p0, float& p1) {
+  float x0, x1;
+  f2unpack(x2, x0, x1);
+  const uint64_t xc = f2pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t t = fadd2_rm(xc, f2pack(12582912.f, 12582912.f));  // floor(x) + 1.5*2^23
+  const uint64_t n = fadd2(t, f2pack(-12582912.f, -12582912.f));    // floor(x), exact
+  const uint64_t f = ffma2(n, f2pack(-1.f, -1.f), xc);               // x - floor(x), exact
+  uint64_t p = ffma2(f, f2pack(0.07802403f, 0.07802403f), f2pack(0.22606707f, 0.22606707f));
+  p = ffma2(p, f, f2pack(0.69583398f, 0.69583398f));
+  p = ffma2(p, f, f2pack(0.99992514f, 0.99992514f));
+  float q0, q1, t0, t1;
+  f2unpack(p, q0, q1);
+  f2unpack(t, t0, t1);
+  p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+}
+
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -456,9 +497,16 @@ __global__ void __launch_bounds__(kThreads, 2)
           uint32_t pk[kPStore];
 #pragma unroll
           for (int c = c0; c < c0 + 2 * kPStore; c += 2) {
-            float e0, e1;
-            f2unpack(ffma2(f2pack(sv[c], sv[c + 1]), sc2, nmb2), e0, e1);
-            const float p0 = ex2(e0), p1 = ex2(e1);
+            const uint64_t e2 = ffma2(f2pack(sv[c], sv[c + 1]), sc2, nmb2);
+            float p0, p1;
+            if (((c - c0) / 2) % 8 < kPolyPairs) {
+              exp2_poly2(e2, p0, p1);
+            } else {
+              float e0, e1;
+              f2unpack(e2, e0, e1);
+              p0 = ex2(e0);
+              p1 = ex2(e1);
+            }
             l2[(c >> 1) & 1] = fadd2(l2[(c >> 1) & 1], f2pack(p0, p1));
             pk[(c - c0) / 2] = pack2(p0, p1, kBf16);
           }
@@ -796,9 +844,16 @@ __global__ void __launch_bounds__(kThreads, 2)
             uint32_t pk[8];
 #pragma unroll
             for (int c = c0; c < c0 + 16; c += 2) {
-              float e0, e1;
-              f2unpack(ffma2(f2pack(sv[c], sv[c + 1]), sc2, nmb2), e0, e1);
-              const float p0 = ex2(e0), p1 = ex2(e1);
+              const uint64_t e2 = ffma2(f2pack(sv[c], sv[c + 1]), sc2, nmb2);
+              float p0, p1;
+              if ((c - c0) / 2 < kPolyPairs) {
+                exp2_poly2(e2, p0, p1);
+              } else {
+                float e0, e1;
+                f2unpack(e2, e0, e1);
+                p0 = ex2(e0);
+                p1 = ex2(e1);
+              }
               l2[(c >> 1) & 1] = fadd2(l2[(c >> 1) & 1], f2pack(p0, p1));
               pk[(c - c0) / 2] = pack2(p0, p1, kBf16);
             }

@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <mutex>
 
 #include "../../include/sam3cu.h"
 #include "gemm_sm100.cuh"
@@ -13,6 +14,40 @@ using namespace s3;
 namespace {
 
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// The library's own stream-ordered pool for per-call temporaries (the
+// 16-bit copies of a Q8_0 weight and of F32 activations): its release
+// threshold keeps freed memory mapped, so a steady stream of calls does not
+// map and unmap device memory (the default pool returns it at every
+// synchronisation).  One pool per device, created on first use.
+cudaMemPool_t call_pool() {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!pools[dev]) {
+    cudaMemPoolProps props;
+    memset(&props, 0, sizeof(props));
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t p = nullptr;
+    if (cudaMemPoolCreate(&p, &props) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    uint64_t keep = ~0ull;
+    cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+    pools[dev] = p;
+  }
+  return pools[dev];
+}
+
+cudaError_t pool_alloc(void** p, size_t n, cudaStream_t st) {
+  cudaMemPool_t pool = call_pool();
+  return pool ? cudaMallocFromPoolAsync(p, n, pool, st) : cudaMallocAsync(p, n, st);
+}
 
 int linear_common(const void* x, int x_dtype, const void* w, const int8_t* q, const float* sc, const float* bias,
                   const float* residual, void* y, int y_dtype, int M, int K, int N, int act, void* stream) {
@@ -27,7 +62,7 @@ int linear_common(const void* x, int x_dtype, const void* w, const int8_t* q, co
     cudaStream_t st = as_stream(stream);
     void* xb = nullptr;
     const size_t nb = static_cast<size_t>(M) * K * 2;
-    if (cudaMallocAsync(&xb, nb, st) != cudaSuccess) {
+    if (pool_alloc(&xb, nb, st) != cudaSuccess) {
       cudaGetLastError();
       return SAM3CU_ENOMEM2;
     }
@@ -55,7 +90,7 @@ int linear_common(const void* x, int x_dtype, const void* w, const int8_t* q, co
   // again for every row tile); small M keeps the in-GEMM path.
   if (q && M >= 2048 && K % 32 == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {
     void* w16 = nullptr;
-    if (cudaMallocAsync(&w16, static_cast<size_t>(N) * K * 2, st) == cudaSuccess) {
+    if (pool_alloc(&w16, static_cast<size_t>(N) * K * 2, st) == cudaSuccess) {
       int rc = launch_q8_dequant_w16(q, sc, w16, N, K, x_dtype == SAM3CU_F16 ? 2 : 0, st);
       if (!rc) rc = launch_gemm(x, K, w16, K, nullptr, nullptr, x_dtype, shp, ep, st, 0);
       cudaFreeAsync(w16, st);

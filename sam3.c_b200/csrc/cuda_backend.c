@@ -311,7 +311,7 @@ static enum sam3_error cu_init(struct sam3_backend *be)
 	}
 	m->hx = hxfer_create();  /* NULL: plain cudaMemcpyAsync transfers */
 	const char *pv = getenv("SAM3CU_VTABLE_PROFILE");
-	m->prof = pv && *pv && *pv != '0';
+	m->prof = pv && *pv ? atoi(pv) : 0;
 	cb->impl = m;
 	return SAM3_OK;
 }
@@ -1311,6 +1311,10 @@ static enum sam3_error cu_graph_eval(struct sam3_backend *be,
 			if (rc != 0)
 				err = SAM3_EBACKEND;
 			m->prof_b[1] += (double)tbytes(t);
+			if (m->prof > 1)
+				fprintf(stderr, "[sam3cu profile] read back node %d op %d dims %d,%d,%d,%d (%zu B)\n",
+					i, (int)g->nodes[i].op, t->dims[0], t->n_dims > 1 ? t->dims[1] : 0,
+					t->n_dims > 2 ? t->dims[2] : 0, t->n_dims > 3 ? t->dims[3] : 0, tbytes(t));
 		}
 	}
 	if (sam3cu_stream_sync(m->stream) != 0 && err == SAM3_OK)

@@ -265,6 +265,28 @@ __global__ void q8_quantize_kernel(const float* __restrict__ src, uint8_t* __res
   }
 }
 
+// F32 -> 16-bit, 8 elements per thread (two 16-byte loads, one 16-byte store)
+template <int TO>
+__global__ void cast_f32_16_v8(const float4* __restrict__ x, uint4* __restrict__ y, int64_t n8) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 a = __ldg(x + 2 * i), b = __ldg(x + 2 * i + 1);
+    uint32_t o[4];
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (TO == kBF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+        o[k] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+        o[k] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+    y[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 template <int TI, int TO>
 __global__ void cast_kernel(const void* __restrict__ x, void* __restrict__ y, int64_t n) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -567,6 +589,15 @@ int launch_q8_quantize(const float* src, void* blocks, int64_t n, cudaStream_t s
 
 int launch_cast(const void* x, int tin, void* y, int tout, int64_t n, cudaStream_t st) {
   count_launches(1);
+  if (tin == kF32 && (tout == kBF16 || tout == kF16) && n % 8 == 0 &&
+      !((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15)) {
+    const int g8 = grid_for(n / 8, 256);
+    if (tout == kBF16)
+      cast_f32_16_v8<kBF16><<<g8, 256, 0, st>>>(static_cast<const float4*>(x), static_cast<uint4*>(y), n / 8);
+    else
+      cast_f32_16_v8<kF16><<<g8, 256, 0, st>>>(static_cast<const float4*>(x), static_cast<uint4*>(y), n / 8);
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+  }
   const int grid = grid_for(n, 256);
 #define S3_CAST(TI, TO) \
   if (tin == TI && tout == TO) { cast_kernel<TI, TO><<<grid, 256, 0, st>>>(x, y, n); return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch; }

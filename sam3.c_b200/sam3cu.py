@@ -15,7 +15,8 @@ from typing import Optional
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libsam3cu.so")
+# SAM3CU_LIB selects another build of the library (A/B measurements)
+LIB_PATH = os.environ.get("SAM3CU_LIB") or os.path.join(HERE, "lib", "libsam3cu.so")
 
 F32, F16, BF16, Q8_0 = 0, 1, 2, 5
 ACT_NONE, ACT_GELU_TANH = 0, 1
