@@ -400,8 +400,21 @@ def q8_legs(args, dev, sam3cu):
     ms_enc = _event_ms(g, 10, torch.cuda.ExternalStream(enc.stream, device=dev))
     prof = enc.profile(img, out)
     enc.close()
+    # BASELINE config 4's batch with Q8_0 weights: 64 images, 8 per call
+    enc = sam3cu.VitEncoder(CFG, synth.vit_weights(CFG, seed=0), sam3cu.Q8_0, max_batch=8)
+    imgs = torch.from_numpy(synth.images(CFG, 8, seed=100)).to(dev)
+    out8 = torch.empty((8, enc.np, CFG["embed_dim"]), dtype=torch.float32, device=dev)
+    h = lambda: [enc.encode_async(imgs, out8) for _ in range(8)]
+    h()
+    torch.cuda.synchronize()
+    ms64 = _event_ms(h, 3, torch.cuda.ExternalStream(enc.stream, device=dev))
+    prof8 = enc.profile(imgs, out8)
+    enc.close()
     assert sam3cu.device_error() == 0
     return {
+        "q8_encode_64img": {"value": 64 * 1000.0 / ms64, "unit": "images/s", "ms_per_64": ms64,
+                            "gemm_tflops": gemm_gflop_per_image() * 8 / prof8["gemm"][0],
+                            "dtype": "q8_0w+f16a", "images_per_call": 8},
         "q8_linear_config0": {"tflops": 2 * M * K * N / ms_lin / 1e9, "ms": ms_lin,
                               "dtype": "q8_0w x f32a (bf16 on chip), f32 out",
                               "note": "F32 activations cast inside the call + dequantise-once path "

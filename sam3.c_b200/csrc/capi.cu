@@ -61,7 +61,24 @@ int linear_common(const void* x, int x_dtype, const void* w, const int8_t* q, co
     if (M == 0) return SAM3CU_OK;
     cudaStream_t st = as_stream(stream);
     void* xb = nullptr;
-    const size_t nb = static_cast<size_t>(M) * K * 2;
+    const size_t nb = (static_cast<size_t>(M) * K * 2 + 255) & ~static_cast<size_t>(255);
+    if (M >= 2048 && K % 32 == 0 && ((static_cast<int64_t>(M) * K) % 8) == 0) {
+      // large M: the activations and the dequantised weight in one buffer,
+      // made by one launch, then the 16-bit GEMM
+      const size_t nw = static_cast<size_t>(N) * K * 2;
+      if (pool_alloc(&xb, nb + nw, st) == cudaSuccess) {
+        void* w16 = static_cast<char*>(xb) + nb;
+        int rc = launch_q8_prep(static_cast<const float*>(x), xb, static_cast<int64_t>(M) * K, q, sc, w16, N, K,
+                                st);
+        if (!rc) rc = linear_common(xb, SAM3CU_BF16, w16, nullptr, nullptr, bias, residual, y, y_dtype, M, K, N,
+                                    act, stream);
+        cudaFreeAsync(xb, st);
+        if (rc != kErrShape) return rc;  // misaligned operands: the general path below
+        xb = nullptr;
+      } else {
+        cudaGetLastError();
+      }
+    }
     if (pool_alloc(&xb, nb, st) != cudaSuccess) {
       cudaGetLastError();
       return SAM3CU_ENOMEM2;

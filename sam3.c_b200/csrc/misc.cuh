@@ -18,6 +18,10 @@ int launch_q8_row_shift(float* sc, float* col_scale, int N, int K, cudaStream_t 
 // 16-bit W [N, K] from int8 q [N, K] and scales [K/32, N].  mode: 0 bf16,
 // 1 f16 from row-shifted scales (half2 arithmetic), 2 f16 from any scales
 int launch_q8_dequant_w16(const int8_t* q, const float* sc, void* w, int N, int K, int mode, cudaStream_t st);
+// x F32 [nx] -> xb bf16 and Q8_0 W (int8 [N,K] + scales [K/32,N]) -> w bf16
+// [N,K], in one launch (the inputs of an F32 x Q8_0 linear)
+int launch_q8_prep(const float* x, void* xb, int64_t nx, const int8_t* q, const float* sc, void* w, int N, int K,
+                   cudaStream_t st);
 // The same for up to four weights in one launch (one pass over all of them).
 struct Q8DequantJob {
   const int8_t* q;

@@ -28,6 +28,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <vector>
@@ -98,7 +99,10 @@ struct sam3cu_vit {
   s3::DevBuf raster_to_win;                      // int [np]
   // activations
   s3::DevBuf x, xn, qkv, ao, h;
-  s3::DevBuf wq;  // Q8_0 weights: 16-bit dequantised W of the current block's four linears
+  s3::DevBuf wq;  // Q8_0 weights: 16-bit dequantised W of two blocks' four linears (two slots)
+  // Q8_0: block i+1's weights are dequantised on `side` while block i runs
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_wfree[2] = {}, ev_wready[2] = {}, ev_fork = nullptr;
   // image / feature staging for host-buffer encodes: two sets, so that one
   // chunk's copies overlap the next chunk's compute (img2/out2 on demand)
   s3::DevBuf img, out, img2, out2;
@@ -265,17 +269,42 @@ int run_linear(sam3cu_vit* v, const Linear& L, const void* a, int lda, int M, co
 // the start of the block into consecutive 16-bit slots of v->wq (27.8 MB at
 // the ViT-L sizes, so the GEMMs read them from L2); slot[k] = qkv, proj,
 // fc1, fc2.
-int dequant_block(sam3cu_vit* v, const Block& B, const void* (&slot)[4]) {
+// the 16-bit slots of block B's linears in half `buf` of v->wq
+void slot_ptrs(sam3cu_vit* v, const Block& B, const void* (&slot)[4], int buf) {
+  const Linear* L[4] = {&B.qkv, &B.proj, &B.fc1, &B.fc2};
+  uint8_t* p = static_cast<uint8_t*>(v->wq.p) + static_cast<size_t>(buf) * (v->wq.bytes / 2);
+  for (int k = 0; k < 4; ++k) {
+    slot[k] = p;
+    p += static_cast<size_t>(L[k]->N) * L[k]->K * 2;
+  }
+}
+
+int dequant_block(sam3cu_vit* v, const Block& B, const void* (&slot)[4], int buf = 0,
+                  cudaStream_t st = nullptr) {
   const Linear* L[4] = {&B.qkv, &B.proj, &B.fc1, &B.fc2};
   Q8DequantJobs jobs;
   jobs.n = 4;
-  uint8_t* p = static_cast<uint8_t*>(v->wq.p);
+  uint8_t* p = static_cast<uint8_t*>(v->wq.p) + static_cast<size_t>(buf) * (v->wq.bytes / 2);
   for (int k = 0; k < 4; ++k) {
     jobs.job[k] = Q8DequantJob{L[k]->q.as<int8_t>(), L[k]->sc.as<float>(), p, L[k]->N, L[k]->K};
     slot[k] = p;
     p += static_cast<size_t>(L[k]->N) * L[k]->K * 2;
   }
-  return launch_q8_dequant_w16_multi(jobs, v->act == kF16 ? 1 : 0, v->stream);
+  return launch_q8_dequant_w16_multi(jobs, v->act == kF16 ? 1 : 0, st ? st : v->stream);
+}
+
+// Q8_0, overlapped: block i's slot (i % 2) is filled on the side stream
+// while block i-1 runs on the main stream.  ev_wready[b]: slot b holds the
+// next block's weights; ev_wfree[b]: the block that used slot b finished
+// its last GEMM.  (Profiling runs dequantise in line on the main stream.)
+int dequant_ahead(sam3cu_vit* v, int i) {
+  if (i >= v->c.depth) return kOk;
+  const int b = i & 1;
+  const void* unused[4];
+  if (i >= 2 && cudaStreamWaitEvent(v->side, v->ev_wfree[b], 0) != cudaSuccess) return kErrCuda;
+  int rc = dequant_block(v, v->blocks[i], unused, b, v->side);
+  if (!rc && cudaEventRecord(v->ev_wready[b], v->side) != cudaSuccess) rc = kErrCuda;
+  return rc;
 }
 
 // Launch kinds of the profiling runs: the detailed kinds of
@@ -342,12 +371,26 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
   tick(v, kProfLn);
   if (c.depth == 0)
     return launch_gather_rows(v->x.p, out, M, e * 4, v->raster_to_win.as<int>(), np, v->stream);
+  static const bool ahead_on = [] {  // SAM3CU_Q8_AHEAD=0: dequantise in line (A/B measurements)
+    const char* e = getenv("SAM3CU_Q8_AHEAD");
+    return !(e && atoi(e) == 0);
+  }();
+  const bool q8_ahead = ahead_on && v->wdtype == SAM3CU_Q8_0 && !v->prof_events && v->side;
+  if (q8_ahead) {  // fork the side stream off the main one; blocks 0 and 1 first
+    if (cudaEventRecord(v->ev_fork, v->stream) != cudaSuccess ||
+        cudaStreamWaitEvent(v->side, v->ev_fork, 0) != cudaSuccess)
+      return kErrCuda;
+    if ((rc = dequant_ahead(v, 0)) || (rc = dequant_ahead(v, 1))) return rc;
+  }
   for (int i = 0; i < c.depth; ++i) {
     const Block& B = v->blocks[i];
     const bool glob = is_global_block(i);
     const bool last = i == c.depth - 1;
     const void* w16[4] = {nullptr, nullptr, nullptr, nullptr};
-    if (v->wdtype == SAM3CU_Q8_0) {
+    if (q8_ahead) {
+      slot_ptrs(v, B, w16, i & 1);
+      if (cudaStreamWaitEvent(v->stream, v->ev_wready[i & 1], 0) != cudaSuccess) return kErrCuda;
+    } else if (v->wdtype == SAM3CU_Q8_0) {
       if ((rc = dequant_block(v, B, w16))) return rc;
       tick(v, kProfDequant);
     }
@@ -421,6 +464,15 @@ int forward(sam3cu_vit* v, const float* images, int n, float* out) {
       if ((rc = run_linear(v, B.fc2, v->h.p, c.mlp_dim, M, ep, w16[3]))) return rc;
       tick(v, kProfFc2);
     }
+    if (q8_ahead) {  // slot i % 2 is free: the side stream fills it with block i + 2
+      if (cudaEventRecord(v->ev_wfree[i & 1], v->stream) != cudaSuccess) return kErrCuda;
+      if ((rc = dequant_ahead(v, i + 2))) return rc;
+    }
+  }
+  if (q8_ahead) {  // join: the side stream's last work precedes the end of the forward
+    if (cudaEventRecord(v->ev_fork, v->side) != cudaSuccess ||
+        cudaStreamWaitEvent(v->stream, v->ev_fork, 0) != cudaSuccess)
+      return kErrCuda;
   }
   return kOk;
 }
@@ -536,9 +588,15 @@ int vit_setup(sam3cu_vit* v, const VitSrc& w) {
       !v->img.alloc(static_cast<size_t>(v->max_batch) * 3 * c.img_size * c.img_size * 4) ||
       !v->out.alloc(M * e * 4))
     return kErrNoMem;
-  if (v->wdtype == SAM3CU_Q8_0) {  // one block's four dequantised linears
+  if (v->wdtype == SAM3CU_Q8_0) {  // two blocks' four dequantised linears
     const size_t wsum = (static_cast<size_t>(4) * e + 2 * static_cast<size_t>(c.mlp_dim)) * e * 2;
-    if (!v->wq.alloc(wsum)) return kErrNoMem;
+    if (!v->wq.alloc(2 * wsum)) return kErrNoMem;
+    if (cudaStreamCreateWithFlags(&v->side, cudaStreamNonBlocking) != cudaSuccess) return kErrCuda;
+    for (int b = 0; b < 2; ++b)
+      if (cudaEventCreateWithFlags(&v->ev_wfree[b], cudaEventDisableTiming) != cudaSuccess ||
+          cudaEventCreateWithFlags(&v->ev_wready[b], cudaEventDisableTiming) != cudaSuccess)
+        return kErrCuda;
+    if (cudaEventCreateWithFlags(&v->ev_fork, cudaEventDisableTiming) != cudaSuccess) return kErrCuda;
   }
   return ck(cudaStreamSynchronize(st));
 }
@@ -753,6 +811,14 @@ void sam3cu_vit_destroy(sam3cu_vit* v) {
     for (cudaEvent_t e : {v->ev_in[b], v->ev_done[b], v->ev_out[b]})
       if (e) cudaEventDestroy(e);
   for (auto& g : v->graphs) cudaGraphExecDestroy(g.exec);
+  if (v->side) {
+    cudaStreamSynchronize(v->side);
+    cudaStreamDestroy(v->side);
+  }
+  for (int b = 0; b < 2; ++b)
+    for (cudaEvent_t e : {v->ev_wfree[b], v->ev_wready[b]})
+      if (e) cudaEventDestroy(e);
+  if (v->ev_fork) cudaEventDestroy(v->ev_fork);
   if (v->stream) cudaStreamDestroy(v->stream);
   delete v;
 }
