@@ -311,6 +311,100 @@ __global__ void dwconv3x3_rows(const void* __restrict__ x, void* __restrict__ y,
   }
 }
 
+// Stride-1 row kernel for the memory-bound MBConv pass (4 channels of one
+// column per thread, kRows output rows): every input the thread needs,
+// (kRows + 2) rows x 3 columns, is loaded up front in its storage type (8
+// bytes for 16-bit data), so kRows * 3 + 6 independent loads are in flight
+// per thread instead of the three of one row; the BatchNorm-folded taps and
+// the bias come from shared memory.  ncu of the register-tap version showed
+// DRAM at 10% of peak, 24% of warps active and long-scoreboard stalls: a
+// latency-bound pass.  The grid is a few CTAs per SM, each loading the
+// [9][C] taps once and striding over (channels, column, row block, image).
+template <int TI>
+struct DwRaw {
+  using T = uint2;  // four 16-bit values
+  static __device__ __forceinline__ T ld(const void* p, int64_t i) {
+    return __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + i));
+  }
+  static __device__ __forceinline__ float4 f4(const T& r) {
+    if (TI == kBF16) {
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
+      return make_float4(a.x, a.y, b.x, b.y);
+    }
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  static __device__ __forceinline__ T zero() { return make_uint2(0u, 0u); }
+};
+template <>
+struct DwRaw<kF32> {
+  using T = float4;
+  static __device__ __forceinline__ T ld(const void* p, int64_t i) {
+    return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p) + i));
+  }
+  static __device__ __forceinline__ float4 f4(const T& r) { return r; }
+  static __device__ __forceinline__ T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+};
+
+template <int TI, int TO, bool kGelu, int kRows>
+__global__ void __launch_bounds__(256, 2) dwconv3x3_rows_smem(const void* __restrict__ x, void* __restrict__ y,
+                                                           const float* __restrict__ w9,
+                                                           const float* __restrict__ bias, int H, int W, int C,
+                                                           int row_blocks, unsigned total) {
+  using R = DwRaw<TI>;
+  extern __shared__ float4 sm4[];
+  float* sw = reinterpret_cast<float*>(sm4);  // [9][C] taps, then [C] bias
+  for (int t = threadIdx.x; t < 10 * C / 4; t += blockDim.x)
+    sm4[t] = __ldg(reinterpret_cast<const float4*>(t < 9 * C / 4 ? w9 + 4 * t : bias + 4 * t - 9 * C));
+  __syncthreads();
+  const unsigned c4 = C / 4;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int c = static_cast<int>(i % c4) * 4;
+    unsigned q = i / c4;
+    const int ox = static_cast<int>(q % W);
+    q /= W;
+    const int oy0 = static_cast<int>(q % row_blocks) * kRows;
+    const unsigned img = q / row_blocks;
+    const float4* k = reinterpret_cast<const float4*>(sw + c);  // tap t at k[t * c4]
+    typename R::T raw[kRows + 2][3];
+#pragma unroll
+    for (int r = 0; r < kRows + 2; ++r) {
+      const int iy = oy0 + r - 1;
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) {
+        const int ix = ox + kx - 1;
+        raw[r][kx] = (iy >= 0 && iy < H && ix >= 0 && ix < W)
+                         ? R::ld(x, ((static_cast<int64_t>(img) * H + iy) * W + ix) * C + c)
+                         : R::zero();
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < kRows; ++rr) {
+      const int oy = oy0 + rr;
+      float4 acc = k[9 * c4];  // bias
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+          const float4 v = R::f4(raw[rr + ky][kx]), w = k[(3 * ky + kx) * c4];
+          acc.x = fmaf(v.x, w.x, acc.x);
+          acc.y = fmaf(v.y, w.y, acc.y);
+          acc.z = fmaf(v.z, w.z, acc.z);
+          acc.w = fmaf(v.w, w.w, acc.w);
+        }
+      if (kGelu) {
+        acc.x = gelu_out<TO>(acc.x);
+        acc.y = gelu_out<TO>(acc.y);
+        acc.z = gelu_out<TO>(acc.z);
+        acc.w = gelu_out<TO>(acc.w);
+      }
+      if (oy < H) IO<TO>::st4(y, ((static_cast<int64_t>(img) * H + oy) * W + ox) * C + c, acc);
+    }
+  }
+}
+
 // 3x3 depthwise conv, zero padding 1, stride 1 or 2 (output (H-1)/s+1).
 int launch_dwconv3x3(const void* x, int tin, void* y, int tout, const float* w9, const float* bias, int B,
                      int H, int W, int C, bool gelu, cudaStream_t st, int stride = 1) {
@@ -319,6 +413,37 @@ int launch_dwconv3x3(const void* x, int tin, void* y, int tout, const float* w9,
   // stride 1: the row kernel (F32 blocks 0.369 -> 0.284 ms at 32 images);
   // stride 2: one output per thread measured faster (0.475 vs 0.904 ms per
   // launch; TinyViT 940 vs 919 images/s)
+  static const bool old_rows = [] {  // S3CU_DWCONV=regs: taps in registers (A/B measurements)
+    const char* e = getenv("S3CU_DWCONV");
+    return e && strcmp(e, "regs") == 0;
+  }();
+  if (stride == 1 && !old_rows && 10 * C * 4 <= 48 * 1024) {
+#ifndef S3_DW_ROWS16  // measured at 32 images, F16 (TinyViT images/s): 2 -> 926, 4 -> 956, 6 -> 966, 8 -> 964
+#define S3_DW_ROWS16 6
+#endif
+    constexpr int kR16 = S3_DW_ROWS16, kR32 = 4;  // output rows per thread (16-bit / F32 input)
+    const int rows = tin == kF32 ? kR32 : kR16;
+    const int row_blocks = (OH + rows - 1) / rows;
+    const int64_t total = static_cast<int64_t>(B) * row_blocks * OW * (C / 4);
+    if (total >= (1LL << 31)) return kErrShape;
+    count_launches(1);
+    const int64_t want = (total + 255) / 256;
+    const int grid = static_cast<int>(want < 8LL * num_sms() ? want : 8LL * num_sms());
+    const unsigned t = static_cast<unsigned>(total);
+    const size_t smem = static_cast<size_t>(10) * C * 4;
+#define S3_DWS(TI, TO)                                                                                        \
+  if (tin == TI && tout == TO) {                                                                              \
+    constexpr int R_ = TI == kF32 ? kR32 : kR16;                                                              \
+    if (gelu)                                                                                                 \
+      dwconv3x3_rows_smem<TI, TO, true, R_><<<grid, 256, smem, st>>>(x, y, w9, bias, H, W, C, row_blocks, t); \
+    else                                                                                                      \
+      dwconv3x3_rows_smem<TI, TO, false, R_><<<grid, 256, smem, st>>>(x, y, w9, bias, H, W, C, row_blocks, t); \
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;                                              \
+  }
+    S3_DWS(kF32, kF32) S3_DWS(kBF16, kBF16) S3_DWS(kF16, kF16) S3_DWS(kF32, kBF16) S3_DWS(kF32, kF16)
+#undef S3_DWS
+    return kErrDtype;
+  }
   if (stride == 1) {
     const int row_blocks = (OH + 7) / 8;
     const int64_t total = static_cast<int64_t>(B) * row_blocks * OW * (C / 4);
