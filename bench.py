@@ -570,6 +570,41 @@ def attention_leg(args, dev, sam3cu):
     return res
 
 
+def sdpa_f32_leg(args, dev, sam3cu):
+    """The drop-in path's F32 attention kernel (sam3cu_sdpa_f32_strided)
+    alone: Q|K|V read with strides from a packed [groups*seq, 3*1024] F32
+    buffer (the QKV layout), 16 heads of 64; checked against torch's SDPA in
+    float64; CUDA events over 5 launches after 2 warm-ups."""
+    import ctypes as C
+    import torch
+    L = sam3cu.lib()
+    f = L.sam3cu_sdpa_f32_strided
+    P = C.POINTER(C.c_int64)
+    f.argtypes = [C.c_void_p, P, C.c_void_p, P, C.c_void_p, P, C.c_void_p, C.c_void_p, P] + [C.c_int] * 5 + \
+        [C.c_void_p]
+    S, B, H, D = args.sdpa_seq, args.sdpa_groups, 16, 64
+    E = H * D
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = torch.randn(B * S, 3 * E, device=dev, generator=g)
+    o = torch.empty(B * S, E, device=dev)
+    st = (C.c_int64 * 3)(S * 3 * E, D, 3 * E)
+    so = (C.c_int64 * 3)(S * E, D, E)
+    base = qkv.data_ptr()
+
+    def run():
+        sam3cu.check(f(base, st, base + 4 * E, st, base + 8 * E, st, None, o.data_ptr(), so, B, H, S, S, D,
+                       torch.cuda.current_stream().cuda_stream), "sam3cu_sdpa_f32_strided")
+    for _ in range(2):
+        run()
+    ms = _event_ms(run, 5)
+    q, k, v = [qkv[:, i * E:(i + 1) * E].reshape(B, S, H, D).transpose(1, 2).double() for i in range(3)]
+    ref = torch.nn.functional.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B * S, E)
+    err = float((o.double() - ref).abs().max() / ref.abs().max())
+    assert sam3cu.device_error() == 0
+    return {"groups": B, "seq": S, "ms": ms, "tflops": 4.0 * S * S * D * H * B / ms / 1e9,
+            "rel_err_vs_torch_f64": err}
+
+
 def dropin_leg(args, dev, sam3cu):
     """The drop-in path: the reference's own sam3_vit_build (compiled from
     the sam3.c sources, dropin/_ref) evaluating its F32 Hiera-L graph on one
@@ -608,7 +643,7 @@ def tinyvit_leg(args, dev, sam3cu):
     device-resident images, CUDA-event time of 5 encodes after 3 warm-ups."""
     import torch
     cfg = dict(synth.TINYVIT_21M)
-    B = 32
+    B = args.tinyvit_batch
     tv = sam3cu.TinyViT(cfg, synth.tinyvit_weights(cfg, seed=0), sam3cu.F16, max_batch=B)
     imgs = torch.from_numpy(synth.tinyvit_images(cfg, B, seed=1)).to(dev)
     out = torch.empty((B, tv.grid * tv.grid, cfg["embed_dim"]), dtype=torch.float32, device=dev)
@@ -625,7 +660,7 @@ def tinyvit_leg(args, dev, sam3cu):
     ms = a.elapsed_time(b) / 5
     tv.close()
     assert sam3cu.device_error() == 0
-    return {"workload": "config5_tinyvit21m_1008px_batch32", "dtype": "f16", "value": B / (ms / 1000.0),
+    return {"workload": f"config5_tinyvit21m_1008px_batch{B}", "dtype": "f16", "value": B / (ms / 1000.0),
             "unit": "images/s", "ms_per_batch": ms, "data": "synthetic (seeded images, random-init weights)"}
 
 
@@ -636,7 +671,7 @@ def run_leg(args):
     sam3cu.init(0)
     dev = torch.device("cuda", 0)
     fn = {"dropin": dropin_leg, "sweep": gemm_sweep_leg, "q8": q8_legs, "neck": neck_leg,
-          "tinyvit": tinyvit_leg, "attn": attention_leg}[args.leg]
+          "tinyvit": tinyvit_leg, "attn": attention_leg, "sdpa_f32": sdpa_f32_leg}[args.leg]
     print(json.dumps({"leg": args.leg, "result": fn(args, dev, sam3cu)}))
     return 0
 
@@ -656,8 +691,11 @@ def main():
                     help="with --impl reference: print only the cpu_baseline object (no extrapolation)")
     ap.add_argument("--no-tinyvit", action="store_true", help="skip the config-5 TinyViT leg")
     ap.add_argument("--dropin-iters", type=int, default=3)
+    ap.add_argument("--sdpa-seq", type=int, default=5184, help="sdpa_f32 leg: tokens per group")
+    ap.add_argument("--sdpa-groups", type=int, default=1, help="sdpa_f32 leg: groups (images or windows)")
+    ap.add_argument("--tinyvit-batch", type=int, default=32, help="tinyvit leg: images per call")
     ap.add_argument("--leg", default=None,
-                    choices=["dropin", "sweep", "q8", "neck", "tinyvit", "attn"],
+                    choices=["dropin", "sweep", "q8", "neck", "tinyvit", "attn", "sdpa_f32"],
                     help="run one side leg alone on GPU 0 and print its result")
     args = ap.parse_args()
     if args.leg:
