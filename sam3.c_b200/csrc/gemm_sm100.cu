@@ -116,11 +116,49 @@ __device__ __forceinline__ void q8_dequant_tile_h2(const int8_t* q, const float*
   }
 }
 
+// The (tile, K range) segments one CTA processes.  Plain: whole tiles
+// blockIdx.x, blockIdx.x + gridDim.x, ...  Stream-K (`sk`, in-place F32
+// reduce-add epilogues only): the tiles x k-iterations of the problem are
+// cut into gridDim.x equal contiguous ranges, one per CTA, so every CTA
+// gets the same MMA work whatever the tile count; a tile whose K range is
+// split between CTAs is finished by the reduce-adds of its pieces (the
+// bias with the piece that starts at k = 0).  Every role walks the same
+// sequence.
+struct Segs {
+  int64_t pos, end;
+  int k_iters, tile, kb, ke;
+  bool sk;
+  __device__ __forceinline__ void init(bool sk_, int num_tiles, int k_iters_) {
+    sk = sk_;
+    k_iters = k_iters_;
+    const int64_t total = static_cast<int64_t>(num_tiles) * k_iters;
+    if (sk) {
+      pos = total * blockIdx.x / gridDim.x;
+      end = total * (blockIdx.x + 1) / gridDim.x;
+    } else {
+      pos = static_cast<int64_t>(blockIdx.x) * k_iters;
+      end = total;
+    }
+    if (pos < end) set();
+  }
+  __device__ __forceinline__ bool valid() const { return pos < end; }
+  __device__ __forceinline__ void set() {
+    tile = static_cast<int>(pos / k_iters);
+    kb = static_cast<int>(pos % k_iters);
+    const int64_t rem = end - pos;
+    ke = (sk && rem < k_iters - kb) ? kb + static_cast<int>(rem) : k_iters;
+  }
+  __device__ __forceinline__ void advance() {
+    pos += sk ? static_cast<int64_t>(ke - kb) : static_cast<int64_t>(gridDim.x) * k_iters;
+    if (pos < end) set();
+  }
+};
+
 template <int kBMode>
 __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_o,
-                GemmShape shp, EpiParams ep, uint32_t idesc, int b_is_bf16, int epi_mode) {
+                GemmShape shp, EpiParams ep, uint32_t idesc, int b_is_bf16, int epi_mode, int streamk) {
   using Cfg = GemmCfg<kBMode>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -189,10 +227,11 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
       __syncwarp();
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * kBM;  // N-fastest: A rows stay in L2
-        const int n0 = (tile % n_tiles) * kBN;
-        for (int kt = 0; kt < k_iters; ++kt, ++it) {
+      Segs sg;
+      for (sg.init(streamk != 0, num_tiles, k_iters); sg.valid() && ok; sg.advance()) {
+        const int m0 = (sg.tile / n_tiles) * kBM;  // N-fastest: A rows stay in L2
+        const int n0 = (sg.tile % n_tiles) * kBN;
+        for (int kt = sg.kb; kt < sg.ke; ++kt, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait_warp(&empty_bar[s], ph ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
@@ -219,13 +258,15 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
       uint32_t it = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      Segs sg;
+      for (sg.init(streamk != 0, num_tiles, k_iters); sg.valid() && ok; sg.advance(), ++local) {
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait_warp(&acce_bar[acc], aph ^ 1, kErrAccFree, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
-        for (int kt = 0; kt < k_iters; ++kt, ++it) {
+        for (int kt = sg.kb; kt < sg.ke; ++kt, ++it) {
+          const int kr = kt - sg.kb;  // 0 on the segment's first k-iteration: overwrite the accumulator
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           uint64_t* ready = kBMode == kBQ8 ? &conv_bar[it & 1] : (Cfg::kConv ? &conv_bar[s] : &full_bar[s]);
@@ -240,7 +281,7 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
             const uint64_t bldesc = make_sdesc_sw128(smem_u32(stage_q(s) + kATileBytes));
 #pragma unroll
             for (int k = 0; k < BKe / Cfg::kUmmaKe; ++k) {
-              umma_ss_warp<1>(d_tmem, aldesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+              umma_ss_warp<1>(d_tmem, aldesc + 2 * k, bdesc + 2 * k, idesc, (kr | k) ? 1u : 0u);
               umma_ss_warp<1>(d_tmem, adesc + 2 * k, bldesc + 2 * k, idesc, 1u);
               umma_ss_warp<1>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, 1u);
             }
@@ -248,7 +289,7 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
 #pragma unroll
             for (int k = 0; k < BKe / Cfg::kUmmaKe; ++k) {
               // advance 16 elements = 32 bytes = 2 (16-byte units) along K
-              umma_ss_warp<0>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kt | k) ? 1u : 0u);
+              umma_ss_warp<0>(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kr | k) ? 1u : 0u);
             }
           }
           umma_commit_warp(&empty_bar[s]);  // frees the smem stage when these MMAs finish
@@ -266,9 +307,11 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
     const int half = (warp - 2) / 4;
     uint8_t* my_stage = stage_out + (warp - 2) * Cfg::kStageOutBytes;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int m0 = (tile / n_tiles) * kBM;
-      const int n0 = (tile % n_tiles) * kBN;
+    Segs sg;
+    for (sg.init(streamk != 0, num_tiles, k_iters); sg.valid(); sg.advance(), ++local) {
+      const int m0 = (sg.tile / n_tiles) * kBM;
+      const int n0 = (sg.tile % n_tiles) * kBN;
+      const bool first_k = sg.kb == 0;  // the bias goes with the piece at k = 0
       const int acc = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       // one lane waits, the warp follows its verdict (tcgen05.ld is .aligned)
@@ -292,12 +335,12 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
         if (epi_mode == kEpiDirect) {
           if (row < shp.M) {
-            epilogue_math(ep, v, row, col0, shp.N);
+            epilogue_math(ep, v, row, col0, shp.N, first_k);
             epilogue_store_direct(ep, v, row, col0, shp.N);
           }
         } else {
           // rows >= M and columns >= N are clipped by the TMA store
-          epilogue_math(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N);
+          epilogue_math(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N, first_k);
           // a residual other than the destination (e.g. the periodic pos-embed)
           if (epi_mode == kEpiTmaStore && ep.residual)
             epilogue_residual(ep, v, row < shp.M ? row : shp.M - 1, col0, shp.N);
@@ -325,8 +368,9 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
     const int t = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);
     uint32_t it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      for (int kt = 0; kt < k_iters; ++kt, ++it) {
+    Segs sg;
+    for (sg.init(streamk != 0, num_tiles, k_iters); sg.valid() && ok; sg.advance()) {
+      for (int kt = sg.kb; kt < sg.ke; ++kt, ++it) {
         const int s = it % S;
         const uint32_t ph = (it / S) & 1;
         if (!mbar_wait(&full_bar[s], ph, kErrTmaWait, abort_flag)) { ok = false; break; }
@@ -446,6 +490,32 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
     if (ldw % 8 != 0) return kErrShape;
     return launch_gemm_pair(A, lda, W, ldw, bf, shp, ep, to, mode, stream, max_ctas);
   }
+  // Stream-K for the in-place F32 reduce-add linears (no activation / RoPE)
+  // of the 3xTF32 kernel whose tile count fills the last wave poorly, e.g.
+  // proj at one image: 164 tiles of 128x256 on 148 SMs ran as 1.1 waves.
+  // Every CTA then gets the same number of k-iterations (Segs).  Measured at
+  // M = 5184: F32 proj 81 -> 135 TFLOP/s, fc2 102 -> 183.  The 16-bit
+  // kernels do not gain (BF16 proj 515 -> 497: its reduce-add traffic, which
+  // stream-K doubles, bounds it), so they keep whole tiles.
+  // S3CU_GEMM_STREAMK=0 disables it, =2 also enables it for 16-bit operands.
+  static const int sk_mode = [] {
+    const char* e = getenv("S3CU_GEMM_STREAMK");
+    return e ? atoi(e) : 1;
+  }();
+  int streamk = 0;
+  {
+    const int tiles = m_tiles * n_tiles;
+    const int k_iters = (shp.K + bke - 1) / bke;
+    if ((sk_mode >= 2 || (sk_mode == 1 && f32in)) && mode == kEpiTmaAdd && ep.act == 0 && ep.rope_cols == 0 && k_iters >= 8 &&
+        static_cast<int64_t>(tiles) * k_iters >= 4LL * cap) {
+      const int waves = (tiles + cap - 1) / cap;
+      const double eff = static_cast<double>(tiles) / (static_cast<double>(waves) * cap);
+      if (eff < 0.85) {
+        streamk = 1;
+        grid = cap;
+      }
+    }
+  }
   if (q8) {
     if (shp.K % 64 != 0) return kErrShape;
     if (!make_tmap_2d(&tb, q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, shp.N, shp.K, shp.K, kBN, kBK,
@@ -461,7 +531,7 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       attr = true;
     }
     gemm_kernel<kBQ8><<<grid, GemmCfg<kBQ8>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep, idesc,
-                                                                         bf ? 1 : 0, mode);
+                                                                         bf ? 1 : 0, mode, streamk);
   } else if (f32in) {
     if (ldw % 4 != 0) return kErrShape;
     if (!make_tmap_2d(&tb, W, dt, 4, shp.N, shp.K, ldw, kBN, bke, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -473,7 +543,7 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       attr = true;
     }
     gemm_kernel<kBF32><<<grid, GemmCfg<kBF32>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep, idesc, 0,
-                                                                           mode);
+                                                                           mode, streamk);
   } else {
     if (ldw % 8 != 0) return kErrShape;
     if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, kBN, kBK, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -485,7 +555,7 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       attr = true;
     }
     gemm_kernel<kBTma16><<<grid, GemmCfg<kBTma16>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep,
-                                                                              idesc, bf ? 1 : 0, mode);
+                                                                              idesc, bf ? 1 : 0, mode, streamk);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
 }

@@ -62,7 +62,8 @@ def test_linear_gelu_bf16out(cuda, M, K, N):
 # the fc2-sized shapes run split-K on the pair kernel (4 K slices
 # reduce-added into the residual; the bias is added by the first slice only)
 @pytest.mark.parametrize("M,K,N", [(300, 256, 128), (5184, 4736, 1024), (5184, 1024, 1024), (10368, 4736, 1024),
-                                   (5000, 4736, 1000)])  # ragged M and N tiles under split-K
+                                   (5000, 4736, 1000),  # ragged M and N tiles under split-K
+                                   (2000, 2048, 1000)])
 def test_linear_residual_inplace(cuda, M, K, N):
     import torch
     import sam3cu
@@ -167,3 +168,36 @@ def test_linear_separate_residual(cuda, out_dtype, M, K, N):
     assert np.array_equal(to_np(tres), res)  # the residual is only read
     tol = 2e-4 * max(1.0, K / 1024) if out_dtype == "f32" else 1e-2
     assert rel_err(to_np(y), ref) < tol
+
+
+@pytest.mark.parametrize("kind", ["f32", "q8"])
+def test_streamk_residual_f32_and_q8(cuda, kind):
+    """x += x . W^T + b on the 1-SM kernel with 64 / 48 tiles for 148 SMs: the
+    3xTF32 kernel runs it stream-K (equal k-ranges per CTA, pieces of a tile
+    reduce-added); the in-GEMM Q8_0 kernel runs it with whole tiles (or
+    stream-K under S3CU_GEMM_STREAMK=2)."""
+    import torch
+    import sam3cu
+    rng = np.random.default_rng(12)
+    M, K, N = (2000, 1024, 1000) if kind == "f32" else (1500, 2048, 1024)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w = rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(K))
+    b = rng.standard_normal(N, dtype=np.float32)
+    res = rng.standard_normal((M, N), dtype=np.float32)
+    tres = torch.from_numpy(res).cuda()
+    if kind == "f32":
+        sam3cu.linear(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), bias=torch.from_numpy(b).cuda(),
+                      residual=tres, out=tres)
+        ref, tol = O.linear(x, w, b, res=res), 1e-4
+    else:
+        blocks = O.q8_quantize(w)
+        wdq = O.q8_dequantize(blocks, N * K).reshape(N, K)
+        tb = torch.from_numpy(np.frombuffer(blocks.tobytes(), np.uint8).copy()).cuda()
+        q, sc = sam3cu.q8_repack(tb, N, K)
+        xb = O.round_bf16(x)
+        sam3cu.linear_q8(torch.from_numpy(xb).cuda().bfloat16(), q, sc, bias=torch.from_numpy(b).cuda(),
+                         residual=tres, out=tres)
+        ref, tol = O.linear(xb, wdq, b, res=res), 1e-2
+    torch.cuda.synchronize()
+    assert sam3cu.device_error() == 0
+    assert rel_err(to_np(tres), ref) < tol
