@@ -62,9 +62,19 @@ S3_DEV_ERROR_ACCESSOR(dev_error_attn_tc)
 namespace {
 
 constexpr int kQ = 128;                  // query rows per CTA
-constexpr int kKV = 128;                 // keys per tile
-constexpr int kStages = 3;               // K/V ring depth
-constexpr int kTmemCols = 256;           // S: 0..127, O: 128.., P: 192..255
+#ifndef S3_ATTN_KV
+#define S3_ATTN_KV 128
+#endif
+constexpr int kKV = S3_ATTN_KV;          // keys per tile
+static_assert(kKV == 64 || kKV == 128, "64- or 128-key tiles");
+// 128-key tiles: S [0,128), O [128,192), P [192,256) in the CTA's 256 TMEM
+// columns, one buffer each.  64-key tiles leave room to double-buffer S and
+// P: S0 [0,64) S1 [64,128), O [128,192), P0 [192,224) P1 [224,256), so the
+// softmax of tile j+1 neither waits for S_j to be released nor for P_j to
+// be consumed (P.V of tile j).
+constexpr int kNB = kKV == 64 ? 2 : 1;   // S / P buffers
+constexpr int kStages = kKV == 64 ? 6 : 3;  // K/V ring depth (same bytes)
+constexpr int kTmemCols = 256;
 
 // Per head dimension: a Q, K or V tile is 128 rows of kD 16-bit elements,
 // 128-byte rows (kD 64, 128-byte swizzle) or 64-byte rows (kD 32, 64-byte
@@ -72,8 +82,9 @@ constexpr int kTmemCols = 256;           // S: 0..127, O: 128.., P: 192..255
 template <int kD>
 struct HeadCfg {
   static constexpr int kRowBytes = kD * 2;
-  static constexpr int kTile = kQ * kRowBytes;
-  static constexpr int kSmem = kTile * (1 + 2 * kStages);  // Q | K0 V0 | K1 V1 | ...
+  static constexpr int kTile = kQ * kRowBytes;     // Q tile
+  static constexpr int kKVTile = kKV * kRowBytes;  // K or V tile
+  static constexpr int kSmem = kTile + 2 * kStages * kKVTile;  // Q | K0 V0 | K1 V1 | ...
   static_assert(kD == 32 || kD == 64, "head_dim 32 or 64");
 };
 #ifndef S3_ATTN_SPLIT
@@ -85,6 +96,7 @@ constexpr int kSplit = S3_ATTN_SPLIT;
 constexpr int kSoftWarps = 4 * kSplit;
 constexpr int kThreads = 64 + 32 * kSoftWarps;  // 2 control warps + softmax
 constexpr int kHalf = kKV / kSplit;             // keys per softmax warp
+static_assert(kSplit == 1 || kNB == 1, "split softmax rows only with single-buffered S and P");
 #ifndef S3_ATTN_PSTORE
 #define S3_ATTN_PSTORE 8
 #endif
@@ -259,17 +271,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr int kTile = HC::kTile;
   constexpr int kOHalf = kD / kSplit;  // O columns per softmax warp
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ uint64_t bars[8 + 2 * kStages];
+  __shared__ uint64_t bars[10 + 2 * kStages];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag_s;
   uint64_t* q_full = &bars[0];
-  uint64_t* s_full = &bars[1];
-  uint64_t* s_empty = &bars[2];
-  uint64_t* p_full = &bars[3];
-  uint64_t* p_empty = &bars[4];
-  uint64_t* o_full = &bars[5];
-  uint64_t* kv_full = &bars[6];              // [kStages]
-  uint64_t* kv_empty = &bars[6 + kStages];   // [kStages]
+  uint64_t* o_full = &bars[1];
+  uint64_t* s_full = &bars[2];               // [kNB]
+  uint64_t* s_empty = &bars[4];              // [kNB]
+  uint64_t* p_full = &bars[6];               // [kNB]
+  uint64_t* p_empty = &bars[8];              // [kNB]
+  uint64_t* kv_full = &bars[10];             // [kStages]
+  uint64_t* kv_empty = &bars[10 + kStages];  // [kStages]
   volatile int* abort_flag = &abort_flag_s;
 
   const int seq = prm.seq;
@@ -289,8 +301,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
   uint8_t* sQ = smem;
-  auto sK = [&](int st) { return smem + (1 + 2 * st) * kTile; };
-  auto sV = [&](int st) { return smem + (2 + 2 * st) * kTile; };
+  auto sK = [&](int st) { return smem + kTile + 2 * st * HC::kKVTile; };
+  auto sV = [&](int st) { return smem + kTile + (2 * st + 1) * HC::kKVTile; };
   auto sdesc_k = [](uint32_t a) { return kD == 64 ? make_sdesc_sw128(a) : make_sdesc_sw64(a); };
   auto sdesc_mn = [](uint32_t a) { return kD == 64 ? make_sdesc_sw128_mn(a) : make_sdesc_sw64_mn(a); };
 
@@ -300,10 +312,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_empty, kSoftWarps);
-    mbar_init(p_full, kSoftWarps);
-    mbar_init(p_empty, 1);
+    for (int b = 0; b < kNB; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], kSoftWarps);
+      mbar_init(&p_full[b], kSoftWarps);
+      mbar_init(&p_empty[b], 1);
+    }
     mbar_init(o_full, 1);
     abort_flag_s = 0;
     fence_barrier_init();
@@ -316,7 +330,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128, tP = tmem + 192;
+  const uint32_t tO = tmem + 128;
+  auto tS = [&](int b) { return tmem + static_cast<uint32_t>(b * kKV); };
+  auto tP = [&](int b) { return tmem + 192u + static_cast<uint32_t>(b * (kKV / 2)); };
 
   if (warp == 0) {
     // TMA producer: the whole warp runs the loop, one elected lane issues
@@ -332,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int st = j % kStages;
       if (!mbar_wait_warp(&kv_empty[st], ((j / kStages) & 1) ^ 1, kErrStageFree, abort_flag)) break;
       if (elect_one()) {
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * HC::kKVTile);
         tma_load_2d(sK(st), &tk, &kv_full[st], hx, row0 + j * kKV);
         tma_load_2d(sV(st), &tv, &kv_full[st], hx, row0 + j * kKV);
       }
@@ -351,23 +367,26 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     // S_j = Q K_j^T into TMEM once K_j landed and the softmax read S_{j-1}
     auto issue_s = [&](int j) -> bool {
-      const int st = j % kStages;
+      const int st = j % kStages, b = j % kNB;
       if (!mbar_wait_warp(&kv_full[st], (j / kStages) & 1, kErrTmaWait, abort_flag)) return false;
-      if (!mbar_wait_warp(s_empty, (j & 1) ^ 1, kErrAccFree, abort_flag)) return false;
+      if (!mbar_wait_warp(&s_empty[b], ((j / kNB) & 1) ^ 1, kErrAccFree, abort_flag)) return false;
       tc_fence_after();
       const uint64_t kdesc = sdesc_k(smem_u32(sK(st)));
       const uint32_t idesc_s = make_idesc(fmt, kQ, keys_in(j));
 #pragma unroll
       for (int kk = 0; kk < kD / 16; ++kk)  // 16 elements = 32 bytes along K
-        umma_ss_warp(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
-      umma_commit_warp(s_full);
+        umma_ss_warp(tS(b), qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
+      umma_commit_warp(&s_full[b]);
       return true;
     };
     if (ok) ok = issue_s(0);
+    if (ok && kNB == 2 && n_kv > 1) ok = issue_s(1);
     for (int j = 0; ok && j < n_kv; ++j) {
       // the next S = Q K^T runs while the softmax of tile j is computed
-      if (j + 1 < n_kv && !issue_s(j + 1)) break;
-      if (!mbar_wait_warp(p_full, j & 1, kErrAccFull, abort_flag)) break;
+      // (double-buffered: S_{j+1} is already issued, S_{j+2} follows P_j.V_j)
+      if (kNB == 1 && j + 1 < n_kv && !issue_s(j + 1)) break;
+      const int pb = j % kNB;
+      if (!mbar_wait_warp(&p_full[pb], (j / kNB) & 1, kErrAccFull, abort_flag)) break;
       tc_fence_after();
       const int st = j % kStages, n = keys_in(j);
       const uint64_t vdesc = sdesc_mn(smem_u32(sV(st)));
@@ -375,13 +394,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (n == kKV) {
 #pragma unroll
         for (int kk = 0; kk < kKV / 16; ++kk)  // A = P from TMEM: 16 keys = 8 columns
-          umma_ts_warp(tO, tP + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
+          umma_ts_warp(tO, tP(pb) + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
       } else {
         for (int kk = 0; kk < n / 16; ++kk)
-          umma_ts_warp(tO, tP + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
+          umma_ts_warp(tO, tP(pb) + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
       }
-      umma_commit_warp(p_empty);
+      umma_commit_warp(&p_empty[pb]);
       umma_commit_warp(&kv_empty[st]);
+      if (kNB == 2 && j + 2 < n_kv && !issue_s(j + 2)) break;
     }
     umma_commit_warp(o_full);
   } else {
@@ -406,10 +426,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     if constexpr (kBias) brow = prm.bias + (static_cast<int64_t>(head) * brows + qrow_t) * prm.bias_ld;
     // S columns [c0, c0+64) of key tile j -> sv (scaled and biased if kBias,
     // keys >= seq set to -inf)
+    int sb = 0;  // S buffer of the current tile
     auto load_s = [&](float* sv, uint32_t* su, uint32_t c0, int kfirst) {
 #pragma unroll
       for (int c = 0; c < kHalf / 32; ++c)
-        tmem_ld_32x32b_x32(tS + lane_off + c0 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
+        tmem_ld_32x32b_x32(tS(sb) + lane_off + c0 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
       tmem_ld_wait();
       if constexpr (kBias) {
 #pragma unroll
@@ -442,7 +463,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool rows_live = qt * kQ + quarter * 32 < span;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!warp_wait(s_full, j & 1, kErrAccFull, abort_flag, lane)) { ok = false; break; }
+      sb = j % kNB;
+      if (!warp_wait(&s_full[sb], (j / kNB) & 1, kErrAccFull, abort_flag, lane)) { ok = false; break; }
       tc_fence_after();
       const int kb = j * kKV + scol;
       // keys of this half exist (the ragged last tile of a window has none
@@ -462,17 +484,28 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (live) load_s(sv, su, scol, kb);  // this warp's 64 S columns
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty);  // S may be overwritten
+      if (lane == 0) mbar_arrive(&s_empty[sb]);  // S may be overwritten
       if (live) mt = fmaxf(mt, max_row(sv));
       const bool need = (mt - m_used) * sl2 > kRescaleLog2;
-      // P buffer and O are free once the previous P.V finished
-      if (j > 0 && !warp_wait(p_empty, (j - 1) & 1, kErrAccFree, abort_flag, lane)) { ok = false; break; }
+      // P buffer sb is free once the P.V of tile j - kNB finished (with one
+      // buffer: the previous P.V, which also leaves O quiescent)
+      if (j >= kNB && !warp_wait(&p_empty[sb], ((j / kNB) & 1) ^ 1, kErrAccFree, abort_flag, lane)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       if (__any_sync(0xffffffffu, need)) {  // same rows, same verdict in both halves
         const float m_new = fmaxf(m_used, mt);
         const float corr = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * sl2);
         l *= corr;
         m_used = m_new;
+        // two buffers: O is quiescent once the P.V of tile j - 1 finished too
+        if (kNB == 2 && j > 0 &&
+            !warp_wait(&p_empty[(j - 1) % kNB], ((j - 1) / kNB) & 1, kErrAccFree, abort_flag, lane)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         if (j > 0) {  // this half rescales O columns [kOHalf*half, kOHalf*(half+1))
 #pragma unroll
           for (int c = 0; c < kOHalf / 8; ++c) {  // 8 columns at a time: few live registers
@@ -510,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             l2[(c >> 1) & 1] = fadd2(l2[(c >> 1) & 1], f2pack(p0, p1));
             pk[(c - c0) / 2] = pack2(p0, p1, kBf16);
           }
-          const uint32_t ta = tP + lane_off + half * (kHalf / 2) + c0 / 2;
+          const uint32_t ta = tP(sb) + lane_off + half * (kHalf / 2) + c0 / 2;
           if constexpr (kPStore == 8)
             tmem_st_32x32b_x8(ta, *reinterpret_cast<const uint32_t(*)[8]>(pk));
           else if constexpr (kPStore == 16)
@@ -525,13 +558,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[sb]);
     }
     // all MMAs done: O complete, S columns free for the row-sum exchange
     // (both warps of a quarter reach the exchange, also after an abort)
     const bool o_ok = ok && warp_wait(o_full, 0, kErrAccFull, abort_flag, lane);
     tc_fence_after();
-    if (kSplit == 2 && rows_live) l += pair_exchange(tS, lane_off, half, l, quarter);
+    if (kSplit == 2 && rows_live) l += pair_exchange(tS(0), lane_off, half, l, quarter);
     if (o_ok) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int qrow = qt * kQ + r;
@@ -594,19 +627,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   using HC = HeadCfg<kD>;
   constexpr int kTile = HC::kTile;
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ uint64_t bars[10 + 2 * kStages];
+  __shared__ uint64_t bars[12 + 2 * kStages];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag_s;
   uint64_t* q_full = &bars[0];
-  uint64_t* s_full = &bars[1];
-  uint64_t* s_empty = &bars[2];
-  uint64_t* p_full = &bars[3];
-  uint64_t* p_empty = &bars[4];
-  uint64_t* o_full = &bars[5];
-  uint64_t* q_empty = &bars[6];              // all S MMAs of an item done: Q may be replaced
-  uint64_t* o_empty = &bars[7];              // the epilogue read O: the next item may overwrite it
-  uint64_t* kv_full = &bars[8];              // [kStages]
-  uint64_t* kv_empty = &bars[8 + kStages];   // [kStages]
+  uint64_t* o_full = &bars[1];
+  uint64_t* q_empty = &bars[2];              // all S MMAs of an item done: Q may be replaced
+  uint64_t* o_empty = &bars[3];              // the epilogue read O: the next item may overwrite it
+  uint64_t* s_full = &bars[4];               // [kNB]
+  uint64_t* s_empty = &bars[6];              // [kNB]
+  uint64_t* p_full = &bars[8];               // [kNB]
+  uint64_t* p_empty = &bars[10];             // [kNB]
+  uint64_t* kv_full = &bars[12];             // [kStages]
+  uint64_t* kv_empty = &bars[12 + kStages];  // [kStages]
   volatile int* abort_flag = &abort_flag_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -618,8 +651,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
   uint8_t* sQ = smem;
-  auto sK = [&](int st) { return smem + (1 + 2 * st) * kTile; };
-  auto sV = [&](int st) { return smem + (2 + 2 * st) * kTile; };
+  auto sK = [&](int st) { return smem + kTile + 2 * st * HC::kKVTile; };
+  auto sV = [&](int st) { return smem + kTile + (2 * st + 1) * HC::kKVTile; };
   auto sdesc_k = [](uint32_t a) { return kD == 64 ? make_sdesc_sw128(a) : make_sdesc_sw64(a); };
   auto sdesc_mn = [](uint32_t a) { return kD == 64 ? make_sdesc_sw128_mn(a) : make_sdesc_sw64_mn(a); };
 
@@ -630,10 +663,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_empty, kSoftWarps);
-    mbar_init(p_full, kSoftWarps);
-    mbar_init(p_empty, 1);
+    for (int b = 0; b < kNB; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], kSoftWarps);
+      mbar_init(&p_full[b], kSoftWarps);
+      mbar_init(&p_empty[b], 1);
+    }
     mbar_init(o_full, 1);
     mbar_init(o_empty, kSoftWarps);
     abort_flag_s = 0;
@@ -647,7 +682,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 128, tP = tmem + 192;
+  const uint32_t tO = tmem + 128;
+  auto tS = [&](int b) { return tmem + static_cast<uint32_t>(b * kKV); };
+  auto tP = [&](int b) { return tmem + 192u + static_cast<uint32_t>(b * (kKV / 2)); };
 
   if (warp == 0) {
     // TMA producer: the whole warp runs the loop, one elected lane issues
@@ -676,7 +713,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         if (elect_one()) {
-          mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+          mbar_arrive_expect_tx(&kv_full[st], 2 * HC::kKVTile);
           tma_load_2d(sK(st), &tk, &kv_full[st], hx, it.row0 + j * kKV);
           tma_load_2d(sV(st), &tv, &kv_full[st], hx, it.row0 + j * kKV);
         }
@@ -699,24 +736,27 @@ __global__ void __launch_bounds__(kThreads, 2)
       };
       // S_j = Q K_j^T into TMEM once K_j landed and the softmax read S_{j-1}
       auto issue_s = [&](int j, int tt) -> bool {
-        const int st = tt % kStages;
+        const int st = tt % kStages, b = tt % kNB;
         if (!mbar_wait_warp(&kv_full[st], (tt / kStages) & 1, kErrTmaWait, abort_flag)) return false;
-        if (!mbar_wait_warp(s_empty, (tt & 1) ^ 1, kErrAccFree, abort_flag)) return false;
+        if (!mbar_wait_warp(&s_empty[b], ((tt / kNB) & 1) ^ 1, kErrAccFree, abort_flag)) return false;
         tc_fence_after();
         const uint64_t kdesc = sdesc_k(smem_u32(sK(st)));
         const uint32_t idesc_s = make_idesc(fmt, kQ, keys_in(j));
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk)  // 16 elements = 32 bytes along K
-          umma_ss_warp(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
-        umma_commit_warp(s_full);
+          umma_ss_warp(tS(b), qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk ? 1u : 0u);
+        umma_commit_warp(&s_full[b]);
         if (j == it.n_kv - 1) umma_commit_warp(q_empty);  // the item's last read of Q
         return true;
       };
       if (!mbar_wait_warp(q_full, n & 1, kErrTmaWait, abort_flag) || !issue_s(0, t)) break;
+      if (kNB == 2 && it.n_kv > 1 && !issue_s(1, t + 1)) break;
       for (int j = 0; j < it.n_kv; ++j, ++t) {
         // the next S = Q K^T runs while the softmax of tile j is computed
-        if (j + 1 < it.n_kv && !issue_s(j + 1, t + 1)) { ok = false; break; }
-        if (!mbar_wait_warp(p_full, t & 1, kErrAccFull, abort_flag)) { ok = false; break; }
+        // (double-buffered: S_{j+1} is already issued, S_{j+2} follows P_j.V_j)
+        if (kNB == 1 && j + 1 < it.n_kv && !issue_s(j + 1, t + 1)) { ok = false; break; }
+        const int pb = t % kNB;
+        if (!mbar_wait_warp(&p_full[pb], (t / kNB) & 1, kErrAccFull, abort_flag)) { ok = false; break; }
         // the first P.V of an item overwrites O: the epilogue of the previous
         // item must have read it
         if (j == 0 && n > 0 && !mbar_wait_warp(o_empty, (n - 1) & 1, kErrAccFree, abort_flag)) {
@@ -730,13 +770,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (nk == kKV) {
 #pragma unroll
           for (int kk = 0; kk < kKV / 16; ++kk)  // A = P from TMEM: 16 keys = 8 columns
-            umma_ts_warp(tO, tP + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
+            umma_ts_warp(tO, tP(pb) + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
         } else {
           for (int kk = 0; kk < nk / 16; ++kk)
-            umma_ts_warp(tO, tP + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
+            umma_ts_warp(tO, tP(pb) + kk * 8, vdesc + kk * kVStep, idesc_pv, (j | kk) ? 1u : 0u);
         }
-        umma_commit_warp(p_empty);
+        umma_commit_warp(&p_empty[pb]);
         umma_commit_warp(&kv_empty[st]);
+        if (kNB == 2 && j + 2 < it.n_kv && !issue_s(j + 2, t + 2)) { ok = false; break; }
       }
       if (ok) umma_commit_warp(o_full);
     }
@@ -767,10 +808,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       if constexpr (kBias) brow = prm.bias + (static_cast<int64_t>(it.head) * brows + qrow_t) * prm.bias_ld;
       // S columns of key tile j -> sv (scaled and biased if kBias, keys >= seq
       // set to -inf)
-      auto load_s = [&](float* sv, uint32_t* su, int kfirst) {
+      auto load_s = [&](float* sv, uint32_t* su, int kfirst, int b) {
 #pragma unroll
         for (int c = 0; c < kKV / 32; ++c)
-          tmem_ld_32x32b_x32(tS + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
+          tmem_ld_32x32b_x32(tS(b) + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(su + c * 32));
         tmem_ld_wait();
         if constexpr (kBias) {
 #pragma unroll
@@ -801,25 +842,38 @@ __global__ void __launch_bounds__(kThreads, 2)
       // tile of a 576-token window) only keeps the barrier protocol going.
       const bool live = it.qt * kQ + quarter * 32 < span;
       for (int j = 0; j < it.n_kv; ++j, ++t) {
-        if (!warp_wait(s_full, t & 1, kErrAccFull, abort_flag, lane)) { ok = false; break; }
+        const int sb = t % kNB;
+        if (!warp_wait(&s_full[sb], (t / kNB) & 1, kErrAccFull, abort_flag, lane)) { ok = false; break; }
         tc_fence_after();
         uint32_t su[kKV];  // S bits, loaded in place
         float* sv = reinterpret_cast<float*>(su);
-        if (live) load_s(sv, su, j * kKV);
+        if (live) load_s(sv, su, j * kKV, sb);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(s_empty);  // S may be overwritten
-        const float mt = live ? max128(sv) : -INFINITY;
+        if (lane == 0) mbar_arrive(&s_empty[sb]);  // S may be overwritten
+        const float mt = live ? (kKV == 64 ? max64(sv) : max128(sv)) : -INFINITY;
         const bool need = (mt - m_used) * sl2 > kRescaleLog2;
-        // P buffer and O are free once the previous P.V finished (for j = 0
-        // that P.V belongs to the previous item, finished before its o_full)
-        if (t > 0 && !warp_wait(p_empty, (t - 1) & 1, kErrAccFree, abort_flag, lane)) { ok = false; break; }
+        // P buffer sb is free once the P.V of tile t - kNB finished (one
+        // buffer: the previous P.V, which also leaves O quiescent; for j = 0
+        // that P.V may belong to the previous item, finished before its
+        // o_full)
+        if (t >= kNB && !warp_wait(&p_empty[sb], ((t / kNB) & 1) ^ 1, kErrAccFree, abort_flag, lane)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         if (__any_sync(0xffffffffu, need)) {
           const float m_new = fmaxf(m_used, mt);
           const float corr = (m_used == -INFINITY) ? 0.f : ex2((m_used - m_new) * sl2);
           l *= corr;
           m_used = m_new;
+          // two buffers: O is quiescent once the P.V of tile t - 1 finished too
+          if (kNB == 2 && j > 0 &&
+              !warp_wait(&p_empty[(t - 1) % kNB], ((t - 1) / kNB) & 1, kErrAccFree, abort_flag, lane)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           if (j > 0) {
 #pragma unroll
             for (int c = 0; c < kD / 8; ++c) {  // 8 columns at a time: few live registers
@@ -857,7 +911,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               l2[(c >> 1) & 1] = fadd2(l2[(c >> 1) & 1], f2pack(p0, p1));
               pk[(c - c0) / 2] = pack2(p0, p1, kBf16);
             }
-            tmem_st_32x32b_x8(tP + lane_off + c0 / 2, *reinterpret_cast<const uint32_t(*)[8]>(pk));
+            tmem_st_32x32b_x8(tP(sb) + lane_off + c0 / 2, *reinterpret_cast<const uint32_t(*)[8]>(pk));
           }
           float a0, a1;
           f2unpack(fadd2(l2[0], l2[1]), a0, a1);
@@ -866,7 +920,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full);
+        if (lane == 0) mbar_arrive(&p_full[sb]);
       }
       // all MMAs of the item done: O complete
       if (!ok || !warp_wait(o_full, n & 1, kErrAccFull, abort_flag, lane)) break;
@@ -907,9 +961,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 // [rows, width] 16-bit matrix of row pitch ld, boxes of 128 rows x head_dim
 // columns (128- or 64-byte swizzle, matching the kernel's descriptors).
 bool make_head_map(CUtensorMap* m, const void* base, int dtype, int64_t rows, int64_t width, int64_t ld,
-                   int head_dim) {
+                   int head_dim, int box_rows) {
   const CUtensorMapDataType dt = dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return make_tmap_2d(m, base, dt, 2, rows, width, ld, kQ, head_dim,
+  return make_tmap_2d(m, base, dt, 2, rows, width, ld, box_rows, head_dim,
                       head_dim == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
@@ -951,9 +1005,9 @@ int launch_attention_tc_ex(const AttnArgs& a, cudaStream_t st) {
   if (rows > 0x7fffffffLL) return kErrShape;
   const int64_t width = static_cast<int64_t>(a.heads - 1) * in_hs + a.head_dim;  // last head ends here
   CUtensorMap mq, mk, mv;
-  if (!make_head_map(&mq, a.q, a.dtype, rows, width, a.ldq, a.head_dim) ||
-      !make_head_map(&mk, a.k, a.dtype, rows, width, a.ldq, a.head_dim) ||
-      !make_head_map(&mv, a.v, a.dtype, rows, width, a.ldq, a.head_dim))
+  if (!make_head_map(&mq, a.q, a.dtype, rows, width, a.ldq, a.head_dim, kQ) ||
+      !make_head_map(&mk, a.k, a.dtype, rows, width, a.ldq, a.head_dim, kKV) ||
+      !make_head_map(&mv, a.v, a.dtype, rows, width, a.ldq, a.head_dim, kKV))
     return kErrTma;
   AttnParams prm;
   prm.o = static_cast<uint16_t*>(a.o);
@@ -989,7 +1043,7 @@ int launch_attention_tc_ex(const AttnArgs& a, cudaStream_t st) {
     const char* e = getenv("S3CU_ATTN_PERSIST");
     return e ? atoi(e) : -1;
   }();
-  const int n_kv = ((prm.pack > 1 ? prm.pack * a.seq : a.seq) + kKV - 1) / kKV;
+  const int n_kv = ((prm.pack > 1 ? prm.pack * a.seq : a.seq) + 127) / 128;  // in 128-key units
   // (Not with a bias: the biased variant spills in the persistent form and
   // measured slower on TinyViT.)
   const bool persist = force >= 0 ? force != 0 : (n_kv <= 8 && !a.bias);

@@ -79,7 +79,7 @@ struct impl {
 	int              nflags;
 };
 
-enum { F_SKIP = 1, F_LAZY_T = 2, F_BIAS_FUSED = 4, F_GELU_FUSED = 8 };
+enum { F_SKIP = 1, F_LAZY_T = 2, F_BIAS_FUSED = 4, F_GELU_FUSED = 8, F_RES_FUSED = 16 };
 
 static size_t dsize(enum sam3_dtype d)
 {
@@ -455,6 +455,7 @@ static int is_contig(const struct sam3_tensor *t, const int64_t *str)
 }
 
 static int uses_of(struct sam3_graph *g, const struct sam3_tensor *t);
+static int res_partner(struct sam3_graph *g, int i, int j);
 
 /* device pointer (and element strides) of a tensor produced in this graph
  * or a graph input; a view is returned as such */
@@ -714,13 +715,21 @@ static enum sam3_error op_matmul(struct impl *m, struct sam3_graph *g, int ni)
 		return SAM3_EINVAL;
 	/* epilogue fusion target: the ADD / GELU output if fused */
 	struct sam3_tensor *dst = out;
-	const struct sam3_tensor *bias = NULL;
+	const struct sam3_tensor *bias = NULL, *resid = NULL;
 	int act = 0;
 	if (m->flags[ni] & F_BIAS_FUSED) {
 		for (int j = ni + 1; j < g->n_nodes; j++)
 			if (g->nodes[j].op == SAM3_OP_ADD && g->nodes[j].inputs[0] == out) {
 				bias = g->nodes[j].inputs[1];
 				dst = g->nodes[j].output;
+				if (m->flags[j] & F_RES_FUSED) {
+					int r = res_partner(g, ni, j);
+					if (r <= 0)
+						return SAM3_EINVAL;
+					struct sam3_node *rn = &g->nodes[r];
+					resid = rn->inputs[0] == dst ? rn->inputs[1] : rn->inputs[0];
+					dst = rn->output;
+				}
 				if (m->flags[j] & F_GELU_FUSED) {
 					for (int k = j + 1; k < g->n_nodes; k++)
 						if (g->nodes[k].op == SAM3_OP_GELU &&
@@ -793,6 +802,16 @@ static enum sam3_error op_matmul(struct impl *m, struct sam3_graph *g, int ni)
 			int dims[2] = {K, N}, perm[2] = {1, 0};
 			TRY(sam3cu_permute(pbk, pw, (int)dsize(b->dtype), 2, dims, perm, m->stream));
 		}
+	}
+	if (resid) {  /* dst = resid + linear: a copy of resid, then the in-place reduce-add */
+		void *pr;
+		if (dst->dtype != SAM3_DTYPE_F32 || act)
+			return SAM3_EINVAL;
+		TRY(dev_of(m, resid, produced_in(g, ni, resid), &pr));
+		TRY(sam3cu_memcpy_d2d(py, pr, tbytes(dst), m->stream));
+		TRY(sam3cu_linear(pa, a->dtype, pw, pb, py, py, SAM3_DTYPE_F32, (int)M, K, N, 0,
+				  m->stream));
+		return SAM3_OK;
 	}
 	TRY(sam3cu_linear(pa, a->dtype, pw, pb, NULL, py, dst->dtype, (int)M, K, N, act,
 			  m->stream));
@@ -1186,6 +1205,37 @@ static int uses_of(struct sam3_graph *g, const struct sam3_tensor *t)
 	return count_uses(g, 0, t);
 }
 
+static int producer_of(struct sam3_graph *g, const struct sam3_tensor *t)
+{
+	for (int i = 0; i < g->n_nodes; i++)
+		if (g->nodes[i].output == t)
+			return i;
+	return -1;
+}
+
+/* The ADD node r that is the only consumer of bias-ADD j's output and adds
+ * an F32 tensor of the same shape that exists before MATMUL i runs; 0 if
+ * there is none. */
+static int res_partner(struct sam3_graph *g, int i, int j)
+{
+	const struct sam3_tensor *y = g->nodes[j].output;
+	if (y->dtype != SAM3_DTYPE_F32 || count_uses(g, j + 1, y) != 1)
+		return 0;
+	for (int r = j + 1; r < g->n_nodes; r++) {
+		struct sam3_node *nd = &g->nodes[r];
+		if (nd->op != SAM3_OP_ADD || nd->n_inputs < 2)
+			continue;
+		if (nd->inputs[0] != y && nd->inputs[1] != y)
+			continue;
+		const struct sam3_tensor *x = nd->inputs[0] == y ? nd->inputs[1] : nd->inputs[0];
+		if (!x || x == y || x->dtype != SAM3_DTYPE_F32 || nelems(x) != nelems(y) ||
+		    nd->output->dtype != SAM3_DTYPE_F32)
+			return 0;
+		return producer_of(g, x) < i ? r : 0;
+	}
+	return 0;
+}
+
 /* mark the peepholes: lazy W transposes, bias / GELU fusion into MATMUL */
 static void plan(struct impl *m, struct sam3_graph *g)
 {
@@ -1227,6 +1277,14 @@ static void plan(struct impl *m, struct sam3_graph *g)
 								m->flags[k] |= F_SKIP;
 								break;
 							}
+					}
+					/* F32 x + linear(...) (the residual ADDs after proj
+					 * and fc2, image_encoder.c:793-900): the GEMM adds
+					 * into a copy of x in place (reduce-add epilogue) */
+					int r = res_partner(g, i, j);
+					if (!(m->flags[j] & F_GELU_FUSED) && r > 0) {
+						m->flags[j] |= F_RES_FUSED;
+						m->flags[r] |= F_SKIP;
 					}
 				}
 				break;

@@ -10,8 +10,9 @@
  * pool of host threads, and the DMA of one chunk overlaps the host copy of
  * the next.  Small copies (< 1 MiB) take the plain path.
  *
- * SAM3CU_XFER_THREADS sets the pool size (default: online CPUs, at most 8;
- * 1 = no pool, plain cudaMemcpyAsync for every size).
+ * SAM3CU_XFER_THREADS sets the pool size (default: the online CPUs, at most
+ * 8; the variable allows up to 16; 1 = no pool, plain cudaMemcpyAsync for
+ * every size).
  */
 #include "host_xfer.h"
 
@@ -25,7 +26,7 @@
 #define HX_CHUNK   ((size_t)4 << 20)
 #define HX_SMALL   ((size_t)1 << 20)
 #define HX_MAXEV   64
-#define HX_MAXT    8
+#define HX_MAXT    16
 
 struct hxjob {
 	char       *dst;
@@ -126,7 +127,7 @@ struct hxfer *hxfer_create(void)
 	if (!x)
 		return NULL;
 	long ncpu = sysconf(_SC_NPROCESSORS_ONLN);
-	int nt = ncpu > 0 ? (int)(ncpu < HX_MAXT ? ncpu : HX_MAXT) : 1;
+	int nt = ncpu > 0 ? (int)(ncpu < 8 ? ncpu : 8) : 1;
 	const char *e = getenv("SAM3CU_XFER_THREADS");
 	if (e && atoi(e) > 0)
 		nt = atoi(e) < HX_MAXT ? atoi(e) : HX_MAXT;
