@@ -97,6 +97,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   cluster_sync();  // both CTAs' barriers and TMEM exist before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // set-up done; from here on the inputs of the previous kernel are read
 
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs): own A rows, own W half; the
@@ -310,7 +311,8 @@ int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, Ge
   }
   ConvGeom off;
   memset(&off, 0, sizeof(off));
-  gemm2_kernel<<<2 * pairs, kPThreads, kPSmem, stream>>>(ta, tb, to, shp, ep, idesc, mode, splits, off);
+  return launch_pdl(gemm2_kernel, 2 * pairs, kPThreads, kPSmem, stream, ta, tb, to, shp, ep, idesc, mode, splits,
+                    off);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
@@ -356,7 +358,8 @@ int launch_conv3x3_implicit(const void* x, const void* w, int ab_dtype, int n, i
     attr = true;
   }
   count_launches(1);
-  gemm2_kernel<<<2 * pairs, kPThreads, kPSmem, stream>>>(ta, tb, to, shp, ep, idesc, kEpiTmaStore, 1, cg);
+  return launch_pdl(gemm2_kernel, 2 * pairs, kPThreads, kPSmem, stream, ta, tb, to, shp, ep, idesc, kEpiTmaStore,
+                    1, cg);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 

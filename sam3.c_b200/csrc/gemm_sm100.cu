@@ -204,6 +204,7 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // set-up done; from here on the inputs of the previous kernel are read
 
   auto stage_a = [&](int s) { return smem + s * Cfg::kStageBytes; };
   // W operand of k-iteration `it`: in the stage, or (Q8) in ring slot it & 1
@@ -406,6 +407,9 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
 
 int g_num_sms = 0;
 
+
+
+
 // 2-SM pair tiles (gemm2_sm100.cu) for the 16-bit path unless SAM3CU_GEMM=1sm
 // or the problem is too small to keep the SMs busy with 256x256 tiles.
 bool use_pair_gemm(const GemmShape& shp, bool additive) {
@@ -421,6 +425,14 @@ bool use_pair_gemm(const GemmShape& shp, bool additive) {
 std::atomic<uint64_t> g_launches{0};
 
 }  // namespace
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("S3CU_PDL");
+    return !(e && atoi(e) == 0);
+  }();
+  return on;
+}
 
 uint64_t count_launches(int64_t delta) {
   return g_launches.fetch_add(static_cast<uint64_t>(delta)) + static_cast<uint64_t>(delta);
@@ -530,8 +542,8 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       cudaFuncSetAttribute(gemm_kernel<kBQ8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       attr = true;
     }
-    gemm_kernel<kBQ8><<<grid, GemmCfg<kBQ8>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep, idesc,
-                                                                         bf ? 1 : 0, mode, streamk);
+    return launch_pdl(gemm_kernel<kBQ8>, grid, GemmCfg<kBQ8>::kThreads, smem, stream, ta, tb, ts, to, shp, ep, idesc,
+                      bf ? 1 : 0, mode, streamk);
   } else if (f32in) {
     if (ldw % 4 != 0) return kErrShape;
     if (!make_tmap_2d(&tb, W, dt, 4, shp.N, shp.K, ldw, kBN, bke, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -542,8 +554,8 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       cudaFuncSetAttribute(gemm_kernel<kBF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       attr = true;
     }
-    gemm_kernel<kBF32><<<grid, GemmCfg<kBF32>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep, idesc, 0,
-                                                                           mode, streamk);
+    return launch_pdl(gemm_kernel<kBF32>, grid, GemmCfg<kBF32>::kThreads, smem, stream, ta, tb, ts, to, shp, ep,
+                      idesc, 0, mode, streamk);
   } else {
     if (ldw % 8 != 0) return kErrShape;
     if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, kBN, kBK, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -554,8 +566,8 @@ int launch_gemm(const void* A, int lda, const void* W, int ldw, const int8_t* q8
       cudaFuncSetAttribute(gemm_kernel<kBTma16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       attr = true;
     }
-    gemm_kernel<kBTma16><<<grid, GemmCfg<kBTma16>::kThreads, smem, stream>>>(ta, tb, ts, to, shp, ep,
-                                                                              idesc, bf ? 1 : 0, mode, streamk);
+    return launch_pdl(gemm_kernel<kBTma16>, grid, GemmCfg<kBTma16>::kThreads, smem, stream, ta, tb, ts, to, shp,
+                      ep, idesc, bf ? 1 : 0, mode, streamk);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : kErrLaunch;
 }

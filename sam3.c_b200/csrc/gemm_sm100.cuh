@@ -36,6 +36,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 
 #include "sm100_ptx.cuh"
 
@@ -126,6 +127,26 @@ struct GemmCfg {
   static constexpr int kSmemBytes = kStages * kStageBytes + kBRing * kBTileBytes + kEpiWarps * kStageOutBytes +
                                     1024 /*align*/ + 256 /*barriers*/;
 };
+
+// Launch with programmatic stream serialisation (the kernel's set-up may
+// overlap the end of the previous kernel in the stream; the kernel calls
+// griddep_wait() before it reads anything that kernel wrote).
+// S3CU_PDL=0 launches normally.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, int threads, int smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) == cudaSuccess ? 0 : -103;  // kErrLaunch
+}
 
 // K slices per output tile the pair kernel uses (1 unless `additive`: an
 // in-place F32 reduce-add epilogue without activation or RoPE).

@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(256) layernorm_rows(const void* __restrict__ x
                                                       const float* __restrict__ b, int rows, int cols,
                                                       const int* __restrict__ out_row_map,
                                                       int out_row_period) {
+  griddep_launch();  // the GEMM that follows may start its set-up
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -549,6 +550,7 @@ namespace {
 __global__ void q8_prep_kernel(const float4* __restrict__ x, uint4* __restrict__ xb, int64_t n8, int nblk_x,
                                const uint4* __restrict__ q, const float* __restrict__ sc, uint4* __restrict__ w,
                                int N, int K16, int64_t total_w) {
+  griddep_launch();  // the GEMM that follows may start its set-up
   if (static_cast<int>(blockIdx.x) < nblk_x) {
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
          i += static_cast<int64_t>(nblk_x) * blockDim.x) {

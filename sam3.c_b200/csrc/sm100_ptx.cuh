@@ -52,6 +52,14 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic
+// stream serialisation may start its set-up while the kernel before it in the
+// stream is finishing; griddep_wait() blocks until that kernel has completed
+// and its memory is visible (a no-op for a normal launch).  griddep_launch()
+// lets the next kernel start early (the preceding kernel calls it).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
