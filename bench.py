@@ -390,6 +390,12 @@ def q8_legs(args, dev, sam3cu):
             g_()
     ms_bf = _event_ms(fb, 20)
     ms_gemm = _event_ms(fg, 20)
+    lin = {"tflops": 2 * M * K * N / ms_lin / 1e9, "ms": ms_lin,
+           "dtype": "q8_0w x f32a (bf16 on chip), f32 out",
+           "note": "F32 activations cast inside the call + dequantise-once path (M >= 2048) of sam3cu_linear_q8",
+           "breakdown_ms": {"f32_x_call": ms_lin, "bf16_x_call": ms_bf, "bf16_gemm_only_f32_out": ms_gemm}}
+    if args.leg == "q8lin":  # config 0 alone (the ncu capture of its kernels)
+        return {"q8_linear_config0": lin}
     enc = sam3cu.VitEncoder(CFG, synth.vit_weights(CFG, seed=0), sam3cu.Q8_0, max_batch=1)
     img = torch.from_numpy(synth.images(CFG, 1, seed=100)).to(dev)
     out = torch.empty((1, enc.np, CFG["embed_dim"]), dtype=torch.float32, device=dev)
@@ -415,12 +421,7 @@ def q8_legs(args, dev, sam3cu):
         "q8_encode_64img": {"value": 64 * 1000.0 / ms64, "unit": "images/s", "ms_per_64": ms64,
                             "gemm_tflops": gemm_gflop_per_image() * 8 / prof8["gemm"][0],
                             "dtype": "q8_0w+f16a", "images_per_call": 8},
-        "q8_linear_config0": {"tflops": 2 * M * K * N / ms_lin / 1e9, "ms": ms_lin,
-                              "dtype": "q8_0w x f32a (bf16 on chip), f32 out",
-                              "note": "F32 activations cast inside the call + dequantise-once path "
-                                      "(M >= 2048) of sam3cu_linear_q8",
-                              "breakdown_ms": {"f32_x_call": ms_lin, "bf16_x_call": ms_bf,
-                                               "bf16_gemm_only_f32_out": ms_gemm}},
+        "q8_linear_config0": lin,
         "q8_encode_config2": {"value": 1000.0 / ms_enc, "unit": "images/s", "ms_per_image": ms_enc,
                               "gemm_tflops": gemm_gflop_per_image() / prof["gemm"][0],
                               "dtype": "q8_0w+f16a", "batch": 1},
@@ -670,7 +671,7 @@ def run_leg(args):
     torch.cuda.set_device(0)
     sam3cu.init(0)
     dev = torch.device("cuda", 0)
-    fn = {"dropin": dropin_leg, "sweep": gemm_sweep_leg, "q8": q8_legs, "neck": neck_leg,
+    fn = {"dropin": dropin_leg, "sweep": gemm_sweep_leg, "q8": q8_legs, "q8lin": q8_legs, "neck": neck_leg,
           "tinyvit": tinyvit_leg, "attn": attention_leg, "sdpa_f32": sdpa_f32_leg}[args.leg]
     print(json.dumps({"leg": args.leg, "result": fn(args, dev, sam3cu)}))
     return 0
@@ -695,7 +696,7 @@ def main():
     ap.add_argument("--sdpa-groups", type=int, default=1, help="sdpa_f32 leg: groups (images or windows)")
     ap.add_argument("--tinyvit-batch", type=int, default=32, help="tinyvit leg: images per call")
     ap.add_argument("--leg", default=None,
-                    choices=["dropin", "sweep", "q8", "neck", "tinyvit", "attn", "sdpa_f32"],
+                    choices=["dropin", "sweep", "q8", "q8lin", "neck", "tinyvit", "attn", "sdpa_f32"],
                     help="run one side leg alone on GPU 0 and print its result")
     args = ap.parse_args()
     if args.leg:

@@ -544,26 +544,28 @@ __global__ void q8_dequant_w16_multi_kernel(Q8DequantJobs jobs, int f16) {
 }  // namespace
 
 namespace {
-// F32 activations -> bf16 (blocks [0, nblk_x), grid-stride, 8 per thread)
-// and a Q8_0 weight -> bf16 (the remaining blocks, 16 values per thread) in
-// one launch: the two inputs of an F32 x Q8_0 linear.
-__global__ void q8_prep_kernel(const float4* __restrict__ x, uint4* __restrict__ xb, int64_t n8, int nblk_x,
+// F32 activations -> bf16 (8 per thread) and a Q8_0 weight -> bf16 (16
+// values per thread) in one launch: the two inputs of an F32 x Q8_0 linear.
+__global__ void q8_prep_kernel(const float4* __restrict__ x, uint4* __restrict__ xb, int64_t n8,
                                const uint4* __restrict__ q, const float* __restrict__ sc, uint4* __restrict__ w,
                                int N, int K16, int64_t total_w) {
   griddep_launch();  // the GEMM that follows may start its set-up
-  if (static_cast<int>(blockIdx.x) < nblk_x) {
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
-         i += static_cast<int64_t>(nblk_x) * blockDim.x) {
-      const float4 a = __ldg(x + 2 * i), b = __ldg(x + 2 * i + 1);
-      __nv_bfloat162 h0 = __floats2bfloat162_rn(a.x, a.y), h1 = __floats2bfloat162_rn(a.z, a.w);
-      __nv_bfloat162 h2 = __floats2bfloat162_rn(b.x, b.y), h3 = __floats2bfloat162_rn(b.z, b.w);
-      xb[i] = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
-                         *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
-    }
-    return;
+  // thread i: activation group i (8 values) and weight group i (16 values),
+  // both in flight at once; no grid cap, one pass
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+  const bool has_x = i < n8;
+  if (has_x) {
+    a = __ldg(x + 2 * i);
+    b = __ldg(x + 2 * i + 1);
   }
-  const int64_t i = static_cast<int64_t>(blockIdx.x - nblk_x) * blockDim.x + threadIdx.x;
   if (i < total_w) q8_dequant_w16_one(q, sc, w, N, K16, i, 0);
+  if (has_x) {
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(a.x, a.y), h1 = __floats2bfloat162_rn(a.z, a.w);
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(b.x, b.y), h3 = __floats2bfloat162_rn(b.z, b.w);
+    xb[i] = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                       *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+  }
 }
 }  // namespace
 
@@ -574,12 +576,12 @@ int launch_q8_prep(const float* x, void* xb, int64_t nx, const int8_t* q, const 
         reinterpret_cast<uintptr_t>(w)) & 15))
     return kErrShape;
   const int64_t total_w = static_cast<int64_t>(N) * (K / 16);
-  const int nblk_x = grid_for(nx / 8, 256);
-  const int64_t nblk = nblk_x + (total_w + 255) / 256;
+  const int64_t items = nx / 8 > total_w ? nx / 8 : total_w;
+  const int64_t nblk = (items + 255) / 256;
   if (nblk >= (1LL << 31)) return kErrShape;
   count_launches(1);
   q8_prep_kernel<<<static_cast<unsigned>(nblk), 256, 0, st>>>(
-      static_cast<const float4*>(static_cast<const void*>(x)), static_cast<uint4*>(xb), nx / 8, nblk_x,
+      static_cast<const float4*>(static_cast<const void*>(x)), static_cast<uint4*>(xb), nx / 8,
       reinterpret_cast<const uint4*>(q), sc, static_cast<uint4*>(w), N, K / 16, total_w);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
