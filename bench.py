@@ -302,7 +302,7 @@ def run_ours(args):
             "metric": "images_per_sec_1008px_hiera_l", "value": value, "unit": "images/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": {"bf16": "bf16", "f16": "f16", "q8": "q8_0w+f16"}[args.dtype],
+            "dtype": {"bf16": "bf16", "f16": "f16", "q8": "q8_0w+bf16"}[args.dtype],
             "data": "synthetic (seeded images and random-init weights of the Hiera-L ViT)",
             "config": {"workload": "config4_batched_encode_64x1008px_hiera_l",
                        "global_batch": n_total, "images_per_encode_call": B, "seq_len": 5184,
@@ -420,11 +420,11 @@ def q8_legs(args, dev, sam3cu):
     return {
         "q8_encode_64img": {"value": 64 * 1000.0 / ms64, "unit": "images/s", "ms_per_64": ms64,
                             "gemm_tflops": gemm_gflop_per_image() * 8 / prof8["gemm"][0],
-                            "dtype": "q8_0w+f16a", "images_per_call": 8},
+                            "dtype": "q8_0w+bf16a", "images_per_call": 8},
         "q8_linear_config0": lin,
         "q8_encode_config2": {"value": 1000.0 / ms_enc, "unit": "images/s", "ms_per_image": ms_enc,
                               "gemm_tflops": gemm_gflop_per_image() / prof["gemm"][0],
-                              "dtype": "q8_0w+f16a", "batch": 1},
+                              "dtype": "q8_0w+bf16a", "batch": 1},
     }
 
 

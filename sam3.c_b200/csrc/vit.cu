@@ -205,7 +205,7 @@ int upload_w16(DevBuf& d, const WSrc& s, int N, int K, int ldk, int dt, cudaStre
   return ck(cudaStreamSynchronize(st));  // tmp / pad are freed on return
 }
 
-int upload_linear(Linear& L, const WSrc& w, const WSrc& b, int N, int K, int wdtype, cudaStream_t st) {
+int upload_linear(Linear& L, const WSrc& w, const WSrc& b, int N, int K, int wdtype, int act, cudaStream_t st) {
   L.N = N;
   L.K = K;
   int rc = upload_f32(L.bias, b, st);
@@ -233,9 +233,12 @@ int upload_linear(Linear& L, const WSrc& w, const WSrc& b, int N, int K, int wdt
     if (!L.q.alloc(n) || !L.sc.alloc((n / 32) * 4)) return kErrNoMem;
     if ((rc = launch_q8_repack(blocks.p, L.q.as<int8_t>(), L.sc.as<float>(), N, K, st))) return rc;
     // f16 activations: scales shifted per row into f16's normal range for the
-    // half2 dequantiser, the shift undone in the GEMM epilogue
-    if (!L.cs.alloc(static_cast<size_t>(N) * 4)) return kErrNoMem;
-    if ((rc = launch_q8_row_shift(L.sc.as<float>(), L.cs.as<float>(), N, K, st))) return rc;
+    // half2 dequantiser, the shift undone in the GEMM epilogue (bf16
+    // activations dequantise in f32 arithmetic and need no shift)
+    if (act == kF16) {
+      if (!L.cs.alloc(static_cast<size_t>(N) * 4)) return kErrNoMem;
+      if ((rc = launch_q8_row_shift(L.sc.as<float>(), L.cs.as<float>(), N, K, st))) return rc;
+    }
     return ck(cudaStreamSynchronize(st));
   }
   return upload_w16(L.w, w, N, K, K, wdtype == SAM3CU_F16 ? kF16 : kBF16, st);
@@ -258,7 +261,7 @@ int run_linear(sam3cu_vit* v, const Linear& L, const void* a, int lda, int M, co
   if (L.q.p) {
     if (!w16) return kErrShape;
     EpiParams ep = ep_in;
-    ep.col_scale = L.cs.as<float>();  // undoes the per-row scale shift
+    ep.col_scale = L.cs.p ? L.cs.as<float>() : nullptr;  // undoes the per-row scale shift (f16)
     return launch_gemm(a, lda, w16, L.K, nullptr, nullptr, v->act, shp, ep, v->stream, 0);
   }
   const EpiParams& ep = ep_in;
@@ -575,10 +578,10 @@ int vit_setup(sam3cu_vit* v, const VitSrc& w) {
     if ((rc = upload_f32(B.ln1_w, bw.ln1_w, st)) || (rc = upload_f32(B.ln1_b, bw.ln1_b, st)) ||
         (rc = upload_f32(B.ln2_w, bw.ln2_w, st)) || (rc = upload_f32(B.ln2_b, bw.ln2_b, st)))
       return rc;
-    if ((rc = upload_linear(B.qkv, bw.qkv_w, bw.qkv_b, 3 * e, e, v->wdtype, st))) return rc;
-    if ((rc = upload_linear(B.proj, bw.proj_w, bw.proj_b, e, e, v->wdtype, st))) return rc;
-    if ((rc = upload_linear(B.fc1, bw.fc1_w, bw.fc1_b, c.mlp_dim, e, v->wdtype, st))) return rc;
-    if ((rc = upload_linear(B.fc2, bw.fc2_w, bw.fc2_b, e, c.mlp_dim, v->wdtype, st))) return rc;
+    if ((rc = upload_linear(B.qkv, bw.qkv_w, bw.qkv_b, 3 * e, e, v->wdtype, v->act, st))) return rc;
+    if ((rc = upload_linear(B.proj, bw.proj_w, bw.proj_b, e, e, v->wdtype, v->act, st))) return rc;
+    if ((rc = upload_linear(B.fc1, bw.fc1_w, bw.fc1_b, c.mlp_dim, e, v->wdtype, v->act, st))) return rc;
+    if ((rc = upload_linear(B.fc2, bw.fc2_w, bw.fc2_b, e, c.mlp_dim, v->wdtype, v->act, st))) return rc;
   }
   // activations for max_batch images
   const size_t M = static_cast<size_t>(v->max_batch) * np;
@@ -619,9 +622,16 @@ sam3cu_vit* vit_create(const sam3cu_vit_config* cfg, const VitSrc& w, int weight
   std::unique_ptr<sam3cu_vit> v(new sam3cu_vit());
   v->c = *cfg;
   v->wdtype = weight_dtype;
-  // Q8_0 weights pair with f16 activations: the int8 tiles are dequantised in
-  // half2 arithmetic (gemm_sm100.cu), and f16 keeps 3 more mantissa bits
-  v->act = (weight_dtype == SAM3CU_F16 || weight_dtype == SAM3CU_Q8_0) ? kF16 : kBF16;
+  // Q8_0 weights pair with bf16 activations: the weights are dequantised
+  // (f32 arithmetic, one rounding) on a side stream and the GEMMs then run
+  // exactly as the BF16 encoder's.  SAM3CU_Q8_ACT=f16 selects f16
+  // activations instead (half2 dequantisation with per-row scale shifts,
+  // undone in the GEMM epilogue), which measured slower at one image.
+  static const bool q8_f16 = [] {
+    const char* e = getenv("SAM3CU_Q8_ACT");
+    return e && strcmp(e, "f16") == 0;
+  }();
+  v->act = (weight_dtype == SAM3CU_F16 || (weight_dtype == SAM3CU_Q8_0 && q8_f16)) ? kF16 : kBF16;
   v->max_batch = max_batch;
   if (cudaStreamCreateWithFlags(&v->stream, cudaStreamNonBlocking) != cudaSuccess) {
     *status_p = kErrCuda;
