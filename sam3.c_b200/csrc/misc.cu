@@ -8,6 +8,7 @@
 #include "misc.cuh"
 #include "sam3cu_internal.h"
 #include "sm100_ptx.cuh"
+#include "gemm_sm100.cuh"
 
 namespace s3 {
 
@@ -32,6 +33,7 @@ __global__ void __launch_bounds__(256) layernorm_rows(const void* __restrict__ x
                                                       const int* __restrict__ out_row_map,
                                                       int out_row_period) {
   griddep_launch();  // the GEMM that follows may start its set-up
+  griddep_wait();    // launched early behind a GEMM: its output is read below
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -113,15 +115,15 @@ int ln_dispatch(const void* x, void* y, const float* g, const float* b, int rows
   const int blocks = (rows + 7) / 8;
   const bool al = (cols % 128 == 0);
   if (al && cols == 1024)
-    layernorm_rows<TI, TO, 8><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+    return launch_pdl(layernorm_rows<TI, TO, 8>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
   else if (al && cols == 512)
-    layernorm_rows<TI, TO, 4><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+    return launch_pdl(layernorm_rows<TI, TO, 4>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
   else if (al && cols == 256)
-    layernorm_rows<TI, TO, 2><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+    return launch_pdl(layernorm_rows<TI, TO, 2>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
   else if (al && cols == 128)
-    layernorm_rows<TI, TO, 1><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+    return launch_pdl(layernorm_rows<TI, TO, 1>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
   else if (al && cols == 2048)
-    layernorm_rows<TI, TO, 16><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period);
+    return launch_pdl(layernorm_rows<TI, TO, 16>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
   else if (!map)
     layernorm_rows_generic<TI, TO><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols);
   else
