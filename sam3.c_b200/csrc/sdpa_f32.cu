@@ -15,8 +15,8 @@
 //     broadcast), row max / sum across the 8 lanes of a query by shuffles,
 //     P written to shared memory, then O (4 queries x 8 of the head dims)
 //     += P.V with V rows read as float4;
-//   * the next K / V tile is fetched with cp.async into the second buffer
-//     while the current one is used.
+//   * the next K / V tile is fetched with cp.async once every thread is done
+//     with the current one; three CTAs per SM hide the fetch.
 // Tensors are addressed through (batch, head, row) strides, so the
 // reference's [B,S,H,hd] -> permute(0,2,1,3) copies before and after SDPA
 // (graph_helpers.c:840-880) become strides: the vtable hands this kernel
@@ -37,6 +37,14 @@ constexpr int kBr = 64;      // queries per CTA
 constexpr int kBc = 64;      // keys per tile
 constexpr int kPitch = 68;   // shared row pitch (floats) of Q, K and P
 constexpr int kThreads = 128;
+#ifndef S3_SDPA_NBUF
+#define S3_SDPA_NBUF 1
+#endif
+// K/V buffers: 2 = the next tile is fetched (cp.async) while the current one
+// is used, 2 CTAs per SM; 1 = fetched after it, 3 CTAs per SM, the other
+// CTAs covering the fetch.  Measured (global / window TFLOP/s): 2 -> 35.0 /
+// 33.3, 1 -> 39.2 / 37.5.
+constexpr int kNBuf = S3_SDPA_NBUF;
 
 struct SdpaArgs {
   const float* q;
@@ -74,14 +82,14 @@ __device__ __forceinline__ void load_tile(float* sm, int pitch, const float* bas
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads) sdpa_f32_tiled(SdpaArgs a) {
+__global__ void __launch_bounds__(kThreads, kNBuf == 1 ? 3 : 2) sdpa_f32_tiled(SdpaArgs a) {
   constexpr int kDPer = HD / 8;  // head dims per thread in the P.V product
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
   float* Qs = sm;                              // [64][68]
   float* Ks = Qs + kBr * kPitch;               // 2 x [64][68]
-  float* Vs = Ks + 2 * kBc * kPitch;           // 2 x [64][HD]
-  float* Ps = Vs + 2 * kBc * HD;               // [64][68]
+  float* Vs = Ks + kNBuf * kBc * kPitch;       // kNBuf x [64][HD]
+  float* Ps = Vs + kNBuf * kBc * HD;           // [64][68]
 
   const int tid = threadIdx.x;
   const int qg = tid >> 3, kg = tid & 7;
@@ -108,10 +116,10 @@ __global__ void __launch_bounds__(kThreads) sdpa_f32_tiled(SdpaArgs a) {
 
   const int ntiles = (a.sk + kBc - 1) / kBc;
   for (int t = 0; t < ntiles; ++t) {
-    const int buf = t & 1;
+    const int buf = kNBuf == 2 ? (t & 1) : 0;
     cp_async_wait_all();
     __syncthreads();  // tile t visible; every thread is done with tile t-1
-    if (t + 1 < ntiles) {
+    if (kNBuf == 2 && t + 1 < ntiles) {
       load_tile<HD>(Ks + (buf ^ 1) * kBc * kPitch, kPitch, kbase, a.ks, (t + 1) * kBc, a.sk);
       load_tile<HD>(Vs + (buf ^ 1) * kBc * HD, HD, vbase, a.vs, (t + 1) * kBc, a.sk);
     }
@@ -209,6 +217,12 @@ __global__ void __launch_bounds__(kThreads) sdpa_f32_tiled(SdpaArgs a) {
         }
       }
     }
+    if (kNBuf == 1 && t + 1 < ntiles) {  // one buffer: refill it once every thread is done with it
+      __syncthreads();
+      load_tile<HD>(Ks, kPitch, kbase, a.ks, (t + 1) * kBc, a.sk);
+      load_tile<HD>(Vs, HD, vbase, a.vs, (t + 1) * kBc, a.sk);
+      cp_async_commit();
+    }
   }
   cp_async_wait_all();
 
@@ -233,7 +247,7 @@ __global__ void __launch_bounds__(kThreads) sdpa_f32_tiled(SdpaArgs a) {
 
 template <int HD>
 constexpr int smem_bytes() {
-  return static_cast<int>(sizeof(float)) * (kBr * kPitch + 2 * kBc * kPitch + 2 * kBc * HD + kBr * kPitch);
+  return static_cast<int>(sizeof(float)) * (kBr * kPitch + kNBuf * kBc * kPitch + kNBuf * kBc * HD + kBr * kPitch);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -274,10 +288,12 @@ int sam3cu_sdpa_f32_strided(const float* q, const int64_t* q_strides, const floa
   if (hd == 64) {
     constexpr int sb = smem_bytes<64>();
     cudaFuncSetAttribute(sdpa_f32_tiled<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, sb);
+    cudaFuncSetAttribute(sdpa_f32_tiled<64>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     sdpa_f32_tiled<64><<<grid, kThreads, sb, st>>>(a);
   } else {
     constexpr int sb = smem_bytes<32>();
     cudaFuncSetAttribute(sdpa_f32_tiled<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sb);
+    cudaFuncSetAttribute(sdpa_f32_tiled<32>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     sdpa_f32_tiled<32><<<grid, kThreads, sb, st>>>(a);
   }
   return cudaGetLastError() == cudaSuccess ? SAM3CU_OK : SAM3CU_ELAUNCH;
