@@ -30,24 +30,32 @@ S3_DEV_ERROR_ACCESSOR(dev_error_gemm2)
 namespace {
 
 constexpr int kPM = 128;                 // rows per CTA (256 per pair)
-constexpr int kPN = 256;                 // output columns per tile
+constexpr int kPN = 256;                 // output columns per tile (the 128-column variant: kN)
 constexpr int kPK = 64;
 constexpr int kPStages = 6;
-constexpr int kPTile = kPM * kPK * 2;    // 16 KiB: A tile or W half-tile
-constexpr int kPStage = 2 * kPTile;
+constexpr int kPTile = kPM * kPK * 2;    // 16 KiB: A tile (or W half-tile of a 256-column tile)
 constexpr int kPEpiWarps = 8;
 constexpr int kPThreads = 64 + kPEpiWarps * 32;
 constexpr int kPOut = 32 * 32 * 4;
-constexpr int kPSmem = kPStages * kPStage + kPEpiWarps * kPOut + 1024 + 256;
-constexpr int kPTmemCols = 2 * kPN;
+// Per tile width kN (256, or 128 for shapes whose 256-column tiles fill the
+// last wave of CTA pairs poorly): W half-tile bytes, stage bytes, smem, TMEM.
+template <int kN>
+struct PairCfg {
+  static constexpr int kWTile = (kN / 2) * kPK * 2;
+  static constexpr int kStage = kPTile + kWTile;
+  static constexpr int kSmem = kPStages * kStage + kPEpiWarps * kPOut + 1024 + 256;
+  static constexpr int kTmemCols = 2 * kN;
+};
 
+template <int kN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  const __grid_constant__ CUtensorMap tmap_o, GemmShape shp, EpiParams ep, uint32_t idesc,
                  int epi_mode, int splits, ConvGeom cg) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stage_out = smem + kPStages * kPStage;
+  using PC = PairCfg<kN>;
+  uint8_t* stage_out = smem + kPStages * PC::kStage;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(stage_out + kPEpiWarps * kPOut);
   uint64_t* empty_bar = full_bar + kPStages;
   uint64_t* accf_bar = empty_bar + kPStages;  // [2]
@@ -60,7 +68,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   // conv: one M tile = two 128-pixel blocks (this CTA's = 2 * tile + rank)
   const int m_tiles = cg.on ? (cg.n_img * cg.n_by * cg.n_bx + 1) / 2 : (shp.M + 2 * kPM - 1) / (2 * kPM);
-  const int n_tiles = (shp.N + kPN - 1) / kPN;
+  const int n_tiles = (shp.N + kN - 1) / kN;
   // conv block b -> (image, first output row, first column, flat output row)
   auto conv_block = [&](int b, int& img, int& y0, int& x0) {
     const int bx = b % cg.n_bx, t = b / cg.n_bx;
@@ -74,8 +82,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   const int k_iters = (shp.K + kPK - 1) / kPK;
   auto k_begin = [&](int tile) { return (tile % splits) * k_iters / splits; };
   auto k_end = [&](int tile) { return (tile % splits + 1) * k_iters / splits; };
-  auto stage_a = [&](int s) { return smem + s * kPStage; };
-  auto stage_b = [&](int s) { return smem + s * kPStage + kPTile; };
+  auto stage_a = [&](int s) { return smem + s * PC::kStage; };
+  auto stage_b = [&](int s) { return smem + s * PC::kStage + kPTile; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPStages; ++s) {
@@ -90,7 +98,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, kPTmemCols);
+    tmem_alloc_pair(tmem_slot, PC::kTmemCols);
     tmem_relinquish_pair();
   }
   tc_fence_before();
@@ -114,7 +122,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         const int mn = tile / splits;
         const int m0 = (mn / n_tiles) * 2 * kPM + rank * kPM;
-        const int n0 = (mn % n_tiles) * kPN + rank * (kPN / 2);
+        const int n0 = (mn % n_tiles) * kN + rank * (kN / 2);
         int cimg = 0, cy0 = 0, cx0 = 0;
         if (cg.on) conv_block((mn / n_tiles) * 2 + rank, cimg, cy0, cx0);
         const int cchunks = cg.C / kPK;
@@ -124,7 +132,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           if (!mbar_wait_warp(&empty_bar[s], ph ^ 1, kErrStageFree, abort_flag)) { ok = false; break; }
           const uint32_t lead_full = mapa_shared(smem_u32(&full_bar[s]), 0);
           if (elect_one()) {
-            if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * kPStage);  // both CTAs' bytes
+            if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * PC::kStage);  // both CTAs' bytes
             if (cg.on) {  // tap (ky, kx), channels c0..c0+63, shifted by the padding
               const int tap = kt / cchunks, c0 = (kt - tap * cchunks) * kPK;
               tma_load_4d_pair(stage_a(s), &tmap_a, lead_full, c0, cx0 + tap % 3 - 1, cy0 + tap / 3 - 1, cimg);
@@ -149,7 +157,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait_warp(&acce_bar[acc], aph ^ 1, kErrAccFree, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * kPN;
+        const uint32_t d_tmem = tmem_base + acc * kN;
         const int kt0 = k_begin(tile);
         for (int kt = kt0; kt < k_end(tile); ++kt, ++it) {
           const int s = it % kPStages;
@@ -174,7 +182,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   } else {
     // ---------------- epilogue (both CTAs): this CTA's 128 rows
     const int quarter = warp & 3;
-    constexpr int kChunks = kPN / 32 / (kPEpiWarps / 4);
+    constexpr int kChunks = kN / 32 / (kPEpiWarps / 4);
     const int half = (warp - 2) / 4;
     uint8_t* my_stage = stage_out + (warp - 2) * kPOut;
     const uint32_t lead_acce0 = mapa_shared(smem_u32(&acce_bar[0]), 0);
@@ -183,7 +191,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
       const int mn = tile / splits;
       int m0 = (mn / n_tiles) * 2 * kPM + rank * kPM;
-      const int n0 = (mn % n_tiles) * kPN;
+      const int n0 = (mn % n_tiles) * kN;
       const bool first_slice = tile % splits == 0;
       // conv: this warp's 32 rows are output row y0 + quarter, columns x0..x0+31
       int conv_row = 0;
@@ -201,7 +209,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       if (!got) break;
       tc_fence_after();
       const int row = m0 + quarter * 32 + lane;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kPN;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kN;
 #pragma unroll 1
       for (int cc = 0; cc < kChunks; ++cc) {
         const int c = half * kChunks + cc;
@@ -254,7 +262,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   cluster_sync();  // no CTA leaves while its peer may still signal it
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem_base, kPTmemCols);
+    tmem_dealloc_pair(tmem_base, PC::kTmemCols);
   }
 }
 
@@ -298,23 +306,51 @@ int launch_gemm_pair(const void* A, int lda, const void* W, int ldw, bool bf, Ge
   const CUtensorMapDataType dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap ta, tb;
   if (!make_tmap_2d(&ta, A, dt, 2, shp.M, shp.K, lda, kPM, kPK, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
-  if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, kPN / 2, kPK, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
-  const int m_tiles = (shp.M + 2 * kPM - 1) / (2 * kPM), n_tiles = (shp.N + kPN - 1) / kPN;
+  const int m_tiles = (shp.M + 2 * kPM - 1) / (2 * kPM);
   const int cap = (max_ctas > 0 ? max_ctas : num_sms()) / 2;
   const int splits = pair_splits(shp, mode == kEpiTmaAdd && ep.act == 0 && ep.rope_cols == 0, cap);
-  int pairs = m_tiles * n_tiles * splits;
-  if (pairs > cap) pairs = cap;
+  // 128-column tiles (S3CU_GEMM_N128=1, or =-1: when 256-column ones leave
+  // the last wave of pairs poorly filled and the narrower tiles fill it
+  // clearly better; no split-K).  Off by default: at one image (M = 5184)
+  // they measured slower despite the fuller waves, QKV 1098 -> 869 and fc1
+  // 1119 -> 882 TFLOP/s, so a tile's fixed costs outweigh the wave gain.
+  auto wave_eff = [&](long tiles) {
+    return static_cast<double>(tiles) / (static_cast<double>((tiles + cap - 1) / cap) * cap);
+  };
+  static const int n128 = [] {  // S3CU_GEMM_N128=0 / 1 / -1: never / always / by waves
+    const char* e = getenv("S3CU_GEMM_N128");
+    return e ? atoi(e) : 0;
+  }();
+  const long t256 = static_cast<long>(m_tiles) * ((shp.N + 255) / 256) * splits;
+  const long t128 = static_cast<long>(m_tiles) * ((shp.N + 127) / 128);
+  const bool narrow = splits == 1 && shp.N % 128 == 0 &&
+                      (n128 >= 0 ? n128 == 1 : wave_eff(t128) > wave_eff(t256) + 0.05);
+  ConvGeom off;
+  memset(&off, 0, sizeof(off));
+  if (narrow) {
+    using PC = PairCfg<128>;
+    if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, 64, kPK, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
+    const long pairs = t128 < cap ? t128 : cap;
+    const uint32_t idesc = make_idesc(bf ? 1u : 0u, 2 * kPM, 128);
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(gemm2_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, PC::kSmem);
+      attr = true;
+    }
+    return launch_pdl(gemm2_kernel<128>, static_cast<int>(2 * pairs), kPThreads, PC::kSmem, stream, ta, tb, to, shp,
+                      ep, idesc, mode, 1, off);
+  }
+  using PC = PairCfg<kPN>;
+  if (!make_tmap_2d(&tb, W, dt, 2, shp.N, shp.K, ldw, kPN / 2, kPK, CU_TENSOR_MAP_SWIZZLE_128B)) return kErrTma;
+  const long pairs = t256 < cap ? t256 : cap;
   const uint32_t idesc = make_idesc(bf ? 1u : 0u, 2 * kPM, kPN);
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
+    cudaFuncSetAttribute(gemm2_kernel<kPN>, cudaFuncAttributeMaxDynamicSharedMemorySize, PC::kSmem);
     attr = true;
   }
-  ConvGeom off;
-  memset(&off, 0, sizeof(off));
-  return launch_pdl(gemm2_kernel, 2 * pairs, kPThreads, kPSmem, stream, ta, tb, to, shp, ep, idesc, mode, splits,
-                    off);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+  return launch_pdl(gemm2_kernel<kPN>, static_cast<int>(2 * pairs), kPThreads, PC::kSmem, stream, ta, tb, to, shp,
+                    ep, idesc, mode, splits, off);
 }
 
 int launch_conv3x3_implicit(const void* x, const void* w, int ab_dtype, int n, int H, int W, int C, int OC,
@@ -355,11 +391,11 @@ int launch_conv3x3_implicit(const void* x, const void* w, int ab_dtype, int n, i
   const uint32_t idesc = make_idesc(bf ? 1u : 0u, 2 * kPM, kPN);
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
+    cudaFuncSetAttribute(gemm2_kernel<kPN>, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg<kPN>::kSmem);
     attr = true;
   }
   count_launches(1);
-  return launch_pdl(gemm2_kernel, 2 * pairs, kPThreads, kPSmem, stream, ta, tb, to, shp, ep, idesc, kEpiTmaStore,
+  return launch_pdl(gemm2_kernel<kPN>, 2 * pairs, kPThreads, PairCfg<kPN>::kSmem, stream, ta, tb, to, shp, ep, idesc, kEpiTmaStore,
                     1, cg);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
