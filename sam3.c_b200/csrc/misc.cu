@@ -109,21 +109,34 @@ __global__ void layernorm_rows_generic(const void* __restrict__ x, void* __restr
   }
 }
 
+#ifndef S3_PDL_LN
+#define S3_PDL_LN 1
+#endif
+// S3_PDL_LN: LayerNorm launched with programmatic dependent launch behind a
+// GEMM (which then triggers its dependents after set-up)
+#if S3_PDL_LN
+#define S3_LN_LAUNCH(...) launch_pdl(__VA_ARGS__, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period)
+#else
+#define S3_LN_LAUNCH(...) \
+  (__VA_ARGS__<<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols, map, period), \
+   cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch)
+#endif
+
 template <int TI, int TO>
 int ln_dispatch(const void* x, void* y, const float* g, const float* b, int rows, int cols,
                 const int* map, int period, cudaStream_t st) {
   const int blocks = (rows + 7) / 8;
   const bool al = (cols % 128 == 0);
   if (al && cols == 1024)
-    return launch_pdl(layernorm_rows<TI, TO, 8>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
+    return S3_LN_LAUNCH(layernorm_rows<TI, TO, 8>);
   else if (al && cols == 512)
-    return launch_pdl(layernorm_rows<TI, TO, 4>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
+    return S3_LN_LAUNCH(layernorm_rows<TI, TO, 4>);
   else if (al && cols == 256)
-    return launch_pdl(layernorm_rows<TI, TO, 2>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
+    return S3_LN_LAUNCH(layernorm_rows<TI, TO, 2>);
   else if (al && cols == 128)
-    return launch_pdl(layernorm_rows<TI, TO, 1>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
+    return S3_LN_LAUNCH(layernorm_rows<TI, TO, 1>);
   else if (al && cols == 2048)
-    return launch_pdl(layernorm_rows<TI, TO, 16>, blocks, 256, 0, st, x, y, g, b, rows, cols, map, period);
+    return S3_LN_LAUNCH(layernorm_rows<TI, TO, 16>);
   else if (!map)
     layernorm_rows_generic<TI, TO><<<blocks, 256, 0, st>>>(x, y, g, b, rows, cols);
   else
