@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(GemmCfg<kBMode>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-#if !defined(S3_PDL_LN) || S3_PDL_LN
+#if defined(S3_PDL_LN) && S3_PDL_LN
   griddep_launch();  // a LayerNorm launched behind this GEMM may start (it waits for completion)
 #endif
   griddep_wait();  // set-up done; from here on the inputs of the previous kernel are read

@@ -110,7 +110,7 @@ __global__ void layernorm_rows_generic(const void* __restrict__ x, void* __restr
 }
 
 #ifndef S3_PDL_LN
-#define S3_PDL_LN 1
+#define S3_PDL_LN 0
 #endif
 // S3_PDL_LN: LayerNorm launched with programmatic dependent launch behind a
 // GEMM (which then triggers its dependents after set-up)
